@@ -1,0 +1,415 @@
+#!/usr/bin/env python3
+"""Headline benchmark: copy GB/s (read + write) of the DataCopyExt strided gather on B200.
+
+Workload: fp32 source [4096, 4096]; copy the column slab
+[all rows, cols 1024..2047] into a contiguous [4096, 1024] destination, i.e.
+DataCopyExt{blockCount=4096, blockLen=128x32 B, srcStride=384x32 B, dstStride=0}.
+Algorithmic bytes per gather: 16 MiB read + 16 MiB written.
+
+One *step* gathers from each of 16 rotating buffer sets (512 MiB touched per
+step, > the 126 MB L2), so every launch reads cold data; the step's 16 launches
+are captured once in a CUDA graph and the graph is replayed K times between two
+CUDA events on the launching stream (host launch overhead stays out of the
+device timing).  `value` = bytes moved by all ranks / max-over-ranks time.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl dcopy|reference]
+
+`--impl reference` times the reference's CPU path instead: the C restatement of
+its tiling semantics (oracle/, the reference's Ascend C CPU-debug build cannot
+be built offline) on all host threads, same workload and metric.
+Multi-GPU (torchrun): one rank per GPU, every rank runs the same workload on its
+own GPU with no data-path collective (weak scaling).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "data-copy_b200"))
+sys.path.insert(0, str(ROOT))
+
+MIB = 1 << 20
+ROWS, COLS, C0, C1 = 4096, 4096, 1024, 2048
+BLOCK_LEN = (C1 - C0) * 4          # 4096 B = 128 x 32 B
+SRC_GAP = (COLS - (C1 - C0)) * 4   # 12288 B = 384 x 32 B
+BYTES_PER_GATHER = 2 * ROWS * BLOCK_LEN  # 16 MiB read + 16 MiB written
+SETS = 16
+METRIC = "copy GB/s (R+W) vs 8 TB/s HBM peak by burst/stride; aggregate at 1/2/4/8 GPUs"
+WORKLOAD = ("config2_strided_gather: fp32 [4096,4096] cols 1024..2047 -> [4096,1024]; "
+            "DataCopyExt blockCount=4096 blockLen=128x32B srcStride=384x32B dstStride=0")
+NVML_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+                0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+                0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+                0x100: "display_clock_setting"}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["dcopy", "reference"], default="dcopy")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="skip the secondary measurements (sweep, NZ, transpose)")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------- helpers
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def load_traffic():
+    p = ROOT / "profiles" / "ncu_traffic.json"
+    if p.exists():
+        return json.loads(p.read_text())
+    return {}
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML while the timed region runs."""
+
+    def __init__(self, device_index: int, period_s: float = 0.01):
+        self.samples = []
+        self.reasons = 0
+        self.max_mhz = None
+        self.ok = False
+        self._stop = threading.Event()
+        self._period = period_s
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:  # NVML missing: clocks reported as unavailable
+            self._nvml = None
+
+    def _run(self):
+        n = self._nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(n.nvmlDeviceGetClockInfo(self._h, n.NVML_CLOCK_SM))
+                try:
+                    r = n.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                except AttributeError:
+                    r = n.nvmlDeviceGetCurrentClocksThrottleReasons(self._h)
+                self.reasons |= int(r)
+            except Exception:
+                pass
+            time.sleep(self._period)
+
+    def __enter__(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ok:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"],
+                    "samples": len(self.samples)}
+        names = [v for k, v in NVML_REASONS.items() if self.reasons & k and k != 0x1]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": names, "samples": len(self.samples)}
+
+
+def cpu_baseline_gather(seconds: float = 8.0, threads=None):
+    """The oracle's DataCopyExt gap copy (C, pthreads) on config 2, host memory."""
+    import numpy as np
+    from oracle import oracle as O
+    O.build()
+    threads = threads or os.cpu_count() or 1
+    src = np.random.default_rng(1).random((ROWS, COLS), dtype=np.float32)
+    dst = np.empty((ROWS, C1 - C0), dtype=np.float32)
+    view = src[:, C0:]
+    O.copy_ext(dst, view, ROWS, BLOCK_LEN, SRC_GAP, 0, threads=threads)  # warm-up
+    ref = src[:, C0:C1]
+    assert (dst == ref).all(), "oracle gather mismatch"
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        O.copy_ext(dst, view, ROWS, BLOCK_LEN, SRC_GAP, 0, threads=threads)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return BYTES_PER_GATHER * reps / el / 1e9, reps, el, threads
+
+
+# ---------------------------------------------------------------------------- dcopy arm
+
+def run_dcopy(args, rank, world, local_rank):
+    import torch
+    import dcopy
+
+    torch.cuda.set_device(local_rank)
+    dcopy.lib()
+    dev = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist_mod
+        dist = dist_mod
+
+    def barrier():
+        if dist is not None:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize()
+
+    g = torch.Generator(device=dev).manual_seed(1 + rank)
+    base = torch.rand(ROWS, COLS, generator=g, device=dev)
+    srcs = [base.clone() for _ in range(SETS)]
+    dsts = [torch.empty(ROWS, C1 - C0, device=dev) for _ in range(SETS)]
+    stream = torch.cuda.current_stream()
+
+    def one_step():
+        for i in range(SETS):
+            dcopy.copy_ext_32b(dsts[i], srcs[i][:, C0:], ROWS, BLOCK_LEN // 32, SRC_GAP // 32, 0)
+
+    # Correctness first: bit-exact against the strided view before anything is timed.
+    one_step()
+    torch.cuda.synchronize()
+    ref = base[:, C0:C1].contiguous().view(torch.int32)
+    for d in dsts:
+        assert torch.equal(d.view(torch.int32), ref), "gather mismatch"
+
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+        one_step()
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    barrier()
+
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        barrier()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        ev1.record(stream)
+        ev1.synchronize()
+        barrier()
+    ms = ev0.elapsed_time(ev1)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    launches = args.steps * SETS
+    bytes_rank = BYTES_PER_GATHER * launches
+    value = bytes_rank * world / (ms_max / 1e3) / 1e9
+    launch_ms = ms / launches
+    achieved = BYTES_PER_GATHER / (launch_ms / 1e3) / 1e9
+    peak, peak_kind = load_peaks()
+    traffic = load_traffic().get("strided_copy_kernel/config2")
+
+    # End to end through the public call with host buffers: pinned H2D of the full
+    # source, the gather, D2H of the destination, every step.
+    e2e_steps = max(3, min(args.steps, 30))
+    h_src = base.cpu().pin_memory()
+    h_dst = torch.empty(ROWS, C1 - C0).pin_memory()
+    d_src = torch.empty_like(base)
+    d_dst = torch.empty(ROWS, C1 - C0, device=dev)
+
+    def e2e_step():
+        d_src.copy_(h_src, non_blocking=True)
+        dcopy.copy_ext_32b(d_dst, d_src[:, C0:], ROWS, BLOCK_LEN // 32, SRC_GAP // 32, 0)
+        h_dst.copy_(d_dst, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    e1.synchronize()
+    assert torch.equal(h_dst.view(torch.int32), h_src[:, C0:C1].contiguous().view(torch.int32))
+    te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if dist is not None:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = BYTES_PER_GATHER * e2e_steps * world / (float(te.item()) / 1e3) / 1e9
+
+    secondary = None
+    if not args.no_secondary and rank == 0:
+        secondary = run_secondary(torch, dcopy, dev)
+
+    line = None
+    if rank == 0:
+        cpu = None
+        if world == 1:
+            v, reps, el, thr = cpu_baseline_gather()
+            cpu = {"value": round(v, 3), "unit": "GB/s", "cores": thr, "kind": "port",
+                   "sample": f"config 2 gather on host memory, {reps} reps in {el:.1f} s "
+                             f"(oracle/dcopy_oracle.c oracle_copy_ext_mt, {thr} threads)"}
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+            "data": "synthetic (torch.rand fp32 from seed 1+rank; copies are value-agnostic)",
+            "config": {"workload": WORKLOAD, "gathers_per_step": SETS,
+                       "bytes_per_gather": BYTES_PER_GATHER,
+                       "l2": "inputs larger than L2: 16 rotating buffer sets, 512 MiB touched "
+                             "per step vs 126 MB L2",
+                       "timing": "CUDA graph of one step replayed K times between CUDA events",
+                       "parallelism": f"independent per-GPU copies x{world} (no collective)"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": traffic, "kernel": "strided_copy_kernel<uint4,4>",
+                         "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_value, 3), "unit": "GB/s",
+                    "h2d_bytes_per_step": ROWS * COLS * 4,
+                    "d2h_bytes_per_step": ROWS * (C1 - C0) * 4,
+                    "steps": e2e_steps,
+                    "path": "pinned H2D of the full source, dcopy_copy_ext_32b, D2H of the "
+                            "destination"},
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
+        }
+        if secondary is not None:
+            line["secondary"] = secondary
+    return line
+
+
+def _time_graph(torch, fn, reps=10, warm=3):
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, capture_error_mode="thread_local"):
+        fn()
+    for _ in range(warm):
+        g.replay()
+    s = torch.cuda.current_stream()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(s)
+    for _ in range(reps):
+        g.replay()
+    b.record(s)
+    b.synchronize()
+    return a.elapsed_time(b) / reps
+
+
+def run_secondary(torch, dcopy, dev):
+    """Short measurements of the other BASELINE configs (GB/s, R+W, one GPU)."""
+    out = {}
+    # Config 3 sweep: 256 MiB moved per point (> L2); int32 index-filled source.
+    sweep = {}
+    moved = 256 * MIB
+    src = torch.empty((moved * 17) // 4, dtype=torch.int32, device=dev)
+    dst = torch.empty(moved // 4, dtype=torch.int32, device=dev)
+    for blen in (32, 64, 128, 512, 4096, 65536):
+        for gx in (0, 1, 4, 16):
+            count = moved // blen
+            ms = _time_graph(torch, lambda: dcopy.copy_ext(dst, src, count, blen, gx * blen, 0),
+                             reps=5, warm=2)
+            sweep[f"{blen}B_gap{gx}x"] = round(2 * moved / (ms / 1e3) / 1e9, 1)
+    out["config3_sweep_GBps"] = sweep
+    del src, dst
+    # Config 4: ND<->NZ fp16 [16, 4096, 4096] (512 MiB each way, > L2).
+    shape = [16, 4096, 4096]
+    nd = torch.empty(shape, dtype=torch.float16, device=dev).normal_()
+    nz = torch.empty(16, 256, 256, 16, 16, dtype=torch.float16, device=dev)
+    nbytes = nd.numel() * 2
+    ms = _time_graph(torch, lambda: dcopy.nd_to_nz(nz, nd, shape, 2, 16), reps=10)
+    ms2 = _time_graph(torch, lambda: dcopy.nz_to_nd(nd, nz, shape, 2, 16), reps=10)
+    out["config4_nd_to_nz_GBps"] = round(2 * nbytes / (ms / 1e3) / 1e9, 1)
+    out["config4_nz_to_nd_GBps"] = round(2 * nbytes / (ms2 / 1e3) / 1e9, 1)
+    del nd, nz
+    # Standalone transpose at the 64 MiB maximum (rows 4088 x cols 4104 int32).
+    rows, cols = 4088, 4104
+    x = torch.empty(rows * cols, dtype=torch.int32, device=dev)
+    ys = [torch.empty_like(x) for _ in range(4)]
+    t = dcopy.plan_tiling(rows, cols, 240, 1)
+    xs = [x] + [torch.empty_like(x) for _ in range(3)]
+
+    def four():
+        for i in range(4):
+            dcopy.datacopy_large(xs[i], ys[i], t)
+    ms = _time_graph(torch, four, reps=5) / 4
+    out["standalone_large_64MiB_GBps"] = round(2 * x.numel() * 4 / (ms / 1e3) / 1e9, 1)
+    # Config 1: contiguous fp16 512 KiB (L2-resident: latency, not bandwidth).
+    a = torch.empty(262144, dtype=torch.float16, device=dev)
+    b = torch.empty_like(a)
+    ms = _time_graph(torch, lambda: dcopy.copy_ext_32b(b, a, 128, 128, 0, 0), reps=50)
+    out["config1_contiguous_512KiB_us"] = round(ms * 1e3, 2)
+    return out
+
+
+# ---------------------------------------------------------------------------- reference arm
+
+def run_reference(args):
+    threads = os.cpu_count() or 1
+    import numpy as np
+    from oracle import oracle as O
+    O.build()
+    src = np.random.default_rng(1).random((ROWS, COLS), dtype=np.float32)
+    dst = np.empty((ROWS, C1 - C0), dtype=np.float32)
+    view = src[:, C0:]
+    for _ in range(max(args.warmup, 3)):
+        O.copy_ext(dst, view, ROWS, BLOCK_LEN, SRC_GAP, 0, threads=threads)
+    assert (dst == src[:, C0:C1]).all()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.copy_ext(dst, view, ROWS, BLOCK_LEN, SRC_GAP, 0, threads=threads)
+    el = time.perf_counter() - t0
+    value = BYTES_PER_GATHER * args.steps / el / 1e9
+    sample = (f"full config 2 gather per step on host memory (oracle_copy_ext_mt, the C "
+              f"restatement of the reference's DataCopyExt semantics), {threads} threads")
+    return {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(el * 1e3 / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "config": {"workload": WORKLOAD},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference(args)), flush=True)
+        return 0
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        line = run_dcopy(args, rank, world, local_rank)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,377 @@
+// GM->GM copies: contiguous bursts, DataCopyExtParams strided bursts and the
+// DataCopyNddma N-D box.
+//
+// Design (HBM-bound byte movement, no tensor cores):
+//  * every thread keeps U independent loads in flight before its stores, and
+//    the grid is a multiple of the SM count (8 CTAs of 256 threads per SM), so
+//    each SM holds 2048 x U x 16 B of reads in flight -- well above the
+//    bandwidth-latency product of one SM's share of HBM3e;
+//  * the widest element (16, 8, 4, 2 or 1 bytes) that divides both base
+//    addresses, the burst length and both pitches is chosen on the host, so
+//    16-byte aligned bursts move as 128-bit loads/stores and anything else
+//    still moves bit-exactly;
+//  * a strided copy is a flat index over blockCount x elements-per-burst,
+//    split with one multiply-high division (FastDiv) per element.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "copy.cuh"
+
+namespace dcopy {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kCtasPerSm = 8;
+
+template <typename T>
+struct Unroll {
+  static constexpr int value = sizeof(T) >= 16 ? 4 : (sizeof(T) >= 8 ? 8 : 8);
+};
+
+// Contiguous copy of `head` bytes, then `n` elements of T, then `tail` bytes.
+// dst + head and src + head are aligned to sizeof(T).
+template <typename T, int U>
+__global__ void __launch_bounds__(kThreads) linear_copy_kernel(uint8_t *__restrict__ dst,
+                                                               const uint8_t *__restrict__ src,
+                                                               uint32_t head, uint64_t n,
+                                                               uint32_t tail) {
+  T *__restrict__ d = reinterpret_cast<T *>(dst + head);
+  const T *__restrict__ s = reinterpret_cast<const T *>(src + head);
+  const uint64_t tile = (uint64_t)kThreads * U;
+  for (uint64_t base = (uint64_t)blockIdx.x * tile + threadIdx.x; base < n;
+       base += (uint64_t)gridDim.x * tile) {
+    T v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint64_t i = base + (uint64_t)u * kThreads;
+      if (i < n) v[u] = ld_stream(s + i);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint64_t i = base + (uint64_t)u * kThreads;
+      if (i < n) d[i] = v[u];
+    }
+  }
+  if (blockIdx.x == 0) {
+    if (threadIdx.x < head) dst[threadIdx.x] = src[threadIdx.x];
+    if (threadIdx.x < tail) {
+      const uint64_t o = head + n * sizeof(T) + threadIdx.x;
+      dst[o] = src[o];
+    }
+  }
+}
+
+// Load-only pass over n elements of 16 bytes (plus bytes of head/tail): the
+// reads are kept (volatile) and nothing is written.
+__global__ void __launch_bounds__(kThreads) linear_load_kernel(const uint8_t *__restrict__ src,
+                                                               uint32_t head, uint64_t n,
+                                                               uint32_t tail) {
+  const uint8_t *s = src + head;
+  const uint64_t tile = (uint64_t)kThreads * 4;
+  for (uint64_t base = (uint64_t)blockIdx.x * tile + threadIdx.x; base < n;
+       base += (uint64_t)gridDim.x * tile) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const uint64_t i = base + (uint64_t)u * kThreads;
+      if (i < n) (void)ld_keep_v4(s + i * 16);
+    }
+  }
+  if (blockIdx.x == 0) {
+    if (threadIdx.x < head) (void)ld_keep_u8(src + threadIdx.x);
+    if (threadIdx.x < tail) (void)ld_keep_u8(s + n * 16 + threadIdx.x);
+  }
+}
+
+// Strided copy: element i of the flat [rows x epr] index space moves from
+// src + row*src_pitch + col*sizeof(T) to dst + row*dst_pitch + col*sizeof(T).
+template <typename T, int U>
+__global__ void __launch_bounds__(kThreads) strided_copy_kernel(uint8_t *__restrict__ dst,
+                                                                const uint8_t *__restrict__ src,
+                                                                uint32_t total, FastDiv epr,
+                                                                uint64_t src_pitch,
+                                                                uint64_t dst_pitch) {
+  const uint32_t stride = gridDim.x * kThreads * U;
+  for (uint32_t base = blockIdx.x * kThreads * U + threadIdx.x; base < total; base += stride) {
+    T v[U];
+    uint64_t doff[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t i = base + u * kThreads;
+      if (i < total) {
+        const uint32_t r = epr.div(i);
+        const uint32_t c = i - r * epr.d;
+        v[u] = ld_stream(reinterpret_cast<const T *>(src + (uint64_t)r * src_pitch) + c);
+        doff[u] = (uint64_t)r * dst_pitch + (uint64_t)c * sizeof(T);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t i = base + u * kThreads;
+      if (i < total) *reinterpret_cast<T *>(dst + doff[u]) = v[u];
+    }
+  }
+}
+
+unsigned grid_for(uint64_t work_items, uint64_t items_per_cta) {
+  const uint64_t need = (work_items + items_per_cta - 1) / items_per_cta;
+  const uint64_t cap = (uint64_t)sm_count() * kCtasPerSm;
+  return (unsigned)std::max<uint64_t>(1, std::min(need, cap));
+}
+
+uint32_t widest(uint64_t x) {
+  if (x % 16 == 0) return 16;
+  if (x % 8 == 0) return 8;
+  if (x % 4 == 0) return 4;
+  if (x % 2 == 0) return 2;
+  return 1;
+}
+
+template <typename T>
+int launch_linear(uint8_t *dst, const uint8_t *src, uint64_t bytes, cudaStream_t s) {
+  constexpr int U = Unroll<T>::value;
+  const uint64_t w = sizeof(T);
+  uint64_t head = (w - ((uintptr_t)dst % w)) % w;
+  if (head > bytes) head = bytes;
+  const uint64_t n = (bytes - head) / w;
+  const uint32_t tail = (uint32_t)(bytes - head - n * w);
+  linear_copy_kernel<T, U><<<grid_for(std::max<uint64_t>(n, 1), (uint64_t)kThreads * U), kThreads,
+                             0, s>>>(dst, src, (uint32_t)head, n, tail);
+  return check_launch("linear_copy_kernel");
+}
+
+template <typename T>
+int launch_strided(uint8_t *dst, const uint8_t *src, uint64_t rows, uint64_t row_bytes,
+                   uint64_t src_pitch, uint64_t dst_pitch, cudaStream_t s) {
+  constexpr int U = Unroll<T>::value;
+  const uint64_t epr = row_bytes / sizeof(T);
+  // Keep the flat index (and its grid-stride increments) inside 32 bits.
+  const uint64_t max_rows = std::max<uint64_t>(1, (uint64_t(1) << 30) / epr);
+  const FastDiv div((uint32_t)epr);
+  for (uint64_t r0 = 0; r0 < rows; r0 += max_rows) {
+    const uint64_t nr = std::min(max_rows, rows - r0);
+    const uint32_t total = (uint32_t)(nr * epr);
+    strided_copy_kernel<T, U><<<grid_for(total, (uint64_t)kThreads * U), kThreads, 0, s>>>(
+        dst + r0 * dst_pitch, src + r0 * src_pitch, total, div, src_pitch, dst_pitch);
+    int rc = check_launch("strided_copy_kernel");
+    if (rc) return rc;
+  }
+  return DCOPY_OK;
+}
+
+}  // namespace
+
+int copy_linear(void *dst, const void *src, uint64_t bytes, cudaStream_t s) {
+  if (!bytes) return DCOPY_OK;
+  uint8_t *d = static_cast<uint8_t *>(dst);
+  const uint8_t *sp = static_cast<const uint8_t *>(src);
+  const uint64_t delta = (uint64_t)((uintptr_t)d - (uintptr_t)sp);
+  switch (widest(delta)) {
+    case 16: return launch_linear<uint4>(d, sp, bytes, s);
+    case 8: return launch_linear<uint2>(d, sp, bytes, s);
+    case 4: return launch_linear<uint32_t>(d, sp, bytes, s);
+    case 2: return launch_linear<uint16_t>(d, sp, bytes, s);
+    default: return launch_linear<uint8_t>(d, sp, bytes, s);
+  }
+}
+
+int load_linear(const void *src, uint64_t bytes, cudaStream_t s) {
+  if (!bytes) return DCOPY_OK;
+  const uint8_t *sp = static_cast<const uint8_t *>(src);
+  uint64_t head = (16 - ((uintptr_t)sp % 16)) % 16;
+  if (head > bytes) head = bytes;
+  const uint64_t n = (bytes - head) / 16;
+  const uint32_t tail = (uint32_t)(bytes - head - n * 16);
+  linear_load_kernel<<<grid_for(std::max<uint64_t>(n, 1), (uint64_t)kThreads * 4), kThreads, 0,
+                       s>>>(sp, (uint32_t)head, n, tail);
+  return check_launch("linear_load_kernel");
+}
+
+int copy2d(void *dst, const void *src, uint64_t rows, uint64_t row_bytes, uint64_t src_pitch,
+           uint64_t dst_pitch, cudaStream_t s) {
+  if (!rows || !row_bytes) return DCOPY_OK;
+  if (rows == 1 || (src_pitch == row_bytes && dst_pitch == row_bytes))
+    return copy_linear(dst, src, rows * row_bytes, s);
+  uint8_t *d = static_cast<uint8_t *>(dst);
+  const uint8_t *sp = static_cast<const uint8_t *>(src);
+  uint32_t w = widest((uintptr_t)d | (uintptr_t)sp | row_bytes | src_pitch | dst_pitch);
+  if (row_bytes / w >= (uint64_t(1) << 30)) {  // gigantic bursts: one linear copy each
+    for (uint64_t r = 0; r < rows; ++r) {
+      int rc = copy_linear(d + r * dst_pitch, sp + r * src_pitch, row_bytes, s);
+      if (rc) return rc;
+    }
+    return DCOPY_OK;
+  }
+  switch (w) {
+    case 16: return launch_strided<uint4>(d, sp, rows, row_bytes, src_pitch, dst_pitch, s);
+    case 8: return launch_strided<uint2>(d, sp, rows, row_bytes, src_pitch, dst_pitch, s);
+    case 4: return launch_strided<uint32_t>(d, sp, rows, row_bytes, src_pitch, dst_pitch, s);
+    case 2: return launch_strided<uint16_t>(d, sp, rows, row_bytes, src_pitch, dst_pitch, s);
+    default: return launch_strided<uint8_t>(d, sp, rows, row_bytes, src_pitch, dst_pitch, s);
+  }
+}
+
+// ---- N-D box copy --------------------------------------------------------------
+
+namespace {
+
+constexpr int kMaxNd = 5;
+
+struct NdDesc {
+  int ndim;
+  uint32_t size[kMaxNd];
+  FastDiv div[kMaxNd];
+  int64_t ss[kMaxNd];  // elements
+  int64_t ds[kMaxNd];  // elements
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) nd_copy_kernel(uint8_t *__restrict__ dst,
+                                                           const uint8_t *__restrict__ src,
+                                                           uint32_t total, NdDesc d) {
+  const T *s = reinterpret_cast<const T *>(src);
+  T *o = reinterpret_cast<T *>(dst);
+  for (uint32_t i = blockIdx.x * kThreads + threadIdx.x; i < total; i += gridDim.x * kThreads) {
+    uint32_t rem = i;
+    int64_t so = 0, dof = 0;
+#pragma unroll
+    for (int k = kMaxNd - 1; k >= 0; --k) {
+      if (k < d.ndim) {
+        const uint32_t q = d.div[k].div(rem);
+        const uint32_t idx = rem - q * d.size[k];
+        so += (int64_t)idx * d.ss[k];
+        dof += (int64_t)idx * d.ds[k];
+        rem = q;
+      }
+    }
+    o[dof] = ld_stream(s + so);
+  }
+}
+
+template <typename T>
+int launch_nd(uint8_t *dst, const uint8_t *src, const NdDesc &desc0, cudaStream_t s) {
+  // Chunk the outermost dimension so the flat index stays below 2^30.
+  uint64_t inner = 1;
+  for (int k = 1; k < desc0.ndim; ++k) inner *= desc0.size[k];
+  if (inner >= (uint64_t(1) << 30))
+    return set_error(DCOPY_ERR_UNSUPPORTED, "copy_nd: inner box of %llu elements is too large",
+                     (unsigned long long)inner);
+  const uint64_t chunk = std::max<uint64_t>(1, (uint64_t(1) << 30) / inner);
+  for (uint64_t o0 = 0; o0 < desc0.size[0]; o0 += chunk) {
+    NdDesc d = desc0;
+    d.size[0] = (uint32_t)std::min<uint64_t>(chunk, desc0.size[0] - o0);
+    d.div[0] = FastDiv(d.size[0]);
+    const uint32_t total = (uint32_t)(d.size[0] * inner);
+    nd_copy_kernel<T><<<grid_for(total, kThreads * 4), kThreads, 0, s>>>(
+        dst + (int64_t)o0 * desc0.ds[0] * (int64_t)sizeof(T),
+        src + (int64_t)o0 * desc0.ss[0] * (int64_t)sizeof(T), total, d);
+    int rc = check_launch("nd_copy_kernel");
+    if (rc) return rc;
+  }
+  return DCOPY_OK;
+}
+
+}  // namespace
+
+}  // namespace dcopy
+
+using namespace dcopy;
+
+extern "C" int dcopy_copy_ext(void *dst, const void *src, const DcopyExtParams *p,
+                              dcopy_stream_t stream) {
+  DCOPY_API_BEGIN
+  if (!p) return set_error(DCOPY_ERR_PARAM_INVALID, "copy_ext: params is NULL");
+  const uint64_t count = p->blockCount, len = p->blockLen;
+  if (!count || !len) return DCOPY_OK;
+  const uint64_t sp = len + p->srcStride, dp = len + p->dstStride;
+  if (p->srcStride > (1ull << 48) || p->dstStride > (1ull << 48))
+    return set_error(DCOPY_ERR_PARAM_INVALID, "copy_ext: stride beyond 2^48 bytes");
+  const uint64_t src_span = (count - 1) * sp + len, dst_span = (count - 1) * dp + len;
+  int rc = check_device_span(src, src_span, "copy_ext src");
+  if (!rc) rc = check_device_span(dst, dst_span, "copy_ext dst");
+  if (!rc) rc = check_disjoint(src, src_span, dst, dst_span, "copy_ext");
+  if (rc) return rc;
+  return copy2d(dst, src, count, len, sp, dp, reinterpret_cast<cudaStream_t>(stream));
+  DCOPY_API_END
+}
+
+extern "C" int dcopy_copy_ext_32b(void *dst, const void *src, uint32_t blockCount,
+                                  uint32_t blockLen32, uint32_t srcStride32, uint32_t dstStride32,
+                                  dcopy_stream_t stream) {
+  const uint64_t len = (uint64_t)blockLen32 * 32u;
+  if (len > 0xFFFFFFFFull) {
+    clear_error();
+    return set_error(DCOPY_ERR_PARAM_INVALID, "copy_ext_32b: blockLen %u x 32 B exceeds 4 GiB",
+                     blockLen32);
+  }
+  DcopyExtParams p{blockCount, (uint32_t)len, (uint64_t)srcStride32 * 32u,
+                   (uint64_t)dstStride32 * 32u};
+  return dcopy_copy_ext(dst, src, &p, stream);
+}
+
+extern "C" int dcopy_copy_nd(void *dst, const void *src, int ndim, const uint64_t *sizes,
+                             const int64_t *src_strides, const int64_t *dst_strides,
+                             uint32_t elem_bytes, dcopy_stream_t stream) {
+  DCOPY_API_BEGIN
+  if (ndim < 1 || ndim > kMaxNd || !sizes || !src_strides || !dst_strides)
+    return set_error(DCOPY_ERR_PARAM_INVALID, "copy_nd: ndim must be 1..%d with non-NULL arrays",
+                     kMaxNd);
+  if (elem_bytes != 1 && elem_bytes != 2 && elem_bytes != 4 && elem_bytes != 8 &&
+      elem_bytes != 16)
+    return set_error(DCOPY_ERR_DATATYPE_INVALID, "copy_nd: elem_bytes %u not in {1,2,4,8,16}",
+                     elem_bytes);
+  uint64_t total = 1;
+  uint64_t src_last = 0, dst_last = 0;  // element offset of the last element
+  for (int k = 0; k < ndim; ++k) {
+    if (src_strides[k] < 0 || dst_strides[k] < 0)
+      return set_error(DCOPY_ERR_PARAM_INVALID, "copy_nd: negative stride in dim %d", k);
+    if (dst_strides[k] == 0 && sizes[k] > 1)
+      return set_error(DCOPY_ERR_PARAM_INVALID,
+                       "copy_nd: dst stride 0 in dim %d would write one element twice", k);
+    if (sizes[k] > 0xFFFFFFFFull)
+      return set_error(DCOPY_ERR_UNSUPPORTED, "copy_nd: dim %d size beyond 2^32", k);
+    total *= sizes[k];
+    if (sizes[k]) {
+      src_last += (sizes[k] - 1) * (uint64_t)src_strides[k];
+      dst_last += (sizes[k] - 1) * (uint64_t)dst_strides[k];
+    }
+  }
+  if (!total) return DCOPY_OK;
+  const uint64_t src_span = (src_last + 1) * elem_bytes, dst_span = (dst_last + 1) * elem_bytes;
+  int rc = check_device_span(src, src_span, "copy_nd src");
+  if (!rc) rc = check_device_span(dst, dst_span, "copy_nd dst");
+  if (!rc) rc = check_disjoint(src, src_span, dst, dst_span, "copy_nd");
+  if (rc) return rc;
+  if (((uintptr_t)dst | (uintptr_t)src) % elem_bytes)
+    return set_error(DCOPY_ERR_PARAM_INVALID, "copy_nd: buffers not aligned to elem_bytes %u",
+                     elem_bytes);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // Unit-stride innermost dim with <= 2 dims total: a burst copy.
+  if (ndim <= 2 && src_strides[ndim - 1] == 1 && dst_strides[ndim - 1] == 1) {
+    const uint64_t rows = ndim == 2 ? sizes[0] : 1;
+    const uint64_t row_bytes = sizes[ndim - 1] * elem_bytes;
+    const uint64_t sp = ndim == 2 ? (uint64_t)src_strides[0] * elem_bytes : row_bytes;
+    const uint64_t dp = ndim == 2 ? (uint64_t)dst_strides[0] * elem_bytes : row_bytes;
+    if (sp >= row_bytes && dp >= row_bytes)
+      return copy2d(dst, src, rows, row_bytes, sp, dp, s);
+  }
+  NdDesc d{};
+  d.ndim = ndim;
+  for (int k = 0; k < ndim; ++k) {
+    d.size[k] = (uint32_t)sizes[k];
+    d.div[k] = FastDiv(d.size[k]);
+    d.ss[k] = src_strides[k];
+    d.ds[k] = dst_strides[k];
+  }
+  uint8_t *o = static_cast<uint8_t *>(dst);
+  const uint8_t *i = static_cast<const uint8_t *>(src);
+  switch (elem_bytes) {
+    case 16: return launch_nd<uint4>(o, i, d, s);
+    case 8: return launch_nd<uint2>(o, i, d, s);
+    case 4: return launch_nd<uint32_t>(o, i, d, s);
+    case 2: return launch_nd<uint16_t>(o, i, d, s);
+    default: return launch_nd<uint8_t>(o, i, d, s);
+  }
+  DCOPY_API_END
+}

@@ -1,0 +1,147 @@
+// Status reporting, buffer checks and device queries shared by every entry point.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace dcopy {
+namespace {
+
+thread_local char g_message[1024] = {0};
+
+typedef CUresult (*PfnPointerGetAttributes)(unsigned int, CUpointer_attribute *, void **,
+                                            CUdeviceptr);
+
+PfnPointerGetAttributes pointer_attrs_fn() {
+  static PfnPointerGetAttributes fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuPointerGetAttributes", &p, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PfnPointerGetAttributes>(p);
+  });
+  return fn;
+}
+
+bool checks_enabled() {
+  static const bool enabled = [] {
+    const char *v = std::getenv("DCOPY_CHECK_POINTERS");
+    return !(v && v[0] == '0');
+  }();
+  return enabled;
+}
+
+}  // namespace
+
+int set_error(int code, const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  std::vsnprintf(g_message, sizeof(g_message), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+void clear_error() { g_message[0] = 0; }
+
+int cuda_fail(cudaError_t err, const char *what) {
+  return set_error(DCOPY_ERR_CUDA, "%s failed: %s (%s)", what, cudaGetErrorName(err),
+                   cudaGetErrorString(err));
+}
+
+int check_launch(const char *kernel) {
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess)
+    return set_error(DCOPY_ERR_CUDA, "launch of %s failed: %s (%s)", kernel,
+                     cudaGetErrorName(err), cudaGetErrorString(err));
+  return DCOPY_OK;
+}
+
+int check_device_span(const void *ptr, uint64_t bytes, const char *name) {
+  if (bytes == 0) return DCOPY_OK;
+  if (!ptr) return set_error(DCOPY_ERR_PARAM_INVALID, "%s is NULL for %llu bytes", name,
+                             (unsigned long long)bytes);
+  if (!checks_enabled()) return DCOPY_OK;
+  PfnPointerGetAttributes fn = pointer_attrs_fn();
+  if (!fn) return DCOPY_OK;  // no driver entry point: cannot check, launch decides
+  unsigned int mem_type = 0;
+  CUdeviceptr start = 0;
+  size_t size = 0;
+  CUpointer_attribute attrs[3] = {CU_POINTER_ATTRIBUTE_MEMORY_TYPE,
+                                  CU_POINTER_ATTRIBUTE_RANGE_START_ADDR,
+                                  CU_POINTER_ATTRIBUTE_RANGE_SIZE};
+  void *data[3] = {&mem_type, &start, &size};
+  CUresult r = fn(3, attrs, data, (CUdeviceptr)(uintptr_t)ptr);
+  if (r != CUDA_SUCCESS || mem_type == 0)
+    return set_error(DCOPY_ERR_PARAM_INVALID,
+                     "%s (%p) is not memory the GPU can address (plain host memory?)", name, ptr);
+  if (start != 0 && size != 0) {
+    const uint64_t p = (uint64_t)(uintptr_t)ptr;
+    if (p < start || p - start > size || bytes > size - (p - start))
+      return set_error(DCOPY_ERR_PARAM_INVALID,
+                       "%s: %llu bytes at %p run past its allocation [%p, +%llu)", name,
+                       (unsigned long long)bytes, ptr, (void *)(uintptr_t)start,
+                       (unsigned long long)size);
+  }
+  return DCOPY_OK;
+}
+
+int check_disjoint(const void *a, uint64_t an, const void *b, uint64_t bn, const char *what) {
+  if (!an || !bn) return DCOPY_OK;
+  const uint64_t pa = (uint64_t)(uintptr_t)a, pb = (uint64_t)(uintptr_t)b;
+  if (pa < pb + bn && pb < pa + an)
+    return set_error(DCOPY_ERR_PARAM_INVALID, "%s: source and destination ranges overlap",
+                     what);
+  return DCOPY_OK;
+}
+
+int current_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  return dev;
+}
+
+int sm_count() {
+  static std::atomic<int> cache[128];
+  const int dev = current_device();
+  if (dev < 0 || dev >= 128) return 148;
+  int v = cache[dev].load(std::memory_order_relaxed);
+  if (v > 0) return v;
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+    n = 148;
+  cache[dev].store(n, std::memory_order_relaxed);
+  return n;
+}
+
+}  // namespace dcopy
+
+extern "C" {
+
+const char *dcopy_last_error_message(void) { return dcopy::g_message; }
+
+uint32_t dcopy_status_to_ge(int status) {
+  switch (status) {
+    case DCOPY_OK: return 0u;
+    case DCOPY_ERR_PARAM_INVALID: return 145000u;
+    case DCOPY_ERR_SHAPE_INVALID: return 145021u;
+    case DCOPY_ERR_DATATYPE_INVALID: return 145022u;
+    case DCOPY_ERR_FORMAT_INVALID: return 145020u;
+    case DCOPY_ERR_CUDA: return 245002u;     // ACL_ERROR_GE_DEVICE_MEMORY_OPERATE_FAILED
+    case DCOPY_ERR_TIMEOUT: return 545601u;  // ACL_ERROR_GE_MODEL_EXECUTE_TIMEOUT
+    default: return 545000u;                 // ACL_ERROR_GE_INTERNAL_ERROR
+  }
+}
+
+int dcopy_version(void) { return 100; }
+
+}  // extern "C"

@@ -1,0 +1,241 @@
+"""dcopy: Python binding of the B200 data-movement library (libdcopy.so).
+
+A thin ctypes layer over the C ABI declared in include/dcopy/dcopy.h.  Every
+call goes to the CUDA kernels in libdcopy.so; there is no CPU implementation
+behind this module, and it raises ``DcopyUnavailable`` when the library has not
+been built.
+
+Buffers may be given as CUDA ``torch.Tensor`` objects (their ``data_ptr()`` is
+used) or as raw integer device addresses.  ``stream`` defaults to torch's
+current CUDA stream when torch is loaded, else the legacy default stream.
+
+Names follow the reference's host interface:
+  * ``plan_tiling`` / ``datacopy_small|large|pretranspose|contiguous``
+    -- standalone_datacopy/datacopy_data_collection.asc:64-123;
+  * ``copy_ext`` -- AscendC::DataCopyExtParams via DataCopyPadExtend
+    (compiler/graph/optimize/autofuse/ascendc/api/datacopy.h:14-40);
+  * ``copy_nd`` -- DataCopyNddma (v35/ascendc/api_regbase/datacopy_nddma.h);
+  * ``nz_shape`` / ``nd_to_nz`` / ``nz_to_nd`` -- TransShapeToFracNz and the
+    FRACTAL_NZ transfers (base/formats/format_transfers/format_transfer_fractal_nz.cc).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import sys
+from typing import Optional, Sequence
+
+__all__ = [
+    "DataCopyTiling", "DcopyExtParams", "DcopyError", "DcopyUnavailable", "lib", "lib_path",
+    "plan_tiling", "datacopy_small", "datacopy_large", "datacopy_pretranspose",
+    "datacopy_contiguous", "copy_ext", "copy_ext_32b", "copy_nd", "nz_shape", "nd_to_nz",
+    "nz_to_nd", "status_to_ge",
+    "OK", "ERR_PARAM_INVALID", "ERR_SHAPE_INVALID", "ERR_DATATYPE_INVALID",
+    "ERR_FORMAT_INVALID", "ERR_CUDA", "ERR_TIMEOUT", "ERR_UNSUPPORTED",
+]
+
+OK = 0
+ERR_PARAM_INVALID = -1
+ERR_SHAPE_INVALID = -2
+ERR_DATATYPE_INVALID = -3
+ERR_FORMAT_INVALID = -4
+ERR_CUDA = -5
+ERR_TIMEOUT = -6
+ERR_UNSUPPORTED = -7
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+lib_path = os.path.join(_HERE, "libdcopy.so")
+
+
+class DcopyUnavailable(RuntimeError):
+    """libdcopy.so is missing or cannot be loaded (build it with __graft_entry__.build())."""
+
+
+class DcopyError(RuntimeError):
+    """A libdcopy call returned a non-zero status."""
+
+    def __init__(self, code: int, message: str, func: str):
+        super().__init__(f"{func}: status {code}: {message}")
+        self.code = code
+        self.message = message
+
+
+class DataCopyTiling(ctypes.Structure):
+    """Byte-identical to the reference's DataCopyTiling (tiling_datacopy.h:7-13)."""
+    _fields_ = [("rows", ctypes.c_uint32), ("cols", ctypes.c_uint32),
+                ("tile_cols", ctypes.c_uint32), ("ub_bytes", ctypes.c_uint32),
+                ("store", ctypes.c_uint32)]
+
+    def as_dict(self):
+        return {k: getattr(self, k) for k, _ in self._fields_}
+
+
+class DcopyExtParams(ctypes.Structure):
+    """blockCount bursts of blockLen bytes; srcStride/dstStride are gaps in bytes."""
+    _fields_ = [("blockCount", ctypes.c_uint32), ("blockLen", ctypes.c_uint32),
+                ("srcStride", ctypes.c_uint64), ("dstStride", ctypes.c_uint64)]
+
+
+assert ctypes.sizeof(DataCopyTiling) == 20
+assert ctypes.sizeof(DcopyExtParams) == 24
+
+_lib = None
+
+_vp = ctypes.c_void_p
+_i64p = ctypes.POINTER(ctypes.c_int64)
+_u64p = ctypes.POINTER(ctypes.c_uint64)
+_SIGNATURES = {
+    "dcopy_last_error_message": (ctypes.c_char_p, []),
+    "dcopy_status_to_ge": (ctypes.c_uint32, [ctypes.c_int]),
+    "dcopy_version": (ctypes.c_int, []),
+    "dcopy_plan_tiling": (ctypes.c_int, [ctypes.c_uint32] * 4 + [ctypes.POINTER(DataCopyTiling)]),
+    "dcopy_datacopy_small": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(DataCopyTiling), _vp]),
+    "dcopy_datacopy_large": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(DataCopyTiling), _vp]),
+    "dcopy_datacopy_pretranspose": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(DataCopyTiling), _vp]),
+    "dcopy_datacopy_contiguous": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(DataCopyTiling), _vp]),
+    "dcopy_copy_ext": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(DcopyExtParams), _vp]),
+    "dcopy_copy_ext_32b": (ctypes.c_int, [_vp, _vp] + [ctypes.c_uint32] * 4 + [_vp]),
+    "dcopy_copy_nd": (ctypes.c_int, [_vp, _vp, ctypes.c_int, _u64p, _i64p, _i64p,
+                                     ctypes.c_uint32, _vp]),
+    "dcopy_nz_shape": (ctypes.c_int, [_i64p, ctypes.c_int, ctypes.c_int64, _i64p,
+                                      ctypes.POINTER(ctypes.c_int), _i64p]),
+    "dcopy_nd_to_nz": (ctypes.c_int, [_vp, _vp, _i64p, ctypes.c_int, ctypes.c_int,
+                                      ctypes.c_int64, _vp]),
+    "dcopy_nz_to_nd": (ctypes.c_int, [_vp, _vp, _i64p, ctypes.c_int, ctypes.c_int,
+                                      ctypes.c_int64, _vp]),
+}
+
+
+def lib() -> ctypes.CDLL:
+    """Load libdcopy.so once and bind the declared signatures."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(lib_path):
+            raise DcopyUnavailable(f"{lib_path} is not built; run __graft_entry__.build()")
+        try:
+            handle = ctypes.CDLL(lib_path)
+        except OSError as exc:  # pragma: no cover - depends on the machine
+            raise DcopyUnavailable(f"cannot load {lib_path}: {exc}") from exc
+        for name, (res, args) in _SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+def _ptr(x) -> Optional[int]:
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    if hasattr(x, "data_ptr"):
+        if getattr(x, "is_cuda", True) is False:
+            raise ValueError("dcopy kernels need CUDA tensors (got a CPU tensor)")
+        return x.data_ptr()
+    raise TypeError(f"expected a CUDA tensor or a device address, got {type(x).__name__}")
+
+
+def _stream(stream) -> Optional[int]:
+    if stream is None:
+        torch = sys.modules.get("torch")
+        if torch is not None and torch.cuda.is_available() and torch.cuda.is_initialized():
+            return torch.cuda.current_stream().cuda_stream or None
+        return None
+    if isinstance(stream, int):
+        return stream or None
+    return stream.cuda_stream or None
+
+
+def _check(rc: int, func: str) -> None:
+    if rc != OK:
+        msg = lib().dcopy_last_error_message() or b""
+        raise DcopyError(rc, msg.decode(errors="replace"), func)
+
+
+def status_to_ge(status: int) -> int:
+    return lib().dcopy_status_to_ge(status)
+
+
+def plan_tiling(rows: int, cols: int, tile_kib: int, store: int = 1) -> DataCopyTiling:
+    """asc:115-123: validate and plan; raises DcopyError(ERR_PARAM_INVALID) like the reference."""
+    for v in (rows, cols, tile_kib, store):
+        if not 0 <= v <= 0xFFFFFFFF:
+            raise DcopyError(ERR_PARAM_INVALID, "Integer overflow", "dcopy_plan_tiling")
+    t = DataCopyTiling()
+    _check(lib().dcopy_plan_tiling(rows, cols, tile_kib, store, ctypes.byref(t)),
+           "dcopy_plan_tiling")
+    return t
+
+
+def _datacopy(name: str, src, dst, tiling: DataCopyTiling, stream=None) -> None:
+    fn = getattr(lib(), name)
+    _check(fn(_ptr(src), _ptr(dst), ctypes.byref(tiling), _stream(stream)), name)
+
+
+def datacopy_small(x, y, tiling: DataCopyTiling, stream=None) -> None:
+    _datacopy("dcopy_datacopy_small", x, y, tiling, stream)
+
+
+def datacopy_large(x, y, tiling: DataCopyTiling, stream=None) -> None:
+    _datacopy("dcopy_datacopy_large", x, y, tiling, stream)
+
+
+def datacopy_pretranspose(x, b, tiling: DataCopyTiling, stream=None) -> None:
+    _datacopy("dcopy_datacopy_pretranspose", x, b, tiling, stream)
+
+
+def datacopy_contiguous(b, y, tiling: DataCopyTiling, stream=None) -> None:
+    _datacopy("dcopy_datacopy_contiguous", b, y, tiling, stream)
+
+
+def copy_ext(dst, src, block_count: int, block_len: int, src_stride: int = 0,
+             dst_stride: int = 0, stream=None) -> None:
+    """blockCount bursts of blockLen bytes; strides are gap bytes (test_address_model.py:24)."""
+    p = DcopyExtParams(block_count, block_len, src_stride, dst_stride)
+    _check(lib().dcopy_copy_ext(_ptr(dst), _ptr(src), ctypes.byref(p), _stream(stream)),
+           "dcopy_copy_ext")
+
+
+def copy_ext_32b(dst, src, block_count: int, block_len32: int, src_stride32: int = 0,
+                 dst_stride32: int = 0, stream=None) -> None:
+    _check(lib().dcopy_copy_ext_32b(_ptr(dst), _ptr(src), block_count, block_len32,
+                                    src_stride32, dst_stride32, _stream(stream)),
+           "dcopy_copy_ext_32b")
+
+
+def copy_nd(dst, src, sizes: Sequence[int], src_strides: Sequence[int],
+            dst_strides: Sequence[int], elem_bytes: int, stream=None) -> None:
+    n = len(sizes)
+    s = (ctypes.c_uint64 * n)(*sizes)
+    ss = (ctypes.c_int64 * n)(*src_strides)
+    ds = (ctypes.c_int64 * n)(*dst_strides)
+    _check(lib().dcopy_copy_nd(_ptr(dst), _ptr(src), n, s, ss, ds, elem_bytes, _stream(stream)),
+           "dcopy_copy_nd")
+
+
+def nz_shape(nd_shape: Sequence[int], w0: int):
+    """TransShapeToFracNz: returns (nz_shape, (times, H, W))."""
+    n = len(nd_shape)
+    src = (ctypes.c_int64 * max(n, 1))(*nd_shape)
+    out = (ctypes.c_int64 * (n + 4))()
+    rank = ctypes.c_int(0)
+    hw = (ctypes.c_int64 * 3)()
+    _check(lib().dcopy_nz_shape(src, n, w0, out, ctypes.byref(rank), hw), "dcopy_nz_shape")
+    return [out[i] for i in range(rank.value)], tuple(hw)
+
+
+def _shape_arg(shape: Sequence[int]):
+    return (ctypes.c_int64 * max(len(shape), 1))(*shape), len(shape)
+
+
+def nd_to_nz(dst, src, nd_shape: Sequence[int], elem_bytes: int, w0: int, stream=None) -> None:
+    arr, n = _shape_arg(nd_shape)
+    _check(lib().dcopy_nd_to_nz(_ptr(dst), _ptr(src), arr, n, elem_bytes, w0, _stream(stream)),
+           "dcopy_nd_to_nz")
+
+
+def nz_to_nd(dst, src, nd_shape: Sequence[int], elem_bytes: int, w0: int, stream=None) -> None:
+    arr, n = _shape_arg(nd_shape)
+    _check(lib().dcopy_nz_to_nd(_ptr(dst), _ptr(src), arr, n, elem_bytes, w0, _stream(stream)),
+           "dcopy_nz_to_nd")

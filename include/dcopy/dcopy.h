@@ -1,0 +1,152 @@
+/*
+ * dcopy -- B200 (sm_100a) data-movement library: C ABI.
+ *
+ * Drop-in boundary for the data-movement hot path of the reference:
+ *   - the standalone_datacopy kernels and their DataCopyTiling contract
+ *     (standalone_datacopy/datacopy_data_collection.asc, tiling_datacopy.h);
+ *   - the DataCopyExtParams strided copy that GE's DataCopyPadExtend wrappers
+ *     drive (compiler/graph/optimize/autofuse/ascendc/api/datacopy.h) and the
+ *     N-D DataCopyNddma box copy (v35/ascendc/api_regbase/datacopy_nddma.h);
+ *   - the ND <-> FRACTAL_NZ TransData layout conversion
+ *     (base/formats/format_transfers/format_transfer_fractal_nz.cc).
+ *
+ * Conventions
+ *   - Every function returns an int status: DCOPY_OK (0) or a negative
+ *     DCOPY_ERR_* code.  Nothing throws across this ABI.  After a failure,
+ *     dcopy_last_error_message() (thread-local) describes it.
+ *   - The caller owns every buffer.  Buffers passed to kernels must be device
+ *     memory of the current CUDA device (or memory mapped into it); each one is
+ *     checked against its allocation before any launch, so a wrong pointer or a
+ *     size that runs past the allocation is refused on the host instead of
+ *     faulting on the GPU.
+ *   - Launches are asynchronous on `stream` (NULL = the legacy default stream);
+ *     no function synchronises unless its comment says so.
+ *   - All copies move bits: any element type, NaN payloads included, comes out
+ *     byte-identical.
+ */
+#ifndef DCOPY_DCOPY_H_
+#define DCOPY_DCOPY_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "tiling_datacopy.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same type as cudaStream_t / CUstream, without requiring the CUDA headers. */
+typedef struct CUstream_st *dcopy_stream_t;
+
+/* ---- status codes ---------------------------------------------------------
+ * The first four mirror the GE status classes the reference returns
+ * (inc/external/ge/ge_error_codes.h:34,51-53); the demo host's validation
+ * failures (asc:115-123, a std::runtime_error there) map to PARAM_INVALID. */
+#define DCOPY_OK 0
+#define DCOPY_ERR_PARAM_INVALID (-1)    /* ACL_ERROR_GE_PARAM_INVALID    145000 */
+#define DCOPY_ERR_SHAPE_INVALID (-2)    /* ACL_ERROR_GE_SHAPE_INVALID    145021 */
+#define DCOPY_ERR_DATATYPE_INVALID (-3) /* ACL_ERROR_GE_DATATYPE_INVALID 145022 */
+#define DCOPY_ERR_FORMAT_INVALID (-4)   /* ACL_ERROR_GE_FORMAT_INVALID   145020 */
+#define DCOPY_ERR_CUDA (-5)             /* a CUDA runtime/driver call failed */
+#define DCOPY_ERR_TIMEOUT (-6)          /* a bounded device-side wait gave up */
+#define DCOPY_ERR_UNSUPPORTED (-7)      /* valid request outside this build's limits */
+
+/* Thread-local description of the last failure on this thread ("" if none). */
+const char *dcopy_last_error_message(void);
+/* The GE status code (ACL_ERROR_GE_*) for a DCOPY_ERR_* code; 0 for DCOPY_OK. */
+uint32_t dcopy_status_to_ge(int status);
+/* Library version, major*10000 + minor*100 + patch. */
+int dcopy_version(void);
+
+/* ---- standalone_datacopy ---------------------------------------------------- */
+
+/* Tile planner.  Replaces the host planning in datacopy_data_collection.asc:108-123
+ * (and its Python twin profile.py:88-99 tile_plan): validates rows (8..4088,
+ * multiple of 8), cols (1..65535), tile_kib (1..240), store (0/1) and the 64 MiB
+ * input limit, then fills tile_cols = min(cols, tile_kib*1024/(rows*4)) and
+ * ub_bytes = tile_cols*rows*4.  Returns DCOPY_ERR_PARAM_INVALID on any rule the
+ * reference rejects. */
+int dcopy_plan_tiling(uint32_t rows, uint32_t cols, uint32_t tile_kib, uint32_t store,
+                      DataCopyTiling *out);
+
+/* The four kernels of datacopy_data_collection.asc:64-71, launched by the
+ * reference as kernel<<<1, nullptr, stream>>>(x, y, tiling) (asc:141-147).
+ * `tiling` may point to host or device memory; a device pointer costs one
+ * synchronising 20-byte read on `stream`, a host pointer none.  The library
+ * chooses the grid.
+ *   small / large   : y[c*rows + r] = x[r*cols + c] if tiling->store, else
+ *                     x is read and y is left untouched (load-only timing mode);
+ *   pretranspose    : b[c*rows + r] = x[r*cols + c] always (store ignored);
+ *   contiguous      : y = b (rows*cols int32) if tiling->store, else load only.
+ * x, y, b are int32 buffers of rows*cols elements. */
+int dcopy_datacopy_small(const void *x, void *y, const DataCopyTiling *tiling,
+                         dcopy_stream_t stream);
+int dcopy_datacopy_large(const void *x, void *y, const DataCopyTiling *tiling,
+                         dcopy_stream_t stream);
+int dcopy_datacopy_pretranspose(const void *x, void *b, const DataCopyTiling *tiling,
+                                dcopy_stream_t stream);
+int dcopy_datacopy_contiguous(const void *b, void *y, const DataCopyTiling *tiling,
+                              dcopy_stream_t stream);
+
+/* ---- DataCopyExtParams strided copy ---------------------------------------- */
+
+/* AscendC::DataCopyExtParams as filled by DataCopyPadExtend (ascendc/api/
+ * datacopy.h:14-40) and by RunTiles (asc:32-40), widened so every BASELINE
+ * configuration fits: blockLen in bytes, strides are GAPS in bytes between the
+ * end of one block and the start of the next (test_address_model.py:24):
+ *   src block i = src + i*(blockLen + srcStride)
+ *   dst block i = dst + i*(blockLen + dstStride)                            */
+typedef struct DcopyExtParams {
+  uint32_t blockCount;
+  uint32_t blockLen;   /* bytes */
+  uint64_t srcStride;  /* gap bytes */
+  uint64_t dstStride;  /* gap bytes */
+} DcopyExtParams;
+
+/* GM->GM copy of blockCount bursts.  Any byte alignment is accepted; 16-byte
+ * aligned bursts take the vectorised path.  Source and destination ranges must
+ * not overlap (DCOPY_ERR_PARAM_INVALID). */
+int dcopy_copy_ext(void *dst, const void *src, const DcopyExtParams *params,
+                   dcopy_stream_t stream);
+
+/* Same copy with blockLen and both gaps in 32-byte units (AscendC DataCopyParams
+ * units; BASELINE expresses configs 1, 2, 3 and 5 this way). */
+int dcopy_copy_ext_32b(void *dst, const void *src, uint32_t blockCount, uint32_t blockLen32,
+                       uint32_t srcStride32, uint32_t dstStride32, dcopy_stream_t stream);
+
+/* DataCopyNddma<T, dim> (v35/ascendc/api_regbase/datacopy_nddma.h:15-29): an
+ * N-D box copy, 1 <= ndim <= 5.  sizes, src_strides and dst_strides are
+ * outermost-first (like its output_dims argument) and strides count elements
+ * of elem_bytes (1, 2, 4, 8 or 16) bytes.  Negative strides are refused. */
+int dcopy_copy_nd(void *dst, const void *src, int ndim, const uint64_t *sizes,
+                  const int64_t *src_strides, const int64_t *dst_strides, uint32_t elem_bytes,
+                  dcopy_stream_t stream);
+
+/* ---- ND <-> FRACTAL_NZ ------------------------------------------------------ */
+
+/* TransShapeToFracNz (format_transfer_fractal_nz.cc:65-111): ND [..., H, W] ->
+ * NZ [..., ceil(W/w0), ceil(H/16), 16, w0]; rank 1 [N] -> [ceil(N/w0), 1, 16, w0].
+ * nz_shape needs room for rank+2 (rank 1: 4) entries; hw_shape (3 entries,
+ * may be NULL) receives {times, H, W}.  Also a host-only query. */
+int dcopy_nz_shape(const int64_t *nd_shape, int rank, int64_t w0, int64_t *nz_shape,
+                   int *nz_rank, int64_t *hw_shape);
+
+/* TransFormatFromNdToFracNz (:131-213) on the GPU.  dst holds prod(nz_shape)
+ * elements of elem_bytes bytes; its H and W padding is written as zeros (the
+ * reference zero-initialises its output, :139).  w0 is the C0 of the NZ format
+ * (16 for fp16/fp32 in the reference tests, 32 for 1-byte types). */
+int dcopy_nd_to_nz(void *dst, const void *src, const int64_t *nd_shape, int rank,
+                   int elem_bytes, int64_t w0, dcopy_stream_t stream);
+
+/* TransFormatFromFracNzToNd (:215-298) on the GPU: the exact inverse; padding
+ * is dropped.  nd_shape is the DESTINATION (ND) shape. */
+int dcopy_nz_to_nd(void *dst, const void *src, const int64_t *nd_shape, int rank,
+                   int elem_bytes, int64_t w0, dcopy_stream_t stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+static_assert(sizeof(DcopyExtParams) == 24, "DcopyExtParams layout");
+#endif
+
+#endif /* DCOPY_DCOPY_H_ */

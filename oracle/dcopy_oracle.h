@@ -1,0 +1,104 @@
+/*
+ * dcopy oracle -- TEST INFRASTRUCTURE ONLY.
+ *
+ * A plain-C, single-address-space restatement of the reference's algorithms for
+ * the data-movement hot path.  It exists to CHECK the CUDA library: only tests/,
+ * __graft_entry__.smoke() and bench.py's cpu_baseline / reference arm may load it.
+ * The product (libdcopy.so) never links, calls or falls back to it.
+ *
+ * Parity pins (checked by tests/test_oracle_*.py):
+ *   - tiling planner and RunTiles address model: fixtures generated from the
+ *     reference's own Python twin (standalone_datacopy/profile.py:88-99,
+ *     test_address_model.py:13-34) by tests/golden/make_golden.py;
+ *   - ND<->FRACTAL_NZ and N-D transpose: GE's golden vectors
+ *     (tests/ge/ut/ge/common/format_transfer_fractal_nz_unittest.cc,
+ *      format_transfer_transpose_unittest.cc), parsed at test time.
+ *   - DataCopyExt gap addressing: test_address_model.py:24 (pinned through the
+ *     RunTiles model, which is a DataCopyExt gather with blockLen=4).
+ * Normal-mode UB padding and LoopModeParams have no reference vectors: unpinned.
+ */
+#ifndef DCOPY_ORACLE_H_
+#define DCOPY_ORACLE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../include/dcopy/tiling_datacopy.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status classes, numerically equal to the library's DCOPY_ERR_* codes. */
+enum {
+  ORACLE_OK = 0,
+  ORACLE_EPARAM = -1,   /* ACL_ERROR_GE_PARAM_INVALID / std::runtime_error in the demo host */
+  ORACLE_ESHAPE = -2,   /* ACL_ERROR_GE_SHAPE_INVALID */
+  ORACLE_EDTYPE = -3,   /* ACL_ERROR_GE_DATATYPE_INVALID */
+  ORACLE_EFORMAT = -4,  /* ACL_ERROR_GE_FORMAT_INVALID */
+};
+
+/* ---- standalone_datacopy ------------------------------------------------ */
+
+/* Tile planner: datacopy_data_collection.asc:115-123 and profile.py:88-99. */
+int oracle_plan_tiling(uint32_t rows, uint32_t cols, uint32_t tile_kib, uint32_t store,
+                       DataCopyTiling *out);
+
+/* Validates a caller-filled tiling against what RunTiles can execute
+ * (a tiling that would loop forever or overflow its UB buffer is rejected). */
+int oracle_check_tiling(const DataCopyTiling *t);
+
+/* RunTiles<phase> (datacopy_data_collection.asc:16-62), byte for byte, through
+ * a UB buffer of t->ub_bytes bytes.  phase 0 = small/large, 1 = pretranspose,
+ * 2 = contiguous.  `output` is only written when phase == 1 or t->store. */
+int oracle_run_tiles(int phase, const void *input, void *output, const DataCopyTiling *t);
+
+/* The demo host's input pattern input[i] = int32(i*17+3) (asc:124-125). */
+void oracle_fill_pattern(int32_t *dst, uint64_t n);
+
+/* ---- DataCopyExtParams (gap semantics) ----------------------------------- */
+
+/* Block i: src + i*(block_len+src_gap) -> dst + i*(block_len+dst_gap), block_len
+ * bytes.  test_address_model.py:24; ascendc/api/datacopy.h:14-40.
+ * Regions must not overlap. */
+void oracle_copy_ext(void *dst, const void *src, uint64_t block_count, uint64_t block_len,
+                     uint64_t src_gap, uint64_t dst_gap);
+/* Same, blockCount range split over `nthreads` pthreads (CPU baseline). */
+int oracle_copy_ext_mt(void *dst, const void *src, uint64_t block_count, uint64_t block_len,
+                       uint64_t src_gap, uint64_t dst_gap, int nthreads);
+
+/* DataCopyNddma (v35/ascendc/api_regbase/datacopy_nddma.h:15-29): an N-D box
+ * copy.  sizes/strides are outermost-first, strides in elements. */
+int oracle_copy_nd(void *dst, const void *src, int ndim, const uint64_t *sizes,
+                   const int64_t *src_strides, const int64_t *dst_strides, uint32_t elem_bytes);
+
+/* ---- ND <-> FRACTAL_NZ ---------------------------------------------------- */
+
+/* TransShapeToFracNz (format_transfer_fractal_nz.cc:65-111).  dst_shape needs
+ * room for rank+2 entries; hw_shape receives {times, H, W}. */
+int oracle_nz_shape(const int64_t *nd_shape, int rank, int64_t w0, int64_t *dst_shape,
+                    int *dst_rank, int64_t *hw_shape);
+/* TransFormatFromNdToFracNz (:131-213).  dst is zero-filled first (:139). */
+int oracle_nd_to_nz(void *dst, const void *src, const int64_t *nd_shape, int rank,
+                    int elem_bytes, int64_t w0);
+/* TransFormatFromFracNzToNd (:215-298).  Padding is dropped. */
+int oracle_nz_to_nd(void *dst, const void *src, const int64_t *nd_shape, int rank,
+                    int elem_bytes, int64_t w0);
+/* Multi-threaded versions (times x H split over pthreads) for the CPU baseline. */
+int oracle_nd_to_nz_mt(void *dst, const void *src, const int64_t *nd_shape, int rank,
+                       int elem_bytes, int64_t w0, int nthreads);
+int oracle_nz_to_nd_mt(void *dst, const void *src, const int64_t *nd_shape, int rank,
+                       int elem_bytes, int64_t w0, int nthreads);
+
+/* ---- N-D transpose -------------------------------------------------------- */
+
+/* Transpose (format_transfer_transpose.cc:94-197): dst[i] = src[sum idx_k *
+ * src_heads[perm_k]] over the dst odometer. */
+int oracle_transpose(void *dst, const void *src, const int64_t *src_shape, const int64_t *perm,
+                     int rank, int elem_bytes);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif  /* DCOPY_ORACLE_H_ */

@@ -1,0 +1,176 @@
+"""ctypes binding of the C oracle (dcopy_oracle.c) -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline / reference arm
+use this module, as the checker or as the timed CPU restatement of the
+reference.  The product library never imports it.
+
+Arrays are numpy arrays (C-contiguous); the functions work on raw bytes, so any
+dtype moves bit-exactly.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from typing import Sequence
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "_build", "liboracle.so")
+
+OK, EPARAM, ESHAPE, EDTYPE, EFORMAT = 0, -1, -2, -3, -4
+
+
+class Tiling(ctypes.Structure):
+    _fields_ = [("rows", ctypes.c_uint32), ("cols", ctypes.c_uint32),
+                ("tile_cols", ctypes.c_uint32), ("ub_bytes", ctypes.c_uint32),
+                ("store", ctypes.c_uint32)]
+
+
+_lib = None
+_vp = ctypes.c_void_p
+_i64p = ctypes.POINTER(ctypes.c_int64)
+_u64p = ctypes.POINTER(ctypes.c_uint64)
+
+
+def build() -> str:
+    """Compile liboracle.so with make (a no-op when it is up to date)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        h = ctypes.CDLL(LIB_PATH)
+        sig = {
+            "oracle_plan_tiling": [ctypes.c_uint32] * 4 + [ctypes.POINTER(Tiling)],
+            "oracle_check_tiling": [ctypes.POINTER(Tiling)],
+            "oracle_run_tiles": [ctypes.c_int, _vp, _vp, ctypes.POINTER(Tiling)],
+            "oracle_fill_pattern": [_vp, ctypes.c_uint64],
+            "oracle_copy_ext": [_vp, _vp] + [ctypes.c_uint64] * 4,
+            "oracle_copy_ext_mt": [_vp, _vp] + [ctypes.c_uint64] * 4 + [ctypes.c_int],
+            "oracle_copy_nd": [_vp, _vp, ctypes.c_int, _u64p, _i64p, _i64p, ctypes.c_uint32],
+            "oracle_nz_shape": [_i64p, ctypes.c_int, ctypes.c_int64, _i64p,
+                                ctypes.POINTER(ctypes.c_int), _i64p],
+            "oracle_nd_to_nz": [_vp, _vp, _i64p, ctypes.c_int, ctypes.c_int, ctypes.c_int64],
+            "oracle_nz_to_nd": [_vp, _vp, _i64p, ctypes.c_int, ctypes.c_int, ctypes.c_int64],
+            "oracle_nd_to_nz_mt": [_vp, _vp, _i64p, ctypes.c_int, ctypes.c_int, ctypes.c_int64,
+                                   ctypes.c_int],
+            "oracle_nz_to_nd_mt": [_vp, _vp, _i64p, ctypes.c_int, ctypes.c_int, ctypes.c_int64,
+                                   ctypes.c_int],
+            "oracle_transpose": [_vp, _vp, _i64p, _i64p, ctypes.c_int, ctypes.c_int],
+        }
+        for name, args in sig.items():
+            fn = getattr(h, name)
+            fn.argtypes = args
+            fn.restype = None if name in ("oracle_fill_pattern", "oracle_copy_ext") else ctypes.c_int
+        _lib = h
+    return _lib
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data
+
+
+def _i64(vals: Sequence[int]):
+    return (ctypes.c_int64 * max(len(vals), 1))(*vals)
+
+
+def plan_tiling(rows, cols, kib, store=1):
+    t = Tiling()
+    rc = lib().oracle_plan_tiling(rows, cols, kib, store, ctypes.byref(t))
+    return rc, t
+
+
+def check_tiling(t: Tiling) -> int:
+    return lib().oracle_check_tiling(ctypes.byref(t))
+
+
+def run_tiles(phase: int, inp: np.ndarray, out, t: Tiling) -> int:
+    return lib().oracle_run_tiles(phase, _p(inp), _p(out), ctypes.byref(t))
+
+
+def fill_pattern(n: int) -> np.ndarray:
+    a = np.empty(n, dtype=np.int32)
+    lib().oracle_fill_pattern(_p(a), n)
+    return a
+
+
+def copy_ext(dst: np.ndarray, src: np.ndarray, count, blen, sgap=0, dgap=0, threads=1) -> None:
+    if threads > 1:
+        lib().oracle_copy_ext_mt(_p(dst), _p(src), count, blen, sgap, dgap, threads)
+    else:
+        lib().oracle_copy_ext(_p(dst), _p(src), count, blen, sgap, dgap)
+
+
+def copy_nd(dst, src, sizes, src_strides, dst_strides, elem_bytes) -> int:
+    n = len(sizes)
+    return lib().oracle_copy_nd(_p(dst), _p(src), n, (ctypes.c_uint64 * n)(*sizes),
+                                _i64(src_strides), _i64(dst_strides), elem_bytes)
+
+
+def nz_shape(nd_shape: Sequence[int], w0: int):
+    out = (ctypes.c_int64 * (len(nd_shape) + 4))()
+    rank = ctypes.c_int(0)
+    hw = (ctypes.c_int64 * 3)()
+    rc = lib().oracle_nz_shape(_i64(nd_shape), len(nd_shape), w0, out, ctypes.byref(rank), hw)
+    return rc, [out[i] for i in range(rank.value)], tuple(hw)
+
+
+def nd_to_nz(dst, src, nd_shape, elem_bytes, w0, threads=1) -> int:
+    if threads > 1:
+        return lib().oracle_nd_to_nz_mt(_p(dst), _p(src), _i64(nd_shape), len(nd_shape),
+                                        elem_bytes, w0, threads)
+    return lib().oracle_nd_to_nz(_p(dst), _p(src), _i64(nd_shape), len(nd_shape), elem_bytes, w0)
+
+
+def nz_to_nd(dst, src, nd_shape, elem_bytes, w0, threads=1) -> int:
+    if threads > 1:
+        return lib().oracle_nz_to_nd_mt(_p(dst), _p(src), _i64(nd_shape), len(nd_shape),
+                                        elem_bytes, w0, threads)
+    return lib().oracle_nz_to_nd(_p(dst), _p(src), _i64(nd_shape), len(nd_shape), elem_bytes, w0)
+
+
+def transpose(dst, src, src_shape, perm, elem_bytes) -> int:
+    if len(perm) != len(src_shape):
+        raise ValueError("perm and src_shape must have the same rank")
+    return lib().oracle_transpose(_p(dst), _p(src), _i64(src_shape), _i64(perm), len(src_shape),
+                                  elem_bytes)
+
+
+# ---- convenience wrappers returning new arrays -------------------------------------
+
+def nd_to_nz_array(src: np.ndarray, w0: int, threads: int = 1) -> np.ndarray:
+    rc, nz, _ = nz_shape(src.shape, w0)
+    if rc:
+        raise ValueError(f"nz_shape rc={rc}")
+    out = np.empty(nz, dtype=src.dtype)
+    rc = nd_to_nz(out, np.ascontiguousarray(src), src.shape, src.dtype.itemsize, w0, threads)
+    if rc:
+        raise ValueError(f"nd_to_nz rc={rc}")
+    return out
+
+
+def nz_to_nd_array(src: np.ndarray, nd_shape, w0: int, threads: int = 1) -> np.ndarray:
+    out = np.empty(nd_shape, dtype=src.dtype)
+    rc = nz_to_nd(out, np.ascontiguousarray(src), nd_shape, src.dtype.itemsize, w0, threads)
+    if rc:
+        raise ValueError(f"nz_to_nd rc={rc}")
+    return out
+
+
+def transpose_rows_cols(a: np.ndarray) -> np.ndarray:
+    """RunTiles small/large output for A[rows, cols] int32 with store=1, via the tile model."""
+    rows, cols = a.shape
+    rc, t = plan_tiling(rows, cols, 240, 1)
+    if rc:
+        raise ValueError(f"plan_tiling rc={rc}")
+    out = np.empty((cols, rows), dtype=np.int32)
+    rc = run_tiles(0, np.ascontiguousarray(a), out, t)
+    if rc:
+        raise ValueError(f"run_tiles rc={rc}")
+    return out

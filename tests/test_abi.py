@@ -1,0 +1,110 @@
+"""CPU checks of the C ABI: the library loads, exports every declared symbol, and its
+host-only entry points (planner, NZ shape rules, status mapping, argument
+validation that precedes any launch) agree with the oracle and the reference.
+No kernel is launched here."""
+import json
+import re
+
+import pytest
+
+from conftest import GOLDEN, ROOT
+
+
+def _declared_symbols():
+    names = set()
+    for h in (ROOT / "include").rglob("*.h"):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        names.update(re.findall(r"\b(dcopy_\w+)\s*\(", text))
+    return sorted(names)
+
+
+def test_library_exports_every_declared_symbol(dcopy):
+    names = _declared_symbols()
+    assert len(names) >= 14
+    lib = dcopy.lib()
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_version_and_status_mapping(dcopy):
+    assert dcopy.lib().dcopy_version() >= 100
+    assert dcopy.status_to_ge(0) == 0
+    assert dcopy.status_to_ge(dcopy.ERR_PARAM_INVALID) == 145000
+    assert dcopy.status_to_ge(dcopy.ERR_SHAPE_INVALID) == 145021
+    assert dcopy.status_to_ge(dcopy.ERR_DATATYPE_INVALID) == 145022
+    assert dcopy.status_to_ge(dcopy.ERR_FORMAT_INVALID) == 145020
+
+
+def test_plan_tiling_matches_reference_fixture(dcopy):
+    cases = json.loads((GOLDEN / "standalone_plans.json").read_text())["cases"]
+    for rows, cols, kib, tile_cols, tile_bytes, _count in cases:
+        if tile_cols is None:
+            with pytest.raises(dcopy.DcopyError) as e:
+                dcopy.plan_tiling(rows, cols, kib, 1)
+            assert e.value.code == dcopy.ERR_PARAM_INVALID
+        else:
+            t = dcopy.plan_tiling(rows, cols, kib, 1)
+            assert (t.rows, t.cols, t.tile_cols, t.ub_bytes, t.store) == \
+                (rows, cols, tile_cols, tile_bytes, 1)
+
+
+def test_plan_tiling_messages_follow_reference(dcopy):
+    with pytest.raises(dcopy.DcopyError, match="Tile budget must hold a complete transposed row"):
+        dcopy.plan_tiling(512, 768, 1, 1)
+    with pytest.raises(dcopy.DcopyError, match="64 MiB"):
+        dcopy.plan_tiling(4088, 65535, 240, 1)
+    with pytest.raises(dcopy.DcopyError, match="store: 0/1"):
+        dcopy.plan_tiling(8, 8, 8, 2)
+
+
+@pytest.mark.parametrize("shape", [[1], [100], [0], [2, 2, 17, 4], [5, 33], [3, 0, 7],
+                                   [16, 4096, 4096], [1, 1, 1, 1, 1, 1, 31, 17]])
+@pytest.mark.parametrize("w0", [1, 8, 16, 32, 0, -1])
+def test_nz_shape_matches_oracle(dcopy, oracle, shape, w0):
+    rc, nz, hw = oracle.nz_shape(shape, w0)
+    if rc:
+        with pytest.raises(dcopy.DcopyError) as e:
+            dcopy.nz_shape(shape, w0)
+        assert e.value.code == dcopy.ERR_SHAPE_INVALID
+    else:
+        assert dcopy.nz_shape(shape, w0) == (nz, hw)
+
+
+def test_validation_before_launch(dcopy):
+    # Each of these fails on the host before any device work.
+    with pytest.raises(dcopy.DcopyError) as e:
+        dcopy.nd_to_nz(0, 0, [4, 4], 0, 16)
+    assert e.value.code == dcopy.ERR_DATATYPE_INVALID
+    with pytest.raises(dcopy.DcopyError) as e:
+        dcopy.nd_to_nz(0, 0, [4, -1], 2, 16)
+    assert e.value.code == dcopy.ERR_SHAPE_INVALID
+    with pytest.raises(dcopy.DcopyError) as e:
+        dcopy.nd_to_nz(0, 0, [4, 4], 2, 16)  # NULL buffers with bytes to move
+    assert e.value.code == dcopy.ERR_PARAM_INVALID
+    with pytest.raises(dcopy.DcopyError) as e:
+        dcopy.copy_ext(0, 0, 4, 16, 0, 0)
+    assert e.value.code == dcopy.ERR_PARAM_INVALID
+    with pytest.raises(dcopy.DcopyError) as e:
+        dcopy.copy_nd(0, 0, [2, 2], [2, 1], [0, 1], 4)  # dst stride 0 aliases
+    assert e.value.code == dcopy.ERR_PARAM_INVALID
+    with pytest.raises(dcopy.DcopyError) as e:
+        dcopy.copy_nd(0, 0, [2, 2], [2, 1], [2, 1], 3)
+    assert e.value.code == dcopy.ERR_DATATYPE_INVALID
+    dcopy.copy_ext(0, 0, 0, 16, 0, 0)  # nothing to move: OK without touching memory
+    dcopy.nd_to_nz(0, 0, [0, 16], 2, 16)
+    bad = dcopy.DataCopyTiling(60, 100, 8, 1920, 1)
+    with pytest.raises(dcopy.DcopyError) as e:
+        dcopy.datacopy_small(0, 0, bad)
+    assert e.value.code == dcopy.ERR_PARAM_INVALID
+
+
+def test_error_message_is_thread_local(dcopy):
+    import threading
+    with pytest.raises(dcopy.DcopyError):
+        dcopy.plan_tiling(7, 7, 7, 1)
+    seen = []
+    t = threading.Thread(target=lambda: seen.append(dcopy.lib().dcopy_last_error_message()))
+    t.start()
+    t.join()
+    assert seen == [b""]
+    assert b"rows" in dcopy.lib().dcopy_last_error_message()

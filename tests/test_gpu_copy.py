@@ -1,0 +1,161 @@
+"""GPU parity: DataCopyExt strided copies and DataCopyNddma boxes vs the oracle, bit-exact.
+
+Destinations are pre-filled with a canary so bytes in the destination gaps must
+stay untouched, as in the oracle.  BASELINE configs 1-3 and 5 run at full size
+through size-independent checks (the strided view of the source equals the
+packed destination), and at reduced size against the oracle byte for byte.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+CANARY = 0xA5
+
+
+def _canary(torch, n):
+    return torch.full((n,), CANARY, dtype=torch.uint8, device="cuda")
+
+
+def _rand_bytes(n, seed):
+    return np.random.default_rng(seed).integers(0, 256, size=n, dtype=np.uint8)
+
+
+CASES = [  # (blockCount, blockLen, srcGap, dstGap, src_offset, dst_offset)
+    (1, 1, 0, 0, 0, 0), (7, 3, 5, 1, 1, 2), (64, 4, 28, 0, 0, 0), (33, 16, 16, 16, 0, 0),
+    (33, 16, 16, 16, 4, 8), (100, 32, 0, 0, 0, 0), (100, 32, 32, 0, 0, 0),
+    (257, 48, 80, 16, 0, 0), (1000, 64, 192, 0, 16, 0), (300, 100, 3, 7, 5, 1),
+    (1023, 128, 512, 0, 0, 0), (64, 512, 2048, 512, 0, 0), (17, 4096, 12288, 0, 0, 0),
+    (5, 65536, 65536, 32, 0, 0), (3, 1 << 20, 1 << 16, 0, 0, 0), (1, 1 << 22, 0, 0, 3, 7),
+    (4096, 4, 4092, 0, 0, 0), (65536, 2, 6, 0, 2, 0),
+]
+
+
+@pytest.mark.parametrize("case", CASES, ids=lambda c: "x".join(map(str, c)))
+def test_copy_ext_matches_oracle(torch_cuda, dcopy, oracle, case):
+    torch = torch_cuda
+    count, blen, sgap, dgap, soff, doff = case
+    src_span = (count - 1) * (blen + sgap) + blen
+    dst_span = (count - 1) * (blen + dgap) + blen
+    src_np = _rand_bytes(src_span + soff, seed=count * 31 + blen)
+    dst_np = np.full(dst_span + doff + 64, CANARY, dtype=np.uint8)
+    oracle.copy_ext(dst_np[doff:], src_np[soff:], count, blen, sgap, dgap)
+    src = torch.from_numpy(src_np).cuda()
+    dst = _canary(torch, dst_span + doff + 64)
+    dcopy.copy_ext(dst.data_ptr() + doff, src.data_ptr() + soff, count, blen, sgap, dgap)
+    torch.cuda.synchronize()
+    assert dst.cpu().numpy().tobytes() == dst_np.tobytes()
+
+
+def test_copy_ext_32b_units(torch_cuda, dcopy):
+    torch = torch_cuda
+    src = torch.from_numpy(_rand_bytes(1 << 20, 1)).cuda()
+    a = _canary(torch, 1 << 19)
+    b = _canary(torch, 1 << 19)
+    dcopy.copy_ext_32b(a, src, 100, 4, 12, 2)
+    dcopy.copy_ext(b, src, 100, 128, 384, 64)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+
+
+def test_config1_contiguous_fp16(torch_cuda, dcopy):
+    """262,144 fp16, 8 'cores' x 16 tiles of blockLen 4 KiB."""
+    torch = torch_cuda
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = (torch.rand(262144, generator=g, device="cuda") * 2 - 1).half()
+    y = torch.full_like(x, float("nan"))
+    # As one DataCopyExt call (blockCount=128 tiles, blockLen=128 x 32 B, gaps 0) ...
+    dcopy.copy_ext_32b(y, x, 128, 128, 0, 0)
+    torch.cuda.synchronize()
+    assert torch.equal(x.view(torch.int16), y.view(torch.int16))
+    # ... and as the per-core tiles of the reference's tiling (8 cores x 16 tiles x 2,048 elems).
+    y2 = torch.full_like(x, float("nan"))
+    for core in range(8):
+        off = core * 16 * 2048
+        for tile in range(16):
+            o = off + tile * 2048
+            dcopy.copy_ext(y2[o:], x[o:], 1, 4096, 0, 0)
+    torch.cuda.synchronize()
+    assert torch.equal(x.view(torch.int16), y2.view(torch.int16))
+
+
+def test_config2_strided_gather_fp32(torch_cuda, dcopy):
+    """fp32 [4096, 4096] cols 1024..2047 -> [4096, 1024]."""
+    torch = torch_cuda
+    g = torch.Generator(device="cuda").manual_seed(1)
+    src = torch.rand(4096, 4096, generator=g, device="cuda")
+    dst = torch.full((4096, 1024), float("nan"), device="cuda")
+    dcopy.copy_ext_32b(dst, src[:, 1024:], 4096, 128, 384, 0)
+    torch.cuda.synchronize()
+    assert torch.equal(dst.view(torch.int32), src[:, 1024:2048].contiguous().view(torch.int32))
+
+
+@pytest.mark.parametrize("blen", [32, 64, 128, 512, 4096, 65536])
+@pytest.mark.parametrize("gapx", [0, 1, 4, 16])
+def test_config3_sweep_point(torch_cuda, dcopy, blen, gapx):
+    """BASELINE config 3 point at 1/16 size (16 MiB moved); int32 element-index source."""
+    torch = torch_cuda
+    moved = 16 << 20
+    count = moved // blen
+    gap = gapx * blen
+    src = torch.arange((count * (blen + gap)) // 4, dtype=torch.int32, device="cuda")
+    dst = torch.full((moved // 4,), -1, dtype=torch.int32, device="cuda")
+    dcopy.copy_ext(dst, src, count, blen, gap, 0)
+    torch.cuda.synchronize()
+    expect = src.view(count, (blen + gap) // 4)[:, : blen // 4].reshape(-1)
+    assert torch.equal(dst, expect)
+
+
+def test_config3_full_size_point(torch_cuda, dcopy):
+    """One full-size config 3 point (256 MiB moved, gap 16x, 4.25 GiB source)."""
+    torch = torch_cuda
+    blen, gap = 4096, 16 * 4096
+    count = (256 << 20) // blen
+    src = torch.empty((count * (blen + gap)) // 4, dtype=torch.int32, device="cuda")
+    src.copy_(torch.arange(src.numel(), dtype=torch.int32, device="cuda"))
+    dst = torch.full(((256 << 20) // 4,), -1, dtype=torch.int32, device="cuda")
+    dcopy.copy_ext(dst, src, count, blen, gap, 0)
+    torch.cuda.synchronize()
+    expect = src.view(count, (blen + gap) // 4)[:, : blen // 4].reshape(-1)
+    assert torch.equal(dst, expect)
+    del src, dst, expect
+    torch.cuda.empty_cache()
+
+
+def test_overlap_and_extent_refused(torch_cuda, dcopy, cuda_malloc):
+    torch = torch_cuda
+    buf = torch.zeros(1 << 16, dtype=torch.uint8, device="cuda")
+    with pytest.raises(dcopy.DcopyError) as e:
+        dcopy.copy_ext(buf.data_ptr() + 100, buf.data_ptr(), 10, 64, 0, 0)
+    assert e.value.code == dcopy.ERR_PARAM_INVALID
+    with cuda_malloc(4096) as p:
+        with pytest.raises(dcopy.DcopyError) as e:
+            dcopy.copy_ext(buf, p, 2, 4096, 0, 0)  # source runs past its 4 KiB allocation
+        assert e.value.code == dcopy.ERR_PARAM_INVALID
+    dcopy.copy_ext(buf, buf, 0, 64, 0, 0)  # empty copies are a no-op
+
+
+ND_CASES = [  # (sizes, src_strides, dst_strides, elem_bytes)
+    ([9, 6, 7], [1, 63, 9], [42, 7, 1], 4),
+    ([3, 5], [8, 1], [5, 1], 2),
+    ([2, 3, 4, 5, 6], [360, 120, 30, 6, 1], [1, 2, 6, 24, 120], 1),
+    ([100, 33], [40, 1], [33, 1], 8),
+    ([7, 9, 11], [1, 7, 63], [99, 11, 1], 16),
+    ([4, 4], [0, 1], [4, 1], 4),  # broadcast source rows
+]
+
+
+@pytest.mark.parametrize("case", ND_CASES, ids=lambda c: str(c[0]))
+def test_copy_nd_matches_oracle(torch_cuda, dcopy, oracle, case):
+    torch = torch_cuda
+    sizes, ss, ds, eb = case
+    src_elems = sum((s - 1) * st for s, st in zip(sizes, ss)) + 1
+    dst_elems = sum((s - 1) * st for s, st in zip(sizes, ds)) + 1
+    src_np = _rand_bytes(src_elems * eb, seed=len(sizes))
+    dst_np = np.full(dst_elems * eb, CANARY, dtype=np.uint8)
+    assert oracle.copy_nd(dst_np, src_np, sizes, ss, ds, eb) == 0
+    src = torch.from_numpy(src_np).cuda()
+    dst = _canary(torch, dst_elems * eb)
+    dcopy.copy_nd(dst, src, sizes, ss, ds, eb)
+    torch.cuda.synchronize()
+    assert dst.cpu().numpy().tobytes() == dst_np.tobytes()
