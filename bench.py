@@ -53,7 +53,7 @@ NVML_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_po
 def parse_args():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["dcopy", "reference"], default="dcopy")
     ap.add_argument("--no-secondary", action="store_true",
@@ -81,8 +81,9 @@ def load_traffic():
 class ClockSampler:
     """Samples SM clock and clock-event reasons through NVML while the timed region runs."""
 
-    def __init__(self, device_index: int, period_s: float = 0.01):
-        self.samples = []
+    def __init__(self, cuda_index: int, period_s: float = 0.002):
+        self.samples = []  # (host time, SM MHz)
+        self.window = None
         self.reasons = 0
         self.max_mhz = None
         self.ok = False
@@ -92,7 +93,13 @@ class ClockSampler:
             import pynvml
             pynvml.nvmlInit()
             self._nvml = pynvml
-            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            import torch
+            p = torch.cuda.get_device_properties(cuda_index)
+            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+            try:  # NVML and CUDA may order devices differently: match by PCI address
+                self._h = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+            except Exception:
+                self._h = pynvml.nvmlDeviceGetHandleByIndex(cuda_index)
             self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
             self.ok = True
         except Exception:  # NVML missing: clocks reported as unavailable
@@ -102,7 +109,8 @@ class ClockSampler:
         n = self._nvml
         while not self._stop.is_set():
             try:
-                self.samples.append(n.nvmlDeviceGetClockInfo(self._h, n.NVML_CLOCK_SM))
+                self.samples.append((time.perf_counter(),
+                                     n.nvmlDeviceGetClockInfo(self._h, n.NVML_CLOCK_SM)))
                 try:
                     r = n.nvmlDeviceGetCurrentClocksEventReasons(self._h)
                 except AttributeError:
@@ -123,13 +131,23 @@ class ClockSampler:
             self._stop.set()
             self._t.join()
 
+    def mark(self, t0, t1):
+        """Host-time bounds of the timed region."""
+        self.window = (t0, t1)
+
     def summary(self):
         if not self.ok or not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"],
                     "samples": len(self.samples)}
         names = [v for k, v in NVML_REASONS.items() if self.reasons & k and k != 0x1]
-        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
-                "reasons": names, "samples": len(self.samples)}
+        inside = [mhz for t, mhz in self.samples
+                  if self.window and self.window[0] <= t <= self.window[1]]
+        window = "timed region"
+        if len(inside) < 3:  # very short timed region: use the loaded warm-up as well
+            inside = [mhz for _, mhz in self.samples]
+            window = "warm-up soak + timed region"
+        return {"sm_mhz": statistics.median(inside), "sm_max_mhz": self.max_mhz,
+                "reasons": names, "samples": len(inside), "window": window}
 
 
 def cpu_baseline_gather(seconds: float = 8.0, threads=None):
@@ -199,12 +217,19 @@ def run_dcopy(args, rank, world, local_rank):
 
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clk:
+        # Untimed soak (~0.3 s of replays) so the clock record sees a loaded GPU.
+        for _ in range(30):
+            for _ in range(100):
+                graph.replay()
+            torch.cuda.synchronize()
         barrier()
+        t0 = time.perf_counter()
         ev0.record(stream)
         for _ in range(args.steps):
             graph.replay()
         ev1.record(stream)
         ev1.synchronize()
+        clk.mark(t0, time.perf_counter())
         barrier()
     ms = ev0.elapsed_time(ev1)
     t = torch.tensor([ms], dtype=torch.float64, device=dev)
