@@ -98,6 +98,14 @@ __device__ __forceinline__ uint8_t ld_stream<uint8_t>(const uint8_t *p) {
   return (uint8_t)v;
 }
 
+// L2 prefetch hint for the line holding p.  Kernels issue these for their source
+// before waiting on the previous kernel of the stream (programmatic dependent
+// launch): a prefetch returns no data to the SM and has no effect on memory
+// ordering, so it is safe even when that kernel writes the same addresses.
+__device__ __forceinline__ void prefetch_l2(const void *p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 // A read that the compiler must keep even though its value is unused: the
 // load-only (store == 0) modes of the standalone kernels time reads alone.
 __device__ __forceinline__ uint32_t ld_keep_u32(const void *p) {

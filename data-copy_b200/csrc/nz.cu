@@ -18,9 +18,17 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "launch.cuh"
 
 namespace dcopy {
 namespace {
+
+#ifndef DCOPY_NZ_SMEM
+#define DCOPY_NZ_SMEM 1
+#endif
+#ifndef DCOPY_PREFETCH
+#define DCOPY_PREFETCH 1  // L2-prefetch the first tile while waiting on the previous kernel
+#endif
 
 constexpr int kThreads = 256;
 constexpr int kTileUnits = 1024;  // 4 units per thread
@@ -47,6 +55,9 @@ __global__ void __launch_bounds__(kThreads) nz_kernel(T *__restrict__ dst,
                                                       const T *__restrict__ src, NzGeom g,
                                                       uint32_t ntiles) {
   constexpr int U = kTileUnits / kThreads;
+  pdl_trigger_at_entry();
+  pdl_wait();
+  pdl_launch_dependents();
   for (uint32_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     const uint32_t q = g.f_pgroups.div(tile);
     const uint32_t pg = tile - q * g.pgroups;
@@ -93,6 +104,114 @@ __global__ void __launch_bounds__(kThreads) nz_kernel(T *__restrict__ dst,
       for (int u = 0; u < U; ++u)
         if (ok[u]) db[doff[u]] = v[u];
     }
+  }
+}
+
+// Shared-memory staged variant for a power-of-two `upr` with 16-byte units: the
+// tile is read from global memory in source order (each warp 512 contiguous
+// bytes), permuted through shared memory, and written in destination order
+// (again 512 contiguous bytes per warp).  Shared memory holds the tile in NZ
+// order [panel][row][unit]; the 16-byte unit index is XOR-swizzled with
+// (panel * upr) mod 8 so that the ND-order accesses (fixed row, consecutive
+// panels) and the NZ-order accesses (fixed panel, consecutive rows) both hit 8
+// distinct 16-byte bank groups per 128-byte wavefront.
+template <bool kToNz>
+__global__ void __launch_bounds__(kThreads) nz_smem_kernel(uint4 *__restrict__ dst,
+                                                           const uint4 *__restrict__ src,
+                                                           NzGeom g, uint32_t ntiles,
+                                                           uint32_t upr_shift) {
+  constexpr int U = kTileUnits / kThreads;
+  __shared__ uint4 tile[kTileUnits];
+  pdl_trigger_at_entry();
+  // The tile is 16 rows x 64 units (1024 units), so a tile row (ND order) is 64
+  // units and a panel fragment (NZ order) is 16 * upr units.
+  const uint32_t upr = g.upr;
+  constexpr uint32_t kRowShift = 6;  // log2(kTileUnits / kRowsPerTile)
+  static_assert(kTileUnits / kRowsPerTile == 64, "tile row must be 64 units");
+  const uint32_t panel_shift = 4 + upr_shift;
+  const uint32_t panel_units = 1u << panel_shift;
+  if (DCOPY_PREFETCH && blockIdx.x < ntiles) {
+    // L2-prefetch the first tile's source, one prefetch per 128-byte line.
+    const uint32_t q = g.f_pgroups.div(blockIdx.x);
+    const uint32_t pg = blockIdx.x - q * g.pgroups;
+    const uint32_t t = g.f_hblocks.div(q);
+    const uint32_t hb = q - t * g.hblocks;
+    const uint4 *sb = src + (uint64_t)t * (kToNz ? g.nd_batch : g.nz_batch);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t j = threadIdx.x + u * kThreads;
+      if (j % 8) continue;
+      if (kToNz) {
+        const uint32_t h = hb * kRowsPerTile + (j >> kRowShift), col = pg * g.PG * upr + (j & 63);
+        if (h < g.H && col < g.Wu) prefetch_l2(sb + (uint64_t)h * g.Wu + col);
+      } else {
+        const uint32_t pin = j >> panel_shift;
+        if (pg * g.PG + pin < g.W1)
+          prefetch_l2(sb + (uint64_t)(pg * g.PG + pin) * g.panel +
+                      (uint64_t)hb * kRowsPerTile * upr + (j & (panel_units - 1)));
+      }
+    }
+  }
+  pdl_wait();
+  pdl_launch_dependents();
+  for (uint32_t tile_id = blockIdx.x; tile_id < ntiles; tile_id += gridDim.x) {
+    const uint32_t q = g.f_pgroups.div(tile_id);
+    const uint32_t pg = tile_id - q * g.pgroups;
+    const uint32_t t = g.f_hblocks.div(q);
+    const uint32_t hb = q - t * g.hblocks;
+    const uint32_t w1_0 = pg * g.PG, h_0 = hb * kRowsPerTile;
+    const uint4 *sb = src + (uint64_t)t * (kToNz ? g.nd_batch : g.nz_batch);
+    uint4 *db = dst + (uint64_t)t * (kToNz ? g.nz_batch : g.nd_batch);
+    // ---- load: source order into swizzled NZ-order shared memory
+    uint4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t j = threadIdx.x + u * kThreads;
+      v[u] = make_uint4(0, 0, 0, 0);
+      if (kToNz) {  // ND order [row][unit]
+        const uint32_t hin = j >> kRowShift, uin = j & 63;
+        const uint32_t h = h_0 + hin, col = w1_0 * upr + uin;
+        if (h < g.H && col < g.Wu) v[u] = ld_stream(sb + (uint64_t)h * g.Wu + col);
+      } else {  // NZ order [panel][row][unit]
+        const uint32_t pin = j >> panel_shift, rem = j & (panel_units - 1);
+        if (w1_0 + pin < g.W1)
+          v[u] = ld_stream(sb + (uint64_t)(w1_0 + pin) * g.panel + (uint64_t)h_0 * upr + rem);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t j = threadIdx.x + u * kThreads;
+      uint32_t pin, rem;
+      if (kToNz) {
+        const uint32_t hin = j >> kRowShift, uin = j & 63;
+        pin = uin >> upr_shift;
+        rem = (hin << upr_shift) + (uin & (upr - 1));
+      } else {
+        pin = j >> panel_shift;
+        rem = j & (panel_units - 1);
+      }
+      tile[pin * panel_units + (rem ^ ((pin << upr_shift) & 7))] = v[u];
+    }
+    __syncthreads();
+    // ---- store: destination order out of shared memory
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t j = threadIdx.x + u * kThreads;
+      if (kToNz) {  // NZ order
+        const uint32_t pin = j >> panel_shift, rem = j & (panel_units - 1);
+        if (w1_0 + pin < g.W1)
+          db[(uint64_t)(w1_0 + pin) * g.panel + (uint64_t)h_0 * upr + rem] =
+              tile[pin * panel_units + (rem ^ ((pin << upr_shift) & 7))];
+      } else {  // ND order
+        const uint32_t hin = j >> kRowShift, uin = j & 63;
+        const uint32_t h = h_0 + hin, col = w1_0 * upr + uin;
+        const uint32_t pin = uin >> upr_shift;
+        const uint32_t rem = (hin << upr_shift) + (uin & (upr - 1));
+        if (h < g.H && col < g.Wu)
+          db[(uint64_t)h * g.Wu + col] = tile[pin * panel_units + (rem ^ ((pin << upr_shift) & 7))];
+      }
+    }
+    __syncthreads();
   }
 }
 
@@ -148,17 +267,31 @@ int nz_shape(const int64_t *nd, int rank, int64_t w0, int64_t *nz, int *nz_rank,
   return DCOPY_OK;
 }
 
+
 template <typename T>
 int launch_nz(void *dst, const void *src, const NzGeom &g, uint32_t ntiles, bool to_nz,
               cudaStream_t s) {
-  const uint32_t grid = std::max(1u, std::min<uint32_t>(ntiles, (uint32_t)sm_count() * 8));
+  if (DCOPY_NZ_SMEM && sizeof(T) == 16 && g.tile_units == kTileUnits &&
+      (g.upr & (g.upr - 1)) == 0 && g.upr <= 64) {
+    uint32_t shift = 0;
+    while ((1u << shift) < g.upr) ++shift;
+    const uint32_t grid = std::max(1u, std::min<uint32_t>(ntiles, 0x7FFFFFFFu));
+    uint4 *d = static_cast<uint4 *>(dst);
+    const uint4 *sp = static_cast<const uint4 *>(src);
+    if (to_nz)
+      return launch(nz_smem_kernel<true>, grid, dim3(kThreads), 0, s, "nz_smem_kernel", d, sp, g,
+                    ntiles, shift);
+    return launch(nz_smem_kernel<false>, grid, dim3(kThreads), 0, s, "nz_smem_kernel", d, sp, g,
+                  ntiles, shift);
+  }
+  // One tile per CTA: on B200 many short-lived CTAs stream better than a
+  // persistent grid (the grid-stride loop only matters past 2^31 - 1 tiles).
+  const uint32_t grid = std::max(1u, std::min<uint32_t>(ntiles, 0x7FFFFFFFu));
+  T *d = static_cast<T *>(dst);
+  const T *sp = static_cast<const T *>(src);
   if (to_nz)
-    nz_kernel<T, true><<<grid, kThreads, 0, s>>>(static_cast<T *>(dst),
-                                                 static_cast<const T *>(src), g, ntiles);
-  else
-    nz_kernel<T, false><<<grid, kThreads, 0, s>>>(static_cast<T *>(dst),
-                                                  static_cast<const T *>(src), g, ntiles);
-  return check_launch("nz_kernel");
+    return launch(nz_kernel<T, true>, grid, dim3(kThreads), 0, s, "nz_kernel", d, sp, g, ntiles);
+  return launch(nz_kernel<T, false>, grid, dim3(kThreads), 0, s, "nz_kernel", d, sp, g, ntiles);
 }
 
 int nz_transfer(void *dst, const void *src, const int64_t *nd_shape, int rank, int elem_bytes,

@@ -44,7 +44,9 @@ ERR_TIMEOUT = -6
 ERR_UNSUPPORTED = -7
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-lib_path = os.path.join(_HERE, "libdcopy.so")
+# DCOPY_LIBRARY selects an alternative build of the same library (e.g. one built
+# with different compile-time options); the default is the in-tree libdcopy.so.
+lib_path = os.environ.get("DCOPY_LIBRARY") or os.path.join(_HERE, "libdcopy.so")
 
 
 class DcopyUnavailable(RuntimeError):
