@@ -1,0 +1,401 @@
+// GE TransData level on device buffers: the format-transfer registry
+// (base/formats/formats.cc, register_format_transfer.{h,cc}), the
+// FormatTransferFractalNz / FormatTransferFractalNzND / FormatTransferTranspose
+// classes' argument checks, and Transpose (format_transfer_transpose.cc) on the
+// GPU.  Every check happens on the host, in the reference's order and with its
+// status class, before any launch; the data movement goes to the NZ kernels and
+// to the N-D box copy.
+#include <cuda_runtime.h>
+
+#include <cstring>
+
+#include "common.cuh"
+#include "internal.cuh"
+
+namespace dcopy {
+namespace {
+
+constexpr int kMaxRank = 30;
+
+// GetSizeByDataType for GE's DataType enum (api/python/ge/ge/graph/types.py:15-58).
+// Types without a fixed byte size (string, resource, variant, sub-byte
+// floats/ints, undefined) report -1.
+int32_t type_size(int32_t dt) {
+  switch (dt) {
+    case 0: return 4;    // DT_FLOAT
+    case 1: return 2;    // DT_FLOAT16
+    case 2: return 1;    // DT_INT8
+    case 3: return 4;    // DT_INT32
+    case 4: return 1;    // DT_UINT8
+    case 6: return 2;    // DT_INT16
+    case 7: return 2;    // DT_UINT16
+    case 8: return 4;    // DT_UINT32
+    case 9: return 8;    // DT_INT64
+    case 10: return 8;   // DT_UINT64
+    case 11: return 8;   // DT_DOUBLE
+    case 12: return 1;   // DT_BOOL
+    case 14: return 1;   // DT_DUAL_SUB_INT8
+    case 15: return 1;   // DT_DUAL_SUB_UINT8
+    case 16: return 8;   // DT_COMPLEX64
+    case 17: return 16;  // DT_COMPLEX128
+    case 18: return 1;   // DT_QINT8
+    case 19: return 2;   // DT_QINT16
+    case 20: return 4;   // DT_QINT32
+    case 21: return 1;   // DT_QUINT8
+    case 22: return 2;   // DT_QUINT16
+    case 27: return 2;   // DT_BF16
+    case 33: return 4;   // DT_COMPLEX32
+    case 34: return 1;   // DT_HIFLOAT8
+    case 35: return 1;   // DT_FLOAT8_E5M2
+    case 36: return 1;   // DT_FLOAT8_E4M3FN
+    case 37: return 1;   // DT_FLOAT8_E8M0
+    default: return -1;
+  }
+}
+
+// format_transfer_transpose.cc:26-43.
+struct PermEntry {
+  int32_t src, dst;
+  int64_t perm[4];
+};
+constexpr PermEntry kPerms[] = {
+    {DCOPY_FORMAT_NCHW, DCOPY_FORMAT_NHWC, {0, 2, 3, 1}},
+    {DCOPY_FORMAT_NCHW, DCOPY_FORMAT_HWCN, {2, 3, 1, 0}},
+    {DCOPY_FORMAT_NCHW, DCOPY_FORMAT_CHWN, {1, 2, 3, 0}},
+    {DCOPY_FORMAT_NHWC, DCOPY_FORMAT_NCHW, {0, 3, 1, 2}},
+    {DCOPY_FORMAT_NHWC, DCOPY_FORMAT_CHWN, {3, 1, 2, 0}},
+    {DCOPY_FORMAT_NHWC, DCOPY_FORMAT_HWCN, {1, 2, 3, 0}},
+    {DCOPY_FORMAT_HWCN, DCOPY_FORMAT_NCHW, {3, 2, 0, 1}},
+    {DCOPY_FORMAT_HWCN, DCOPY_FORMAT_NHWC, {3, 0, 1, 2}},
+    {DCOPY_FORMAT_HWCN, DCOPY_FORMAT_CHWN, {2, 0, 1, 3}},
+    {DCOPY_FORMAT_CHWN, DCOPY_FORMAT_NCHW, {3, 0, 1, 2}},
+    {DCOPY_FORMAT_CHWN, DCOPY_FORMAT_NHWC, {3, 1, 2, 0}},
+    {DCOPY_FORMAT_CHWN, DCOPY_FORMAT_HWCN, {1, 2, 0, 3}},
+};
+
+const PermEntry *find_perm(int32_t src, int32_t dst) {
+  for (const PermEntry &e : kPerms)
+    if (e.src == src && e.dst == dst) return &e;
+  return nullptr;
+}
+
+// The registry: which transfer class a (src, dst) primary-format pair builds
+// (REGISTER_FORMAT_TRANSFER lines of both transfer files); 0 = none.
+int registered_class(int32_t src, int32_t dst) {
+  const bool nd_like = src == DCOPY_FORMAT_ND || src == DCOPY_FORMAT_NCHW ||
+                       src == DCOPY_FORMAT_NHWC;
+  const bool nd_like_dst = dst == DCOPY_FORMAT_ND || dst == DCOPY_FORMAT_NCHW ||
+                           dst == DCOPY_FORMAT_NHWC;
+  if (nd_like && dst == DCOPY_FORMAT_FRACTAL_NZ) return DCOPY_TRANSFER_FRACTAL_NZ;
+  if (src == DCOPY_FORMAT_FRACTAL_NZ && nd_like_dst) return DCOPY_TRANSFER_FRACTAL_NZ_ND;
+  if (find_perm(src, dst)) return DCOPY_TRANSFER_TRANSPOSE;
+  return 0;
+}
+
+bool same_shape(const int64_t *a, int an, const int64_t *b, int bn) {
+  if (an != bn) return false;
+  for (int i = 0; i < an; ++i)
+    if (a[i] != b[i]) return false;
+  return true;
+}
+
+int64_t item_count(const int64_t *s, int n) {  // GetItemNumByShape: empty -> 1
+  int64_t v = 1;
+  for (int i = 0; i < n; ++i) v *= s[i];
+  return v;
+}
+
+// CheckShapeForTransShapeToFracNz (format_transfer_fractal_nz.cc:39-57).
+bool check_shape_for_nz(int32_t format, const int64_t *shape, int rank) {
+  switch (format) {
+    case DCOPY_FORMAT_ND: return shape_valid(shape, rank);
+    case DCOPY_FORMAT_NCHW:
+    case DCOPY_FORMAT_NHWC: return rank == 4 && shape_valid(shape, rank);
+    default: return false;
+  }
+}
+
+// IsShapeArgValid (format_transfer_transpose.cc:45-77).
+bool shape_arg_valid(const int64_t *shape, int rank, const int64_t *perm, int perm_rank) {
+  if (rank <= 0 || !shape) return false;
+  for (int i = 0; i < rank; ++i)
+    if (shape[i] < 0) return false;
+  if (perm_rank != rank) return false;
+  int seen[kMaxRank] = {0};
+  for (int i = 0; i < perm_rank; ++i) {
+    if (perm[i] < 0 || perm[i] >= perm_rank || seen[perm[i]]) return false;
+    seen[perm[i]] = 1;
+  }
+  return true;
+}
+
+int check_args(const DcopyTransArgs *a) {
+  if (!a) return set_error(DCOPY_ERR_PARAM_INVALID, "TransArgs is NULL");
+  if (a->src_rank < 0 || a->src_rank > kMaxRank || a->dst_rank < 0 || a->dst_rank > kMaxRank ||
+      (a->src_rank && !a->src_shape) || (a->dst_rank && !a->dst_shape))
+    return set_error(DCOPY_ERR_PARAM_INVALID, "TransArgs shapes: rank must be 0..%d", kMaxRank);
+  return DCOPY_OK;
+}
+
+int store_length(uint64_t *len, uint64_t v) {
+  if (len) *len = v;
+  return DCOPY_OK;
+}
+
+// FormatTransferFractalNz::TransFormat (fractal_nz.cc:301-353).
+int fractal_nz_format(const DcopyTransArgs *a, void *dst, uint64_t cap, uint64_t *len,
+                      dcopy_stream_t s) {
+  const int32_t size = type_size(a->data_type);
+  if (size <= 0)
+    return set_error(DCOPY_ERR_DATATYPE_INVALID, "data type %d is not supported", a->data_type);
+  if (!check_shape_for_nz(a->src_format, a->src_shape, a->src_rank) ||
+      !shape_valid(a->dst_shape, a->dst_rank))
+    return set_error(DCOPY_ERR_SHAPE_INVALID, "trans format %d -> FRACTAL_NZ: invalid shapes",
+                     a->src_format);
+  int64_t expect[kMaxRank + 2], hw[3];
+  int erank = 0;
+  int rc = nz_shape(a->src_shape, a->src_rank, a->dst_c0, expect, &erank, hw);
+  if (rc) return rc;
+  if (a->dst_rank && !same_shape(a->dst_shape, a->dst_rank, expect, erank))  // :349-351
+    return set_error(DCOPY_ERR_SHAPE_INVALID, "dst shape differs from the FRACTAL_NZ shape");
+  const uint64_t bytes = (uint64_t)item_count(a->dst_shape, a->dst_rank) * size;
+  if (bytes == 0) return store_length(len, 0);  // :134-137
+  if (cap < bytes)
+    return set_error(DCOPY_ERR_PARAM_INVALID, "dst holds %llu bytes, result needs %llu",
+                     (unsigned long long)cap, (unsigned long long)bytes);
+  rc = nz_transfer(dst, a->data, a->src_shape, a->src_rank, size, a->dst_c0, true, s);
+  return rc ? rc : store_length(len, bytes);
+}
+
+// FormatTransferFractalNzND::TransFormat (fractal_nz.cc:397-446).
+int fractal_nz_nd_format(const DcopyTransArgs *a, void *dst, uint64_t cap, uint64_t *len,
+                         dcopy_stream_t s) {
+  const int32_t size = type_size(a->data_type);
+  if (size <= 0)
+    return set_error(DCOPY_ERR_DATATYPE_INVALID, "data type %d is not supported", a->data_type);
+  if (!shape_valid(a->src_shape, a->src_rank) ||
+      !check_shape_for_nz(a->dst_format, a->dst_shape, a->dst_rank))
+    return set_error(DCOPY_ERR_SHAPE_INVALID, "trans format FRACTAL_NZ -> %d: invalid shapes",
+                     a->dst_format);
+  int64_t expect[kMaxRank + 2], hw[3];  // CheckShapeRelationForTransShapeToFracNz, :113-129
+  int erank = 0;
+  int rc = nz_shape(a->dst_shape, a->dst_rank, a->src_c0, expect, &erank, hw);
+  if (rc) return rc;
+  if (!same_shape(a->src_shape, a->src_rank, expect, erank))
+    return set_error(DCOPY_ERR_SHAPE_INVALID, "src shape is not the FRACTAL_NZ shape of dst");
+  const uint64_t bytes = (uint64_t)item_count(a->dst_shape, a->dst_rank) * size;
+  if (bytes == 0) return store_length(len, 0);
+  if (cap < bytes)
+    return set_error(DCOPY_ERR_PARAM_INVALID, "dst holds %llu bytes, result needs %llu",
+                     (unsigned long long)cap, (unsigned long long)bytes);
+  rc = nz_transfer(dst, a->data, a->dst_shape, a->dst_rank, size, a->src_c0, false, s);
+  return rc ? rc : store_length(len, bytes);
+}
+
+// Transpose (transpose.cc:142-197) as an N-D box copy: the destination is
+// contiguous and the source strides are the permuted row-major heads.
+int transpose_impl(void *dst, const void *src, const int64_t *shape, const int64_t *perm,
+                   int rank, int32_t data_type, uint64_t cap, uint64_t *len, dcopy_stream_t s) {
+  const int32_t size = type_size(data_type);
+  if (!src) return set_error(DCOPY_ERR_PARAM_INVALID, "Transpose: the src is null");
+  if (size < 0)
+    return set_error(DCOPY_ERR_PARAM_INVALID, "Transpose: data type %d is not supported",
+                     data_type);
+  if (!shape_arg_valid(shape, rank, perm, rank))
+    return set_error(DCOPY_ERR_PARAM_INVALID, "Transpose: invalid shape or perm");
+  int64_t heads[kMaxRank];
+  for (int i = rank - 1; i >= 0; --i) heads[i] = (i == rank - 1) ? 1 : shape[i + 1] * heads[i + 1];
+  uint64_t sizes[kMaxRank];
+  int64_t ss[kMaxRank], ds[kMaxRank];
+  int64_t n = 1;
+  for (int i = 0; i < rank; ++i) {
+    sizes[i] = (uint64_t)shape[perm[i]];
+    ss[i] = heads[perm[i]];
+    n *= shape[perm[i]];
+  }
+  for (int i = rank - 1; i >= 0; --i) ds[i] = (i == rank - 1) ? 1 : (int64_t)sizes[i + 1] * ds[i + 1];
+  const uint64_t bytes = (uint64_t)n * size;
+  if (n == 0) return store_length(len, 0);
+  if (cap < bytes)
+    return set_error(DCOPY_ERR_PARAM_INVALID, "dst holds %llu bytes, result needs %llu",
+                     (unsigned long long)cap, (unsigned long long)bytes);
+  // Merge destination-adjacent dims that are also adjacent in the source, so
+  // that NCHW -> NHWC style permutes become a few long runs.
+  int m = 0;
+  uint64_t ms[kMaxRank];
+  int64_t mss[kMaxRank], mds[kMaxRank];
+  for (int i = 0; i < rank; ++i) {
+    if (sizes[i] == 1) continue;
+    if (m > 0 && mss[m - 1] == ss[i] * (int64_t)sizes[i] && mds[m - 1] == ds[i] * (int64_t)sizes[i]) {
+      ms[m - 1] *= sizes[i];
+      mss[m - 1] = ss[i];
+      mds[m - 1] = ds[i];
+      continue;
+    }
+    ms[m] = sizes[i];
+    mss[m] = ss[i];
+    mds[m] = ds[i];
+    ++m;
+  }
+  if (m == 0) {
+    ms[0] = 1;
+    mss[0] = 1;
+    mds[0] = 1;
+    m = 1;
+  }
+  if (m > 5)
+    return set_error(DCOPY_ERR_UNSUPPORTED, "Transpose: %d non-trivial dims (at most 5)", m);
+  const int rc = dcopy_copy_nd(dst, src, m, ms, mss, mds, (uint32_t)size, s);
+  return rc ? rc : store_length(len, bytes);
+}
+
+// FormatTransferTranspose::TransShape (transpose.cc:253-266).
+int transpose_shape(int32_t src_format, const int64_t *src_shape, int rank, int32_t dst_format,
+                    int64_t *dst_shape, int32_t *dst_rank) {
+  const PermEntry *e = find_perm(src_format, dst_format);
+  if (!e)
+    return set_error(DCOPY_ERR_FORMAT_INVALID, "no transpose from format %d to %d", src_format,
+                     dst_format);
+  if (!shape_arg_valid(src_shape, rank, e->perm, 4))
+    return set_error(DCOPY_ERR_SHAPE_INVALID, "transpose: invalid src shape for the perm");
+  for (int i = 0; i < 4; ++i) dst_shape[i] = src_shape[e->perm[i]];
+  *dst_rank = 4;
+  return DCOPY_OK;
+}
+
+// FormatTransferTranspose::TransFormat (transpose.cc:239-251).
+int transpose_format(const DcopyTransArgs *a, void *dst, uint64_t cap, uint64_t *len,
+                     dcopy_stream_t s) {
+  int64_t expect[4];
+  int32_t erank = 0;
+  int rc = transpose_shape(a->src_format, a->src_shape, a->src_rank, a->dst_format, expect, &erank);
+  if (rc) return rc;
+  if (a->dst_rank && !same_shape(a->dst_shape, a->dst_rank, expect, erank))
+    return set_error(DCOPY_ERR_SHAPE_INVALID, "transpose: dst shape differs from the permuted shape");
+  const PermEntry *e = find_perm(a->src_format, a->dst_format);
+  return transpose_impl(dst, a->data, a->src_shape, e->perm, a->src_rank, a->data_type, cap, len,
+                        s);
+}
+
+int class_format(int cls, const DcopyTransArgs *a, void *dst, uint64_t cap, uint64_t *len,
+                 dcopy_stream_t s) {
+  switch (cls) {
+    case DCOPY_TRANSFER_FRACTAL_NZ: return fractal_nz_format(a, dst, cap, len, s);
+    case DCOPY_TRANSFER_FRACTAL_NZ_ND: return fractal_nz_nd_format(a, dst, cap, len, s);
+    case DCOPY_TRANSFER_TRANSPOSE: return transpose_format(a, dst, cap, len, s);
+    default: return set_error(DCOPY_ERR_PARAM_INVALID, "unknown transfer class %d", cls);
+  }
+}
+
+int class_shape(int cls, int32_t src_format, const int64_t *src_shape, int32_t src_rank,
+                int32_t data_type, int32_t dst_format, int64_t c0, int64_t *dst_shape,
+                int32_t *dst_rank) {
+  if (!dst_shape || !dst_rank || src_rank < 0 || src_rank > kMaxRank || (src_rank && !src_shape))
+    return set_error(DCOPY_ERR_PARAM_INVALID, "TransShape: invalid arguments");
+  switch (cls) {
+    case DCOPY_TRANSFER_FRACTAL_NZ: {  // fractal_nz.cc:355-395
+      if (type_size(data_type) <= 0)
+        return set_error(DCOPY_ERR_DATATYPE_INVALID, "data type %d is not supported", data_type);
+      if (!check_shape_for_nz(src_format, src_shape, src_rank))
+        return set_error(DCOPY_ERR_SHAPE_INVALID, "format %d shape cannot become FRACTAL_NZ",
+                         src_format);
+      int64_t hw[3];
+      int n = 0;
+      const int rc = nz_shape(src_shape, src_rank, c0, dst_shape, &n, hw);
+      *dst_rank = n;
+      return rc;
+    }
+    case DCOPY_TRANSFER_FRACTAL_NZ_ND:  // fractal_nz.cc:448-457
+      return set_error(DCOPY_ERR_FORMAT_INVALID,
+                       "the shape derivation from FRACTAL_NZ is not unique");
+    case DCOPY_TRANSFER_TRANSPOSE:
+      return transpose_shape(src_format, src_shape, src_rank, dst_format, dst_shape, dst_rank);
+    default: return set_error(DCOPY_ERR_PARAM_INVALID, "unknown transfer class %d", cls);
+  }
+}
+
+}  // namespace
+}  // namespace dcopy
+
+using namespace dcopy;
+
+extern "C" int32_t dcopy_data_type_size(int32_t data_type) { return type_size(data_type); }
+
+extern "C" int dcopy_trans_data_format(const DcopyTransArgs *args, void *dst,
+                                       uint64_t dst_capacity, uint64_t *dst_length,
+                                       dcopy_stream_t stream) {
+  DCOPY_API_BEGIN
+  int rc = check_args(args);
+  if (rc) return rc;
+  const int cls = registered_class(args->src_format, args->dst_format);  // formats.cc:31-38
+  if (!cls)
+    return set_error(DCOPY_ERR_FORMAT_INVALID, "Failed to trans data from format %d to %d",
+                     args->src_format, args->dst_format);
+  if (!args->data && item_count(args->src_shape, args->src_rank) != 0)  // :40-49
+    return set_error(DCOPY_ERR_PARAM_INVALID, "input data is null and the shape is not empty");
+  return class_format(cls, args, dst, dst_capacity, dst_length, stream);
+  DCOPY_API_END
+}
+
+extern "C" int dcopy_trans_format(int transfer_class, const DcopyTransArgs *args, void *dst,
+                                  uint64_t dst_capacity, uint64_t *dst_length,
+                                  dcopy_stream_t stream) {
+  DCOPY_API_BEGIN
+  int rc = check_args(args);
+  if (rc) return rc;
+  return class_format(transfer_class, args, dst, dst_capacity, dst_length, stream);
+  DCOPY_API_END
+}
+
+extern "C" int dcopy_trans_shape(int transfer_class, int32_t src_format, const int64_t *src_shape,
+                                 int32_t src_rank, int32_t data_type, int32_t dst_format, int64_t c0,
+                                 int64_t *dst_shape, int32_t *dst_rank) {
+  DCOPY_API_BEGIN
+  return class_shape(transfer_class, src_format, src_shape, src_rank, data_type, dst_format, c0,
+                     dst_shape, dst_rank);
+  DCOPY_API_END
+}
+
+extern "C" int dcopy_trans_tensor_shape(int32_t src_format, const int64_t *src_shape,
+                                        int32_t src_rank, int32_t data_type, int32_t dst_format,
+                                        int64_t c0, int64_t *dst_shape, int32_t *dst_rank) {
+  DCOPY_API_BEGIN
+  const int cls = registered_class(src_format, dst_format);
+  if (!cls)
+    return set_error(DCOPY_ERR_FORMAT_INVALID, "Failed to trans shape from format %d to %d",
+                     src_format, dst_format);
+  return class_shape(cls, src_format, src_shape, src_rank, data_type, dst_format, c0, dst_shape,
+                     dst_rank);
+  DCOPY_API_END
+}
+
+extern "C" int dcopy_transpose(void *dst, const void *src, const int64_t *src_shape,
+                               const int64_t *perm, int32_t rank, int32_t data_type,
+                               dcopy_stream_t stream) {
+  DCOPY_API_BEGIN
+  if (rank < 0 || rank > kMaxRank || !perm)
+    return set_error(DCOPY_ERR_PARAM_INVALID, "Transpose: rank %d", rank);
+  return transpose_impl(dst, src, src_shape, perm, rank, data_type, UINT64_MAX, nullptr, stream);
+  DCOPY_API_END
+}
+
+extern "C" int dcopy_transpose_with_shape_check(void *dst, const void *src,
+                                                const int64_t *src_shape, const int64_t *dst_shape,
+                                                const int64_t *perm, int32_t rank,
+                                                int32_t data_type, dcopy_stream_t stream) {
+  DCOPY_API_BEGIN
+  if (rank < 0 || rank > kMaxRank || !perm)
+    return set_error(DCOPY_ERR_PARAM_INVALID, "Transpose: rank %d", rank);
+  // transpose.cc:203-205: the argument check comes first.
+  const int32_t size = type_size(data_type);
+  if (!src || size < 0 || !shape_arg_valid(src_shape, rank, perm, rank))
+    return set_error(DCOPY_ERR_PARAM_INVALID, "Transpose: invalid arguments");
+  bool mismatch = !dst_shape;
+  for (int i = 0; !mismatch && i < rank; ++i) mismatch = dst_shape[i] != src_shape[perm[i]];
+  const int rc =
+      transpose_impl(dst, src, src_shape, perm, rank, data_type, UINT64_MAX, nullptr, stream);
+  // transpose.cc:207-212 logs a dst_shape mismatch and carries on.
+  if (!rc && mismatch) set_error(DCOPY_OK, "Failed to trans axis: invalid dst shape");
+  return rc;
+  DCOPY_API_END
+}

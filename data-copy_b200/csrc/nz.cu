@@ -18,6 +18,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "internal.cuh"
 #include "launch.cuh"
 
 namespace dcopy {
@@ -215,6 +216,8 @@ __global__ void __launch_bounds__(kThreads) nz_smem_kernel(uint4 *__restrict__ d
   }
 }
 
+}  // namespace
+
 // Shape rules of TransShapeToFracNz (:65-111) and IsShapeValid
 // (formats_trans_utils.cc:88-107).
 constexpr int64_t kShapeItemNumMax = 1099511627776LL;
@@ -267,6 +270,8 @@ int nz_shape(const int64_t *nd, int rank, int64_t w0, int64_t *nz, int *nz_rank,
   return DCOPY_OK;
 }
 
+namespace {
+
 
 template <typename T>
 int launch_nz(void *dst, const void *src, const NzGeom &g, uint32_t ntiles, bool to_nz,
@@ -293,6 +298,8 @@ int launch_nz(void *dst, const void *src, const NzGeom &g, uint32_t ntiles, bool
     return launch(nz_kernel<T, true>, grid, dim3(kThreads), 0, s, "nz_kernel", d, sp, g, ntiles);
   return launch(nz_kernel<T, false>, grid, dim3(kThreads), 0, s, "nz_kernel", d, sp, g, ntiles);
 }
+
+}  // namespace
 
 int nz_transfer(void *dst, const void *src, const int64_t *nd_shape, int rank, int elem_bytes,
                 int64_t w0, bool to_nz, dcopy_stream_t stream) {
@@ -372,7 +379,6 @@ int nz_transfer(void *dst, const void *src, const int64_t *nd_shape, int rank, i
   }
 }
 
-}  // namespace
 }  // namespace dcopy
 
 using namespace dcopy;

@@ -29,7 +29,10 @@ __all__ = [
     "DataCopyTiling", "DcopyExtParams", "DcopyError", "DcopyUnavailable", "lib", "lib_path",
     "plan_tiling", "datacopy_small", "datacopy_large", "datacopy_pretranspose",
     "datacopy_contiguous", "copy_ext", "copy_ext_32b", "copy_nd", "nz_shape", "nd_to_nz",
-    "nz_to_nd", "status_to_ge",
+    "nz_to_nd", "status_to_ge", "DcopyTransArgs", "data_type_size", "trans_data_format",
+    "trans_format", "trans_shape", "trans_tensor_shape", "transpose",
+    "transpose_with_shape_check", "FORMAT", "DATA_TYPE", "TRANSFER_FRACTAL_NZ",
+    "TRANSFER_FRACTAL_NZ_ND", "TRANSFER_TRANSPOSE",
     "OK", "ERR_PARAM_INVALID", "ERR_SHAPE_INVALID", "ERR_DATATYPE_INVALID",
     "ERR_FORMAT_INVALID", "ERR_CUDA", "ERR_TIMEOUT", "ERR_UNSUPPORTED",
 ]
@@ -78,6 +81,23 @@ class DcopyExtParams(ctypes.Structure):
                 ("srcStride", ctypes.c_uint64), ("dstStride", ctypes.c_uint64)]
 
 
+class DcopyTransArgs(ctypes.Structure):
+    """TransArgs (register_format_transfer.h:25-42) with device data and primary formats."""
+    _fields_ = [("data", ctypes.c_void_p), ("src_format", ctypes.c_int32),
+                ("dst_format", ctypes.c_int32), ("src_c0", ctypes.c_int64),
+                ("dst_c0", ctypes.c_int64), ("src_shape", ctypes.POINTER(ctypes.c_int64)),
+                ("src_rank", ctypes.c_int32), ("dst_shape", ctypes.POINTER(ctypes.c_int64)),
+                ("dst_rank", ctypes.c_int32), ("data_type", ctypes.c_int32)]
+
+
+# GE enum values (metadef graph/types.h; api/python/ge/ge/graph/types.py).
+FORMAT = {"NCHW": 0, "NHWC": 1, "ND": 2, "NC1HWC0": 3, "FRACTAL_Z": 4, "C1HWNC0": 9,
+          "CHWN": 14, "HWCN": 16, "FRACTAL_NZ": 29, "RESERVED": 40}
+DATA_TYPE = {"FLOAT": 0, "FLOAT16": 1, "INT8": 2, "INT32": 3, "UINT8": 4, "INT16": 6,
+             "UINT16": 7, "UINT32": 8, "INT64": 9, "UINT64": 10, "DOUBLE": 11, "BOOL": 12,
+             "STRING": 13, "COMPLEX64": 16, "COMPLEX128": 17, "BF16": 27, "UNDEFINED": 28}
+TRANSFER_FRACTAL_NZ, TRANSFER_FRACTAL_NZ_ND, TRANSFER_TRANSPOSE = 1, 2, 3
+
 assert ctypes.sizeof(DataCopyTiling) == 20
 assert ctypes.sizeof(DcopyExtParams) == 24
 
@@ -105,6 +125,21 @@ _SIGNATURES = {
                                       ctypes.c_int64, _vp]),
     "dcopy_nz_to_nd": (ctypes.c_int, [_vp, _vp, _i64p, ctypes.c_int, ctypes.c_int,
                                       ctypes.c_int64, _vp]),
+    "dcopy_data_type_size": (ctypes.c_int32, [ctypes.c_int32]),
+    "dcopy_trans_data_format": (ctypes.c_int, [ctypes.POINTER(DcopyTransArgs), _vp,
+                                               ctypes.c_uint64, _u64p, _vp]),
+    "dcopy_trans_format": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(DcopyTransArgs), _vp,
+                                          ctypes.c_uint64, _u64p, _vp]),
+    "dcopy_trans_shape": (ctypes.c_int, [ctypes.c_int, ctypes.c_int32, _i64p, ctypes.c_int32,
+                                         ctypes.c_int32, ctypes.c_int32, ctypes.c_int64, _i64p,
+                                         ctypes.POINTER(ctypes.c_int32)]),
+    "dcopy_trans_tensor_shape": (ctypes.c_int, [ctypes.c_int32, _i64p, ctypes.c_int32,
+                                                ctypes.c_int32, ctypes.c_int32, ctypes.c_int64,
+                                                _i64p, ctypes.POINTER(ctypes.c_int32)]),
+    "dcopy_transpose": (ctypes.c_int, [_vp, _vp, _i64p, _i64p, ctypes.c_int32, ctypes.c_int32,
+                                       _vp]),
+    "dcopy_transpose_with_shape_check": (ctypes.c_int, [_vp, _vp, _i64p, _i64p, _i64p,
+                                                        ctypes.c_int32, ctypes.c_int32, _vp]),
 }
 
 
@@ -241,3 +276,86 @@ def nz_to_nd(dst, src, nd_shape: Sequence[int], elem_bytes: int, w0: int, stream
     arr, n = _shape_arg(nd_shape)
     _check(lib().dcopy_nz_to_nd(_ptr(dst), _ptr(src), arr, n, elem_bytes, w0, _stream(stream)),
            "dcopy_nz_to_nd")
+
+
+# ---- GE TransData level -------------------------------------------------------------
+
+def data_type_size(data_type: int) -> int:
+    """GetSizeByDataType: bytes per element, -1 for types without a fixed size."""
+    return lib().dcopy_data_type_size(data_type)
+
+
+def _trans_args(data, src_format, dst_format, src_shape, dst_shape, data_type, src_c0=16,
+                dst_c0=16):
+    src = (ctypes.c_int64 * max(len(src_shape), 1))(*src_shape)
+    dst = (ctypes.c_int64 * max(len(dst_shape), 1))(*dst_shape)
+    a = DcopyTransArgs(_ptr(data), src_format, dst_format, src_c0, dst_c0, src, len(src_shape),
+                       dst, len(dst_shape), data_type)
+    a._keep = (src, dst)
+    return a
+
+
+def trans_data_format(dst, data, src_format, dst_format, src_shape, dst_shape, data_type,
+                      dst_capacity, src_c0=16, dst_c0=16, stream=None) -> int:
+    """TransDataFormat (formats.cc:30-52) into `dst`; returns the result length in bytes."""
+    a = _trans_args(data, src_format, dst_format, src_shape, dst_shape, data_type, src_c0, dst_c0)
+    n = ctypes.c_uint64(0)
+    _check(lib().dcopy_trans_data_format(ctypes.byref(a), _ptr(dst), dst_capacity,
+                                         ctypes.byref(n), _stream(stream)),
+           "dcopy_trans_data_format")
+    return n.value
+
+
+def trans_format(transfer_class, dst, data, src_format, dst_format, src_shape, dst_shape,
+                 data_type, dst_capacity, src_c0=16, dst_c0=16, stream=None) -> int:
+    """FormatTransfer<class>::TransFormat; returns the result length in bytes."""
+    a = _trans_args(data, src_format, dst_format, src_shape, dst_shape, data_type, src_c0, dst_c0)
+    n = ctypes.c_uint64(0)
+    _check(lib().dcopy_trans_format(transfer_class, ctypes.byref(a), _ptr(dst), dst_capacity,
+                                    ctypes.byref(n), _stream(stream)), "dcopy_trans_format")
+    return n.value
+
+
+def _shape_call(fn, name, *head, src_shape, rest):
+    src = (ctypes.c_int64 * max(len(src_shape), 1))(*src_shape)
+    out = (ctypes.c_int64 * (len(src_shape) + 4))()
+    rank = ctypes.c_int32(0)
+    _check(fn(*head, src, len(src_shape), *rest, out, ctypes.byref(rank)), name)
+    return [out[i] for i in range(rank.value)]
+
+
+def trans_shape(transfer_class, src_format, src_shape, data_type, dst_format, c0=16):
+    """FormatTransfer<class>::TransShape."""
+    return _shape_call(lib().dcopy_trans_shape, "dcopy_trans_shape", transfer_class, src_format,
+                       src_shape=src_shape, rest=(data_type, dst_format, c0))
+
+
+def trans_tensor_shape(src_format, src_shape, data_type, dst_format, c0=16):
+    """TransTensorShape (formats.cc:54-71)."""
+    return _shape_call(lib().dcopy_trans_tensor_shape, "dcopy_trans_tensor_shape", src_format,
+                       src_shape=src_shape, rest=(data_type, dst_format, c0))
+
+
+def transpose(dst, src, src_shape, perm, data_type, stream=None) -> None:
+    """Transpose (format_transfer_transpose.cc:142-197) on the GPU."""
+    n = len(src_shape)
+    s = (ctypes.c_int64 * max(n, 1))(*src_shape)
+    p = (ctypes.c_int64 * max(len(perm), 1))(*perm)
+    if len(perm) != n:
+        raise DcopyError(ERR_PARAM_INVALID, "perm and shape ranks differ", "dcopy_transpose")
+    _check(lib().dcopy_transpose(_ptr(dst), _ptr(src), s, p, n, data_type, _stream(stream)),
+           "dcopy_transpose")
+
+
+def transpose_with_shape_check(dst, src, src_shape, dst_shape, perm, data_type,
+                               stream=None) -> None:
+    n = len(src_shape)
+    if len(perm) != n or len(dst_shape) != n:
+        raise DcopyError(ERR_PARAM_INVALID, "perm/shape ranks differ",
+                         "dcopy_transpose_with_shape_check")
+    s = (ctypes.c_int64 * max(n, 1))(*src_shape)
+    d = (ctypes.c_int64 * max(n, 1))(*dst_shape)
+    p = (ctypes.c_int64 * max(n, 1))(*perm)
+    _check(lib().dcopy_transpose_with_shape_check(_ptr(dst), _ptr(src), s, d, p, n, data_type,
+                                                  _stream(stream)),
+           "dcopy_transpose_with_shape_check")

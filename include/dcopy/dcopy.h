@@ -144,6 +144,84 @@ int dcopy_nd_to_nz(void *dst, const void *src, const int64_t *nd_shape, int rank
 int dcopy_nz_to_nd(void *dst, const void *src, const int64_t *nd_shape, int rank,
                    int elem_bytes, int64_t w0, dcopy_stream_t stream);
 
+/* ---- GE TransData level ------------------------------------------------------
+ * The format-transfer registry of GE (base/formats/formats.cc:30-71,
+ * register_format_transfer.h:25-95) on device buffers.  Formats and data types
+ * use GE's enum values (metadef graph/types.h, mirrored in
+ * api/python/ge/ge/graph/types.py); only PRIMARY formats are passed, with the
+ * C0 of each side given explicitly (TransArgs::src_c0_format/dst_c0_format).
+ * Registered pairs: {ND, NCHW, NHWC} <-> FRACTAL_NZ
+ * (format_transfer_fractal_nz.cc:459-464) and the 12 transposes among NCHW,
+ * NHWC, HWCN, CHWN (format_transfer_transpose.cc:268-279). */
+#define DCOPY_FORMAT_NCHW 0
+#define DCOPY_FORMAT_NHWC 1
+#define DCOPY_FORMAT_ND 2
+#define DCOPY_FORMAT_CHWN 14
+#define DCOPY_FORMAT_HWCN 16
+#define DCOPY_FORMAT_FRACTAL_NZ 29
+
+/* Transfer classes (the reference's FormatTransfer subclasses). */
+#define DCOPY_TRANSFER_FRACTAL_NZ 1    /* FormatTransferFractalNz   (ND/NCHW/NHWC -> NZ) */
+#define DCOPY_TRANSFER_FRACTAL_NZ_ND 2 /* FormatTransferFractalNzND (NZ -> ND/NCHW/NHWC) */
+#define DCOPY_TRANSFER_TRANSPOSE 3     /* FormatTransferTranspose   (4-D permutes)       */
+
+/* TransArgs (register_format_transfer.h:25-42) with device data. */
+typedef struct DcopyTransArgs {
+  const void *data;         /* source, device memory */
+  int32_t src_format;       /* primary GE Format of the source */
+  int32_t dst_format;       /* primary GE Format of the destination */
+  int64_t src_c0;           /* C0 of the source format (used by NZ -> ND) */
+  int64_t dst_c0;           /* C0 of the destination format (used by ND -> NZ) */
+  const int64_t *src_shape;
+  int32_t src_rank;
+  const int64_t *dst_shape; /* required by the transfers, as in the reference */
+  int32_t dst_rank;
+  int32_t data_type;        /* GE DataType */
+} DcopyTransArgs;
+
+/* GetSizeByDataType: bytes of one element, or -1 for types without a fixed
+ * byte size (string, resource, sub-byte types, undefined). */
+int32_t dcopy_data_type_size(int32_t data_type);
+
+/* TransDataFormat (formats.cc:30-52): FORMAT_INVALID for an unregistered pair,
+ * PARAM_INVALID for a NULL source with a non-empty shape, then the registered
+ * transfer's TransFormat.  The result (prod(dst_shape) elements) is written to
+ * `dst` (device, dst_capacity bytes; too small -> PARAM_INVALID) and its byte
+ * length stored in *dst_length. */
+int dcopy_trans_data_format(const DcopyTransArgs *args, void *dst, uint64_t dst_capacity,
+                            uint64_t *dst_length, dcopy_stream_t stream);
+
+/* FormatTransfer::TransFormat of one transfer class, with that class's own
+ * checks and status codes (format_transfer_fractal_nz.cc:301-353, 397-446;
+ * format_transfer_transpose.cc:239-251). */
+int dcopy_trans_format(int transfer_class, const DcopyTransArgs *args, void *dst,
+                       uint64_t dst_capacity, uint64_t *dst_length, dcopy_stream_t stream);
+
+/* FormatTransfer::TransShape of one transfer class (fractal_nz.cc:355-395,
+ * 448-457; transpose.cc:253-266).  `c0` is the C0 of dst_format.  dst_shape
+ * needs room for src_rank + 2 entries. */
+int dcopy_trans_shape(int transfer_class, int32_t src_format, const int64_t *src_shape,
+                      int32_t src_rank, int32_t data_type, int32_t dst_format, int64_t c0,
+                      int64_t *dst_shape, int32_t *dst_rank);
+
+/* TransTensorShape (formats.cc:54-71): registry dispatch of TransShape. */
+int dcopy_trans_tensor_shape(int32_t src_format, const int64_t *src_shape, int32_t src_rank,
+                             int32_t data_type, int32_t dst_format, int64_t c0,
+                             int64_t *dst_shape, int32_t *dst_rank);
+
+/* Transpose (format_transfer_transpose.cc:142-197) on the GPU:
+ * dst[i] = src[sum_k idx_k * src_heads[perm_k]] over the destination odometer,
+ * rank 1..5.  Every argument failure is PARAM_INVALID, as in the reference. */
+int dcopy_transpose(void *dst, const void *src, const int64_t *src_shape, const int64_t *perm,
+                    int32_t rank, int32_t data_type, dcopy_stream_t stream);
+
+/* TransposeWithShapeCheck (transpose.cc:200-215): like the reference, a
+ * dst_shape that differs from the permuted source shape is reported in
+ * dcopy_last_error_message() but does not fail the call. */
+int dcopy_transpose_with_shape_check(void *dst, const void *src, const int64_t *src_shape,
+                                     const int64_t *dst_shape, const int64_t *perm,
+                                     int32_t rank, int32_t data_type, dcopy_stream_t stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 static_assert(sizeof(DcopyExtParams) == 24, "DcopyExtParams layout");
