@@ -28,6 +28,8 @@ int check_launch(const char *kernel);
 // IPC mapping).  bytes == 0 only checks nothing.  Disabled when the environment
 // sets DCOPY_CHECK_POINTERS=0.
 int check_device_span(const void *ptr, uint64_t bytes, const char *name);
+// Start address of the allocation holding ptr (0 when it cannot be determined).
+uint64_t allocation_base(const void *ptr);
 // 0 when the byte ranges [a, a+an) and [b, b+bn) are disjoint, else PARAM_INVALID.
 int check_disjoint(const void *a, uint64_t an, const void *b, uint64_t bn, const char *what);
 

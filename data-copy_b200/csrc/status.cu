@@ -95,6 +95,16 @@ int check_device_span(const void *ptr, uint64_t bytes, const char *name) {
   return DCOPY_OK;
 }
 
+uint64_t allocation_base(const void *ptr) {
+  PfnPointerGetAttributes fn = pointer_attrs_fn();
+  if (!fn || !ptr) return 0;
+  CUdeviceptr start = 0;
+  CUpointer_attribute attr = CU_POINTER_ATTRIBUTE_RANGE_START_ADDR;
+  void *data = &start;
+  if (fn(1, &attr, &data, (CUdeviceptr)(uintptr_t)ptr) != CUDA_SUCCESS) return 0;
+  return (uint64_t)start;
+}
+
 int check_disjoint(const void *a, uint64_t an, const void *b, uint64_t bn, const char *what) {
   if (!an || !bn) return DCOPY_OK;
   const uint64_t pa = (uint64_t)(uintptr_t)a, pb = (uint64_t)(uintptr_t)b;

@@ -32,7 +32,9 @@ __all__ = [
     "nz_to_nd", "status_to_ge", "DcopyTransArgs", "data_type_size", "trans_data_format",
     "trans_format", "trans_shape", "trans_tensor_shape", "transpose",
     "transpose_with_shape_check", "FORMAT", "DATA_TYPE", "TRANSFER_FRACTAL_NZ",
-    "TRANSFER_FRACTAL_NZ_ND", "TRANSFER_TRANSPOSE",
+    "TRANSFER_FRACTAL_NZ_ND", "TRANSFER_TRANSPOSE", "shard_range", "enable_peer_access",
+    "p2p_copy", "p2p_ring_shift", "ipc_get_handle", "ipc_open_handle", "ipc_close_handle",
+    "signal", "wait_signal", "DcopyDevCopy", "copy_ext_multi",
     "OK", "ERR_PARAM_INVALID", "ERR_SHAPE_INVALID", "ERR_DATATYPE_INVALID",
     "ERR_FORMAT_INVALID", "ERR_CUDA", "ERR_TIMEOUT", "ERR_UNSUPPORTED",
 ]
@@ -98,6 +100,12 @@ DATA_TYPE = {"FLOAT": 0, "FLOAT16": 1, "INT8": 2, "INT32": 3, "UINT8": 4, "INT16
              "STRING": 13, "COMPLEX64": 16, "COMPLEX128": 17, "BF16": 27, "UNDEFINED": 28}
 TRANSFER_FRACTAL_NZ, TRANSFER_FRACTAL_NZ_ND, TRANSFER_TRANSPOSE = 1, 2, 3
 
+
+class DcopyDevCopy(ctypes.Structure):
+    """One device's strided copy for dcopy_copy_ext_multi."""
+    _fields_ = [("device", ctypes.c_int32), ("dst", ctypes.c_void_p), ("src", ctypes.c_void_p),
+                ("params", DcopyExtParams), ("stream", ctypes.c_void_p)]
+
 assert ctypes.sizeof(DataCopyTiling) == 20
 assert ctypes.sizeof(DcopyExtParams) == 24
 
@@ -140,6 +148,21 @@ _SIGNATURES = {
                                        _vp]),
     "dcopy_transpose_with_shape_check": (ctypes.c_int, [_vp, _vp, _i64p, _i64p, _i64p,
                                                         ctypes.c_int32, ctypes.c_int32, _vp]),
+    "dcopy_shard_range": (ctypes.c_int, [ctypes.c_uint64, ctypes.c_int32, ctypes.c_int32, _u64p,
+                                         _u64p]),
+    "dcopy_copy_ext_multi": (ctypes.c_int, [ctypes.POINTER(DcopyDevCopy), ctypes.c_int32]),
+    "dcopy_enable_peer_access": (ctypes.c_int, [ctypes.c_int32, ctypes.c_int32]),
+    "dcopy_p2p_copy": (ctypes.c_int, [_vp, _vp, ctypes.c_uint64, _vp]),
+    "dcopy_p2p_ring_shift": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int32),
+                                            ctypes.POINTER(ctypes.c_void_p),
+                                            ctypes.POINTER(ctypes.c_void_p),
+                                            ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32,
+                                            ctypes.c_uint64]),
+    "dcopy_ipc_get_handle": (ctypes.c_int, [_vp, ctypes.c_char_p, _u64p]),
+    "dcopy_ipc_open_handle": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "dcopy_ipc_close_handle": (ctypes.c_int, [_vp]),
+    "dcopy_signal": (ctypes.c_int, [_vp, ctypes.c_uint32, _vp]),
+    "dcopy_wait_signal": (ctypes.c_int, [_vp, ctypes.c_uint32, ctypes.c_uint64, _vp, _vp]),
 }
 
 
@@ -359,3 +382,74 @@ def transpose_with_shape_check(dst, src, src_shape, dst_shape, perm, data_type,
     _check(lib().dcopy_transpose_with_shape_check(_ptr(dst), _ptr(src), s, d, p, n, data_type,
                                                   _stream(stream)),
            "dcopy_transpose_with_shape_check")
+
+
+# ---- multi-GPU ------------------------------------------------------------------------
+
+def shard_range(block_count: int, rank: int, world: int):
+    """(begin, count) of the blocks `rank` of `world` owns (contiguous split)."""
+    b, c = ctypes.c_uint64(0), ctypes.c_uint64(0)
+    _check(lib().dcopy_shard_range(block_count, rank, world, ctypes.byref(b), ctypes.byref(c)),
+           "dcopy_shard_range")
+    return b.value, c.value
+
+
+def copy_ext_multi(copies) -> None:
+    """copies: iterable of (device, dst, src, (count, blen, sgap, dgap), stream)."""
+    items = list(copies)
+    arr = (DcopyDevCopy * max(len(items), 1))()
+    for i, (dev, dst, src, prm, stream) in enumerate(items):
+        arr[i] = DcopyDevCopy(dev, _ptr(dst), _ptr(src), DcopyExtParams(*prm),
+                              _stream(stream) if stream is not None else None)
+    _check(lib().dcopy_copy_ext_multi(arr, len(items)), "dcopy_copy_ext_multi")
+
+
+def enable_peer_access(device: int, peer: int) -> None:
+    _check(lib().dcopy_enable_peer_access(device, peer), "dcopy_enable_peer_access")
+
+
+def p2p_copy(dst, src, nbytes: int, stream=None) -> None:
+    """nbytes from local src to dst (this GPU's or a peer's memory), pushed over NVLink."""
+    _check(lib().dcopy_p2p_copy(_ptr(dst), _ptr(src), nbytes, _stream(stream)), "dcopy_p2p_copy")
+
+
+def p2p_ring_shift(devices, srcs, dsts, nbytes: int, streams=None) -> None:
+    """One process: device i copies srcs[i] into dsts[(i+1) % n]."""
+    n = len(devices)
+    devs = (ctypes.c_int32 * n)(*devices)
+    s = (ctypes.c_void_p * n)(*[_ptr(x) for x in srcs])
+    d = (ctypes.c_void_p * n)(*[_ptr(x) for x in dsts])
+    st = None
+    if streams is not None:
+        st = (ctypes.c_void_p * n)(*[_stream(x) for x in streams])
+    _check(lib().dcopy_p2p_ring_shift(devs, s, d, st, n, nbytes), "dcopy_p2p_ring_shift")
+
+
+def ipc_get_handle(ptr):
+    """(64-byte handle, offset) of the allocation holding a device pointer/tensor."""
+    buf = ctypes.create_string_buffer(64)
+    off = ctypes.c_uint64(0)
+    _check(lib().dcopy_ipc_get_handle(_ptr(ptr), buf, ctypes.byref(off)), "dcopy_ipc_get_handle")
+    return buf.raw, off.value
+
+
+def ipc_open_handle(handle: bytes) -> int:
+    """Maps another process's allocation; returns its base address here."""
+    out = ctypes.c_void_p()
+    _check(lib().dcopy_ipc_open_handle(handle, ctypes.byref(out)), "dcopy_ipc_open_handle")
+    return out.value
+
+
+def ipc_close_handle(base: int) -> None:
+    _check(lib().dcopy_ipc_close_handle(base), "dcopy_ipc_close_handle")
+
+
+def signal(flag, value: int, stream=None) -> None:
+    """Release-store `value` into a (possibly peer) 4-byte flag after earlier stream work."""
+    _check(lib().dcopy_signal(_ptr(flag), value, _stream(stream)), "dcopy_signal")
+
+
+def wait_signal(flag, value: int, timeout_ns: int, status, stream=None) -> None:
+    """Bounded device-side wait for *flag == value; writes 0 (seen) / 1 (timeout) to status."""
+    _check(lib().dcopy_wait_signal(_ptr(flag), value, timeout_ns, _ptr(status), _stream(stream)),
+           "dcopy_wait_signal")

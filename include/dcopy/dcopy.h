@@ -222,6 +222,65 @@ int dcopy_transpose_with_shape_check(void *dst, const void *src, const int64_t *
                                      const int64_t *dst_shape, const int64_t *perm,
                                      int32_t rank, int32_t data_type, dcopy_stream_t stream);
 
+/* ---- multi-GPU ----------------------------------------------------------------
+ * No counterpart in the reference (single-core Ascend kernels; SURVEY row e).
+ * Copies shard by splitting the blockCount range over devices with no
+ * exchange; the separate ring shift moves each device's shard to the next
+ * device with in-kernel stores over NVLink.  No TMA multicast is used. */
+
+/* Contiguous block range [*begin, *begin + *count) of `block_count` blocks that
+ * `rank` of `world` owns: the first block_count % world ranks get one more. */
+int dcopy_shard_range(uint64_t block_count, int32_t rank, int32_t world, uint64_t *begin,
+                      uint64_t *count);
+
+/* One strided copy per device, launched from one host thread (each on its own
+ * device and stream).  The current device is restored on return. */
+typedef struct DcopyDevCopy {
+  int32_t device;
+  void *dst;
+  const void *src;
+  DcopyExtParams params;
+  dcopy_stream_t stream;
+} DcopyDevCopy;
+int dcopy_copy_ext_multi(const DcopyDevCopy *copies, int32_t n);
+
+/* Lets `device` address `peer`'s memory (cudaDeviceEnablePeerAccess); OK when
+ * already enabled, PARAM_INVALID when the pair cannot be peers.  Process-wide
+ * and released with the process; it changes no setting of the GPU itself. */
+int dcopy_enable_peer_access(int32_t device, int32_t peer);
+
+/* bytes from local `src` to `dst`, which may be another GPU's memory mapped into
+ * this process (peer access or IPC): 128-bit stores pushed over NVLink. */
+int dcopy_p2p_copy(void *dst, const void *src, uint64_t bytes, dcopy_stream_t stream);
+
+/* Ring shift inside one process: device devices[i] copies src[i] (its own
+ * memory) into dst[(i + 1) % n] (memory of the next device), on streams[i]
+ * (NULL entries = that device's legacy default stream).  Peer access between
+ * ring neighbours is enabled as needed. */
+int dcopy_p2p_ring_shift(const int32_t *devices, void *const *src, void *const *dst,
+                         const dcopy_stream_t *streams, int32_t n, uint64_t bytes);
+
+/* CUDA IPC (multi-process): the 64-byte handle of the allocation holding
+ * dev_ptr and dev_ptr's byte offset inside it; another process of the same node
+ * opens the handle (peer access enabled lazily) and adds the offset.  Close the
+ * BASE pointer that dcopy_ipc_open_handle returned. */
+#define DCOPY_IPC_HANDLE_BYTES 64
+int dcopy_ipc_get_handle(const void *dev_ptr, void *handle, uint64_t *offset);
+int dcopy_ipc_open_handle(const void *handle, void **base_ptr);
+int dcopy_ipc_close_handle(void *base_ptr);
+
+/* Completion flags.  dcopy_signal stores `value` to *flag with release
+ * semantics at system scope after all earlier work on `stream` (the flag may
+ * live on another GPU).  dcopy_wait_signal launches a one-thread kernel that
+ * waits, with acquire loads, until *flag == value, at most timeout_ns
+ * nanoseconds (and a fixed iteration bound), then writes 0 (seen) or 1 (timed
+ * out) to *status (device memory) and returns; later work on `stream` runs
+ * after it either way.  The wait must not run on the same GPU as the kernel
+ * that sets the flag, unless that kernel is already complete. */
+int dcopy_signal(uint32_t *flag, uint32_t value, dcopy_stream_t stream);
+int dcopy_wait_signal(const uint32_t *flag, uint32_t value, uint64_t timeout_ns,
+                      uint32_t *status, dcopy_stream_t stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 static_assert(sizeof(DcopyExtParams) == 24, "DcopyExtParams layout");
