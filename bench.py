@@ -58,6 +58,8 @@ def parse_args():
     ap.add_argument("--impl", choices=["dcopy", "reference"], default="dcopy")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the secondary measurements (sweep, NZ, transpose)")
+    ap.add_argument("--workload", choices=["config2", "config5"], default="config2",
+                    help="config2 (headline, default) or config5 (sharded copy + NVLink ring)")
     return ap.parse_args()
 
 
@@ -381,6 +383,119 @@ def run_secondary(torch, dcopy, dev):
     return out
 
 
+# ---------------------------------------------------------------------------- config 5
+
+def run_config5(args, rank, world, local_rank):
+    """bf16 8 x 1 GiB, blockCount split over ranks for the local
+    strided copy (blockLen 2 KiB, gap 2 KiB), then a ring shift of each rank's
+    1 GiB shard to rank (r+1) mod N over NVLink (CUDA IPC, in-kernel stores)."""
+    import torch
+    import dcopy
+    from dcopy import multi
+    torch.cuda.set_device(local_rank)
+    dcopy.lib()
+    dev = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist_mod
+        dist = dist_mod
+    gib = 1 << 30
+    blen = gap = 2048
+    total_blocks = 8 * gib // (blen + gap)
+    b0, nb = dcopy.shard_range(total_blocks, rank, world)
+    g = torch.Generator(device=dev).manual_seed(3 + rank)
+    src = torch.empty(nb * (blen + gap) // 2, dtype=torch.bfloat16, device=dev)
+    src.view(torch.int16).random_(generator=g)
+    dst = torch.empty(nb * blen // 2, dtype=torch.bfloat16, device=dev)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize()
+
+    dcopy.copy_ext(dst, src, nb, blen, gap, 0)
+    torch.cuda.synchronize()
+    assert torch.equal(dst.view(torch.int16).view(nb, blen // 2),
+                       src.view(torch.int16).view(nb, (blen + gap) // 2)[:, : blen // 2])
+    for _ in range(max(args.warmup, 3)):
+        dcopy.copy_ext(dst, src, nb, blen, gap, 0)
+    barrier()
+    steps = max(1, min(args.steps, 50))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        dcopy.copy_ext(dst, src, nb, blen, gap, 0)
+    e1.record()
+    e1.synchronize()
+    barrier()
+    t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    local_bytes = 2 * (total_blocks * blen)  # all ranks: 4 GiB read + 4 GiB written
+    local_value = local_bytes * steps / (float(t.item()) / 1e3) / 1e9
+    del src
+
+    p2p = None
+    if world > 1:
+        shard = gib
+        send = torch.empty(shard, dtype=torch.uint8, device=dev)
+        send.fill_(rank + 1)
+        recv = torch.zeros(shard, dtype=torch.uint8, device=dev)
+        flags = torch.zeros(4, dtype=torch.int32, device=dev)
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        barrier()
+        peer = multi.map_next_peer(recv, flags, rank, world)
+        try:
+            seq = 0
+
+            def exchange():
+                nonlocal seq
+                seq += 1
+                multi.ring_shift(send, shard, peer, seq)
+                multi.wait_ring(flags, seq, status, timeout_ns=20_000_000_000)
+
+            for _ in range(2):
+                exchange()
+            torch.cuda.synchronize()
+            assert status.item() == 0, "ring shift flag timed out"
+            assert torch.equal(recv[:4096], torch.full((4096,), ((rank - 1) % world) + 1,
+                                                       dtype=torch.uint8, device=dev))
+            barrier()
+            psteps = max(1, min(args.steps, 10))
+            p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            p0.record()
+            for _ in range(psteps):
+                exchange()
+            p1.record()
+            p1.synchronize()
+            ok = torch.tensor([status.item() == 0], dtype=torch.int32, device=dev)
+            pt = torch.tensor([p0.elapsed_time(p1)], dtype=torch.float64, device=dev)
+            barrier()
+            dist.all_reduce(pt, op=dist.ReduceOp.MAX)
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+            per_dir = shard * psteps / (float(pt.item()) / 1e3) / 1e9
+            p2p = {"per_direction_GBps": round(per_dir, 1),
+                   "aggregate_GBps": round(per_dir * world, 1),
+                   "reference_peak_GBps": 770.0, "frac_of_measured_peer_copy": round(per_dir / 770.0, 4),
+                   "bytes_per_rank_per_step": shard, "steps": psteps, "flags_ok": bool(ok.item()),
+                   "path": "dcopy_p2p_copy into the next rank's IPC-mapped buffer + release flag; "
+                           "bounded device-side wait on this rank's flag"}
+        finally:
+            barrier()
+            peer.release()
+    if rank != 0:
+        return None
+    return {"metric": METRIC, "value": round(local_value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": steps, "warmup": args.warmup,
+            "ms_per_step": round(float(t.item()) / steps, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random bf16 bit patterns from seed 3+rank)",
+            "config": {"workload": "config5: bf16 8 x 1 GiB, blockLen 2 KiB, srcStride gap 2 KiB, "
+                                   "blockCount split over ranks; ring shift of 1 GiB per rank",
+                       "blocks_per_rank": nb, "l2": "inputs larger than L2 (8/N GiB per rank)"},
+            "p2p": p2p}
+
+
 # ---------------------------------------------------------------------------- reference arm
 
 def run_reference(args):
@@ -427,11 +542,18 @@ def main():
         import datetime
         import torch
         import torch.distributed as dist
+        # NCCL's version banner goes to stdout at INFO/VERSION level; rank 0's stdout
+        # must carry exactly one JSON line.
+        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+            os.environ["NCCL_DEBUG"] = "WARN"
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        line = run_dcopy(args, rank, world, local_rank)
+        if args.workload == "config5":
+            line = run_config5(args, rank, world, local_rank)
+        else:
+            line = run_dcopy(args, rank, world, local_rank)
         if rank == 0:
             print(json.dumps(line), flush=True)
     finally:
