@@ -1,0 +1,359 @@
+// dcopy_bench: the C++ measurement tool of the library (it replaces the reference's
+// msprof harness standalone_datacopy/profile.py and its host address model
+// test_address_model.py).  Every result is verified on the host before it is timed.
+//
+//   dcopy_bench sweep [--moved-mib M] [--reps R] [--device D]
+//       blockLen x gap sweep of dcopy_copy_ext on an int32
+//       element-index source; one JSON line per point with measured GB/s, the
+//       fraction of the copy peak and a DRAM-atom model of the achievable rate.
+//   dcopy_bench standalone ROWS COLS SMALL_KIB LARGE_KIB [--trials N] [--device D]
+//                          [--output DIR] [--peak GBPS]
+//       profile.py main(): verify small/large/pretranspose with STORE=1, then time
+//       `trials` rounds with STORE=0 in rotated order and write config.json,
+//       raw.csv, stages.csv and summary.json (device time per kernel from CUDA
+//       events in place of msprof's Task Duration).
+//   dcopy_bench nz [--batch B] [--h H] [--w W] [--reps R] [--device D]
+//       fp16 ND -> FRACTAL_NZ -> ND, round trip verified.
+//
+// Timing: CUDA events around each launch; a 512 MiB write between reps flushes
+// the 126 MB L2, so every rep reads cold data.
+#include <cuda_runtime.h>
+#include <sys/stat.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <fstream>
+#include <iostream>
+#include <map>
+#include <sstream>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "dcopy/dcopy.h"
+
+namespace {
+
+void Check(cudaError_t e, const char *what) {
+  if (e != cudaSuccess)
+    throw std::runtime_error(std::string(what) + ": " + cudaGetErrorName(e));
+}
+
+void CheckD(int rc) {
+  if (rc != DCOPY_OK) throw std::runtime_error(dcopy_last_error_message());
+}
+
+struct Args {
+  std::vector<std::string> pos;
+  std::map<std::string, std::string> opt;
+  Args(int argc, char **argv) {
+    for (int i = 2; i < argc; ++i) {
+      std::string a = argv[i];
+      if (a.rfind("--", 0) == 0 && i + 1 < argc)
+        opt[a.substr(2)] = argv[++i];
+      else
+        pos.push_back(a);
+    }
+  }
+  double num(const std::string &k, double d) const {
+    auto it = opt.find(k);
+    return it == opt.end() ? d : std::stod(it->second);
+  }
+  std::string str(const std::string &k, const std::string &d) const {
+    auto it = opt.find(k);
+    return it == opt.end() ? d : it->second;
+  }
+};
+
+struct DevBuf {
+  void *p = nullptr;
+  size_t n = 0;
+  explicit DevBuf(size_t bytes) : n(bytes) { Check(cudaMalloc(&p, bytes), "cudaMalloc"); }
+  ~DevBuf() {
+    if (p) cudaFree(p);
+  }
+  DevBuf(const DevBuf &) = delete;
+  DevBuf &operator=(const DevBuf &) = delete;
+};
+
+// Times `fn` (one or more launches on `s`) `reps` times with an L2 flush between reps.
+template <typename F>
+std::vector<double> time_reps(F fn, int reps, cudaStream_t s, DevBuf &flush) {
+  cudaEvent_t a, b;
+  Check(cudaEventCreate(&a), "event");
+  Check(cudaEventCreate(&b), "event");
+  std::vector<double> us;
+  for (int r = 0; r < reps; ++r) {
+    Check(cudaMemsetAsync(flush.p, r & 0xFF, flush.n, s), "flush");
+    Check(cudaEventRecord(a, s), "record");
+    fn();
+    Check(cudaEventRecord(b, s), "record");
+    Check(cudaEventSynchronize(b), "sync");
+    float ms = 0;
+    Check(cudaEventElapsedTime(&ms, a, b), "elapsed");
+    us.push_back(ms * 1e3);
+  }
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  return us;
+}
+
+double median(std::vector<double> v) {
+  std::sort(v.begin(), v.end());
+  const size_t n = v.size();
+  return n % 2 ? v[n / 2] : 0.5 * (v[n / 2 - 1] + v[n / 2]);
+}
+
+// ---- sweep ---------------------------------------------------------------------
+
+// DRAM-atom model: HBM moves 64-byte atoms, so a burst of blen bytes that starts
+// on a 64-byte boundary costs ceil(blen/64)*64 bytes read unless its neighbour
+// burst shares the atom (gap 0); writes to the packed destination are whole atoms.
+double model_gbps(double peak, uint64_t blen, uint64_t gap) {
+  const double read = gap == 0 ? double(blen) : std::ceil(blen / 64.0) * 64.0;
+  return peak * (2.0 * blen) / (read + blen);
+}
+
+int run_sweep(const Args &a) {
+  const uint64_t moved = uint64_t(a.num("moved-mib", 256)) << 20;
+  const int reps = int(a.num("reps", 10));
+  const double peak = a.num("peak", 6543.4);
+  Check(cudaSetDevice(int(a.num("device", 0))), "cudaSetDevice");
+  cudaStream_t s;
+  Check(cudaStreamCreate(&s), "stream");
+  const uint64_t src_bytes = moved * 17;  // gap 16x
+  DevBuf src(src_bytes), dst(moved), flush(512ull << 20);
+  {  // int32 element-index source
+    std::vector<int32_t> host(src_bytes / 4);
+    for (size_t i = 0; i < host.size(); ++i) host[i] = int32_t(i);
+    Check(cudaMemcpy(src.p, host.data(), src_bytes, cudaMemcpyHostToDevice), "H2D");
+  }
+  std::vector<int32_t> out(moved / 4);
+  for (uint64_t blen : {32ull, 64ull, 128ull, 512ull, 4096ull, 65536ull}) {
+    for (uint64_t gx : {0ull, 1ull, 4ull, 16ull}) {
+      const uint64_t gap = gx * blen, count = moved / blen;
+      DcopyExtParams p{uint32_t(count), uint32_t(blen), gap, 0};
+      Check(cudaMemsetAsync(dst.p, 0xA5, moved, s), "memset");
+      CheckD(dcopy_copy_ext(dst.p, src.p, &p, reinterpret_cast<dcopy_stream_t>(s)));
+      Check(cudaMemcpy(out.data(), dst.p, moved, cudaMemcpyDeviceToHost), "D2H");
+      // Address model (test_address_model.py:24): dst word j comes from block
+      // j / (blen/4) at word offset j % (blen/4) of source byte block*(blen+gap).
+      const uint64_t wpb = blen / 4, spb = (blen + gap) / 4;
+      for (uint64_t j = 0; j < out.size(); ++j) {
+        const int32_t expect = int32_t((j / wpb) * spb + j % wpb);
+        if (out[j] != expect)
+          throw std::runtime_error("sweep mismatch at blen " + std::to_string(blen) + " gap " +
+                                   std::to_string(gap) + " word " + std::to_string(j));
+      }
+      auto us = time_reps(
+          [&] { CheckD(dcopy_copy_ext(dst.p, src.p, &p, reinterpret_cast<dcopy_stream_t>(s))); },
+          reps, s, flush);
+      const double med = median(us), gbps = 2.0 * moved / (med * 1e3);
+      std::cout << "{\"config\": 3, \"blockLen\": " << blen << ", \"gap\": " << gap
+                << ", \"blockCount\": " << count << ", \"moved_bytes\": " << moved
+                << ", \"median_us\": " << med << ", \"GBps\": " << gbps
+                << ", \"frac_of_peak\": " << gbps / peak
+                << ", \"model_GBps\": " << model_gbps(peak, blen, gap)
+                << ", \"frac_of_model\": " << gbps / model_gbps(peak, blen, gap)
+                << ", \"verified\": true}" << std::endl;
+    }
+  }
+  cudaStreamDestroy(s);
+  return 0;
+}
+
+// ---- standalone (profile.py) ------------------------------------------------------
+
+struct Stage {
+  std::string kernel;
+  double us;
+};
+
+int run_standalone(const Args &a) {
+  if (a.pos.size() != 4)
+    throw std::runtime_error("standalone ROWS COLS SMALL_KIB LARGE_KIB [--trials N] ...");
+  const uint32_t rows = std::stoul(a.pos[0]), cols = std::stoul(a.pos[1]);
+  const uint32_t small_kib = std::stoul(a.pos[2]), large_kib = std::stoul(a.pos[3]);
+  const int trials = int(a.num("trials", 3));
+  const int device = int(a.num("device", 0));
+  const std::string outdir = a.str("output", "");
+  if (trials < 1 || device < 0 || device > 255)
+    throw std::runtime_error("trials >= 1; device: 0..255");
+  DataCopyTiling small{}, large{};
+  CheckD(dcopy_plan_tiling(rows, cols, small_kib, 1, &small));  // profile.py:133-137
+  CheckD(dcopy_plan_tiling(rows, cols, large_kib, 1, &large));
+  if (small.ub_bytes >= large.ub_bytes)
+    throw std::runtime_error("Actual small tile must be smaller than large tile");
+  if (!outdir.empty() && mkdir(outdir.c_str(), 0755) != 0)  // profile.py:158 exist_ok=False
+    throw std::runtime_error("output directory must not exist: " + outdir);
+  Check(cudaSetDevice(device), "cudaSetDevice");
+  cudaStream_t s;
+  Check(cudaStreamCreate(&s), "stream");
+  dcopy_stream_t ds = reinterpret_cast<dcopy_stream_t>(s);
+  const size_t bytes = size_t(rows) * cols * 4;
+  DevBuf x(bytes), y(bytes), b(bytes), flush(512ull << 20);
+  std::vector<int32_t> input(bytes / 4), output(bytes / 4);
+  for (size_t i = 0; i < input.size(); ++i) input[i] = int32_t(i * 17 + 3);
+  Check(cudaMemcpy(x.p, input.data(), bytes, cudaMemcpyHostToDevice), "H2D");
+  const std::vector<std::string> modes = {"small", "large", "pretranspose"};
+  auto run_mode = [&](const std::string &mode, uint32_t store, std::vector<Stage> *stages) {
+    DataCopyTiling t = mode == "small" ? small : large;
+    t.store = store;
+    cudaEvent_t e[3];
+    for (auto &ev : e) Check(cudaEventCreate(&ev), "event");
+    Check(cudaMemsetAsync(flush.p, 0x5A, flush.n, s), "flush");
+    Check(cudaEventRecord(e[0], s), "record");
+    if (mode == "small") CheckD(dcopy_datacopy_small(x.p, y.p, &t, ds));
+    if (mode == "large") CheckD(dcopy_datacopy_large(x.p, y.p, &t, ds));
+    if (mode == "pretranspose") CheckD(dcopy_datacopy_pretranspose(x.p, b.p, &t, ds));
+    Check(cudaEventRecord(e[1], s), "record");
+    if (mode == "pretranspose") CheckD(dcopy_datacopy_contiguous(b.p, y.p, &t, ds));
+    Check(cudaEventRecord(e[2], s), "record");
+    Check(cudaEventSynchronize(e[2]), "sync");
+    float m1 = 0, m2 = 0;
+    Check(cudaEventElapsedTime(&m1, e[0], e[1]), "elapsed");
+    Check(cudaEventElapsedTime(&m2, e[1], e[2]), "elapsed");
+    if (stages) {
+      if (mode == "pretranspose") {
+        stages->push_back({"datacopy_pretranspose", m1 * 1e3});
+        stages->push_back({"datacopy_contiguous", m2 * 1e3});
+      } else {
+        stages->push_back({"datacopy_" + mode, m1 * 1e3});
+      }
+    }
+    for (auto &ev : e) cudaEventDestroy(ev);
+  };
+  // Verification runs: STORE=1, every element checked (asc:149-155).
+  for (const auto &mode : modes) {
+    Check(cudaMemset(y.p, 0xA5, bytes), "memset");
+    run_mode(mode, 1, nullptr);
+    Check(cudaMemcpy(output.data(), y.p, bytes, cudaMemcpyDeviceToHost), "D2H");
+    for (uint32_t c = 0; c < cols; ++c)
+      for (uint32_t r = 0; r < rows; ++r)
+        if (output[size_t(c) * rows + r] != input[size_t(r) * cols + c])
+          throw std::runtime_error(mode + " verification failed at " + std::to_string(r) + "," +
+                                   std::to_string(c));
+  }
+  // Timed runs: STORE=0 (pretranspose always writes B), rotated order (profile.py:183-186).
+  std::map<std::string, std::vector<std::vector<Stage>>> rec;
+  for (int trial = 0; trial < trials; ++trial)
+    for (int k = 0; k < 3; ++k) {
+      const std::string &mode = modes[(trial + k) % 3];
+      std::vector<Stage> st;
+      run_mode(mode, 0, &st);
+      rec[mode].push_back(st);
+    }
+  std::ostringstream sum;
+  std::map<std::string, double> med;
+  sum << "{\n  \"metric\": \"device time per workflow (CUDA events; task_duration_us = sum of "
+         "the workflow's kernels)\",\n  \"results\": {";
+  std::ostringstream raw, stages_csv;
+  raw << "mode,trial,rows,cols,tile_cols,tile_bytes,tile_count,task_duration_us\n";
+  stages_csv << "mode,trial,kernel,duration_us\n";
+  for (size_t mi = 0; mi < modes.size(); ++mi) {
+    const std::string &mode = modes[mi];
+    const DataCopyTiling &t = mode == "small" ? small : large;
+    std::vector<double> total, pre, load;
+    for (size_t tr = 0; tr < rec[mode].size(); ++tr) {
+      double tot = 0;
+      for (const auto &st : rec[mode][tr]) {
+        tot += st.us;
+        stages_csv << mode << ',' << tr << ',' << st.kernel << ',' << st.us << '\n';
+      }
+      total.push_back(tot);
+      pre.push_back(mode == "pretranspose" ? rec[mode][tr][0].us : 0.0);
+      load.push_back(rec[mode][tr].back().us);
+      raw << mode << ',' << tr << ',' << rows << ',' << cols << ',' << t.tile_cols << ','
+          << t.ub_bytes << ',' << (cols + t.tile_cols - 1) / t.tile_cols << ',' << tot << '\n';
+    }
+    med[mode] = median(total);
+    sum << (mi ? "," : "") << "\n    \"" << mode << "\": {\"task_duration_us\": " << med[mode]
+        << ", \"pretranspose_duration_us\": " << median(pre)
+        << ", \"load_duration_us\": " << median(load)
+        << ", \"min_task_duration_us\": " << *std::min_element(total.begin(), total.end())
+        << ", \"max_task_duration_us\": " << *std::max_element(total.begin(), total.end())
+        << ", \"GBps\": " << (mode == "pretranspose" ? 3.0 : 1.0) * bytes / (med[mode] * 1e3)
+        << "}";
+  }
+  sum << "\n  },\n  \"small_over_large_duration\": " << med["small"] / med["large"]
+      << ",\n  \"pretranspose_over_large_duration\": " << med["pretranspose"] / med["large"]
+      << ",\n  \"verification\": \"PASS\"\n}\n";
+  std::cout << sum.str();
+  if (!outdir.empty()) {
+    std::ofstream(outdir + "/summary.json") << sum.str();
+    std::ofstream(outdir + "/raw.csv") << raw.str();
+    std::ofstream(outdir + "/stages.csv") << stages_csv.str();
+    std::ofstream(outdir + "/config.json")
+        << "{\"rows\": " << rows << ", \"cols\": " << cols << ", \"small_kib\": " << small_kib
+        << ", \"large_kib\": " << large_kib << ", \"trials\": " << trials
+        << ", \"device\": " << device << ", \"input_bytes\": " << bytes << "}\n";
+  }
+  cudaStreamDestroy(s);
+  return 0;
+}
+
+// ---- nz ---------------------------------------------------------------------------
+
+int run_nz(const Args &a) {
+  const int64_t shape[3] = {int64_t(a.num("batch", 16)), int64_t(a.num("h", 4096)),
+                            int64_t(a.num("w", 4096))};
+  const int reps = int(a.num("reps", 10));
+  const double peak = a.num("peak", 6543.4);
+  Check(cudaSetDevice(int(a.num("device", 0))), "cudaSetDevice");
+  cudaStream_t s;
+  Check(cudaStreamCreate(&s), "stream");
+  dcopy_stream_t ds = reinterpret_cast<dcopy_stream_t>(s);
+  int64_t nz[5], hw[3];
+  int nz_rank = 0;
+  CheckD(dcopy_nz_shape(shape, 3, 16, nz, &nz_rank, hw));
+  uint64_t nd_elems = uint64_t(shape[0]) * shape[1] * shape[2], nz_elems = 1;
+  for (int i = 0; i < nz_rank; ++i) nz_elems *= nz[i];
+  DevBuf nd(nd_elems * 2), z(nz_elems * 2), back(nd_elems * 2), flush(512ull << 20);
+  std::vector<uint16_t> host(nd_elems), host2(nd_elems);
+  uint64_t x = 0x9E3779B97F4A7C15ull;  // splitmix64 bit patterns
+  for (auto &v : host) {
+    x += 0x9E3779B97F4A7C15ull;
+    uint64_t z2 = x;
+    z2 = (z2 ^ (z2 >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z2 = (z2 ^ (z2 >> 27)) * 0x94D049BB133111EBull;
+    v = uint16_t(z2 ^ (z2 >> 31));
+  }
+  Check(cudaMemcpy(nd.p, host.data(), nd_elems * 2, cudaMemcpyHostToDevice), "H2D");
+  CheckD(dcopy_nd_to_nz(z.p, nd.p, shape, 3, 2, 16, ds));
+  CheckD(dcopy_nz_to_nd(back.p, z.p, shape, 3, 2, 16, ds));
+  Check(cudaMemcpy(host2.data(), back.p, nd_elems * 2, cudaMemcpyDeviceToHost), "D2H");
+  if (std::memcmp(host.data(), host2.data(), nd_elems * 2) != 0)
+    throw std::runtime_error("ND -> NZ -> ND round trip differs");
+  auto t1 = time_reps([&] { CheckD(dcopy_nd_to_nz(z.p, nd.p, shape, 3, 2, 16, ds)); }, reps, s,
+                      flush);
+  auto t2 = time_reps([&] { CheckD(dcopy_nz_to_nd(back.p, z.p, shape, 3, 2, 16, ds)); }, reps, s,
+                      flush);
+  const double g1 = double(nd_elems * 2 + nz_elems * 2) / (median(t1) * 1e3);
+  const double g2 = double(nd_elems * 2 + nz_elems * 2) / (median(t2) * 1e3);
+  std::cout << "{\"config\": 4, \"shape\": [" << shape[0] << ", " << shape[1] << ", " << shape[2]
+            << "], \"nd_to_nz_us\": " << median(t1) << ", \"nd_to_nz_GBps\": " << g1
+            << ", \"nz_to_nd_us\": " << median(t2) << ", \"nz_to_nd_GBps\": " << g2
+            << ", \"frac_of_peak\": [" << g1 / peak << ", " << g2 / peak
+            << "], \"round_trip_bit_exact\": true}" << std::endl;
+  cudaStreamDestroy(s);
+  return 0;
+}
+
+}  // namespace
+
+int main(int argc, char **argv) {
+  try {
+    if (argc < 2) throw std::runtime_error("usage: dcopy_bench sweep|standalone|nz [options]");
+    const std::string cmd = argv[1];
+    Args a(argc, argv);
+    if (cmd == "sweep") return run_sweep(a);
+    if (cmd == "standalone") return run_standalone(a);
+    if (cmd == "nz") return run_nz(a);
+    throw std::runtime_error("unknown command " + cmd);
+  } catch (const std::exception &e) {
+    std::cerr << "dcopy_bench: " << e.what() << '\n';
+    return 1;
+  }
+}
