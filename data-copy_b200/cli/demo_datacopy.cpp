@@ -92,11 +92,20 @@ int main(int argc, char **argv) {
       cudaEvent_t e0, e1;
       Check(cudaEventCreate(&e0));
       Check(cudaEventCreate(&e1));
-      // The tiling lives in device memory as in the reference (asc:133); the
-      // library reads it once on the host side, so read it before timing.
+      // The tiling lives in device memory as in the reference (asc:133).  Reading
+      // it costs the library one synchronising 20-byte copy, so the timed launch
+      // below uses a host copy of it.
       DataCopyTiling check{};
       Check(cudaMemcpy(&check, gt, sizeof(check), cudaMemcpyDeviceToHost));
       dcopy_stream_t s = reinterpret_cast<dcopy_stream_t>(stream);
+      // One untimed launch first, with the tiling read from device memory as the
+      // reference passes it: CUDA loads a kernel's module on its first launch,
+      // which would otherwise dominate the single timed run.
+      if (mode == "pretranspose")
+        CheckD(dcopy_datacopy_pretranspose(x.data, b.data, gt, s));
+      else
+        CheckD(dcopy_datacopy_small(x.data, y.data, gt, s));
+      if (t.store) Check(cudaMemsetAsync(y.data, 0xA5, bytes, stream));
       Check(cudaEventRecord(e0, stream));
       if (mode == "small") {
         CheckD(dcopy_datacopy_small(x.data, y.data, &check, s));
