@@ -24,6 +24,7 @@
 
 #include "common.cuh"
 #include "copy.cuh"
+#include "internal.cuh"
 #include "launch.cuh"
 
 namespace dcopy {
@@ -171,6 +172,30 @@ int run_tiles(int phase, const void *in, void *out, const DataCopyTiling *tp,
 }
 
 }  // namespace
+
+int run_pretranspose_workflow(const void *x, void *scratch, uint64_t scratch_bytes, void *y,
+                              const DataCopyTiling *tp, dcopy_stream_t stream) {
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  DataCopyTiling t;
+  int rc = fetch_tiling(tp, s, &t);
+  if (rc) return rc;
+  const uint64_t bytes = (uint64_t)t.rows * t.cols * 4u;
+  if (bytes > scratch_bytes)
+    return set_error(DCOPY_ERR_PARAM_INVALID,
+                     "pretranspose workflow: rows*cols*4 = %llu bytes exceeds the %llu-byte "
+                     "static B buffer",
+                     (unsigned long long)bytes, (unsigned long long)scratch_bytes);
+  rc = check_device_span(x, bytes, "x");
+  if (!rc && t.store) rc = check_device_span(y, bytes, "y");
+  if (!rc && t.store) rc = check_disjoint(x, bytes, y, bytes, "datacopy");
+  if (rc) return rc;
+  if ((uintptr_t)x % 4 || (t.store && (uintptr_t)y % 4))
+    return set_error(DCOPY_ERR_PARAM_INVALID, "datacopy: int32 buffers must be 4-byte aligned");
+  rc = launch_transpose(x, scratch, t.rows, t.cols, true, s);  // RunTiles<1>: B always written
+  if (rc) return rc;
+  return t.store ? copy_linear(y, scratch, bytes, s) : load_linear(scratch, bytes, s);
+}
+
 }  // namespace dcopy
 
 using namespace dcopy;

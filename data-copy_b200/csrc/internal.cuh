@@ -17,4 +17,10 @@ int nz_shape(const int64_t *nd, int rank, int64_t w0, int64_t *nz, int *nz_rank,
 int nz_transfer(void *dst, const void *src, const int64_t *nd_shape, int rank, int elem_bytes,
                 int64_t w0, bool to_nz, dcopy_stream_t stream);
 
+// The reference's pretranspose workflow (asc:144-146): x -> B with RunTiles<1>,
+// then B -> y with RunTiles<2>, through a B buffer of scratch_bytes bytes that
+// the caller of this function guarantees is device memory (it is not checked).
+int run_pretranspose_workflow(const void *x, void *scratch, uint64_t scratch_bytes, void *y,
+                              const DataCopyTiling *tiling, dcopy_stream_t stream);
+
 }  // namespace dcopy

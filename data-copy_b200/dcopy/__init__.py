@@ -28,7 +28,7 @@ from typing import Optional, Sequence
 __all__ = [
     "DataCopyTiling", "DcopyExtParams", "DcopyError", "DcopyUnavailable", "lib", "lib_path",
     "plan_tiling", "datacopy_small", "datacopy_large", "datacopy_pretranspose",
-    "datacopy_contiguous", "copy_ext", "copy_ext_32b", "copy_nd", "nz_shape", "nd_to_nz",
+    "datacopy_contiguous", "datacopy_pretranspose_noalloc", "copy_ext", "copy_ext_32b", "copy_nd", "nz_shape", "nd_to_nz",
     "nz_to_nd", "status_to_ge", "DcopyTransArgs", "data_type_size", "trans_data_format",
     "trans_format", "trans_shape", "trans_tensor_shape", "transpose",
     "transpose_with_shape_check", "FORMAT", "DATA_TYPE", "TRANSFER_FRACTAL_NZ",
@@ -123,6 +123,8 @@ _SIGNATURES = {
     "dcopy_datacopy_large": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(DataCopyTiling), _vp]),
     "dcopy_datacopy_pretranspose": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(DataCopyTiling), _vp]),
     "dcopy_datacopy_contiguous": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(DataCopyTiling), _vp]),
+    "dcopy_datacopy_pretranspose_noalloc": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(DataCopyTiling),
+                                                           _vp]),
     "dcopy_copy_ext": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(DcopyExtParams), _vp]),
     "dcopy_copy_ext_32b": (ctypes.c_int, [_vp, _vp] + [ctypes.c_uint32] * 4 + [_vp]),
     "dcopy_copy_nd": (ctypes.c_int, [_vp, _vp, ctypes.c_int, _u64p, _i64p, _i64p,
@@ -247,6 +249,11 @@ def datacopy_pretranspose(x, b, tiling: DataCopyTiling, stream=None) -> None:
 
 def datacopy_contiguous(b, y, tiling: DataCopyTiling, stream=None) -> None:
     _datacopy("dcopy_datacopy_contiguous", b, y, tiling, stream)
+
+
+def datacopy_pretranspose_noalloc(x, y, tiling: DataCopyTiling, stream=None) -> None:
+    """x -> B -> y without any allocation (B lives in the library's 16 MiB device array)."""
+    _datacopy("dcopy_datacopy_pretranspose_noalloc", x, y, tiling, stream)
 
 
 def copy_ext(dst, src, block_count: int, block_len: int, src_stride: int = 0,

@@ -89,6 +89,24 @@ int dcopy_datacopy_pretranspose(const void *x, void *b, const DataCopyTiling *ti
 int dcopy_datacopy_contiguous(const void *b, void *y, const DataCopyTiling *tiling,
                               dcopy_stream_t stream);
 
+/* The whole pretranspose workflow (x -> B -> y, as datacopy_pretranspose
+ * followed by datacopy_contiguous) for callers that cannot allocate device
+ * memory for B: a runtime that owns the whole device-memory budget, or a
+ * latency-critical path where cudaMalloc/cudaFree would synchronise the device.
+ * No counterpart in the reference (its host allocates B, asc:131).
+ *   - Allocates nothing: B is a 16 MiB array in the library's own device memory,
+ *     held by every GPU that loads this part of the library until exit.
+ *     rows*cols*4 above 16 MiB is refused with DCOPY_ERR_PARAM_INVALID.
+ *   - The first call on a device looks up the array's device address (with that
+ *     device current) and caches it; make that first call before any stream
+ *     capture on the device.
+ *   - Every call on a device shares the one array: calls whose work overlaps on
+ *     the GPU (other streams, other threads) race on it.  B needs no clearing:
+ *     each call overwrites all of the part it reads.
+ *   - y is written only when tiling->store is 1, as for datacopy_contiguous. */
+int dcopy_datacopy_pretranspose_noalloc(const void *x, void *y, const DataCopyTiling *tiling,
+                                        dcopy_stream_t stream);
+
 /* ---- DataCopyExtParams strided copy ---------------------------------------- */
 
 /* AscendC::DataCopyExtParams as filled by DataCopyPadExtend (ascendc/api/
