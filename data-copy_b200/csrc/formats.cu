@@ -17,6 +17,10 @@ namespace {
 
 constexpr int kMaxRank = 30;
 
+// Set while dcopy_trans_format_check runs: the transfer functions stop after
+// their checks, with the result length stored, before touching memory.
+thread_local bool t_check_only = false;
+
 // GetSizeByDataType for GE's DataType enum (api/python/ge/ge/graph/types.py:15-58).
 // Types without a fixed byte size (string, resource, variant, sub-byte
 // floats/ints, undefined) report -1.
@@ -160,6 +164,7 @@ int fractal_nz_format(const DcopyTransArgs *a, void *dst, uint64_t cap, uint64_t
     return set_error(DCOPY_ERR_SHAPE_INVALID, "dst shape differs from the FRACTAL_NZ shape");
   const uint64_t bytes = (uint64_t)item_count(a->dst_shape, a->dst_rank) * size;
   if (bytes == 0) return store_length(len, 0);  // :134-137
+  if (t_check_only) return store_length(len, bytes);
   if (cap < bytes)
     return set_error(DCOPY_ERR_PARAM_INVALID, "dst holds %llu bytes, result needs %llu",
                      (unsigned long long)cap, (unsigned long long)bytes);
@@ -185,6 +190,7 @@ int fractal_nz_nd_format(const DcopyTransArgs *a, void *dst, uint64_t cap, uint6
     return set_error(DCOPY_ERR_SHAPE_INVALID, "src shape is not the FRACTAL_NZ shape of dst");
   const uint64_t bytes = (uint64_t)item_count(a->dst_shape, a->dst_rank) * size;
   if (bytes == 0) return store_length(len, 0);
+  if (t_check_only) return store_length(len, bytes);
   if (cap < bytes)
     return set_error(DCOPY_ERR_PARAM_INVALID, "dst holds %llu bytes, result needs %llu",
                      (unsigned long long)cap, (unsigned long long)bytes);
@@ -216,6 +222,7 @@ int transpose_impl(void *dst, const void *src, const int64_t *shape, const int64
   for (int i = rank - 1; i >= 0; --i) ds[i] = (i == rank - 1) ? 1 : (int64_t)sizes[i + 1] * ds[i + 1];
   const uint64_t bytes = (uint64_t)n * size;
   if (n == 0) return store_length(len, 0);
+  if (t_check_only) return store_length(len, bytes);
   if (cap < bytes)
     return set_error(DCOPY_ERR_PARAM_INVALID, "dst holds %llu bytes, result needs %llu",
                      (unsigned long long)cap, (unsigned long long)bytes);
@@ -334,6 +341,27 @@ extern "C" int dcopy_trans_data_format(const DcopyTransArgs *args, void *dst,
   if (!args->data && item_count(args->src_shape, args->src_rank) != 0)  // :40-49
     return set_error(DCOPY_ERR_PARAM_INVALID, "input data is null and the shape is not empty");
   return class_format(cls, args, dst, dst_capacity, dst_length, stream);
+  DCOPY_API_END
+}
+
+extern "C" int dcopy_trans_format_check(int transfer_class, const DcopyTransArgs *args,
+                                        uint64_t *dst_length) {
+  DCOPY_API_BEGIN
+  int rc = check_args(args);
+  if (rc) return rc;
+  int cls = transfer_class;
+  if (cls == 0) {  // TransDataFormat: registry and NULL-data checks first (formats.cc:31-49)
+    cls = registered_class(args->src_format, args->dst_format);
+    if (!cls)
+      return set_error(DCOPY_ERR_FORMAT_INVALID, "Failed to trans data from format %d to %d",
+                       args->src_format, args->dst_format);
+    if (!args->data && item_count(args->src_shape, args->src_rank) != 0)
+      return set_error(DCOPY_ERR_PARAM_INVALID, "input data is null and the shape is not empty");
+  }
+  t_check_only = true;
+  rc = class_format(cls, args, nullptr, 0, dst_length, nullptr);
+  t_check_only = false;
+  return rc;
   DCOPY_API_END
 }
 

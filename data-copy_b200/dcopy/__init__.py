@@ -34,7 +34,8 @@ __all__ = [
     "transpose_with_shape_check", "FORMAT", "DATA_TYPE", "TRANSFER_FRACTAL_NZ",
     "TRANSFER_FRACTAL_NZ_ND", "TRANSFER_TRANSPOSE", "shard_range", "enable_peer_access",
     "p2p_copy", "p2p_ring_shift", "ipc_get_handle", "ipc_open_handle", "ipc_close_handle",
-    "signal", "wait_signal", "DcopyDevCopy", "copy_ext_multi",
+    "signal", "wait_signal", "DcopyDevCopy", "copy_ext_multi", "DcopyMemcpyInfo", "memcpy_async",
+    "MEMCPY_KIND",
     "OK", "ERR_PARAM_INVALID", "ERR_SHAPE_INVALID", "ERR_DATATYPE_INVALID",
     "ERR_FORMAT_INVALID", "ERR_CUDA", "ERR_TIMEOUT", "ERR_UNSUPPORTED",
 ]
@@ -101,6 +102,18 @@ DATA_TYPE = {"FLOAT": 0, "FLOAT16": 1, "INT8": 2, "INT32": 3, "UINT8": 4, "INT16
 TRANSFER_FRACTAL_NZ, TRANSFER_FRACTAL_NZ_ND, TRANSFER_TRANSPOSE = 1, 2, 3
 
 
+class DcopyMemcpyInfo(ctypes.Structure):
+    """MemcpyAsyncMemInfo (runtime/v1/common/runtime_api_wrapper.h:42-47)."""
+    _fields_ = [("dst", ctypes.c_void_p), ("destMax", ctypes.c_uint64), ("src", ctypes.c_void_p),
+                ("cnt", ctypes.c_uint64)]
+
+
+# rtMemcpyKind_t values (acl_rt_memcpy_kind.h:16-27).
+MEMCPY_KIND = {"HOST_TO_HOST": 0, "HOST_TO_DEVICE": 1, "DEVICE_TO_HOST": 2,
+               "DEVICE_TO_DEVICE": 3, "MANAGED": 4, "ADDR_DEVICE_TO_DEVICE": 5,
+               "HOST_TO_DEVICE_EX": 6, "DEVICE_TO_HOST_EX": 7, "DEFAULT": 8}
+
+
 class DcopyDevCopy(ctypes.Structure):
     """One device's strided copy for dcopy_copy_ext_multi."""
     _fields_ = [("device", ctypes.c_int32), ("dst", ctypes.c_void_p), ("src", ctypes.c_void_p),
@@ -150,6 +163,7 @@ _SIGNATURES = {
                                        _vp]),
     "dcopy_transpose_with_shape_check": (ctypes.c_int, [_vp, _vp, _i64p, _i64p, _i64p,
                                                         ctypes.c_int32, ctypes.c_int32, _vp]),
+    "dcopy_memcpy_async": (ctypes.c_int, [ctypes.POINTER(DcopyMemcpyInfo), ctypes.c_int32, _vp]),
     "dcopy_shard_range": (ctypes.c_int, [ctypes.c_uint64, ctypes.c_int32, ctypes.c_int32, _u64p,
                                          _u64p]),
     "dcopy_copy_ext_multi": (ctypes.c_int, [ctypes.POINTER(DcopyDevCopy), ctypes.c_int32]),
@@ -460,3 +474,19 @@ def wait_signal(flag, value: int, timeout_ns: int, status, stream=None) -> None:
     """Bounded device-side wait for *flag == value; writes 0 (seen) / 1 (timeout) to status."""
     _check(lib().dcopy_wait_signal(_ptr(flag), value, timeout_ns, _ptr(status), _stream(stream)),
            "dcopy_wait_signal")
+
+
+def memcpy_async(dst, dst_max: int, src, count: int, kind, stream=None) -> None:
+    """rtMemcpyAsyncWithCfg(MemcpyAsyncMemInfo{dst, destMax, src, cnt}, kind, stream)."""
+    if isinstance(kind, str):
+        kind = MEMCPY_KIND[kind]
+
+    def addr(x):
+        if hasattr(x, "data_ptr"):
+            return x.data_ptr()
+        if hasattr(x, "ctypes"):
+            return x.ctypes.data
+        return x
+    info = DcopyMemcpyInfo(addr(dst), dst_max, addr(src), count)
+    _check(lib().dcopy_memcpy_async(ctypes.byref(info), kind, _stream(stream)),
+           "dcopy_memcpy_async")

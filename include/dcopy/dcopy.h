@@ -209,6 +209,13 @@ int32_t dcopy_data_type_size(int32_t data_type);
 int dcopy_trans_data_format(const DcopyTransArgs *args, void *dst, uint64_t dst_capacity,
                             uint64_t *dst_length, dcopy_stream_t stream);
 
+/* Every check of dcopy_trans_data_format (transfer_class 0) or of one transfer
+ * class's TransFormat, with the same status, but no data movement: *dst_length
+ * receives the result length in bytes.  args->data is only tested for NULL
+ * (it may be host memory), so callers can size their buffers first. */
+int dcopy_trans_format_check(int transfer_class, const DcopyTransArgs *args,
+                             uint64_t *dst_length);
+
 /* FormatTransfer::TransFormat of one transfer class, with that class's own
  * checks and status codes (format_transfer_fractal_nz.cc:301-353, 397-446;
  * format_transfer_transpose.cc:239-251). */
@@ -239,6 +246,33 @@ int dcopy_transpose(void *dst, const void *src, const int64_t *src_shape, const 
 int dcopy_transpose_with_shape_check(void *dst, const void *src, const int64_t *src_shape,
                                      const int64_t *dst_shape, const int64_t *perm,
                                      int32_t rank, int32_t data_type, dcopy_stream_t stream);
+
+/* ---- runtime memcpy task --------------------------------------------------------
+ * The D2D memcpy task of GE's runtime (runtime/v1/graph/load/model_manager/
+ * task_info/rts/memcpy_async_task_info.cc:88-111 -> rtMemcpyAsyncWithCfg,
+ * runtime/v1/common/runtime_api_wrapper.h:42-49).  Kinds take rtMemcpyKind_t's
+ * values (compiler/engines/rts_engine/ops_kernel_store/op/acl_rt_memcpy_kind.h). */
+#define DCOPY_MEMCPY_HOST_TO_HOST 0
+#define DCOPY_MEMCPY_HOST_TO_DEVICE 1
+#define DCOPY_MEMCPY_DEVICE_TO_HOST 2
+#define DCOPY_MEMCPY_DEVICE_TO_DEVICE 3  /* one device or peer-to-peer */
+#define DCOPY_MEMCPY_MANAGED 4
+#define DCOPY_MEMCPY_HOST_TO_DEVICE_EX 6
+#define DCOPY_MEMCPY_DEVICE_TO_HOST_EX 7
+#define DCOPY_MEMCPY_DEFAULT 8           /* infer the direction from the pointers */
+
+typedef struct DcopyMemcpyInfo {  /* MemcpyAsyncMemInfo */
+  void *dst;
+  uint64_t destMax;               /* capacity of dst in bytes */
+  const void *src;
+  uint64_t cnt;                   /* bytes to copy */
+} DcopyMemcpyInfo;
+
+/* cnt > destMax is PARAM_INVALID (nothing copied).  Device-to-device copies
+ * (DEVICE_TO_DEVICE, or DEFAULT between two device buffers) run the library's
+ * copy kernel on `stream`, peer memory included; host-side kinds go to
+ * cudaMemcpyAsync.  RT_MEMCPY_ADDR_DEVICE_TO_DEVICE (5) is UNSUPPORTED. */
+int dcopy_memcpy_async(const DcopyMemcpyInfo *info, int32_t kind, dcopy_stream_t stream);
 
 /* ---- multi-GPU ----------------------------------------------------------------
  * No counterpart in the reference (single-core Ascend kernels; SURVEY row e).
