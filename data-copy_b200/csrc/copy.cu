@@ -63,13 +63,13 @@ struct Unroll {
 template <typename T, int U>
 __global__ void __launch_bounds__(kThreads, DCOPY_MIN_CTAS)
     linear_copy_kernel(uint8_t *__restrict__ dst, const uint8_t *__restrict__ src, uint32_t head,
-                       uint64_t n, uint32_t tail, uint64_t per_cta) {
+                       uint64_t n, uint32_t tail, uint64_t per_cta, bool prefetch) {
   pdl_trigger_at_entry();
   T *__restrict__ d = reinterpret_cast<T *>(dst + head);
   const T *__restrict__ s = reinterpret_cast<const T *>(src + head);
   const uint64_t begin = (uint64_t)blockIdx.x * per_cta;
   const uint64_t end = begin + per_cta < n ? begin + per_cta : n;
-  if (DCOPY_PREFETCH) {  // one prefetch per 128-byte line of this CTA's first chunk
+  if (DCOPY_PREFETCH && prefetch) {  // one per 128-byte line of this CTA's first chunk
     const uint64_t per_line = 128 / sizeof(T);
     const uint64_t i = begin + (uint64_t)threadIdx.x * per_line;
     if (threadIdx.x * per_line < (uint64_t)kThreads * U && i < end) prefetch_l2(s + i);
@@ -138,11 +138,11 @@ template <typename T, int U>
 __global__ void __launch_bounds__(kThreads, Unroll<T>::strided_min_ctas)
     strided_copy_kernel(uint8_t *__restrict__ dst, const uint8_t *__restrict__ src,
                         uint32_t total, uint32_t per_cta, FastDiv epr, uint64_t src_pitch,
-                        uint64_t dst_pitch) {
+                        uint64_t dst_pitch, bool prefetch) {
   pdl_trigger_at_entry();
   const uint32_t begin = blockIdx.x * per_cta;
   const uint32_t end = begin + per_cta < total ? begin + per_cta : total;
-  if (DCOPY_PREFETCH) {  // this thread's first U elements, one prefetch per 128-byte line
+  if (DCOPY_PREFETCH && prefetch) {  // first U elements, one prefetch per 128-byte line
     constexpr uint32_t per_line = 128 / sizeof(T) > 0 ? 128 / sizeof(T) : 1;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -227,7 +227,7 @@ int launch_linear(uint8_t *dst, const uint8_t *src, uint64_t bytes, cudaStream_t
   auto kernel = linear_copy_kernel<T, U>;
   const Split sp = split_work(kernel, std::max<uint64_t>(n, 1), U);
   return launch(kernel, sp.grid, dim3(kThreads), 0, s, "linear_copy_kernel", dst, src,
-                (uint32_t)head, n, tail, sp.per_cta);
+                (uint32_t)head, n, tail, sp.per_cta, is_local_device_memory(src));
 }
 
 template <typename T>
@@ -238,6 +238,7 @@ int launch_strided(uint8_t *dst, const uint8_t *src, uint64_t rows, uint64_t row
   // Keep the flat index (and its grid-stride increments) inside 32 bits.
   const uint64_t max_rows = std::max<uint64_t>(1, (uint64_t(1) << 30) / epr);
   const FastDiv div((uint32_t)epr);
+  const bool prefetch = is_local_device_memory(src);
   for (uint64_t r0 = 0; r0 < rows; r0 += max_rows) {
     const uint64_t nr = std::min(max_rows, rows - r0);
     const uint32_t total = (uint32_t)(nr * epr);
@@ -245,7 +246,7 @@ int launch_strided(uint8_t *dst, const uint8_t *src, uint64_t rows, uint64_t row
     const Split sp = split_work(kernel, total, U);
     int rc = launch(kernel, sp.grid, dim3(kThreads), 0, s, "strided_copy_kernel",
                     dst + r0 * dst_pitch, src + r0 * src_pitch, total, (uint32_t)sp.per_cta, div,
-                    src_pitch, dst_pitch);
+                    src_pitch, dst_pitch, prefetch);
     if (rc) return rc;
   }
   return DCOPY_OK;

@@ -120,7 +120,7 @@ template <bool kToNz>
 __global__ void __launch_bounds__(kThreads) nz_smem_kernel(uint4 *__restrict__ dst,
                                                            const uint4 *__restrict__ src,
                                                            NzGeom g, uint32_t ntiles,
-                                                           uint32_t upr_shift) {
+                                                           uint32_t upr_shift, bool prefetch) {
   constexpr int U = kTileUnits / kThreads;
   __shared__ uint4 tile[kTileUnits];
   pdl_trigger_at_entry();
@@ -131,7 +131,7 @@ __global__ void __launch_bounds__(kThreads) nz_smem_kernel(uint4 *__restrict__ d
   static_assert(kTileUnits / kRowsPerTile == 64, "tile row must be 64 units");
   const uint32_t panel_shift = 4 + upr_shift;
   const uint32_t panel_units = 1u << panel_shift;
-  if (DCOPY_PREFETCH && blockIdx.x < ntiles) {
+  if (DCOPY_PREFETCH && prefetch && blockIdx.x < ntiles) {
     // L2-prefetch the first tile's source, one prefetch per 128-byte line.
     const uint32_t q = g.f_pgroups.div(blockIdx.x);
     const uint32_t pg = blockIdx.x - q * g.pgroups;
@@ -283,11 +283,12 @@ int launch_nz(void *dst, const void *src, const NzGeom &g, uint32_t ntiles, bool
     const uint32_t grid = std::max(1u, std::min<uint32_t>(ntiles, 0x7FFFFFFFu));
     uint4 *d = static_cast<uint4 *>(dst);
     const uint4 *sp = static_cast<const uint4 *>(src);
+    const bool pf = is_local_device_memory(src);
     if (to_nz)
       return launch(nz_smem_kernel<true>, grid, dim3(kThreads), 0, s, "nz_smem_kernel", d, sp, g,
-                    ntiles, shift);
+                    ntiles, shift, pf);
     return launch(nz_smem_kernel<false>, grid, dim3(kThreads), 0, s, "nz_smem_kernel", d, sp, g,
-                  ntiles, shift);
+                  ntiles, shift, pf);
   }
   // One tile per CTA: on B200 many short-lived CTAs stream better than a
   // persistent grid (the grid-stride loop only matters past 2^31 - 1 tiles).

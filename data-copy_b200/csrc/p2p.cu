@@ -8,11 +8,17 @@
 // timeout through a caller-owned status word instead of hanging.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <atomic>
 #include <cstring>
 
 #include "common.cuh"
 #include "copy.cuh"
 #include "launch.cuh"
+
+#ifndef DCOPY_P2P_BULK
+#define DCOPY_P2P_BULK 1
+#endif
 
 namespace dcopy {
 namespace {
@@ -58,6 +64,135 @@ __global__ void wait_signal_kernel(const uint32_t *flag, uint32_t value, uint64_
     __nanosleep(256);
   }
   *status = result;
+}
+
+// ---- bulk-copy (TMA) push to another GPU ------------------------------------------
+//
+// One thread per CTA drives a kStages-deep pipeline of kChunk-byte chunks:
+//   cp.async.bulk global(local) -> shared, completion on an mbarrier (complete_tx);
+//   cp.async.bulk shared -> global(peer), bulk_group; the stage is refilled once
+//   the store has read it (wait_group.read).
+// Loads read this GPU's memory only; no multicast.  Every mbarrier wait is
+// bounded; on a timeout the kernel records it in g_p2p_error, waits (bounded)
+// for its own copies in flight and returns.
+#ifndef DCOPY_P2P_STAGES
+#define DCOPY_P2P_STAGES 4
+#endif
+#ifndef DCOPY_P2P_CHUNK_KIB
+#define DCOPY_P2P_CHUNK_KIB 16
+#endif
+#ifndef DCOPY_P2P_CTAS_PER_SM
+#define DCOPY_P2P_CTAS_PER_SM 3
+#endif
+constexpr int kStages = DCOPY_P2P_STAGES;
+constexpr uint32_t kChunk = DCOPY_P2P_CHUNK_KIB * 1024;
+constexpr uint32_t kWaitIters = 1u << 22;  // try_wait suspends ~us per call: seconds in total
+
+__device__ uint32_t g_p2p_error;
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
+  for (uint32_t it = 0; it < kWaitIters; ++it)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+
+__device__ __forceinline__ void bulk_load(void *smem_dst, const void *gsrc, uint32_t bytes,
+                                          uint64_t *bar) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(smem_dst)),
+      "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_store(void *gdst, const void *smem_src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst),
+               "r"(smem_u32(smem_src)), "r"(bytes)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// bytes, src and dst are multiples of 16; chunk c of the copy is handled by
+// CTA c mod gridDim.x.
+__global__ void __launch_bounds__(32) p2p_bulk_push_kernel(uint8_t *__restrict__ dst,
+                                                           const uint8_t *__restrict__ src,
+                                                           uint64_t bytes) {
+  extern __shared__ __align__(128) uint8_t stage_mem[];
+  __shared__ __align__(8) uint64_t bars[kStages];
+  pdl_trigger_at_entry();
+  if (threadIdx.x != 0) return;
+  for (int i = 0; i < kStages; ++i)
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&bars[i])));
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  pdl_wait();
+  pdl_launch_dependents();
+  const uint64_t nchunks = (bytes + kChunk - 1) / kChunk;
+  const uint64_t mine = blockIdx.x < nchunks ? (nchunks - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+  auto chunk_off = [&](uint64_t k) { return (blockIdx.x + k * gridDim.x) * (uint64_t)kChunk; };
+  auto chunk_len = [&](uint64_t k) {
+    const uint64_t off = chunk_off(k);
+    return (uint32_t)(bytes - off < kChunk ? bytes - off : kChunk);
+  };
+  const uint64_t pro = mine < (uint64_t)kStages ? mine : (uint64_t)kStages;
+  for (uint64_t k = 0; k < pro; ++k)
+    bulk_load(stage_mem + k * kChunk, src + chunk_off(k), chunk_len(k), &bars[k]);
+  uint64_t issued = pro, k = 0;
+  bool ok = true;
+  for (; k < mine; ++k) {
+    const int st = (int)(k % kStages);
+    if (!mbar_wait_bounded(&bars[st], (uint32_t)((k / kStages) & 1))) {
+      ok = false;
+      break;
+    }
+    bulk_store(dst + chunk_off(k), stage_mem + st * kChunk, chunk_len(k));
+    if (issued < mine) {  // refill this stage once the store has read it
+      asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+      bulk_load(stage_mem + st * kChunk, src + chunk_off(issued), chunk_len(issued), &bars[st]);
+      ++issued;
+    }
+  }
+  if (!ok) {
+    atomicExch(&g_p2p_error, 1u);
+    // Drain every load still in flight (bounded), so no copy outlives the CTA.
+    for (uint64_t j = k; j < issued; ++j)
+      (void)mbar_wait_bounded(&bars[j % kStages], (uint32_t)((j / kStages) & 1));
+  }
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+int launch_bulk_push(void *dst, const void *src, uint64_t bytes, cudaStream_t s) {
+  static std::atomic<bool> configured[128];
+  const int dev = current_device();
+  const size_t smem = (size_t)kStages * kChunk;
+  if (dev >= 0 && dev < 128 && !configured[dev].load()) {
+    cudaError_t e = cudaFuncSetAttribute(p2p_bulk_push_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+    configured[dev] = true;
+  }
+  const uint64_t nchunks = (bytes + kChunk - 1) / kChunk;
+  const uint64_t grid = std::min<uint64_t>(nchunks, (uint64_t)sm_count() * DCOPY_P2P_CTAS_PER_SM);
+  return launch(p2p_bulk_push_kernel, (unsigned)grid, dim3(32), smem, s, "p2p_bulk_push_kernel",
+                static_cast<uint8_t *>(dst), static_cast<const uint8_t *>(src), bytes);
 }
 
 }  // namespace
@@ -118,7 +253,14 @@ extern "C" int dcopy_p2p_copy(void *dst, const void *src, uint64_t bytes, dcopy_
   if (!rc) rc = check_device_span(dst, bytes, "p2p dst");
   if (!rc) rc = check_disjoint(src, bytes, dst, bytes, "p2p_copy");
   if (rc) return rc;
-  return copy_linear(dst, src, bytes, reinterpret_cast<cudaStream_t>(stream));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // Push to another GPU with the bulk-copy pipeline when everything is 16-byte
+  // granular and the source is this GPU's memory; anything else (pulls, odd
+  // sizes, local copies) takes the load/store kernel.
+  if (DCOPY_P2P_BULK && ((uintptr_t)dst | (uintptr_t)src | bytes) % 16 == 0 &&
+      is_local_device_memory(src) && !is_local_device_memory(dst))
+    return launch_bulk_push(dst, src, bytes, s);
+  return copy_linear(dst, src, bytes, s);
   DCOPY_API_END
 }
 
@@ -170,6 +312,16 @@ extern "C" int dcopy_ipc_close_handle(void *dev_ptr) {
   DCOPY_API_BEGIN
   if (!dev_ptr) return DCOPY_OK;
   DCOPY_CUDA_TRY(cudaIpcCloseMemHandle(dev_ptr));
+  return DCOPY_OK;
+  DCOPY_API_END
+}
+
+extern "C" int dcopy_p2p_error(uint32_t *flag) {
+  DCOPY_API_BEGIN
+  if (!flag) return set_error(DCOPY_ERR_PARAM_INVALID, "p2p_error: NULL");
+  uint32_t zero = 0;
+  DCOPY_CUDA_TRY(cudaMemcpyFromSymbol(flag, g_p2p_error, sizeof(uint32_t)));
+  DCOPY_CUDA_TRY(cudaMemcpyToSymbol(g_p2p_error, &zero, sizeof(uint32_t)));
   return DCOPY_OK;
   DCOPY_API_END
 }

@@ -95,6 +95,18 @@ int check_device_span(const void *ptr, uint64_t bytes, const char *name) {
   return DCOPY_OK;
 }
 
+bool is_local_device_memory(const void *ptr) {
+  PfnPointerGetAttributes fn = pointer_attrs_fn();
+  if (!fn || !ptr) return false;
+  unsigned int mem_type = 0;
+  int ordinal = -1;
+  CUpointer_attribute attrs[2] = {CU_POINTER_ATTRIBUTE_MEMORY_TYPE,
+                                  CU_POINTER_ATTRIBUTE_DEVICE_ORDINAL};
+  void *data[2] = {&mem_type, &ordinal};
+  if (fn(2, attrs, data, (CUdeviceptr)(uintptr_t)ptr) != CUDA_SUCCESS) return false;
+  return mem_type == CU_MEMORYTYPE_DEVICE && ordinal == current_device();
+}
+
 uint64_t allocation_base(const void *ptr) {
   PfnPointerGetAttributes fn = pointer_attrs_fn();
   if (!fn || !ptr) return 0;

@@ -302,8 +302,15 @@ int dcopy_copy_ext_multi(const DcopyDevCopy *copies, int32_t n);
 int dcopy_enable_peer_access(int32_t device, int32_t peer);
 
 /* bytes from local `src` to `dst`, which may be another GPU's memory mapped into
- * this process (peer access or IPC): 128-bit stores pushed over NVLink. */
+ * this process (peer access or IPC).  A push of 16-byte granular buffers to
+ * another GPU runs a bulk-copy (TMA, no multicast) pipeline: local loads into
+ * shared memory, bulk stores over NVLink; other cases use 128-bit load/store. */
 int dcopy_p2p_copy(void *dst, const void *src, uint64_t bytes, dcopy_stream_t stream);
+
+/* Reads and clears the current device's P2P error word: 1 when a bulk-copy
+ * push gave up waiting on one of its own copies (the copy is then incomplete),
+ * else 0.  Synchronises the device. */
+int dcopy_p2p_error(uint32_t *flag);
 
 /* Ring shift inside one process: device devices[i] copies src[i] (its own
  * memory) into dst[(i + 1) % n] (memory of the next device), on streams[i]

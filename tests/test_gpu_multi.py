@@ -71,6 +71,18 @@ def test_ring_shift_single_process(torch_cuda, dcopy):
         torch.cuda.synchronize(d)
     for d in range(n):
         assert torch.equal(dsts[(d + 1) % n], srcs[d].to(f"cuda:{(d + 1) % n}"))
+        with torch.cuda.device(d):
+            assert dcopy.p2p_error() == 0
+    # Ragged sizes take the load/store kernel; the result is the same bytes.
+    odd = nbytes - 7
+    for d in range(n):
+        dsts[d].zero_()
+    dcopy.p2p_ring_shift(list(range(n)), srcs, dsts, odd)
+    for d in range(n):
+        torch.cuda.synchronize(d)
+    for d in range(n):
+        got = dsts[(d + 1) % n]
+        assert torch.equal(got[:odd], srcs[d][:odd].to(got.device)) and int(got[odd:].sum()) == 0
 
 
 def _free_port():
