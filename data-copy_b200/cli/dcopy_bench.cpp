@@ -14,6 +14,10 @@
 //       events in place of msprof's Task Duration).
 //   dcopy_bench nz [--batch B] [--h H] [--w W] [--reps R] [--device D]
 //       fp16 ND -> FRACTAL_NZ -> ND, round trip verified.
+//   dcopy_bench p2p [--mib M] [--reps R] [--device D] [--peer P] [--peak GBPS]
+//       NVLink between two GPUs: dcopy_p2p_copy as a push (launched on the
+//       sending GPU) and as a pull (launched on the receiving GPU), and the copy
+//       engine, each with both GPUs sending at once and with one sending.
 //
 // Timing: CUDA events around each launch; a 512 MiB write between reps flushes
 // the 126 MB L2, so every rep reads cold data.
@@ -27,6 +31,7 @@
 #include <fstream>
 #include <iostream>
 #include <map>
+#include <memory>
 #include <sstream>
 #include <stdexcept>
 #include <string>
@@ -341,16 +346,116 @@ int run_nz(const Args &a) {
   return 0;
 }
 
+// ---- p2p --------------------------------------------------------------------------
+
+int run_p2p(const Args &a) {
+  const int dev[2] = {int(a.num("device", 0)), int(a.num("peer", 1))};
+  const uint64_t bytes = uint64_t(a.num("mib", 1024)) << 20;
+  const int reps = int(a.num("reps", 5));
+  const double peak = a.num("peak", 770.0);  // measured per-direction peer copy
+  CheckD(dcopy_enable_peer_access(dev[0], dev[1]));
+  CheckD(dcopy_enable_peer_access(dev[1], dev[0]));
+  std::unique_ptr<DevBuf> src[2], dst[2];
+  cudaStream_t s[2];
+  cudaEvent_t ev[2][2];
+  for (int i = 0; i < 2; ++i) {
+    Check(cudaSetDevice(dev[i]), "cudaSetDevice");
+    src[i] = std::make_unique<DevBuf>(bytes);
+    dst[i] = std::make_unique<DevBuf>(bytes);
+    Check(cudaMemset(src[i]->p, 0x11 * (i + 1), bytes), "memset");
+    Check(cudaStreamCreateWithFlags(&s[i], cudaStreamNonBlocking), "stream");
+    Check(cudaEventCreate(&ev[i][0]), "event");
+    Check(cudaEventCreate(&ev[i][1]), "event");
+  }
+  // GPU i sends src[i] to the other GPU's dst; a pull is launched on the receiver.
+  auto issue = [&](const std::string &mode, int i) {
+    const int peer = 1 - i;
+    const int launch_on = mode == "pull" ? peer : i;
+    Check(cudaSetDevice(dev[launch_on]), "cudaSetDevice");
+    dcopy_stream_t ds = reinterpret_cast<dcopy_stream_t>(s[launch_on]);
+    if (mode == "ce")
+      Check(cudaMemcpyPeerAsync(dst[peer]->p, dev[peer], src[i]->p, dev[i], bytes, s[i]), "peer");
+    else
+      CheckD(dcopy_p2p_copy(dst[peer]->p, src[i]->p, bytes, ds));
+  };
+  auto sync_all = [&] {
+    for (int i = 0; i < 2; ++i) {
+      Check(cudaSetDevice(dev[i]), "cudaSetDevice");
+      Check(cudaDeviceSynchronize(), "sync");
+    }
+  };
+  std::vector<uint8_t> host(bytes);
+  for (const std::string mode : {"push", "pull", "ce"}) {
+    for (int senders = 2; senders >= 1; --senders) {
+      for (int i = 0; i < 2; ++i) {
+        Check(cudaSetDevice(dev[i]), "cudaSetDevice");
+        Check(cudaMemset(dst[i]->p, 0, bytes), "memset");
+      }
+      sync_all();
+      for (int w = 0; w < 2; ++w)
+        for (int i = 0; i < senders; ++i) issue(mode, i);
+      sync_all();
+      // The stream that carries sender i's copy: the receiver's for a pull.
+      auto stream_of = [&](int i) { return mode == "pull" ? 1 - i : i; };
+      for (int i = 0; i < senders; ++i) {
+        Check(cudaSetDevice(dev[stream_of(i)]), "cudaSetDevice");
+        Check(cudaEventRecord(ev[stream_of(i)][0], s[stream_of(i)]), "record");
+      }
+      for (int r = 0; r < reps; ++r)
+        for (int i = 0; i < senders; ++i) issue(mode, i);
+      for (int i = 0; i < senders; ++i) {
+        Check(cudaSetDevice(dev[stream_of(i)]), "cudaSetDevice");
+        Check(cudaEventRecord(ev[stream_of(i)][1], s[stream_of(i)]), "record");
+      }
+      sync_all();
+      double ms = 0;
+      for (int i = 0; i < senders; ++i) {
+        float m = 0;
+        Check(cudaEventElapsedTime(&m, ev[stream_of(i)][0], ev[stream_of(i)][1]), "elapsed");
+        ms = std::max(ms, double(m));
+      }
+      uint32_t gave_up = 0;
+      for (int i = 0; i < 2; ++i) {
+        Check(cudaSetDevice(dev[i]), "cudaSetDevice");
+        uint32_t f = 0;
+        CheckD(dcopy_p2p_error(&f));
+        gave_up |= f;
+      }
+      for (int i = 0; i < senders; ++i) {
+        Check(cudaMemcpy(host.data(), dst[1 - i]->p, bytes, cudaMemcpyDeviceToHost), "D2H");
+        const uint8_t want = uint8_t(0x11 * (i + 1));
+        if (gave_up || std::any_of(host.begin(), host.end(), [&](uint8_t v) { return v != want; }))
+          throw std::runtime_error("p2p " + mode + ": received bytes differ");
+      }
+      const double gbps = double(bytes) * reps / (ms * 1e6);
+      std::cout << "{\"p2p\": \"" << mode << "\", \"senders\": " << senders
+                << ", \"bytes_per_sender\": " << bytes << ", \"GBps_per_direction\": " << gbps
+                << ", \"frac_of_peer_copy\": " << gbps / peak << ", \"verified\": true}"
+                << std::endl;
+    }
+  }
+  for (int i = 0; i < 2; ++i) {
+    Check(cudaSetDevice(dev[i]), "cudaSetDevice");
+    cudaEventDestroy(ev[i][0]);
+    cudaEventDestroy(ev[i][1]);
+    cudaStreamDestroy(s[i]);
+    src[i].reset();
+    dst[i].reset();
+  }
+  return 0;
+}
+
 }  // namespace
 
 int main(int argc, char **argv) {
   try {
-    if (argc < 2) throw std::runtime_error("usage: dcopy_bench sweep|standalone|nz [options]");
+    if (argc < 2) throw std::runtime_error("usage: dcopy_bench sweep|standalone|nz|p2p [options]");
     const std::string cmd = argv[1];
     Args a(argc, argv);
     if (cmd == "sweep") return run_sweep(a);
     if (cmd == "standalone") return run_standalone(a);
     if (cmd == "nz") return run_nz(a);
+    if (cmd == "p2p") return run_p2p(a);
     throw std::runtime_error("unknown command " + cmd);
   } catch (const std::exception &e) {
     std::cerr << "dcopy_bench: " << e.what() << '\n';
