@@ -357,7 +357,13 @@ def run_secondary(torch, dcopy, dev):
     ms2 = _time_graph(torch, lambda: dcopy.nz_to_nd(nd, nz, shape, 2, 16), reps=10)
     out["config4_nd_to_nz_GBps"] = round(2 * nbytes / (ms / 1e3) / 1e9, 1)
     out["config4_nz_to_nd_GBps"] = round(2 * nbytes / (ms2 / 1e3) / 1e9, 1)
-    del nd, nz
+    # The sibling tile format on the same tensor: ND<->FRACTAL_ZZ, c0 = 16.
+    zz = nz.view(16, 256, 256, 16, 16)
+    ms = _time_graph(torch, lambda: dcopy.nd_to_zz(zz, nd, shape, 2, 16), reps=10)
+    ms2 = _time_graph(torch, lambda: dcopy.zz_to_nd(nd, zz, shape, 2, 16), reps=10)
+    out["config4_nd_to_zz_GBps"] = round(2 * nbytes / (ms / 1e3) / 1e9, 1)
+    out["config4_zz_to_nd_GBps"] = round(2 * nbytes / (ms2 / 1e3) / 1e9, 1)
+    del nd, nz, zz
     # Standalone transpose at the 64 MiB maximum (rows 4088 x cols 4104 int32).
     rows, cols = 4088, 4104
     x = torch.empty(rows * cols, dtype=torch.int32, device=dev)

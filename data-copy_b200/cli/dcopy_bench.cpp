@@ -12,8 +12,10 @@
 //       `trials` rounds with STORE=0 in rotated order and write config.json,
 //       raw.csv, stages.csv and summary.json (device time per kernel from CUDA
 //       events in place of msprof's Task Duration).
-//   dcopy_bench nz [--batch B] [--h H] [--w W] [--reps R] [--device D]
-//       fp16 ND -> FRACTAL_NZ -> ND, round trip verified.
+//   dcopy_bench nz [--batch B] [--h H] [--w W] [--c0 C] [--format nz|zz] [--reps R]
+//                  [--device D]
+//       fp16 ND -> FRACTAL_NZ -> ND (or FRACTAL_ZZ), round trip
+//       verified.
 //   dcopy_bench p2p [--mib M] [--reps R] [--device D] [--peer P] [--peak GBPS]
 //       NVLink between two GPUs: dcopy_p2p_copy as a push (launched on the
 //       sending GPU) and as a pull (launched on the receiving GPU), and the copy
@@ -306,13 +308,18 @@ int run_nz(const Args &a) {
                             int64_t(a.num("w", 4096))};
   const int reps = int(a.num("reps", 10));
   const double peak = a.num("peak", 6543.4);
+  const int64_t c0 = int64_t(a.num("c0", 16));
+  const bool zz_format = a.str("format", "nz") == "zz";
   Check(cudaSetDevice(int(a.num("device", 0))), "cudaSetDevice");
   cudaStream_t s;
   Check(cudaStreamCreate(&s), "stream");
   dcopy_stream_t ds = reinterpret_cast<dcopy_stream_t>(s);
+  auto to_frac = zz_format ? dcopy_nd_to_zz : dcopy_nd_to_nz;
+  auto to_nd = zz_format ? dcopy_zz_to_nd : dcopy_nz_to_nd;
   int64_t nz[5], hw[3];
   int nz_rank = 0;
-  CheckD(dcopy_nz_shape(shape, 3, 16, nz, &nz_rank, hw));
+  CheckD(zz_format ? dcopy_zz_shape(shape, 3, c0, nz, &nz_rank, hw)
+                   : dcopy_nz_shape(shape, 3, c0, nz, &nz_rank, hw));
   uint64_t nd_elems = uint64_t(shape[0]) * shape[1] * shape[2], nz_elems = 1;
   for (int i = 0; i < nz_rank; ++i) nz_elems *= nz[i];
   DevBuf nd(nd_elems * 2), z(nz_elems * 2), back(nd_elems * 2), flush(512ull << 20);
@@ -326,20 +333,21 @@ int run_nz(const Args &a) {
     v = uint16_t(z2 ^ (z2 >> 31));
   }
   Check(cudaMemcpy(nd.p, host.data(), nd_elems * 2, cudaMemcpyHostToDevice), "H2D");
-  CheckD(dcopy_nd_to_nz(z.p, nd.p, shape, 3, 2, 16, ds));
-  CheckD(dcopy_nz_to_nd(back.p, z.p, shape, 3, 2, 16, ds));
+  CheckD(to_frac(z.p, nd.p, shape, 3, 2, c0, ds));
+  CheckD(to_nd(back.p, z.p, shape, 3, 2, c0, ds));
   Check(cudaMemcpy(host2.data(), back.p, nd_elems * 2, cudaMemcpyDeviceToHost), "D2H");
   if (std::memcmp(host.data(), host2.data(), nd_elems * 2) != 0)
-    throw std::runtime_error("ND -> NZ -> ND round trip differs");
-  auto t1 = time_reps([&] { CheckD(dcopy_nd_to_nz(z.p, nd.p, shape, 3, 2, 16, ds)); }, reps, s,
-                      flush);
-  auto t2 = time_reps([&] { CheckD(dcopy_nz_to_nd(back.p, z.p, shape, 3, 2, 16, ds)); }, reps, s,
-                      flush);
+    throw std::runtime_error("ND -> tiled -> ND round trip differs");
+  auto t1 = time_reps([&] { CheckD(to_frac(z.p, nd.p, shape, 3, 2, c0, ds)); }, reps, s, flush);
+  auto t2 = time_reps([&] { CheckD(to_nd(back.p, z.p, shape, 3, 2, c0, ds)); }, reps, s, flush);
   const double g1 = double(nd_elems * 2 + nz_elems * 2) / (median(t1) * 1e3);
   const double g2 = double(nd_elems * 2 + nz_elems * 2) / (median(t2) * 1e3);
-  std::cout << "{\"config\": 4, \"shape\": [" << shape[0] << ", " << shape[1] << ", " << shape[2]
-            << "], \"nd_to_nz_us\": " << median(t1) << ", \"nd_to_nz_GBps\": " << g1
-            << ", \"nz_to_nd_us\": " << median(t2) << ", \"nz_to_nd_GBps\": " << g2
+  const std::string f = zz_format ? "zz" : "nz";
+  std::cout << "{\"config\": 4, \"format\": \"" << f << "\", \"c0\": " << c0
+            << ", \"shape\": [" << shape[0] << ", " << shape[1] << ", " << shape[2]
+            << "], \"nd_to_" << f << "_us\": " << median(t1) << ", \"nd_to_" << f
+            << "_GBps\": " << g1 << ", \"" << f << "_to_nd_us\": " << median(t2) << ", \"" << f
+            << "_to_nd_GBps\": " << g2
             << ", \"frac_of_peak\": [" << g1 / peak << ", " << g2 / peak
             << "], \"round_trip_bit_exact\": true}" << std::endl;
   cudaStreamDestroy(s);

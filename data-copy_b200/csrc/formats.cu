@@ -1,8 +1,8 @@
 // GE TransData level on device buffers: the format-transfer registry
 // (base/formats/formats.cc, register_format_transfer.{h,cc}), the
-// FormatTransferFractalNz / FormatTransferFractalNzND / FormatTransferTranspose
-// classes' argument checks, and Transpose (format_transfer_transpose.cc) on the
-// GPU.  Every check happens on the host, in the reference's order and with its
+// FormatTransferFractalNz / FractalNzND / FractalZz / FractalZzND /
+// FormatTransferTranspose classes' argument checks, and Transpose
+// (format_transfer_transpose.cc) on the GPU.  Every check happens on the host, in the reference's order and with its
 // status class, before any launch; the data movement goes to the NZ kernels and
 // to the N-D box copy.
 #include <cuda_runtime.h>
@@ -92,6 +92,8 @@ int registered_class(int32_t src, int32_t dst) {
                            dst == DCOPY_FORMAT_NHWC;
   if (nd_like && dst == DCOPY_FORMAT_FRACTAL_NZ) return DCOPY_TRANSFER_FRACTAL_NZ;
   if (src == DCOPY_FORMAT_FRACTAL_NZ && nd_like_dst) return DCOPY_TRANSFER_FRACTAL_NZ_ND;
+  if (nd_like && dst == DCOPY_FORMAT_FRACTAL_ZZ) return DCOPY_TRANSFER_FRACTAL_ZZ;
+  if (src == DCOPY_FORMAT_FRACTAL_ZZ && nd_like_dst) return DCOPY_TRANSFER_FRACTAL_ZZ_ND;
   if (find_perm(src, dst)) return DCOPY_TRANSFER_TRANSPOSE;
   return 0;
 }
@@ -109,7 +111,8 @@ int64_t item_count(const int64_t *s, int n) {  // GetItemNumByShape: empty -> 1
   return v;
 }
 
-// CheckShapeForTransShapeToFracNz (format_transfer_fractal_nz.cc:39-57).
+// CheckShapeForTransShapeToFracNz (format_transfer_fractal_nz.cc:39-57); the
+// FRACTAL_ZZ file's CheckShape (format_transfer_fractal_zz.cc:48-66) is the same rule.
 bool check_shape_for_nz(int32_t format, const int64_t *shape, int rank) {
   switch (format) {
     case DCOPY_FORMAT_ND: return shape_valid(shape, rank);
@@ -190,11 +193,69 @@ int fractal_nz_nd_format(const DcopyTransArgs *a, void *dst, uint64_t cap, uint6
     return set_error(DCOPY_ERR_SHAPE_INVALID, "src shape is not the FRACTAL_NZ shape of dst");
   const uint64_t bytes = (uint64_t)item_count(a->dst_shape, a->dst_rank) * size;
   if (bytes == 0) return store_length(len, 0);
+  if (a->src_c0 <= 0)  // the reference divides by it (:249)
+    return set_error(DCOPY_ERR_SHAPE_INVALID, "c0 %lld must be positive", (long long)a->src_c0);
   if (t_check_only) return store_length(len, bytes);
   if (cap < bytes)
     return set_error(DCOPY_ERR_PARAM_INVALID, "dst holds %llu bytes, result needs %llu",
                      (unsigned long long)cap, (unsigned long long)bytes);
   rc = nz_transfer(dst, a->data, a->dst_shape, a->dst_rank, size, a->src_c0, false, s);
+  return rc ? rc : store_length(len, bytes);
+}
+
+// FormatTransferFractalZz::TransFormat (fractal_zz.cc:337-389).
+int fractal_zz_format(const DcopyTransArgs *a, void *dst, uint64_t cap, uint64_t *len,
+                      dcopy_stream_t s) {
+  const int32_t size = type_size(a->data_type);
+  if (size <= 0)
+    return set_error(DCOPY_ERR_DATATYPE_INVALID, "data type %d is not supported", a->data_type);
+  if (!check_shape_for_nz(a->src_format, a->src_shape, a->src_rank) ||
+      !shape_valid(a->dst_shape, a->dst_rank))
+    return set_error(DCOPY_ERR_SHAPE_INVALID, "trans format %d -> FRACTAL_ZZ: invalid shapes",
+                     a->src_format);
+  int64_t expect[kMaxRank + 2], hw[3];
+  int erank = 0;
+  int rc = zz_shape(a->src_shape, a->src_rank, a->dst_c0, expect, &erank, hw);
+  if (rc) return rc;
+  if (a->dst_rank && !same_shape(a->dst_shape, a->dst_rank, expect, erank))  // :385-387
+    return set_error(DCOPY_ERR_SHAPE_INVALID, "dst shape differs from the FRACTAL_ZZ shape");
+  const uint64_t bytes = (uint64_t)item_count(a->dst_shape, a->dst_rank) * size;
+  if (bytes == 0) return store_length(len, 0);  // :143-146
+  if (t_check_only) return store_length(len, bytes);
+  if (cap < bytes)
+    return set_error(DCOPY_ERR_PARAM_INVALID, "dst holds %llu bytes, result needs %llu",
+                     (unsigned long long)cap, (unsigned long long)bytes);
+  rc = frac_transfer(FracKind::kZz, dst, a->data, a->src_shape, a->src_rank, size, a->dst_c0,
+                     true, s);
+  return rc ? rc : store_length(len, bytes);
+}
+
+// FormatTransferFractalZzND::TransFormat (fractal_zz.cc:433-481).
+int fractal_zz_nd_format(const DcopyTransArgs *a, void *dst, uint64_t cap, uint64_t *len,
+                         dcopy_stream_t s) {
+  const int32_t size = type_size(a->data_type);
+  if (size <= 0)
+    return set_error(DCOPY_ERR_DATATYPE_INVALID, "data type %d is not supported", a->data_type);
+  if (!shape_valid(a->src_shape, a->src_rank) ||
+      !check_shape_for_nz(a->dst_format, a->dst_shape, a->dst_rank))
+    return set_error(DCOPY_ERR_SHAPE_INVALID, "trans format FRACTAL_ZZ -> %d: invalid shapes",
+                     a->dst_format);
+  int64_t expect[kMaxRank + 2], hw[3];  // CheckShapeRelation, :120-138
+  int erank = 0;
+  int rc = zz_shape(a->dst_shape, a->dst_rank, a->src_c0, expect, &erank, hw);
+  if (rc) return rc;
+  if (!same_shape(a->src_shape, a->src_rank, expect, erank))
+    return set_error(DCOPY_ERR_SHAPE_INVALID, "src shape is not the FRACTAL_ZZ shape of dst");
+  const uint64_t bytes = (uint64_t)item_count(a->dst_shape, a->dst_rank) * size;
+  if (bytes == 0) return store_length(len, 0);
+  if (a->src_c0 <= 0)  // the reference divides by it (:273)
+    return set_error(DCOPY_ERR_SHAPE_INVALID, "c0 %lld must be positive", (long long)a->src_c0);
+  if (t_check_only) return store_length(len, bytes);
+  if (cap < bytes)
+    return set_error(DCOPY_ERR_PARAM_INVALID, "dst holds %llu bytes, result needs %llu",
+                     (unsigned long long)cap, (unsigned long long)bytes);
+  rc = frac_transfer(FracKind::kZz, dst, a->data, a->dst_shape, a->dst_rank, size, a->src_c0,
+                     false, s);
   return rc ? rc : store_length(len, bytes);
 }
 
@@ -290,6 +351,8 @@ int class_format(int cls, const DcopyTransArgs *a, void *dst, uint64_t cap, uint
     case DCOPY_TRANSFER_FRACTAL_NZ: return fractal_nz_format(a, dst, cap, len, s);
     case DCOPY_TRANSFER_FRACTAL_NZ_ND: return fractal_nz_nd_format(a, dst, cap, len, s);
     case DCOPY_TRANSFER_TRANSPOSE: return transpose_format(a, dst, cap, len, s);
+    case DCOPY_TRANSFER_FRACTAL_ZZ: return fractal_zz_format(a, dst, cap, len, s);
+    case DCOPY_TRANSFER_FRACTAL_ZZ_ND: return fractal_zz_nd_format(a, dst, cap, len, s);
     default: return set_error(DCOPY_ERR_PARAM_INVALID, "unknown transfer class %d", cls);
   }
 }
@@ -317,6 +380,21 @@ int class_shape(int cls, int32_t src_format, const int64_t *src_shape, int32_t s
                        "the shape derivation from FRACTAL_NZ is not unique");
     case DCOPY_TRANSFER_TRANSPOSE:
       return transpose_shape(src_format, src_shape, src_rank, dst_format, dst_shape, dst_rank);
+    case DCOPY_TRANSFER_FRACTAL_ZZ: {  // fractal_zz.cc:391-431
+      if (type_size(data_type) <= 0)
+        return set_error(DCOPY_ERR_DATATYPE_INVALID, "data type %d is not supported", data_type);
+      if (!check_shape_for_nz(src_format, src_shape, src_rank))
+        return set_error(DCOPY_ERR_SHAPE_INVALID, "format %d shape cannot become FRACTAL_ZZ",
+                         src_format);
+      int64_t hw[3];
+      int n = 0;
+      const int rc = zz_shape(src_shape, src_rank, c0, dst_shape, &n, hw);
+      *dst_rank = n;
+      return rc;
+    }
+    case DCOPY_TRANSFER_FRACTAL_ZZ_ND:  // fractal_zz.cc:483-492
+      return set_error(DCOPY_ERR_FORMAT_INVALID,
+                       "the shape derivation from FRACTAL_ZZ is not unique");
     default: return set_error(DCOPY_ERR_PARAM_INVALID, "unknown transfer class %d", cls);
   }
 }

@@ -13,7 +13,14 @@ bool shape_valid(const int64_t *shape, int rank);
 // TransShapeToFracNz (format_transfer_fractal_nz.cc:65-111).  Sets the error
 // slot (SHAPE_INVALID) when the result is not a valid shape.
 int nz_shape(const int64_t *nd, int rank, int64_t w0, int64_t *nz, int *nz_rank, int64_t *hw);
-// ND <-> FRACTAL_NZ with all argument checks of dcopy_nd_to_nz / dcopy_nz_to_nd.
+// TransShapeToFracZz (format_transfer_fractal_zz.cc:74-118), same contract.
+int zz_shape(const int64_t *nd, int rank, int64_t c0, int64_t *zz, int *zz_rank, int64_t *hw);
+
+enum class FracKind { kNz, kZz };
+// ND <-> FRACTAL_NZ / FRACTAL_ZZ with all argument checks of the public entries
+// (dcopy_nd_to_nz, dcopy_nz_to_nd, dcopy_nd_to_zz, dcopy_zz_to_nd).
+int frac_transfer(FracKind kind, void *dst, const void *src, const int64_t *nd_shape, int rank,
+                  int elem_bytes, int64_t w0, bool to_frac, dcopy_stream_t stream);
 int nz_transfer(void *dst, const void *src, const int64_t *nd_shape, int rank, int elem_bytes,
                 int64_t w0, bool to_nz, dcopy_stream_t stream);
 

@@ -16,7 +16,9 @@ Names follow the reference's host interface:
     (compiler/graph/optimize/autofuse/ascendc/api/datacopy.h:14-40);
   * ``copy_nd`` -- DataCopyNddma (v35/ascendc/api_regbase/datacopy_nddma.h);
   * ``nz_shape`` / ``nd_to_nz`` / ``nz_to_nd`` -- TransShapeToFracNz and the
-    FRACTAL_NZ transfers (base/formats/format_transfers/format_transfer_fractal_nz.cc).
+    FRACTAL_NZ transfers (base/formats/format_transfers/format_transfer_fractal_nz.cc);
+  * ``zz_shape`` / ``nd_to_zz`` / ``zz_to_nd`` -- the same for FRACTAL_ZZ
+    (base/formats/format_transfers/format_transfer_fractal_zz.cc).
 """
 from __future__ import annotations
 
@@ -29,8 +31,8 @@ __all__ = [
     "DataCopyTiling", "DcopyExtParams", "DcopyError", "DcopyUnavailable", "lib", "lib_path",
     "plan_tiling", "datacopy_small", "datacopy_large", "datacopy_pretranspose",
     "datacopy_contiguous", "datacopy_pretranspose_noalloc", "copy_ext", "copy_ext_32b", "copy_nd", "nz_shape", "nd_to_nz",
-    "nz_to_nd", "status_to_ge", "DcopyTransArgs", "data_type_size", "trans_data_format",
-    "trans_format", "trans_shape", "trans_tensor_shape", "transpose",
+    "nz_to_nd", "zz_shape", "nd_to_zz", "zz_to_nd", "TRANSFER_FRACTAL_ZZ", "TRANSFER_FRACTAL_ZZ_ND", "status_to_ge", "DcopyTransArgs", "data_type_size", "trans_data_format",
+    "trans_format", "trans_format_check", "trans_shape", "trans_tensor_shape", "transpose",
     "transpose_with_shape_check", "FORMAT", "DATA_TYPE", "TRANSFER_FRACTAL_NZ",
     "TRANSFER_FRACTAL_NZ_ND", "TRANSFER_TRANSPOSE", "shard_range", "enable_peer_access",
     "p2p_copy", "p2p_ring_shift", "ipc_get_handle", "ipc_open_handle", "ipc_close_handle",
@@ -95,11 +97,12 @@ class DcopyTransArgs(ctypes.Structure):
 
 # GE enum values (metadef graph/types.h; api/python/ge/ge/graph/types.py).
 FORMAT = {"NCHW": 0, "NHWC": 1, "ND": 2, "NC1HWC0": 3, "FRACTAL_Z": 4, "C1HWNC0": 9,
-          "CHWN": 14, "HWCN": 16, "FRACTAL_NZ": 29, "RESERVED": 40}
+          "CHWN": 14, "HWCN": 16, "FRACTAL_ZZ": 28, "FRACTAL_NZ": 29, "RESERVED": 40}
 DATA_TYPE = {"FLOAT": 0, "FLOAT16": 1, "INT8": 2, "INT32": 3, "UINT8": 4, "INT16": 6,
              "UINT16": 7, "UINT32": 8, "INT64": 9, "UINT64": 10, "DOUBLE": 11, "BOOL": 12,
              "STRING": 13, "COMPLEX64": 16, "COMPLEX128": 17, "BF16": 27, "UNDEFINED": 28}
 TRANSFER_FRACTAL_NZ, TRANSFER_FRACTAL_NZ_ND, TRANSFER_TRANSPOSE = 1, 2, 3
+TRANSFER_FRACTAL_ZZ, TRANSFER_FRACTAL_ZZ_ND = 4, 5
 
 
 class DcopyMemcpyInfo(ctypes.Structure):
@@ -148,9 +151,17 @@ _SIGNATURES = {
                                       ctypes.c_int64, _vp]),
     "dcopy_nz_to_nd": (ctypes.c_int, [_vp, _vp, _i64p, ctypes.c_int, ctypes.c_int,
                                       ctypes.c_int64, _vp]),
+    "dcopy_zz_shape": (ctypes.c_int, [_i64p, ctypes.c_int, ctypes.c_int64, _i64p,
+                                      ctypes.POINTER(ctypes.c_int), _i64p]),
+    "dcopy_nd_to_zz": (ctypes.c_int, [_vp, _vp, _i64p, ctypes.c_int, ctypes.c_int,
+                                      ctypes.c_int64, _vp]),
+    "dcopy_zz_to_nd": (ctypes.c_int, [_vp, _vp, _i64p, ctypes.c_int, ctypes.c_int,
+                                      ctypes.c_int64, _vp]),
     "dcopy_data_type_size": (ctypes.c_int32, [ctypes.c_int32]),
     "dcopy_trans_data_format": (ctypes.c_int, [ctypes.POINTER(DcopyTransArgs), _vp,
                                                ctypes.c_uint64, _u64p, _vp]),
+    "dcopy_trans_format_check": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(DcopyTransArgs),
+                                                ctypes.POINTER(ctypes.c_uint64)]),
     "dcopy_trans_format": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(DcopyTransArgs), _vp,
                                           ctypes.c_uint64, _u64p, _vp]),
     "dcopy_trans_shape": (ctypes.c_int, [ctypes.c_int, ctypes.c_int32, _i64p, ctypes.c_int32,
@@ -323,6 +334,29 @@ def nz_to_nd(dst, src, nd_shape: Sequence[int], elem_bytes: int, w0: int, stream
            "dcopy_nz_to_nd")
 
 
+def zz_shape(nd_shape: Sequence[int], c0: int):
+    """TransShapeToFracZz: returns (zz_shape, (times, H, W))."""
+    n = len(nd_shape)
+    src = (ctypes.c_int64 * max(n, 1))(*nd_shape)
+    out = (ctypes.c_int64 * (n + 4))()
+    rank = ctypes.c_int(0)
+    hw = (ctypes.c_int64 * 3)()
+    _check(lib().dcopy_zz_shape(src, n, c0, out, ctypes.byref(rank), hw), "dcopy_zz_shape")
+    return [out[i] for i in range(rank.value)], tuple(hw)
+
+
+def nd_to_zz(dst, src, nd_shape: Sequence[int], elem_bytes: int, c0: int, stream=None) -> None:
+    arr, n = _shape_arg(nd_shape)
+    _check(lib().dcopy_nd_to_zz(_ptr(dst), _ptr(src), arr, n, elem_bytes, c0, _stream(stream)),
+           "dcopy_nd_to_zz")
+
+
+def zz_to_nd(dst, src, nd_shape: Sequence[int], elem_bytes: int, c0: int, stream=None) -> None:
+    arr, n = _shape_arg(nd_shape)
+    _check(lib().dcopy_zz_to_nd(_ptr(dst), _ptr(src), arr, n, elem_bytes, c0, _stream(stream)),
+           "dcopy_zz_to_nd")
+
+
 # ---- GE TransData level -------------------------------------------------------------
 
 def data_type_size(data_type: int) -> int:
@@ -358,6 +392,17 @@ def trans_format(transfer_class, dst, data, src_format, dst_format, src_shape, d
     n = ctypes.c_uint64(0)
     _check(lib().dcopy_trans_format(transfer_class, ctypes.byref(a), _ptr(dst), dst_capacity,
                                     ctypes.byref(n), _stream(stream)), "dcopy_trans_format")
+    return n.value
+
+
+def trans_format_check(transfer_class, data, src_format, dst_format, src_shape, dst_shape,
+                       data_type, src_c0=16, dst_c0=16) -> int:
+    """Every check of TransDataFormat (class 0) or of one class's TransFormat, no data
+    movement; returns the result length in bytes."""
+    a = _trans_args(data, src_format, dst_format, src_shape, dst_shape, data_type, src_c0, dst_c0)
+    n = ctypes.c_uint64(0)
+    _check(lib().dcopy_trans_format_check(transfer_class, ctypes.byref(a), ctypes.byref(n)),
+           "dcopy_trans_format_check")
     return n.value
 
 

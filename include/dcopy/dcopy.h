@@ -162,6 +162,24 @@ int dcopy_nd_to_nz(void *dst, const void *src, const int64_t *nd_shape, int rank
 int dcopy_nz_to_nd(void *dst, const void *src, const int64_t *nd_shape, int rank,
                    int elem_bytes, int64_t w0, dcopy_stream_t stream);
 
+/* ---- ND <-> FRACTAL_ZZ ------------------------------------------------------ */
+
+/* TransShapeToFracZz (format_transfer_fractal_zz.cc:74-118): ND [..., H, W] ->
+ * ZZ [..., ceil(H/c0), ceil(W/c0), c0, c0]; rank 1 [N] -> [1, ceil(N/c0), c0, c0].
+ * Same buffer contract as dcopy_nz_shape. */
+int dcopy_zz_shape(const int64_t *nd_shape, int rank, int64_t c0, int64_t *zz_shape,
+                   int *zz_rank, int64_t *hw_shape);
+
+/* TransFormatFromNdToFracZz (fractal_zz.cc:140-236) on the GPU: c0 x c0 blocks,
+ * row bands outermost; H and W padding written as zeros (:148). */
+int dcopy_nd_to_zz(void *dst, const void *src, const int64_t *nd_shape, int rank,
+                   int elem_bytes, int64_t c0, dcopy_stream_t stream);
+
+/* TransFormatFromFracZzToNd (fractal_zz.cc:238-334) on the GPU: the exact
+ * inverse; nd_shape is the DESTINATION (ND) shape. */
+int dcopy_zz_to_nd(void *dst, const void *src, const int64_t *nd_shape, int rank,
+                   int elem_bytes, int64_t c0, dcopy_stream_t stream);
+
 /* ---- GE TransData level ------------------------------------------------------
  * The format-transfer registry of GE (base/formats/formats.cc:30-71,
  * register_format_transfer.h:25-95) on device buffers.  Formats and data types
@@ -169,27 +187,31 @@ int dcopy_nz_to_nd(void *dst, const void *src, const int64_t *nd_shape, int rank
  * api/python/ge/ge/graph/types.py); only PRIMARY formats are passed, with the
  * C0 of each side given explicitly (TransArgs::src_c0_format/dst_c0_format).
  * Registered pairs: {ND, NCHW, NHWC} <-> FRACTAL_NZ
- * (format_transfer_fractal_nz.cc:459-464) and the 12 transposes among NCHW,
+ * (format_transfer_fractal_nz.cc:459-464), {ND, NCHW, NHWC} <-> FRACTAL_ZZ
+ * (format_transfer_fractal_zz.cc:494-499) and the 12 transposes among NCHW,
  * NHWC, HWCN, CHWN (format_transfer_transpose.cc:268-279). */
 #define DCOPY_FORMAT_NCHW 0
 #define DCOPY_FORMAT_NHWC 1
 #define DCOPY_FORMAT_ND 2
 #define DCOPY_FORMAT_CHWN 14
 #define DCOPY_FORMAT_HWCN 16
+#define DCOPY_FORMAT_FRACTAL_ZZ 28
 #define DCOPY_FORMAT_FRACTAL_NZ 29
 
 /* Transfer classes (the reference's FormatTransfer subclasses). */
 #define DCOPY_TRANSFER_FRACTAL_NZ 1    /* FormatTransferFractalNz   (ND/NCHW/NHWC -> NZ) */
 #define DCOPY_TRANSFER_FRACTAL_NZ_ND 2 /* FormatTransferFractalNzND (NZ -> ND/NCHW/NHWC) */
 #define DCOPY_TRANSFER_TRANSPOSE 3     /* FormatTransferTranspose   (4-D permutes)       */
+#define DCOPY_TRANSFER_FRACTAL_ZZ 4    /* FormatTransferFractalZz   (ND/NCHW/NHWC -> ZZ) */
+#define DCOPY_TRANSFER_FRACTAL_ZZ_ND 5 /* FormatTransferFractalZzND (ZZ -> ND/NCHW/NHWC) */
 
 /* TransArgs (register_format_transfer.h:25-42) with device data. */
 typedef struct DcopyTransArgs {
   const void *data;         /* source, device memory */
   int32_t src_format;       /* primary GE Format of the source */
   int32_t dst_format;       /* primary GE Format of the destination */
-  int64_t src_c0;           /* C0 of the source format (used by NZ -> ND) */
-  int64_t dst_c0;           /* C0 of the destination format (used by ND -> NZ) */
+  int64_t src_c0;           /* C0 of the source format (used by NZ/ZZ -> ND) */
+  int64_t dst_c0;           /* C0 of the destination format (used by ND -> NZ/ZZ) */
   const int64_t *src_shape;
   int32_t src_rank;
   const int64_t *dst_shape; /* required by the transfers, as in the reference */
@@ -218,13 +240,14 @@ int dcopy_trans_format_check(int transfer_class, const DcopyTransArgs *args,
 
 /* FormatTransfer::TransFormat of one transfer class, with that class's own
  * checks and status codes (format_transfer_fractal_nz.cc:301-353, 397-446;
+ * format_transfer_fractal_zz.cc:337-389, 433-481;
  * format_transfer_transpose.cc:239-251). */
 int dcopy_trans_format(int transfer_class, const DcopyTransArgs *args, void *dst,
                        uint64_t dst_capacity, uint64_t *dst_length, dcopy_stream_t stream);
 
 /* FormatTransfer::TransShape of one transfer class (fractal_nz.cc:355-395,
- * 448-457; transpose.cc:253-266).  `c0` is the C0 of dst_format.  dst_shape
- * needs room for src_rank + 2 entries. */
+ * 448-457; fractal_zz.cc:391-431, 483-492; transpose.cc:253-266).  `c0` is the
+ * C0 of dst_format.  dst_shape needs room for src_rank + 2 entries. */
 int dcopy_trans_shape(int transfer_class, int32_t src_format, const int64_t *src_shape,
                       int32_t src_rank, int32_t data_type, int32_t dst_format, int64_t c0,
                       int64_t *dst_shape, int32_t *dst_rank);

@@ -2,7 +2,7 @@
 //
 // Mirrors the interface GE's callers use (ge/base/formats/formats.h/.cc,
 // register_format_transfer.h:25-48, format_transfer_fractal_nz.h:21-38,
-// format_transfer_transpose.h): TransArgs in, TransResult out, host buffers on
+// format_transfer_fractal_zz.h, format_transfer_transpose.h): TransArgs in, TransResult out, host buffers on
 // both sides, GE status codes.  The data movement runs on the GPU through the C
 // ABI: the source is copied to the device, converted by the library's kernels
 // and copied back into a new host buffer owned by the TransResult, as GE's own
@@ -14,8 +14,9 @@
 // Differences, all on purpose:
 //   * formats are the PRIMARY GE formats; C0 comes from TransArgs'
 //     src_c0_format / dst_c0_format fields (GE decodes it from the full format);
-//   * the registry holds {ND, NCHW, NHWC} <-> FRACTAL_NZ and the 12 transposes
-//     among NCHW/NHWC/HWCN/CHWN; other pairs are ACL_ERROR_GE_FORMAT_INVALID;
+//   * the registry holds {ND, NCHW, NHWC} <-> FRACTAL_NZ / FRACTAL_ZZ and the 12
+//     transposes among NCHW/NHWC/HWCN/CHWN; other pairs are
+//     ACL_ERROR_GE_FORMAT_INVALID;
 //   * device work runs on an internal stream and the call returns after the
 //     result is on the host (GE's transfers are synchronous too).
 #ifndef DCOPY_GE_FORMATS_HPP_
@@ -187,7 +188,8 @@ inline Status TransTensorShape(Format src_format, const std::vector<int64_t> &sr
 }
 
 // The FormatTransfer classes (format_transfer_fractal_nz.h:21-38,
-// format_transfer_transpose.h): TransFormat runs that class's own checks.
+// format_transfer_fractal_zz.h, format_transfer_transpose.h): TransFormat runs
+// that class's own checks.
 template <int kClass>
 class FormatTransferClass {
  public:
@@ -209,6 +211,8 @@ class FormatTransferClass {
 using FormatTransferFractalNz = FormatTransferClass<DCOPY_TRANSFER_FRACTAL_NZ>;
 using FormatTransferFractalNzND = FormatTransferClass<DCOPY_TRANSFER_FRACTAL_NZ_ND>;
 using FormatTransferTranspose = FormatTransferClass<DCOPY_TRANSFER_TRANSPOSE>;
+using FormatTransferFractalZz = FormatTransferClass<DCOPY_TRANSFER_FRACTAL_ZZ>;
+using FormatTransferFractalZzND = FormatTransferClass<DCOPY_TRANSFER_FRACTAL_ZZ_ND>;
 
 // format_transfer_transpose.cc:142-215 with host buffers.
 inline Status TransposeWithShapeCheck(const uint8_t *src, const std::vector<int64_t> &src_shape,

@@ -226,39 +226,80 @@ int oracle_nz_shape(const int64_t *src, int rank, int64_t w0, int64_t *dst, int 
   return shape_valid(dst, n) ? ORACLE_OK : ORACLE_ESHAPE;
 }
 
+/* TransShapeToFracZz, format_transfer_fractal_zz.cc:74-118. */
+int oracle_zz_shape(const int64_t *src, int rank, int64_t c0, int64_t *dst, int *dst_rank,
+                    int64_t *hw) {
+  if (!src || !dst || !dst_rank || !hw || rank <= 0) return ORACLE_ESHAPE;
+  int n = 0;
+  if (rank == 1) {
+    dst[n++] = 1;
+    dst[n++] = ge_ceil(src[0], c0);
+    dst[n++] = c0;
+    dst[n++] = c0;
+    hw[0] = 1;
+    hw[1] = 1;
+    hw[2] = src[0];
+  } else {
+    int64_t times = 1;
+    for (int i = 0; i < rank - 2; ++i) {
+      dst[n++] = src[i];
+      times *= src[i];
+    }
+    dst[n++] = ge_ceil(src[rank - 2], c0);
+    dst[n++] = ge_ceil(src[rank - 1], c0);
+    dst[n++] = c0;
+    dst[n++] = c0;
+    hw[0] = times;
+    hw[1] = src[rank - 2];
+    hw[2] = src[rank - 1];
+  }
+  *dst_rank = n;
+  return shape_valid(dst, n) ? ORACLE_OK : ORACLE_ESHAPE;
+}
+
+/* One job of the FRACTAL_NZ / FRACTAL_ZZ copy loops over ND rows [r0, r1) of
+ * times*H.  ND row hi of batch t starts, in the tiled buffer, at
+ *   t*batch + (hi / band_rows)*band_stride + (hi % band_rows)*w0
+ * and its column block w1 sits `panel` elements further per block:
+ *   NZ: band_rows >= H (no bands; rows of a panel are adjacent), panel = H1*16*w0;
+ *   ZZ: band_rows = h0, band_stride = W1*h0*w0, panel = h0*w0. */
 typedef struct {
   uint8_t *dst;
   const uint8_t *src;
-  int64_t r0, r1; /* flattened (times, h) rows */
-  int64_t h, w, size, w0, h1h0w0, w1h1h0w0, num_w1;
-  int to_nz;
-} nz_job;
+  int64_t r0, r1;
+  int64_t h, w, size, w0, panel, batch, band_rows, band_stride, num_w1;
+  int to_frac;
+} frac_job;
 
-/* The hot triple loop of TransFormatFromNdToFracNz (:168-209) and
- * TransFormatFromFracNzToNd (:251-294), over rows [r0, r1) of times*H. */
-static void *nz_worker(void *arg) {
-  const nz_job *j = (const nz_job *)arg;
+/* The hot loops of TransFormatFromNdToFracNz (fractal_nz.cc:168-209),
+ * TransFormatFromFracNzToNd (:251-294), TransFormatFromNdToFracZz
+ * (fractal_zz.cc:176-230) and TransFormatFromFracZzToNd (:275-328):
+ * whole W0-element runs for the full column blocks, then the W tail
+ * element by element. */
+static void *frac_worker(void *arg) {
+  const frac_job *j = (const frac_job *)arg;
   const int64_t size = j->size, w0 = j->w0;
   for (int64_t r = j->r0; r < j->r1; ++r) {
     const int64_t t = r / j->h, hi = r % j->h;
-    const int64_t nz_h_head = t * j->w1h1h0w0 + hi * w0;
+    const int64_t fr_h_head =
+        t * j->batch + (hi / j->band_rows) * j->band_stride + (hi % j->band_rows) * w0;
     const int64_t nd_h_head = t * j->h * j->w + hi * j->w;
     for (int64_t w1i = 0; w1i < j->num_w1; ++w1i) {
-      const int64_t nz_off = (nz_h_head + w1i * j->h1h0w0) * size;
+      const int64_t fr_off = (fr_h_head + w1i * j->panel) * size;
       const int64_t nd_off = (nd_h_head + w1i * w0) * size;
-      if (j->to_nz)
-        memcpy(j->dst + nz_off, j->src + nd_off, (size_t)(size * w0));
+      if (j->to_frac)
+        memcpy(j->dst + fr_off, j->src + nd_off, (size_t)(size * w0));
       else
-        memcpy(j->dst + nd_off, j->src + nz_off, (size_t)(size * w0));
+        memcpy(j->dst + nd_off, j->src + fr_off, (size_t)(size * w0));
     }
     const int64_t w1_head = j->num_w1 * w0;
     for (int64_t w0i = 0; w1_head + w0i < j->w; ++w0i) {
-      const int64_t nz_off = (nz_h_head + j->num_w1 * j->h1h0w0 + w0i) * size;
+      const int64_t fr_off = (fr_h_head + j->num_w1 * j->panel + w0i) * size;
       const int64_t nd_off = (nd_h_head + w1_head + w0i) * size;
-      if (j->to_nz)
-        memcpy(j->dst + nz_off, j->src + nd_off, (size_t)size);
+      if (j->to_frac)
+        memcpy(j->dst + fr_off, j->src + nd_off, (size_t)size);
       else
-        memcpy(j->dst + nd_off, j->src + nz_off, (size_t)size);
+        memcpy(j->dst + nd_off, j->src + fr_off, (size_t)size);
     }
   }
   return NULL;
@@ -275,16 +316,20 @@ static void *zero_worker(void *arg) {
   return NULL;
 }
 
-static int nz_run(void *dst, const void *src, const int64_t *nd_shape, int rank, int elem_bytes,
-                  int64_t w0, int to_nz, int nthreads) {
-  if (elem_bytes <= 0) return ORACLE_EDTYPE; /* IsDataTypeSupportForTransShapeToFracNz, :36 */
+static int frac_run(int zz, void *dst, const void *src, const int64_t *nd_shape, int rank,
+                    int elem_bytes, int64_t w0, int to_nz, int nthreads) {
+  /* IsDataTypeSupportForTransShapeToFracNz (fractal_nz.cc:36),
+   * CheckDataTypeSupportForFractalZz (fractal_zz.cc:45). */
+  if (elem_bytes <= 0) return ORACLE_EDTYPE;
   if (!shape_valid(nd_shape, rank)) return ORACLE_ESHAPE;
-  /* NZ->ND divides by w0 (:249); a C0 of 0 never comes out of a format's C0 bits. */
+  /* The tiled -> ND loops divide by w0 (fractal_nz.cc:249, fractal_zz.cc:273);
+   * a C0 of 0 never comes out of a format's C0 bits. */
   if (!to_nz && w0 <= 0) return ORACLE_ESHAPE;
   int64_t nz[16], hw[3];
   int nz_rank = 0;
   if (rank > 14) return ORACLE_ESHAPE;
-  int rc = oracle_nz_shape(nd_shape, rank, w0, nz, &nz_rank, hw);
+  int rc = zz ? oracle_zz_shape(nd_shape, rank, w0, nz, &nz_rank, hw)
+              : oracle_nz_shape(nd_shape, rank, w0, nz, &nz_rank, hw);
   if (rc) return rc;
   int64_t nz_items = 1, nd_items = 1;
   for (int i = 0; i < nz_rank; ++i) nz_items *= nz[i];
@@ -295,7 +340,8 @@ static int nz_run(void *dst, const void *src, const int64_t *nd_shape, int rank,
   if (nthreads < 1) nthreads = 1;
   if (nthreads > 256) nthreads = 256;
   pthread_t th[256];
-  if (to_nz) { /* new uint8_t[dst_size]() zero-initialises the padding (:139) */
+  if (to_nz) { /* new uint8_t[dst_size]() zero-initialises the padding (fractal_nz.cc:139,
+                 fractal_zz.cc:148) */
     zero_job zj[256];
     const size_t per = ((size_t)dst_size + nthreads - 1) / nthreads;
     int started = 0;
@@ -314,13 +360,19 @@ static int nz_run(void *dst, const void *src, const int64_t *nd_shape, int rank,
     for (int k = 0; k < started; ++k)
       if (th[k]) pthread_join(th[k], NULL);
   }
-  const int64_t w1 = nz[nz_rank - 4], h1 = nz[nz_rank - 3], h0 = nz[nz_rank - 2];
-  const int64_t h1h0w0 = h1 * h0 * w0;
-  nz_job base = {(uint8_t *)dst, (const uint8_t *)src, 0, 0, hw[1], hw[2], elem_bytes, w0,
-                 h1h0w0, w1 * h1h0w0, hw[2] / w0, to_nz};
+  const int64_t h0 = nz[nz_rank - 2];
+  const int64_t w1 = zz ? nz[nz_rank - 3] : nz[nz_rank - 4];
+  const int64_t h1 = zz ? nz[nz_rank - 4] : nz[nz_rank - 3];
+  const int64_t block = h0 * w0;
   const int64_t rows = hw[0] * hw[1];
   if (rows == 0) return ORACLE_OK;
-  nz_job jobs[256];
+  frac_job base = {(uint8_t *)dst, (const uint8_t *)src, 0, 0, hw[1], hw[2], elem_bytes, w0,
+                   zz ? block : h1 * block,          /* panel */
+                   h1 * w1 * block,                   /* batch */
+                   zz ? h0 : h1 * h0,                 /* band_rows */
+                   zz ? w1 * block : 0,               /* band_stride */
+                   hw[2] / w0, to_nz};
+  frac_job jobs[256];
   const int64_t per = (rows + nthreads - 1) / nthreads;
   int started = 0;
   for (int k = 0; k < nthreads; ++k) {
@@ -330,8 +382,8 @@ static int nz_run(void *dst, const void *src, const int64_t *nd_shape, int rank,
     jobs[k] = base;
     jobs[k].r0 = r0;
     jobs[k].r1 = r1;
-    if (nthreads == 1 || pthread_create(&th[k], NULL, nz_worker, &jobs[k]) != 0) {
-      nz_worker(&jobs[k]);
+    if (nthreads == 1 || pthread_create(&th[k], NULL, frac_worker, &jobs[k]) != 0) {
+      frac_worker(&jobs[k]);
       th[k] = 0;
     }
     started = k + 1;
@@ -343,22 +395,32 @@ static int nz_run(void *dst, const void *src, const int64_t *nd_shape, int rank,
 
 int oracle_nd_to_nz(void *dst, const void *src, const int64_t *nd_shape, int rank,
                     int elem_bytes, int64_t w0) {
-  return nz_run(dst, src, nd_shape, rank, elem_bytes, w0, 1, 1);
+  return frac_run(0, dst, src, nd_shape, rank, elem_bytes, w0, 1, 1);
 }
 
 int oracle_nz_to_nd(void *dst, const void *src, const int64_t *nd_shape, int rank,
                     int elem_bytes, int64_t w0) {
-  return nz_run(dst, src, nd_shape, rank, elem_bytes, w0, 0, 1);
+  return frac_run(0, dst, src, nd_shape, rank, elem_bytes, w0, 0, 1);
 }
 
 int oracle_nd_to_nz_mt(void *dst, const void *src, const int64_t *nd_shape, int rank,
                        int elem_bytes, int64_t w0, int nthreads) {
-  return nz_run(dst, src, nd_shape, rank, elem_bytes, w0, 1, nthreads);
+  return frac_run(0, dst, src, nd_shape, rank, elem_bytes, w0, 1, nthreads);
 }
 
 int oracle_nz_to_nd_mt(void *dst, const void *src, const int64_t *nd_shape, int rank,
                        int elem_bytes, int64_t w0, int nthreads) {
-  return nz_run(dst, src, nd_shape, rank, elem_bytes, w0, 0, nthreads);
+  return frac_run(0, dst, src, nd_shape, rank, elem_bytes, w0, 0, nthreads);
+}
+
+int oracle_nd_to_zz(void *dst, const void *src, const int64_t *nd_shape, int rank,
+                    int elem_bytes, int64_t c0) {
+  return frac_run(1, dst, src, nd_shape, rank, elem_bytes, c0, 1, 1);
+}
+
+int oracle_zz_to_nd(void *dst, const void *src, const int64_t *nd_shape, int rank,
+                    int elem_bytes, int64_t c0) {
+  return frac_run(1, dst, src, nd_shape, rank, elem_bytes, c0, 0, 1);
 }
 
 /* ------------------------------------------------------------------------ */

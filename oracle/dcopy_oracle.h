@@ -10,8 +10,9 @@
  *   - tiling planner and RunTiles address model: fixtures generated from the
  *     reference's own Python twin (standalone_datacopy/profile.py:88-99,
  *     test_address_model.py:13-34) by tests/golden/make_golden.py;
- *   - ND<->FRACTAL_NZ and N-D transpose: GE's golden vectors
+ *   - ND<->FRACTAL_NZ, ND<->FRACTAL_ZZ and N-D transpose: GE's golden vectors
  *     (tests/ge/ut/ge/common/format_transfer_fractal_nz_unittest.cc,
+ *      format_transfer_fractal_zz_unittest.cc,
  *      format_transfer_transpose_unittest.cc), parsed at test time.
  *   - DataCopyExt gap addressing: test_address_model.py:24 (pinned through the
  *     RunTiles model, which is a DataCopyExt gather with blockLen=4).
@@ -89,6 +90,19 @@ int oracle_nd_to_nz_mt(void *dst, const void *src, const int64_t *nd_shape, int 
                        int elem_bytes, int64_t w0, int nthreads);
 int oracle_nz_to_nd_mt(void *dst, const void *src, const int64_t *nd_shape, int rank,
                        int elem_bytes, int64_t w0, int nthreads);
+
+/* ---- ND <-> FRACTAL_ZZ ---------------------------------------------------- */
+
+/* TransShapeToFracZz (format_transfer_fractal_zz.cc:74-118): [..., H, W] ->
+ * [..., ceil(H/c0), ceil(W/c0), c0, c0]; rank 1 [N] -> [1, ceil(N/c0), c0, c0]. */
+int oracle_zz_shape(const int64_t *nd_shape, int rank, int64_t c0, int64_t *dst_shape,
+                    int *dst_rank, int64_t *hw_shape);
+/* TransFormatFromNdToFracZz (:140-236), zero-filled padding (:148). */
+int oracle_nd_to_zz(void *dst, const void *src, const int64_t *nd_shape, int rank,
+                    int elem_bytes, int64_t c0);
+/* TransFormatFromFracZzToNd (:238-334). */
+int oracle_zz_to_nd(void *dst, const void *src, const int64_t *nd_shape, int rank,
+                    int elem_bytes, int64_t c0);
 
 /* ---- N-D transpose -------------------------------------------------------- */
 

@@ -57,6 +57,10 @@ def lib() -> ctypes.CDLL:
             "oracle_nz_shape": [_i64p, ctypes.c_int, ctypes.c_int64, _i64p,
                                 ctypes.POINTER(ctypes.c_int), _i64p],
             "oracle_nd_to_nz": [_vp, _vp, _i64p, ctypes.c_int, ctypes.c_int, ctypes.c_int64],
+            "oracle_zz_shape": [_i64p, ctypes.c_int, ctypes.c_int64, _i64p,
+                                ctypes.POINTER(ctypes.c_int), _i64p],
+            "oracle_nd_to_zz": [_vp, _vp, _i64p, ctypes.c_int, ctypes.c_int, ctypes.c_int64],
+            "oracle_zz_to_nd": [_vp, _vp, _i64p, ctypes.c_int, ctypes.c_int, ctypes.c_int64],
             "oracle_nz_to_nd": [_vp, _vp, _i64p, ctypes.c_int, ctypes.c_int, ctypes.c_int64],
             "oracle_nd_to_nz_mt": [_vp, _vp, _i64p, ctypes.c_int, ctypes.c_int, ctypes.c_int64,
                                    ctypes.c_int],
@@ -135,6 +139,22 @@ def nz_to_nd(dst, src, nd_shape, elem_bytes, w0, threads=1) -> int:
     return lib().oracle_nz_to_nd(_p(dst), _p(src), _i64(nd_shape), len(nd_shape), elem_bytes, w0)
 
 
+def zz_shape(nd_shape: Sequence[int], c0: int):
+    out = (ctypes.c_int64 * (len(nd_shape) + 4))()
+    rank = ctypes.c_int(0)
+    hw = (ctypes.c_int64 * 3)()
+    rc = lib().oracle_zz_shape(_i64(nd_shape), len(nd_shape), c0, out, ctypes.byref(rank), hw)
+    return rc, [out[i] for i in range(rank.value)], tuple(hw)
+
+
+def nd_to_zz(dst, src, nd_shape, elem_bytes, c0) -> int:
+    return lib().oracle_nd_to_zz(_p(dst), _p(src), _i64(nd_shape), len(nd_shape), elem_bytes, c0)
+
+
+def zz_to_nd(dst, src, nd_shape, elem_bytes, c0) -> int:
+    return lib().oracle_zz_to_nd(_p(dst), _p(src), _i64(nd_shape), len(nd_shape), elem_bytes, c0)
+
+
 def transpose(dst, src, src_shape, perm, elem_bytes) -> int:
     if len(perm) != len(src_shape):
         raise ValueError("perm and src_shape must have the same rank")
@@ -160,6 +180,25 @@ def nz_to_nd_array(src: np.ndarray, nd_shape, w0: int, threads: int = 1) -> np.n
     rc = nz_to_nd(out, np.ascontiguousarray(src), nd_shape, src.dtype.itemsize, w0, threads)
     if rc:
         raise ValueError(f"nz_to_nd rc={rc}")
+    return out
+
+
+def nd_to_zz_array(src: np.ndarray, c0: int) -> np.ndarray:
+    rc, zz, _ = zz_shape(src.shape, c0)
+    if rc:
+        raise ValueError(f"zz_shape rc={rc}")
+    out = np.empty(zz, dtype=src.dtype)
+    rc = nd_to_zz(out, np.ascontiguousarray(src), src.shape, src.dtype.itemsize, c0)
+    if rc:
+        raise ValueError(f"nd_to_zz rc={rc}")
+    return out
+
+
+def zz_to_nd_array(src: np.ndarray, nd_shape, c0: int) -> np.ndarray:
+    out = np.empty(nd_shape, dtype=src.dtype)
+    rc = zz_to_nd(out, np.ascontiguousarray(src), nd_shape, src.dtype.itemsize, c0)
+    if rc:
+        raise ValueError(f"zz_to_nd rc={rc}")
     return out
 
 

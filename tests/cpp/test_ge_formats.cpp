@@ -72,6 +72,40 @@ static void nd_nz_round_trip(Format src_fmt, const std::vector<int64_t> &nd, Dat
          ACL_ERROR_GE_FORMAT_INVALID);
 }
 
+static void nd_zz_round_trip(Format src_fmt, const std::vector<int64_t> &nd, DataType dt,
+                             int elem, int64_t c0, unsigned seed) {
+  int64_t zz[40], hw[3];
+  int zz_rank = 0;
+  EXPECT(oracle_zz_shape(nd.data(), (int)nd.size(), c0, zz, &zz_rank, hw) == 0);
+  std::vector<int64_t> zz_shape(zz, zz + zz_rank);
+  size_t n = 1, m = 1;
+  for (auto d : nd) n *= d;
+  for (auto d : zz_shape) m *= d;
+  auto data = random_vec<uint8_t>(n * elem, seed);
+  std::vector<uint8_t> expect(m * elem);
+  EXPECT(oracle_nd_to_zz(expect.data(), data.data(), nd.data(), (int)nd.size(), elem, c0) == 0);
+
+  TransArgs args{data.data(), src_fmt, FORMAT_FRACTAL_ZZ, src_fmt, FORMAT_FRACTAL_ZZ,
+                 FORMAT_RESERVED, FORMAT_RESERVED, c0, c0, nd, zz_shape, dt};
+  TransResult result;
+  EXPECT(FormatTransferFractalZz().TransFormat(args, result) == SUCCESS);
+  EXPECT(result.length == expect.size());
+  EXPECT(result.data && std::memcmp(result.data.get(), expect.data(), expect.size()) == 0);
+  std::vector<int64_t> shape_out;
+  EXPECT(FormatTransferFractalZz().TransShape(src_fmt, nd, dt, FORMAT_FRACTAL_ZZ, shape_out,
+                                              c0) == SUCCESS);
+  EXPECT(shape_out == zz_shape);
+
+  TransArgs args2{expect.data(), FORMAT_FRACTAL_ZZ, src_fmt, FORMAT_FRACTAL_ZZ, src_fmt,
+                  FORMAT_RESERVED, FORMAT_RESERVED, c0, c0, zz_shape, nd, dt};
+  TransResult result2;
+  EXPECT(TransDataFormat(args2, result2) == SUCCESS);
+  EXPECT(result2.length == data.size());
+  EXPECT(result2.data && std::memcmp(result2.data.get(), data.data(), data.size()) == 0);
+  EXPECT(FormatTransferFractalZzND().TransShape(FORMAT_FRACTAL_ZZ, zz_shape, dt, src_fmt,
+                                                shape_out) == ACL_ERROR_GE_FORMAT_INVALID);
+}
+
 static void transposes() {
   const struct {
     Format src, dst;
@@ -131,6 +165,13 @@ static void failures() {
     EXPECT(TransDataFormat(a, result) == ACL_ERROR_GE_PARAM_INVALID);
     EXPECT(IsTransFormatSupport(a));
   }
+  {  // src / dst shape relation (ZZ -> ND)
+    TransArgs a{reinterpret_cast<uint8_t *>(data), FORMAT_FRACTAL_ZZ, FORMAT_NHWC,
+                FORMAT_FRACTAL_ZZ, FORMAT_NHWC, FORMAT_RESERVED, FORMAT_RESERVED, 16, 16,
+                {1, 1, 2, 1, 16, 16}, {1, 1, 15, 17}, DT_FLOAT16};
+    EXPECT(FormatTransferFractalZzND().TransFormat(a, result) == ACL_ERROR_GE_SHAPE_INVALID);
+    EXPECT(IsTransFormatSupport(a));
+  }
   {  // src / dst shape relation (NZ -> ND)
     TransArgs a{reinterpret_cast<uint8_t *>(data), FORMAT_FRACTAL_NZ, FORMAT_NHWC,
                 FORMAT_FRACTAL_NZ, FORMAT_NHWC, FORMAT_RESERVED, FORMAT_RESERVED, 16, 16,
@@ -148,6 +189,9 @@ int main(int argc, char **argv) {
     nd_nz_round_trip(FORMAT_NCHW, {2, 2, 17, 4}, DT_FLOAT, 4, 3);
     nd_nz_round_trip(FORMAT_NHWC, {2, 2, 4, 17}, DT_FLOAT, 4, 4);
     nd_nz_round_trip(FORMAT_ND, {3, 100, 256}, DT_BF16, 2, 5);
+    nd_zz_round_trip(FORMAT_ND, {2, 3, 4, 33}, DT_UINT8, 1, 32, 6);
+    nd_zz_round_trip(FORMAT_NHWC, {2, 2, 17, 4}, DT_FLOAT, 4, 16, 7);
+    nd_zz_round_trip(FORMAT_ND, {3, 100, 256}, DT_BF16, 2, 16, 8);
     transposes();
   }
   std::printf("%s: %d checks, %d failures\n", g_failures ? "FAIL" : "PASS", g_checks, g_failures);

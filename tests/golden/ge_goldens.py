@@ -3,6 +3,7 @@
 The reference's golden vectors for the layout conversions live in gtest sources
 that cannot be built here (they need securec, gtest and the metadef headers):
   tests/ge/ut/ge/common/format_transfer_fractal_nz_unittest.cc
+  tests/ge/ut/ge/common/format_transfer_fractal_zz_unittest.cc
   tests/ge/ut/ge/common/format_transfer_transpose_unittest.cc
 This module reads them as text: for every TEST_F it extracts the literal
 `data` / `ret` arrays, each `TransArgs{...}` (primary formats, shapes, data
@@ -20,6 +21,7 @@ from typing import Dict, List, Optional
 import numpy as np
 
 NZ_TEST = "ge-develop/tests/ge/ut/ge/common/format_transfer_fractal_nz_unittest.cc"
+ZZ_TEST = "ge-develop/tests/ge/ut/ge/common/format_transfer_fractal_zz_unittest.cc"
 TRANSPOSE_TEST = "ge-develop/tests/ge/ut/ge/common/format_transfer_transpose_unittest.cc"
 
 _CTYPES = {"uint8_t": np.uint8, "uint16_t": np.uint16, "float": np.float32,
@@ -32,7 +34,7 @@ DT = {"DT_FLOAT": 0, "DT_FLOAT16": 1, "DT_INT8": 2, "DT_INT32": 3, "DT_UINT8": 4
       "DT_DOUBLE": 11, "DT_BOOL": 12, "DT_STRING": 13, "DT_BF16": 27, "DT_UNDEFINED": 28}
 FMT = {"FORMAT_NCHW": 0, "FORMAT_NHWC": 1, "FORMAT_ND": 2, "FORMAT_NC1HWC0": 3,
        "FORMAT_FRACTAL_Z": 4, "FORMAT_C1HWNC0": 9, "FORMAT_CHWN": 14, "FORMAT_HWCN": 16,
-       "FORMAT_FRACTAL_NZ": 29, "FORMAT_RESERVED": 40}
+       "FORMAT_FRACTAL_ZZ": 28, "FORMAT_FRACTAL_NZ": 29, "FORMAT_RESERVED": 40}
 STATUS = {"SUCCESS": 0, "ACL_ERROR_GE_PARAM_INVALID": 145000,
           "ACL_ERROR_GE_FORMAT_INVALID": 145020, "ACL_ERROR_GE_SHAPE_INVALID": 145021,
           "ACL_ERROR_GE_DATATYPE_INVALID": 145022}
@@ -109,8 +111,17 @@ def parse(path: Path) -> List[Case]:
     for name, body in _split_tests(text):
         arrays = {}
         for m in re.finditer(r"\b(uint8_t|uint16_t|float|int32_t|int64_t|double)\s+(\w+)\s*"
-                             r"\[[^\]]*\]\s*=\s*\{(.*?)\};", body, re.S):
-            arrays[m.group(2)] = _array_values(m.group(3), m.group(1))
+                             r"\[([^\]]*)\]\s*=\s*\{(.*?)\};", body, re.S):
+            values = _array_values(m.group(4), m.group(1))
+            # A shorter initializer list leaves the remaining elements zero (C++
+            # aggregate initialisation): pad to the declared extent when it is
+            # a product of integer literals.
+            dims = m.group(3).split("*")
+            if all(d.strip().isdigit() for d in dims):
+                n = int(np.prod([int(d) for d in dims]))
+                if n > values.size:
+                    values = np.concatenate([values, np.zeros(n - values.size, values.dtype)])
+            arrays[m.group(2)] = values
         args = {}
         for m in re.finditer(r"TransArgs\s+(\w+)\s*\{(.*?)\};", body, re.S):
             args[m.group(1)] = _parse_args(m.group(1), m.group(2))
@@ -152,5 +163,5 @@ def parse(path: Path) -> List[Case]:
 
 
 def load(reference_root: Path, which: str) -> List[Case]:
-    rel = NZ_TEST if which == "nz" else TRANSPOSE_TEST
+    rel = {"nz": NZ_TEST, "zz": ZZ_TEST, "transpose": TRANSPOSE_TEST}[which]
     return parse(Path(reference_root) / rel)

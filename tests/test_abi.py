@@ -70,6 +70,44 @@ def test_nz_shape_matches_oracle(dcopy, oracle, shape, w0):
         assert dcopy.nz_shape(shape, w0) == (nz, hw)
 
 
+@pytest.mark.parametrize("shape", [[1], [100], [0], [2, 2, 17, 4], [30, 33], [3, 0, 7],
+                                   [8, 4096, 4096], [1, 1, 1, 1, 1, 1, 31, 17]])
+@pytest.mark.parametrize("c0", [1, 8, 16, 32, 0, -1])
+def test_zz_shape_matches_oracle(dcopy, oracle, shape, c0):
+    rc, zz, hw = oracle.zz_shape(shape, c0)
+    if rc:
+        with pytest.raises(dcopy.DcopyError) as e:
+            dcopy.zz_shape(shape, c0)
+        assert e.value.code == dcopy.ERR_SHAPE_INVALID
+    else:
+        assert dcopy.zz_shape(shape, c0) == (zz, hw)
+
+
+def test_zz_validation_before_launch(dcopy):
+    with pytest.raises(dcopy.DcopyError) as e:
+        dcopy.nd_to_zz(0, 0, [4, 4], 3, 16)  # element size not in {1,2,4,8,16}
+    assert e.value.code == dcopy.ERR_DATATYPE_INVALID
+    with pytest.raises(dcopy.DcopyError) as e:
+        dcopy.zz_to_nd(0, 0, [4, 4], 2, 0)  # the ZZ -> ND loops divide by c0
+    assert e.value.code == dcopy.ERR_SHAPE_INVALID
+    with pytest.raises(dcopy.DcopyError) as e:
+        dcopy.nd_to_zz(0, 0, [4, 4], 2, 16)  # NULL buffers with bytes to move
+    assert e.value.code == dcopy.ERR_PARAM_INVALID
+    dcopy.nd_to_zz(0, 0, [0, 16], 2, 16)  # empty: nothing to move
+    f, d = dcopy.FORMAT, dcopy.DATA_TYPE
+    assert dcopy.trans_shape(4, f["ND"], [2, 3, 4, 33], d["UINT8"], f["FRACTAL_ZZ"], 32) == \
+        [2, 3, 1, 2, 32, 32]
+    assert dcopy.trans_tensor_shape(f["NCHW"], [1, 2, 4, 17], d["FLOAT"], f["FRACTAL_ZZ"], 16) \
+        == [1, 2, 1, 2, 16, 16]
+    with pytest.raises(dcopy.DcopyError) as e:
+        dcopy.trans_tensor_shape(f["FRACTAL_ZZ"], [1, 1, 16, 16], d["FLOAT"], f["ND"], 16)
+    assert e.value.code == dcopy.ERR_FORMAT_INVALID
+    # Sizing query without data movement.
+    args = dict(src_c0=16, dst_c0=16)
+    assert dcopy.trans_format_check(0, 0x1000, f["ND"], f["FRACTAL_ZZ"], [15, 17],
+                                    [1, 2, 16, 16], d["FLOAT16"], **args) == 1024
+
+
 def test_validation_before_launch(dcopy):
     # Each of these fails on the host before any device work.
     with pytest.raises(dcopy.DcopyError) as e:

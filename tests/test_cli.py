@@ -80,3 +80,8 @@ def test_bench_sweep_and_nz(dcopy, torch_cuda):
     r = _run(BIN / "dcopy_bench", "nz", "--batch", 2, "--h", 1024, "--w", 1024, "--reps", 2)
     assert r.returncode == 0, r.stderr
     assert json.loads(r.stdout)["round_trip_bit_exact"] is True
+    r = _run(BIN / "dcopy_bench", "nz", "--format", "zz", "--batch", 2, "--h", 1000, "--w", 1000,
+             "--reps", 2)
+    assert r.returncode == 0, r.stderr
+    out = json.loads(r.stdout)
+    assert out["round_trip_bit_exact"] is True and out["format"] == "zz"

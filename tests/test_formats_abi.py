@@ -1,10 +1,10 @@
 """CPU checks of the GE TransData-level entry points against GE's own tests.
 
 Every TransFormat / TransShape / TransDataFormat expectation in GE's
-format_transfer_fractal_nz_unittest.cc and format_transfer_transpose_unittest.cc
-whose outcome is decided before any data moves (all failures, all TransShape
-calls) is replayed through the C ABI here; the data-moving successes run in the
-GPU tests.  The status classes map onto GE's codes through dcopy_status_to_ge.
+format_transfer_fractal_nz_unittest.cc, format_transfer_fractal_zz_unittest.cc and
+format_transfer_transpose_unittest.cc whose outcome is decided before any data
+moves (all failures, all TransShape calls) is replayed through the C ABI here;
+the data-moving successes run in the GPU tests.  The status classes map onto GE's codes through dcopy_status_to_ge.
 """
 import numpy as np
 import pytest
@@ -12,7 +12,8 @@ import pytest
 import ge_goldens
 
 CLASS = {"FormatTransferFractalNz": 1, "FormatTransferFractalNzND": 2,
-         "FormatTransferTranspose": 3}
+         "FormatTransferTranspose": 3, "FormatTransferFractalZz": 4,
+         "FormatTransferFractalZzND": 5}
 
 
 def _fmt(name):
@@ -31,7 +32,7 @@ def _status(dcopy, fn, *args, **kw):
         return dcopy.status_to_ge(e.code)
 
 
-@pytest.mark.parametrize("which", ["nz", "transpose"])
+@pytest.mark.parametrize("which", ["nz", "zz", "transpose"])
 def test_ge_expectations_decided_on_host(dcopy, reference_root, which):
     checked = 0
     for case in ge_goldens.load(reference_root, which):
@@ -64,7 +65,7 @@ def test_ge_expectations_decided_on_host(dcopy, reference_root, which):
                 continue
             assert got == e.status, (case.name, e)
             checked += 1
-    assert checked >= (15 if which == "nz" else 8)
+    assert checked >= {"nz": 15, "zz": 23, "transpose": 8}[which]
 
 
 def test_trans_shape_results(dcopy):

@@ -136,3 +136,75 @@ def test_nz_threads_agree(oracle):
     assert oracle.nd_to_nz_array(a, 16).tobytes() == oracle.nd_to_nz_array(a, 16, 5).tobytes()
     nz = oracle.nd_to_nz_array(a, 16)
     assert (oracle.nz_to_nd_array(nz, a.shape, 16, 6) == a).all()
+
+
+# ---- ND <-> FRACTAL_ZZ --------------------------------------------------------------
+
+@pytest.fixture(scope="module")
+def zz_cases(reference_root):
+    return ge_goldens.load(reference_root, "zz")
+
+
+def _zz_numpy(a: np.ndarray, c0: int) -> np.ndarray:
+    """FRACTAL_ZZ by array reshaping, independent of the C oracle: pad [.., H, W]
+    to whole c0 x c0 blocks, split into [.., H1, c0, W1, c0], swap to
+    [.., H1, W1, c0, c0]."""
+    if a.ndim == 1:
+        a = a.reshape(1, -1)
+    *batch, h, w = a.shape
+    h1, w1 = -(-h // c0), -(-w // c0)
+    p = np.zeros((*batch, h1 * c0, w1 * c0), dtype=a.dtype)
+    p[..., :h, :w] = a
+    p = p.reshape(*batch, h1, c0, w1, c0)
+    return np.ascontiguousarray(np.swapaxes(p, -3, -2))
+
+
+def test_zz_golden_vectors(oracle, zz_cases):
+    checked = 0
+    for case in zz_cases:
+        if "data" not in case.arrays or "ret" not in case.arrays:
+            continue
+        fwd = case.args["args"]
+        data, ret = case.arrays["data"], case.arrays["ret"]
+        c0 = fwd.c0[1]
+        rc, zz, _ = oracle.zz_shape(fwd.src_shape, c0)
+        assert rc == 0 and zz == fwd.dst_shape, case.name
+        out = oracle.nd_to_zz_array(data.reshape(fwd.src_shape), c0)
+        assert out.tobytes() == ret.tobytes(), case.name
+        back = oracle.zz_to_nd_array(ret.reshape(fwd.dst_shape), fwd.src_shape, c0)
+        assert back.tobytes() == data.tobytes(), case.name
+        # The reshaping restatement agrees with GE's vectors too.
+        assert _zz_numpy(data.reshape(fwd.src_shape), c0).tobytes() == ret.tobytes(), case.name
+        checked += 1
+    assert checked == 18  # every data-moving case of the ZZ unit test (uint8, fp16, fp32)
+
+
+@pytest.mark.parametrize("shape,c0,expect", [
+    ([1], 32, [1, 1, 32, 32]),
+    ([100], 16, [1, 7, 16, 16]),
+    ([0], 16, [1, 0, 16, 16]),
+    ([30, 33], 32, [1, 2, 32, 32]),
+    ([2, 3, 4, 33], 32, [2, 3, 1, 2, 32, 32]),
+    ([3, 0, 7], 16, [3, 0, 1, 16, 16]),
+    ([8, 4096, 4096], 16, [8, 256, 256, 16, 16]),
+])
+def test_zz_shape_rules(oracle, shape, c0, expect):
+    rc, zz, hw = oracle.zz_shape(shape, c0)
+    assert rc == 0 and zz == expect
+
+
+def test_zz_shape_invalid(oracle):
+    assert oracle.zz_shape([4, 4], -1)[0] == oracle.ESHAPE
+    assert oracle.zz_shape([1 << 21, 1 << 21], 16)[0] == oracle.ESHAPE
+
+
+@pytest.mark.parametrize("dtype", [np.uint8, np.uint16, np.uint32, np.uint64])
+@pytest.mark.parametrize("shape", [[1], [15], [17, 3], [16, 16], [2, 33, 47], [3, 2, 5, 16],
+                                   [40, 1], [1, 40]])
+@pytest.mark.parametrize("c0", [4, 16, 32])
+def test_zz_round_trip(oracle, dtype, shape, c0):
+    rng = np.random.default_rng(13)
+    a = rng.integers(0, np.iinfo(dtype).max, size=shape, dtype=dtype, endpoint=True)
+    zz = oracle.nd_to_zz_array(a, c0)
+    assert zz.tobytes() == _zz_numpy(a, c0).tobytes()
+    assert oracle.zz_to_nd_array(zz, shape, c0).tobytes() == a.tobytes()
