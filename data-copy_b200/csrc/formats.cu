@@ -1,8 +1,8 @@
 // GE TransData level on device buffers: the format-transfer registry
 // (base/formats/formats.cc, register_format_transfer.{h,cc}), the
-// FormatTransferFractalNz / FractalNzND / FractalZz / FractalZzND /
-// FormatTransferTranspose classes' argument checks, and Transpose
-// (format_transfer_transpose.cc) on the GPU.  Every check happens on the host, in the reference's order and with its
+// FormatTransferFractalNz / FractalNzND / FractalZz / FractalZzND / FractalZ /
+// FractalZTbe / FracZNchw / FracZHwcn / FracZNhwc / Transpose classes' argument
+// checks, and Transpose (format_transfer_transpose.cc) on the GPU.  Every check happens on the host, in the reference's order and with its
 // status class, before any launch; the data movement goes to the NZ kernels and
 // to the N-D box copy.
 #include <cuda_runtime.h>
@@ -94,6 +94,16 @@ int registered_class(int32_t src, int32_t dst) {
   if (src == DCOPY_FORMAT_FRACTAL_NZ && nd_like_dst) return DCOPY_TRANSFER_FRACTAL_NZ_ND;
   if (nd_like && dst == DCOPY_FORMAT_FRACTAL_ZZ) return DCOPY_TRANSFER_FRACTAL_ZZ;
   if (src == DCOPY_FORMAT_FRACTAL_ZZ && nd_like_dst) return DCOPY_TRANSFER_FRACTAL_ZZ_ND;
+  if (dst == DCOPY_FORMAT_FRACTAL_Z) {  // fractal_z.cc:606-608, fractal_z_tbe.cc:147
+    if (src == DCOPY_FORMAT_NCHW || src == DCOPY_FORMAT_HWCN || src == DCOPY_FORMAT_NHWC)
+      return DCOPY_TRANSFER_FRACTAL_Z;
+    if (src == DCOPY_FORMAT_ND) return DCOPY_TRANSFER_FRACTAL_Z_TBE;
+  }
+  if (src == DCOPY_FORMAT_FRACTAL_Z) {  // fracz_{nchw,hwcn,nhwc}.cc REGISTER lines
+    if (dst == DCOPY_FORMAT_NCHW) return DCOPY_TRANSFER_FRACZ_NCHW;
+    if (dst == DCOPY_FORMAT_HWCN) return DCOPY_TRANSFER_FRACZ_HWCN;
+    if (dst == DCOPY_FORMAT_NHWC) return DCOPY_TRANSFER_FRACZ_NHWC;
+  }
   if (find_perm(src, dst)) return DCOPY_TRANSFER_TRANSPOSE;
   return 0;
 }
@@ -345,9 +355,95 @@ int transpose_format(const DcopyTransArgs *a, void *dst, uint64_t cap, uint64_t 
                         s);
 }
 
-int class_format(int cls, const DcopyTransArgs *a, void *dst, uint64_t cap, uint64_t *len,
-                 dcopy_stream_t s) {
+// FormatTransferFractalZ::TransShape / FormatTransferFractalZTbe::TransShape
+// (fractal_z.cc:571-604, fractal_z_tbe.cc:131-146).  `groups` is the sub format
+// of the full destination format.
+int fractal_z_shape(int cls, int32_t src_format, const int64_t *src_shape, int32_t src_rank,
+                    int32_t data_type, int32_t dst_format, int64_t c0, int64_t groups,
+                    int64_t *out) {
+  if (type_size(data_type) <= 0)
+    return set_error(DCOPY_ERR_DATATYPE_INVALID, "data type %d is not supported", data_type);
+  const bool tbe = cls == DCOPY_TRANSFER_FRACTAL_Z_TBE;
+  const bool pair_ok =
+      dst_format == DCOPY_FORMAT_FRACTAL_Z &&
+      (tbe ? src_format == DCOPY_FORMAT_ND
+           : (src_format == DCOPY_FORMAT_NCHW || src_format == DCOPY_FORMAT_HWCN ||
+              src_format == DCOPY_FORMAT_NHWC));
+  if (!pair_ok)
+    return set_error(DCOPY_ERR_FORMAT_INVALID, "no FRACTAL_Z transfer from %d to %d", src_format,
+                     dst_format);
+  return fz_shape(src_format, src_shape, src_rank, c0, groups, out);
+}
+
+// FormatTransferFractalZ::TransFormat (fractal_z.cc:540-569) and
+// FormatTransferFractalZTbe::TransFormat (fractal_z_tbe.cc:117-129).
+int fractal_z_format(int cls, const DcopyTransArgs *a, int64_t fmt_groups, void *dst,
+                     uint64_t cap, uint64_t *len, dcopy_stream_t s) {
+  int64_t expect[4];
+  int rc = fractal_z_shape(cls, a->src_format, a->src_shape, a->src_rank, a->data_type,
+                           a->dst_format, a->dst_c0, fmt_groups, expect);
+  if (rc) return rc;
+  if (a->dst_rank && !same_shape(a->dst_shape, a->dst_rank, expect, 4))
+    return set_error(DCOPY_ERR_SHAPE_INVALID, "dst shape differs from the FRACTAL_Z shape");
+  // The HWCN transfer takes its groups from TransArgs::dst_sub_format (:553-556);
+  // NCHW and NHWC data never use groups.
+  const int64_t groups = a->src_format == DCOPY_FORMAT_HWCN ? a->dst_sub_format : 0;
+  if (a->dst_rank == 0 && a->src_format != DCOPY_FORMAT_NCHW && groups <= 1)
+    return set_error(DCOPY_ERR_PARAM_INVALID,
+                     "FRACTAL_Z from format %d sizes its result by dst_shape: pass it",
+                     a->src_format);
+  int64_t elems = 0;
+  rc = fz_out_elems(a->src_format, a->src_shape, a->src_rank, a->dst_c0, groups, &elems);
+  if (rc) return rc;
+  const int32_t size = type_size(a->data_type);
+  const uint64_t bytes = (uint64_t)elems * size;
+  if (bytes == 0) return store_length(len, 0);
+  if (t_check_only) return store_length(len, bytes);
+  if (cap < bytes)
+    return set_error(DCOPY_ERR_PARAM_INVALID, "dst holds %llu bytes, result needs %llu",
+                     (unsigned long long)cap, (unsigned long long)bytes);
+  rc = to_fz(dst, a->data, a->src_format, a->src_shape, a->src_rank, size, a->dst_c0, groups, s);
+  return rc ? rc : store_length(len, bytes);
+}
+
+// FormatTransferFracZ{Nchw,Hwcn,Nhwc}::TransFormat (fracz_nchw.cc:154-195 and
+// its twins): CheckArgsForFracZTo*, then the empty-result rule.
+int fracz_to_format(int cls, const DcopyTransArgs *a, void *dst, uint64_t cap, uint64_t *len,
+                    dcopy_stream_t s) {
+  const int32_t want = cls == DCOPY_TRANSFER_FRACZ_NCHW   ? DCOPY_FORMAT_NCHW
+                       : cls == DCOPY_TRANSFER_FRACZ_HWCN ? DCOPY_FORMAT_HWCN
+                                                          : DCOPY_FORMAT_NHWC;
+  if (a->src_format != DCOPY_FORMAT_FRACTAL_Z || a->dst_format != want)
+    return set_error(DCOPY_ERR_FORMAT_INVALID, "FRACTAL_Z -> %d: formats %d -> %d", want,
+                     a->src_format, a->dst_format);
+  const int32_t size = type_size(a->data_type);
+  if (size <= 0)
+    return set_error(DCOPY_ERR_DATATYPE_INVALID, "data type %d is not supported", a->data_type);
+  int rc = from_fz_check(a->src_shape, a->src_rank, want, a->dst_shape, a->dst_rank, a->src_c0);
+  if (rc) return rc;
+  const uint64_t bytes = (uint64_t)item_count(a->dst_shape, a->dst_rank) * size;
+  if (bytes == 0) {
+    if (item_count(a->src_shape, a->src_rank) == 0) return store_length(len, 0);
+    return set_error(DCOPY_ERR_SHAPE_INVALID, "empty destination from a non-empty FRACTAL_Z");
+  }
+  if (a->src_c0 == 0)  // the reference divides by it
+    return set_error(DCOPY_ERR_SHAPE_INVALID, "c0 0 with data to move");
+  if (t_check_only) return store_length(len, bytes);
+  if (cap < bytes)
+    return set_error(DCOPY_ERR_PARAM_INVALID, "dst holds %llu bytes, result needs %llu",
+                     (unsigned long long)cap, (unsigned long long)bytes);
+  rc = from_fz(dst, a->data, want, a->dst_shape, a->dst_rank, size, a->src_c0, s);
+  return rc ? rc : store_length(len, bytes);
+}
+
+int class_format(int cls, const DcopyTransArgs *a, int64_t fmt_groups, void *dst, uint64_t cap,
+                 uint64_t *len, dcopy_stream_t s) {
   switch (cls) {
+    case DCOPY_TRANSFER_FRACTAL_Z:
+    case DCOPY_TRANSFER_FRACTAL_Z_TBE: return fractal_z_format(cls, a, fmt_groups, dst, cap, len, s);
+    case DCOPY_TRANSFER_FRACZ_NCHW:
+    case DCOPY_TRANSFER_FRACZ_HWCN:
+    case DCOPY_TRANSFER_FRACZ_NHWC: return fracz_to_format(cls, a, dst, cap, len, s);
     case DCOPY_TRANSFER_FRACTAL_NZ: return fractal_nz_format(a, dst, cap, len, s);
     case DCOPY_TRANSFER_FRACTAL_NZ_ND: return fractal_nz_nd_format(a, dst, cap, len, s);
     case DCOPY_TRANSFER_TRANSPOSE: return transpose_format(a, dst, cap, len, s);
@@ -358,11 +454,22 @@ int class_format(int cls, const DcopyTransArgs *a, void *dst, uint64_t cap, uint
 }
 
 int class_shape(int cls, int32_t src_format, const int64_t *src_shape, int32_t src_rank,
-                int32_t data_type, int32_t dst_format, int64_t c0, int64_t *dst_shape,
-                int32_t *dst_rank) {
+                int32_t data_type, int32_t dst_format, int64_t c0, int64_t fmt_groups,
+                int64_t *dst_shape, int32_t *dst_rank) {
   if (!dst_shape || !dst_rank || src_rank < 0 || src_rank > kMaxRank || (src_rank && !src_shape))
     return set_error(DCOPY_ERR_PARAM_INVALID, "TransShape: invalid arguments");
   switch (cls) {
+    case DCOPY_TRANSFER_FRACTAL_Z:
+    case DCOPY_TRANSFER_FRACTAL_Z_TBE: {
+      const int rc = fractal_z_shape(cls, src_format, src_shape, src_rank, data_type, dst_format,
+                                     c0, fmt_groups, dst_shape);
+      *dst_rank = rc ? 0 : 4;
+      return rc;
+    }
+    case DCOPY_TRANSFER_FRACZ_NCHW:  // fracz_nchw.cc:197-208 and its twins
+    case DCOPY_TRANSFER_FRACZ_HWCN:
+    case DCOPY_TRANSFER_FRACZ_NHWC:
+      return set_error(DCOPY_ERR_FORMAT_INVALID, "TransShape from FRACTAL_Z is not supported");
     case DCOPY_TRANSFER_FRACTAL_NZ: {  // fractal_nz.cc:355-395
       if (type_size(data_type) <= 0)
         return set_error(DCOPY_ERR_DATATYPE_INVALID, "data type %d is not supported", data_type);
@@ -406,19 +513,38 @@ using namespace dcopy;
 
 extern "C" int32_t dcopy_data_type_size(int32_t data_type) { return type_size(data_type); }
 
+namespace {
+
+int32_t primary(int32_t format) { return format & 0xff; }           // GetPrimaryFormat
+int64_t sub_format(int32_t format) { return (format >> 8) & 0xffff; }  // GetSubFormat
+
+// The arguments with primary formats; the destination format's sub format
+// (FRACTAL_Z TransShape groups) goes to *fmt_groups.
+DcopyTransArgs normalised(const DcopyTransArgs *a, int64_t *fmt_groups) {
+  DcopyTransArgs b = *a;
+  b.src_format = primary(a->src_format);
+  b.dst_format = primary(a->dst_format);
+  *fmt_groups = sub_format(a->dst_format);
+  return b;
+}
+
+}  // namespace
+
 extern "C" int dcopy_trans_data_format(const DcopyTransArgs *args, void *dst,
                                        uint64_t dst_capacity, uint64_t *dst_length,
                                        dcopy_stream_t stream) {
   DCOPY_API_BEGIN
   int rc = check_args(args);
   if (rc) return rc;
-  const int cls = registered_class(args->src_format, args->dst_format);  // formats.cc:31-38
+  int64_t groups = 0;
+  const DcopyTransArgs a = normalised(args, &groups);
+  const int cls = registered_class(a.src_format, a.dst_format);  // formats.cc:31-38
   if (!cls)
     return set_error(DCOPY_ERR_FORMAT_INVALID, "Failed to trans data from format %d to %d",
-                     args->src_format, args->dst_format);
-  if (!args->data && item_count(args->src_shape, args->src_rank) != 0)  // :40-49
+                     a.src_format, a.dst_format);
+  if (!a.data && item_count(a.src_shape, a.src_rank) != 0)  // :40-49
     return set_error(DCOPY_ERR_PARAM_INVALID, "input data is null and the shape is not empty");
-  return class_format(cls, args, dst, dst_capacity, dst_length, stream);
+  return class_format(cls, &a, groups, dst, dst_capacity, dst_length, stream);
   DCOPY_API_END
 }
 
@@ -427,17 +553,19 @@ extern "C" int dcopy_trans_format_check(int transfer_class, const DcopyTransArgs
   DCOPY_API_BEGIN
   int rc = check_args(args);
   if (rc) return rc;
+  int64_t groups = 0;
+  const DcopyTransArgs a = normalised(args, &groups);
   int cls = transfer_class;
   if (cls == 0) {  // TransDataFormat: registry and NULL-data checks first (formats.cc:31-49)
-    cls = registered_class(args->src_format, args->dst_format);
+    cls = registered_class(a.src_format, a.dst_format);
     if (!cls)
       return set_error(DCOPY_ERR_FORMAT_INVALID, "Failed to trans data from format %d to %d",
-                       args->src_format, args->dst_format);
-    if (!args->data && item_count(args->src_shape, args->src_rank) != 0)
+                       a.src_format, a.dst_format);
+    if (!a.data && item_count(a.src_shape, a.src_rank) != 0)
       return set_error(DCOPY_ERR_PARAM_INVALID, "input data is null and the shape is not empty");
   }
   t_check_only = true;
-  rc = class_format(cls, args, nullptr, 0, dst_length, nullptr);
+  rc = class_format(cls, &a, groups, nullptr, 0, dst_length, nullptr);
   t_check_only = false;
   return rc;
   DCOPY_API_END
@@ -449,7 +577,9 @@ extern "C" int dcopy_trans_format(int transfer_class, const DcopyTransArgs *args
   DCOPY_API_BEGIN
   int rc = check_args(args);
   if (rc) return rc;
-  return class_format(transfer_class, args, dst, dst_capacity, dst_length, stream);
+  int64_t groups = 0;
+  const DcopyTransArgs a = normalised(args, &groups);
+  return class_format(transfer_class, &a, groups, dst, dst_capacity, dst_length, stream);
   DCOPY_API_END
 }
 
@@ -457,8 +587,8 @@ extern "C" int dcopy_trans_shape(int transfer_class, int32_t src_format, const i
                                  int32_t src_rank, int32_t data_type, int32_t dst_format, int64_t c0,
                                  int64_t *dst_shape, int32_t *dst_rank) {
   DCOPY_API_BEGIN
-  return class_shape(transfer_class, src_format, src_shape, src_rank, data_type, dst_format, c0,
-                     dst_shape, dst_rank);
+  return class_shape(transfer_class, primary(src_format), src_shape, src_rank, data_type,
+                     primary(dst_format), c0, sub_format(dst_format), dst_shape, dst_rank);
   DCOPY_API_END
 }
 
@@ -466,12 +596,12 @@ extern "C" int dcopy_trans_tensor_shape(int32_t src_format, const int64_t *src_s
                                         int32_t src_rank, int32_t data_type, int32_t dst_format,
                                         int64_t c0, int64_t *dst_shape, int32_t *dst_rank) {
   DCOPY_API_BEGIN
-  const int cls = registered_class(src_format, dst_format);
+  const int cls = registered_class(primary(src_format), primary(dst_format));
   if (!cls)
     return set_error(DCOPY_ERR_FORMAT_INVALID, "Failed to trans shape from format %d to %d",
-                     src_format, dst_format);
-  return class_shape(cls, src_format, src_shape, src_rank, data_type, dst_format, c0, dst_shape,
-                     dst_rank);
+                     primary(src_format), primary(dst_format));
+  return class_shape(cls, primary(src_format), src_shape, src_rank, data_type,
+                     primary(dst_format), c0, sub_format(dst_format), dst_shape, dst_rank);
   DCOPY_API_END
 }
 

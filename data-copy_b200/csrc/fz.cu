@@ -1,0 +1,493 @@
+// FRACTAL_Z (convolution weights) TransData on sm_100a.
+//
+// Layout (format_transfer_fractal_z.cc:41-537, fracz_{nchw,hwcn,nhwc}.cc):
+// FRACTAL_Z is [C1*H*W, N1, 16, C0], i.e. [c1][h][w][n][c0] with N padded to
+// N1*16 and C to C1*C0 (zeros): element (c1, h, w, n, c0) holds weight
+// (n, c = c1*C0 + c0, h, w).  Three data paths, by where the weight's innermost
+// axis lands:
+//   * NHWC: C is innermost on both sides.  For each (h, w) the weight is an
+//     [N rows x C cols] matrix (row pitch H*W*C) cut into 16 x C0 blocks: the
+//     tiled-format kernels of the NZ/ZZ transfers do it with these strides.
+//   * NCHW, HWCN and ND [C, N]: C0 is innermost in FRACTAL_Z but not in the
+//     source, so every block is a transpose.  fz_transpose_kernel stages a tile
+//     in shared memory: it reads rows of the source's contiguous axis (HW for
+//     NCHW, N for HWCN) and writes rows along FRACTAL_Z's contiguous run
+//     (n*C0 + c0), zero-filling the padding.
+//   * HWCN with groups > 1 (fractal_z.cc:276-359): block-diagonal group layout,
+//     gathered element by element (fz_groups_kernel).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+
+#include "common.cuh"
+#include "internal.cuh"
+#include "launch.cuh"
+
+namespace dcopy {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int64_t kNi = 16;  // kNiSize, formats_definitions.h:19
+enum : int32_t { kNchw = 0, kNhwc = 1, kNd = 2, kHwcn = 16 };
+
+// One transposed tile family: per batch (c1, b2) an R x K block where
+//   source element  = nd_base + ra*s_ra + rb*s_rb + k   (R = ra*RB + rb),
+//   FRACTAL_Z index = fz_base + k*dk + R,
+// valid (else zero / skipped) when ra < ra_valid, c1*C0 + rb < C, k < k_valid.
+struct FzTGeom {
+  uint32_t RT, KT;        // full tile extents
+  uint32_t R_ext, K_ext;  // extents per batch
+  uint32_t rtiles, ktiles, B2;
+  uint32_t RB, ra_valid, k_valid, C, C0;
+  uint32_t rw_last, kw_last;
+  FastDiv f_rb, f_ktiles, f_rtiles, f_b2, f_kw, f_kw_last, f_rw, f_rw_last;
+  uint64_t s_ra, s_rb, nd_c1, nd_b2, dk, fz_c1, fz_b2;
+};
+
+template <typename T, bool kToFz>
+__global__ void __launch_bounds__(kThreads) fz_transpose_kernel(T *__restrict__ dst,
+                                                                const T *__restrict__ src,
+                                                                FzTGeom g, uint32_t ntiles) {
+  extern __shared__ __align__(16) unsigned char fz_smem[];
+  T *tile = reinterpret_cast<T *>(fz_smem);
+  pdl_trigger_at_entry();
+  pdl_wait();
+  pdl_launch_dependents();
+  for (uint32_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
+    const uint32_t q2 = g.f_ktiles.div(t), kt = t - q2 * g.ktiles;
+    const uint32_t q = g.f_rtiles.div(q2), rt = q2 - q * g.rtiles;
+    const uint32_t c1 = g.f_b2.div(q), b2 = q - c1 * g.B2;
+    const bool klast = kt == g.ktiles - 1, rlast = rt == g.rtiles - 1;
+    const uint32_t kw = klast ? g.kw_last : g.KT, rw = rlast ? g.rw_last : g.RT;
+    const FastDiv fkw = klast ? g.f_kw_last : g.f_kw, frw = rlast ? g.f_rw_last : g.f_rw;
+    const uint32_t pitch = kw | 1;  // odd row pitch: the R-fastest reads spread over banks
+    const uint32_t R0 = rt * g.RT, K0 = kt * g.KT;
+    const uint32_t rb_valid = min(g.C0, g.C - c1 * g.C0);
+    const uint64_t nd_base = c1 * g.nd_c1 + b2 * g.nd_b2;
+    const uint64_t fz_base = c1 * g.fz_c1 + b2 * g.fz_b2;
+    const uint32_t n = rw * kw;
+    if (kToFz) {
+      for (uint32_t j = threadIdx.x; j < n; j += kThreads) {  // source order: k fastest
+        const uint32_t r = fkw.div(j), k = j - r * kw;
+        const uint32_t R = R0 + r, ra = g.f_rb.div(R), rb = R - ra * g.RB;
+        T v = T();
+        if (ra < g.ra_valid && rb < rb_valid && K0 + k < g.k_valid)
+          v = ld_stream(src + nd_base + ra * g.s_ra + rb * g.s_rb + K0 + k);
+        tile[r * pitch + k] = v;
+      }
+      __syncthreads();
+      for (uint32_t j = threadIdx.x; j < n; j += kThreads) {  // FRACTAL_Z order: R fastest
+        const uint32_t k = frw.div(j), r = j - k * rw;
+        dst[fz_base + (uint64_t)(K0 + k) * g.dk + R0 + r] = tile[r * pitch + k];
+      }
+    } else {
+      for (uint32_t j = threadIdx.x; j < n; j += kThreads) {
+        const uint32_t k = frw.div(j), r = j - k * rw;
+        tile[r * pitch + k] = ld_stream(src + fz_base + (uint64_t)(K0 + k) * g.dk + R0 + r);
+      }
+      __syncthreads();
+      for (uint32_t j = threadIdx.x; j < n; j += kThreads) {
+        const uint32_t r = fkw.div(j), k = j - r * kw;
+        const uint32_t R = R0 + r, ra = g.f_rb.div(R), rb = R - ra * g.RB;
+        if (ra < g.ra_valid && rb < rb_valid && K0 + k < g.k_valid)
+          dst[nd_base + ra * g.s_ra + rb * g.s_rb + K0 + k] = tile[r * pitch + k];
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// HWCN -> FRACTAL_Z with groups (fractal_z.cc:276-359), destination-linear:
+// destination (gb, c1, hw, co, c0) holds group g = gb*e_mult + e's weight when
+// channel dci = c1*k + c0 and output co both fall in slot e, else zero.
+struct FzGGeom {
+  uint64_t total;
+  uint64_t k, cout_opt, hw, c1_dim, e_mult, groups, cin, cout, n;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) fz_groups_kernel(T *__restrict__ dst,
+                                                             const T *__restrict__ src,
+                                                             FzGGeom g) {
+  pdl_trigger_at_entry();
+  pdl_wait();
+  pdl_launch_dependents();
+  for (uint64_t i = blockIdx.x * (uint64_t)kThreads + threadIdx.x; i < g.total;
+       i += (uint64_t)gridDim.x * kThreads) {
+    uint64_t rest = i;
+    const uint64_t c0 = rest % g.k;
+    rest /= g.k;
+    const uint64_t co = rest % g.cout_opt;
+    rest /= g.cout_opt;
+    const uint64_t hw = rest % g.hw;
+    rest /= g.hw;
+    const uint64_t c1 = rest % g.c1_dim;
+    const uint64_t gb = rest / g.c1_dim;
+    const uint64_t dci = c1 * g.k + c0, e = dci / g.cin;
+    T v = T();
+    if (e < g.e_mult && co / g.cout == e && gb * g.e_mult + e < g.groups) {
+      const uint64_t c = dci - e * g.cin, nn = co - e * g.cout;
+      v = ld_stream(src + (hw * g.cin + c) * g.n + (gb * g.e_mult + e) * g.cout + nn);
+    }
+    dst[i] = v;
+  }
+}
+
+bool fz_dims(int32_t fmt, const int64_t *s, int rank, int64_t *n, int64_t *c, int64_t *h,
+             int64_t *w) {
+  if (!s) return false;
+  switch (fmt) {
+    case kNchw:
+      if (rank != 4) return false;
+      *n = s[0], *c = s[1], *h = s[2], *w = s[3];
+      return true;
+    case kNhwc:
+      if (rank != 4) return false;
+      *n = s[0], *h = s[1], *w = s[2], *c = s[3];
+      return true;
+    case kHwcn:
+      if (rank != 4) return false;
+      *h = s[0], *w = s[1], *c = s[2], *n = s[3];
+      return true;
+    case kNd:  // fractal_z_tbe.cc: a 2-D [C, N] weight, H = W = 1
+      if (rank != 2) return false;
+      *c = s[0], *n = s[1], *h = 1, *w = 1;
+      return true;
+    default:
+      return false;
+  }
+}
+
+int64_t ge_ceil(int64_t n1, int64_t n2) {  // Ceil, formats_trans_utils.h:69-75
+  if (n1 == 0) return 0;
+  return (n2 != 0) ? (((n1 - 1) / n2) + 1) : 0;
+}
+
+int64_t ge_gcd(int64_t x, int64_t y) {  // Measure, formats_trans_utils.h:76-88
+  int64_t z = y;
+  if (y == 0) return -1;
+  while (x % y != 0) {
+    z = x % y;
+    x = y;
+    y = z;
+  }
+  return z;
+}
+
+int64_t ge_lcm(int64_t a, int64_t b) {  // Lcm, formats_trans_utils.h:90-96
+  if (b == 0) return -1;
+  return (a * b) / ge_gcd(a, b);
+}
+
+struct GroupsLayout {
+  int64_t e_mult, c1_dim, g_dim, cout_opt;
+};
+
+// fractal_z.cc:77-87 and :289-298.  cin, cout, k > 0.
+GroupsLayout groups_layout(int64_t cin, int64_t cout, int64_t k, int64_t groups) {
+  GroupsLayout l{};
+  l.e_mult = std::min(ge_lcm(ge_lcm(cin, k) / cin, ge_lcm(cout, kNi) / cout), groups);
+  l.c1_dim = ge_ceil(l.e_mult * cin, k) * k / k;
+  l.g_dim = ge_ceil(groups, l.e_mult);
+  l.cout_opt = ge_ceil(cout * l.e_mult, kNi) * kNi;
+  return l;
+}
+
+template <typename T>
+int launch_transpose(void *dst, const void *src, const FzTGeom &g, uint32_t ntiles, bool to_fz,
+                     cudaStream_t s) {
+  const size_t smem = (size_t)g.RT * (g.KT | 1) * sizeof(T);
+  const uint32_t grid = std::max(1u, std::min<uint32_t>(ntiles, 0x7FFFFFFFu));
+  T *d = static_cast<T *>(dst);
+  const T *sp = static_cast<const T *>(src);
+  if (to_fz)
+    return launch(fz_transpose_kernel<T, true>, grid, dim3(kThreads), smem, s,
+                  "fz_transpose_kernel", d, sp, g, ntiles);
+  return launch(fz_transpose_kernel<T, false>, grid, dim3(kThreads), smem, s,
+                "fz_transpose_kernel", d, sp, g, ntiles);
+}
+
+template <typename T>
+int launch_groups(void *dst, const void *src, const FzGGeom &g, cudaStream_t s) {
+  const uint64_t blocks = (g.total + kThreads - 1) / kThreads;
+  const uint32_t grid = (uint32_t)std::max<uint64_t>(
+      1, std::min<uint64_t>(blocks, (uint64_t)sm_count() * 16));
+  return launch(fz_groups_kernel<T>, grid, dim3(kThreads), 0, s, "fz_groups_kernel",
+                static_cast<T *>(dst), static_cast<const T *>(src), g);
+}
+
+// The NCHW / HWCN / ND (both directions) transposing path.
+int run_transpose(int32_t fmt, void *dst, const void *src, int64_t n, int64_t c, int64_t h,
+                  int64_t w, int eb, int64_t c0, bool to_fz, cudaStream_t s) {
+  const int64_t n1n0 = ge_ceil(n, kNi) * kNi, c1 = ge_ceil(c, c0), hw = h * w;
+  FzTGeom g{};
+  int64_t R_ext, K_ext, B2;
+  if (fmt == kNchw) {  // rows R = (n, c0), columns k = hw
+    R_ext = n1n0 * c0;
+    K_ext = hw;
+    B2 = 1;
+    g.ra_valid = (uint32_t)n;
+    g.k_valid = (uint32_t)hw;
+    g.s_ra = (uint64_t)(c * hw);
+    g.s_rb = (uint64_t)hw;
+    g.nd_c1 = (uint64_t)(c0 * hw);
+    g.nd_b2 = 0;
+    g.dk = (uint64_t)(n1n0 * c0);
+    g.fz_c1 = (uint64_t)(hw * n1n0 * c0);
+    g.fz_b2 = 0;
+  } else {  // HWCN / ND: rows R = c0, columns k = n; one batch per (c1, hw)
+    R_ext = c0;
+    K_ext = n1n0;
+    B2 = hw;
+    g.ra_valid = 1;
+    g.k_valid = (uint32_t)n;
+    g.s_ra = 0;
+    g.s_rb = (uint64_t)n;
+    g.nd_c1 = (uint64_t)(c0 * n);
+    g.nd_b2 = (uint64_t)(c * n);
+    g.dk = (uint64_t)c0;
+    g.fz_c1 = (uint64_t)(hw * n1n0 * c0);
+    g.fz_b2 = (uint64_t)(n1n0 * c0);
+  }
+  if (R_ext > 0x7FFFFFFFll || K_ext > 0x7FFFFFFFll || n > 0x7FFFFFFFll || c > 0x7FFFFFFFll ||
+      c0 > 0x7FFFFFFFll || B2 > 0x7FFFFFFFll)
+    return set_error(DCOPY_ERR_UNSUPPORTED, "FRACTAL_Z: dims beyond 32-bit tile indexing");
+  const int64_t budget = eb <= 4 ? 4096 : (eb == 8 ? 2048 : 1024);  // elements per tile
+  const int64_t KT = std::min<int64_t>(K_ext, R_ext >= 64 ? 64 : std::max<int64_t>(1, budget / R_ext));
+  const int64_t RT = std::min<int64_t>(R_ext, std::max<int64_t>(1, budget / KT));
+  g.RT = (uint32_t)RT;
+  g.KT = (uint32_t)KT;
+  g.R_ext = (uint32_t)R_ext;
+  g.K_ext = (uint32_t)K_ext;
+  g.rtiles = (uint32_t)ge_ceil(R_ext, RT);
+  g.ktiles = (uint32_t)ge_ceil(K_ext, KT);
+  g.B2 = (uint32_t)B2;
+  g.RB = (uint32_t)c0;
+  g.C = (uint32_t)c;
+  g.C0 = (uint32_t)c0;
+  g.rw_last = (uint32_t)(R_ext - (int64_t)(g.rtiles - 1) * RT);
+  g.kw_last = (uint32_t)(K_ext - (int64_t)(g.ktiles - 1) * KT);
+  g.f_rb = FastDiv(g.RB);
+  g.f_ktiles = FastDiv(g.ktiles);
+  g.f_rtiles = FastDiv(g.rtiles);
+  g.f_b2 = FastDiv(g.B2);
+  g.f_kw = FastDiv(g.KT);
+  g.f_kw_last = FastDiv(g.kw_last);
+  g.f_rw = FastDiv(g.RT);
+  g.f_rw_last = FastDiv(g.rw_last);
+  const uint64_t ntiles = (uint64_t)c1 * B2 * g.rtiles * g.ktiles;
+  if (ntiles == 0) return DCOPY_OK;
+  if (ntiles > 0xFFFFFFFFull)
+    return set_error(DCOPY_ERR_UNSUPPORTED, "FRACTAL_Z: %llu tiles exceed 32-bit indexing",
+                     (unsigned long long)ntiles);
+  switch (eb) {
+    case 1: return launch_transpose<uint8_t>(dst, src, g, (uint32_t)ntiles, to_fz, s);
+    case 2: return launch_transpose<uint16_t>(dst, src, g, (uint32_t)ntiles, to_fz, s);
+    case 4: return launch_transpose<uint32_t>(dst, src, g, (uint32_t)ntiles, to_fz, s);
+    case 8: return launch_transpose<uint2>(dst, src, g, (uint32_t)ntiles, to_fz, s);
+    default: return launch_transpose<uint4>(dst, src, g, (uint32_t)ntiles, to_fz, s);
+  }
+}
+
+// NHWC (both directions) through the tiled-format kernels: per (h, w) an
+// [N x C] matrix with row pitch H*W*C, blocks of 16 rows x C0 columns.
+int run_nhwc(void *dst, const void *src, int64_t n, int64_t c, int64_t h, int64_t w, int eb,
+             int64_t c0, bool to_fz, dcopy_stream_t stream) {
+  FracPlan p{};
+  p.elem_bytes = eb;
+  p.times = h * w;
+  p.H = n;
+  p.W = c;
+  p.nd_row = h * w * c;
+  p.nd_batch = c;
+  p.BH = kNi;
+  p.w0 = c0;
+  p.H1 = ge_ceil(n, kNi);
+  p.W1 = ge_ceil(c, c0);
+  p.s_band = kNi * c0;
+  p.fr_batch = p.H1 * kNi * c0;
+  p.s_panel = h * w * p.fr_batch;
+  return frac_launch(p, dst, src, to_fz, stream, "NHWC<->FRACTAL_Z");
+}
+
+bool width_ok(int eb) { return eb == 1 || eb == 2 || eb == 4 || eb == 8 || eb == 16; }
+
+}  // namespace
+
+int fz_shape(int32_t fmt, const int64_t *s, int rank, int64_t c0, int64_t groups, int64_t *out) {
+  int64_t n, c, h, w;
+  if (fmt == kNd) {  // TransShapeNdToFz, fractal_z_tbe.cc:32-62: every failure is FAILED
+    if (!fz_dims(kNd, s, rank, &n, &c, &h, &w) || !shape_valid(s, rank))
+      return set_error(DCOPY_ERR_FAILED, "ND -> FRACTAL_Z takes a valid 2-D [C, N] shape");
+    if (c0 <= 0) return set_error(DCOPY_ERR_FAILED, "ND -> FRACTAL_Z: c0 %lld", (long long)c0);
+    out[0] = ge_ceil(c, c0);
+    out[1] = ge_ceil(n, kNi);
+    out[2] = kNi;
+    out[3] = c0;
+    if (!shape_valid(out, 4)) return set_error(DCOPY_ERR_FAILED, "FRACTAL_Z shape is invalid");
+    return DCOPY_OK;
+  }
+  if (fmt != kNchw && fmt != kNhwc && fmt != kHwcn)
+    return set_error(DCOPY_ERR_FORMAT_INVALID, "no FRACTAL_Z transfer from format %d", fmt);
+  if (!fz_dims(fmt, s, rank, &n, &c, &h, &w) || !shape_valid(s, rank))  // CheckShapeValid(.., 4)
+    return set_error(DCOPY_ERR_SHAPE_INVALID, "FRACTAL_Z source must be a valid 4-D shape");
+  if (c0 < 0) return set_error(DCOPY_ERR_DATATYPE_INVALID, "c0 %lld < 0", (long long)c0);
+  if (groups > 1 && fmt != kNhwc) {  // TransShapeToFzWithGroups, fractal_z.cc:64-99
+    const int64_t cout = n / groups;
+    if (cout == 0)
+      return set_error(DCOPY_ERR_FAILED, "FRACTAL_Z groups: N %lld / groups %lld is 0",
+                       (long long)n, (long long)groups);
+    // The reference divides by zero here (Lcm(cin, k) / cin, Ceil(.., k) / k).
+    if (c == 0 || c0 == 0)
+      return set_error(DCOPY_ERR_FAILED, "FRACTAL_Z groups need C > 0 and c0 > 0");
+    const GroupsLayout l = groups_layout(c, cout, c0, groups);
+    out[0] = l.g_dim * l.c1_dim * h * w;
+    out[1] = l.cout_opt / kNi;
+  } else {  // TransShapeToFz, fractal_z.cc:41-62
+    out[0] = h * w * ge_ceil(c, c0);
+    out[1] = ge_ceil(n, kNi);
+  }
+  out[2] = kNi;
+  out[3] = c0;
+  if (!shape_valid(out, 4))
+    return set_error(DCOPY_ERR_SHAPE_INVALID, "FRACTAL_Z shape is invalid");
+  return DCOPY_OK;
+}
+
+int fz_out_elems(int32_t fmt, const int64_t *s, int rank, int64_t c0, int64_t groups,
+                 int64_t *elems) {
+  int64_t n, c, h, w;
+  if (!fz_dims(fmt, s, rank, &n, &c, &h, &w))
+    return set_error(DCOPY_ERR_SHAPE_INVALID, "FRACTAL_Z: shape of rank %d", rank);
+  if (fmt == kHwcn && groups > 1) {
+    const int64_t cout = n / groups;
+    if (c == 0 || cout == 0 || c0 <= 0)  // GRAPH_FAILED, fractal_z.cc:283-290
+      return set_error(DCOPY_ERR_FAILED, "FRACTAL_Z groups: cin %lld, cout %lld, c0 %lld",
+                       (long long)c, (long long)cout, (long long)c0);
+    const GroupsLayout l = groups_layout(c, cout, c0, groups);
+    *elems = l.g_dim * l.c1_dim * h * w * l.cout_opt * c0;
+    return DCOPY_OK;
+  }
+  *elems = ge_ceil(c, c0) * h * w * ge_ceil(n, kNi) * kNi * c0;
+  return DCOPY_OK;
+}
+
+int to_fz(void *dst, const void *src, int32_t fmt, const int64_t *s, int rank, int eb,
+          int64_t c0, int64_t groups, dcopy_stream_t stream) {
+  if (!width_ok(eb))
+    return set_error(DCOPY_ERR_DATATYPE_INVALID, "elem_bytes %d not in {1,2,4,8,16}", eb);
+  int64_t n, c, h, w;
+  if (!fz_dims(fmt, s, rank, &n, &c, &h, &w) || !shape_valid(s, rank))
+    return set_error(DCOPY_ERR_SHAPE_INVALID, "FRACTAL_Z: source shape of rank %d", rank);
+  if (groups > 1 && fmt != kHwcn)
+    return set_error(DCOPY_ERR_PARAM_INVALID, "FRACTAL_Z groups exist for HWCN sources only");
+  if (c0 < 0) return set_error(DCOPY_ERR_SHAPE_INVALID, "c0 %lld < 0", (long long)c0);
+  int64_t elems = 0;
+  int rc = fz_out_elems(fmt, s, rank, c0, groups, &elems);
+  if (rc) return rc;
+  if (elems == 0) return DCOPY_OK;
+  const uint64_t out_bytes = (uint64_t)elems * eb, in_bytes = (uint64_t)(n * c * h * w) * eb;
+  rc = check_device_span(src, in_bytes, "src");
+  if (!rc) rc = check_device_span(dst, out_bytes, "dst");
+  if (!rc) rc = check_disjoint(src, in_bytes, dst, out_bytes, "to_fractal_z");
+  if (rc) return rc;
+  if (((uintptr_t)src | (uintptr_t)dst) % eb)
+    return set_error(DCOPY_ERR_PARAM_INVALID, "buffers must be aligned to the element size");
+  cudaStream_t s_ = reinterpret_cast<cudaStream_t>(stream);
+  if (fmt == kHwcn && groups > 1) {
+    const int64_t cout = n / groups;
+    const GroupsLayout l = groups_layout(c, cout, c0, groups);
+    FzGGeom g{};
+    g.total = (uint64_t)elems;
+    g.k = (uint64_t)c0;
+    g.cout_opt = (uint64_t)l.cout_opt;
+    g.hw = (uint64_t)(h * w);
+    g.c1_dim = (uint64_t)l.c1_dim;
+    g.e_mult = (uint64_t)l.e_mult;
+    g.groups = (uint64_t)groups;
+    g.cin = (uint64_t)c;
+    g.cout = (uint64_t)cout;
+    g.n = (uint64_t)n;
+    switch (eb) {
+      case 1: return launch_groups<uint8_t>(dst, src, g, s_);
+      case 2: return launch_groups<uint16_t>(dst, src, g, s_);
+      case 4: return launch_groups<uint32_t>(dst, src, g, s_);
+      case 8: return launch_groups<uint2>(dst, src, g, s_);
+      default: return launch_groups<uint4>(dst, src, g, s_);
+    }
+  }
+  if (fmt == kNhwc) return run_nhwc(dst, src, n, c, h, w, eb, c0, true, stream);
+  return run_transpose(fmt, dst, src, n, c, h, w, eb, c0, true, s_);
+}
+
+int from_fz_check(const int64_t *src_shape, int src_rank, int32_t fmt, const int64_t *dst_shape,
+                  int dst_rank, int64_t c0) {
+  // CheckArgsForFracZTo{Nchw,Hwcn,Nhwc} (fracz_nchw.cc:28-79 and its twins).
+  int64_t n, c, h, w;
+  if (fmt != kNchw && fmt != kHwcn && fmt != kNhwc)
+    return set_error(DCOPY_ERR_FORMAT_INVALID, "no transfer from FRACTAL_Z to format %d", fmt);
+  if (src_rank != 4 || !shape_valid(src_shape, src_rank))
+    return set_error(DCOPY_ERR_SHAPE_INVALID, "FRACTAL_Z source must be a valid 4-D shape");
+  if (!fz_dims(fmt, dst_shape, dst_rank, &n, &c, &h, &w) || !shape_valid(dst_shape, dst_rank))
+    return set_error(DCOPY_ERR_SHAPE_INVALID, "destination must be a valid 4-D shape");
+  if (c0 < 0) return set_error(DCOPY_ERR_DATATYPE_INVALID, "c0 %lld < 0", (long long)c0);
+  if (src_shape[0] != h * w * ge_ceil(c, c0) || src_shape[3] != c0 || src_shape[2] != kNi ||
+      src_shape[1] != ge_ceil(n, kNi))
+    return set_error(DCOPY_ERR_SHAPE_INVALID, "FRACTAL_Z shape does not match the weight");
+  return DCOPY_OK;
+}
+
+int from_fz(void *dst, const void *src, int32_t fmt, const int64_t *d, int rank, int eb,
+            int64_t c0, dcopy_stream_t stream) {
+  if (!width_ok(eb))
+    return set_error(DCOPY_ERR_DATATYPE_INVALID, "elem_bytes %d not in {1,2,4,8,16}", eb);
+  int64_t n, c, h, w;
+  if ((fmt != kNchw && fmt != kHwcn && fmt != kNhwc) || !fz_dims(fmt, d, rank, &n, &c, &h, &w) ||
+      !shape_valid(d, rank))
+    return set_error(DCOPY_ERR_SHAPE_INVALID, "FRACTAL_Z: destination shape of rank %d", rank);
+  const int64_t out_elems = n * c * h * w;
+  if (out_elems == 0) return DCOPY_OK;
+  // The reference divides by c0 (c_idx / c0 in GetDstDataAfterTransForFracZToNchw).
+  if (c0 <= 0) return set_error(DCOPY_ERR_SHAPE_INVALID, "c0 %lld must be positive", (long long)c0);
+  const uint64_t in_bytes = (uint64_t)(ge_ceil(c, c0) * h * w * ge_ceil(n, kNi) * kNi * c0) * eb;
+  const uint64_t out_bytes = (uint64_t)out_elems * eb;
+  int rc = check_device_span(src, in_bytes, "src");
+  if (!rc) rc = check_device_span(dst, out_bytes, "dst");
+  if (!rc) rc = check_disjoint(src, in_bytes, dst, out_bytes, "from_fractal_z");
+  if (rc) return rc;
+  if (((uintptr_t)src | (uintptr_t)dst) % eb)
+    return set_error(DCOPY_ERR_PARAM_INVALID, "buffers must be aligned to the element size");
+  if (fmt == kNhwc) return run_nhwc(dst, src, n, c, h, w, eb, c0, false, stream);
+  return run_transpose(fmt, dst, src, n, c, h, w, eb, c0, false,
+                       reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // namespace dcopy
+
+using namespace dcopy;
+
+extern "C" int dcopy_fz_shape(int32_t src_format, const int64_t *src_shape, int rank, int64_t c0,
+                              int64_t groups, int64_t *fz_shape_out) {
+  DCOPY_API_BEGIN
+  if (!fz_shape_out || (rank && !src_shape) || rank < 0)
+    return set_error(DCOPY_ERR_PARAM_INVALID, "fz_shape: invalid arguments");
+  return fz_shape(src_format & 0xff, src_shape, rank, c0, groups, fz_shape_out);
+  DCOPY_API_END
+}
+
+extern "C" int dcopy_to_fractal_z(void *dst, const void *src, int32_t src_format,
+                                  const int64_t *src_shape, int rank, int elem_bytes, int64_t c0,
+                                  int64_t groups, dcopy_stream_t stream) {
+  DCOPY_API_BEGIN
+  return to_fz(dst, src, src_format & 0xff, src_shape, rank, elem_bytes, c0, groups, stream);
+  DCOPY_API_END
+}
+
+extern "C" int dcopy_from_fractal_z(void *dst, const void *src, int32_t dst_format,
+                                    const int64_t *dst_shape, int rank, int elem_bytes,
+                                    int64_t c0, dcopy_stream_t stream) {
+  DCOPY_API_BEGIN
+  return from_fz(dst, src, dst_format & 0xff, dst_shape, rank, elem_bytes, c0, stream);
+  DCOPY_API_END
+}

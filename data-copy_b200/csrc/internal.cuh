@@ -16,6 +16,21 @@ int nz_shape(const int64_t *nd, int rank, int64_t w0, int64_t *nz, int *nz_rank,
 // TransShapeToFracZz (format_transfer_fractal_zz.cc:74-118), same contract.
 int zz_shape(const int64_t *nd, int rank, int64_t c0, int64_t *zz, int *zz_rank, int64_t *hw);
 
+// One tiled-format transfer: `times` ND matrices of H x W elements (row pitch
+// nd_row, batch pitch nd_batch) <-> blocks of BH rows x w0 columns, zero-padded
+// to H1 x W1 blocks, where block (band, panel) of batch t starts at
+// t*fr_batch + band*s_band + panel*s_panel and is stored row-major.  All
+// pitches and strides in elements of elem_bytes bytes.
+struct FracPlan {
+  int64_t times, H, W, nd_row, nd_batch;
+  int64_t BH, w0, H1, W1, s_band, s_panel, fr_batch;
+  int elem_bytes;
+};
+// Launches the shared tiled-format kernels for a plan whose buffers the caller
+// has already checked.
+int frac_launch(const FracPlan &plan, void *dst, const void *src, bool to_frac,
+                dcopy_stream_t stream, const char *name);
+
 enum class FracKind { kNz, kZz };
 // ND <-> FRACTAL_NZ / FRACTAL_ZZ with all argument checks of the public entries
 // (dcopy_nd_to_nz, dcopy_nz_to_nd, dcopy_nd_to_zz, dcopy_zz_to_nd).
@@ -23,6 +38,21 @@ int frac_transfer(FracKind kind, void *dst, const void *src, const int64_t *nd_s
                   int elem_bytes, int64_t w0, bool to_frac, dcopy_stream_t stream);
 int nz_transfer(void *dst, const void *src, const int64_t *nd_shape, int rank, int elem_bytes,
                 int64_t w0, bool to_nz, dcopy_stream_t stream);
+
+// FRACTAL_Z (fz.cu).  Formats are primary GE formats (NCHW 0, NHWC 1, ND 2,
+// HWCN 16).  fz_shape: TransShape with the reference's statuses (out: 4 dims).
+int fz_shape(int32_t fmt, const int64_t *shape, int rank, int64_t c0, int64_t groups,
+             int64_t *out);
+// Elements the reference writes for a (fmt, shape, c0, groups) -> FRACTAL_Z transfer.
+int fz_out_elems(int32_t fmt, const int64_t *shape, int rank, int64_t c0, int64_t groups,
+                 int64_t *elems);
+int to_fz(void *dst, const void *src, int32_t fmt, const int64_t *shape, int rank, int eb,
+          int64_t c0, int64_t groups, dcopy_stream_t stream);
+// CheckArgsForFracZTo{Nchw,Hwcn,Nhwc}.
+int from_fz_check(const int64_t *src_shape, int src_rank, int32_t fmt, const int64_t *dst_shape,
+                  int dst_rank, int64_t c0);
+int from_fz(void *dst, const void *src, int32_t fmt, const int64_t *dst_shape, int rank, int eb,
+            int64_t c0, dcopy_stream_t stream);
 
 // The reference's pretranspose workflow (asc:144-146): x -> B with RunTiles<1>,
 // then B -> y with RunTiles<2>, through a B buffer of scratch_bytes bytes that

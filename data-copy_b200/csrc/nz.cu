@@ -51,7 +51,8 @@ struct FracGeom {
   uint32_t pgroups;     // ceil(W1 / PG)
   uint32_t tile_units;  // BH * PG * upr
   FastDiv f_upr, f_bh, f_pgu, f_pgroups, f_hblocks;
-  uint64_t nd_batch;    // units per ND batch = H * Wu
+  uint64_t nd_row;      // units between ND rows (Wu for a packed matrix)
+  uint64_t nd_batch;    // units between ND batches (H * Wu for packed matrices)
   uint64_t fr_batch;    // units per tiled batch = H1 * W1 * BH * upr
   uint64_t s_band;      // units between row bands
   uint64_t s_panel;     // units between column blocks
@@ -92,7 +93,7 @@ __global__ void __launch_bounds__(kThreads) nz_kernel(T *__restrict__ dst,
           if (w1 >= g.W1) continue;
           const uint32_t col = w1 * g.upr + k;
           v[u] = T();
-          if (hp < g.H && col < g.Wu) v[u] = ld_stream(sb + (uint64_t)hp * g.Wu + col);
+          if (hp < g.H && col < g.Wu) v[u] = ld_stream(sb + (uint64_t)hp * g.nd_row + col);
           doff[u] = band + (uint64_t)w1 * g.s_panel + (uint64_t)hin * g.upr + k;
           ok[u] = true;
         } else {
@@ -105,7 +106,7 @@ __global__ void __launch_bounds__(kThreads) nz_kernel(T *__restrict__ dst,
           const uint32_t k = uin - pin * g.upr;
           v[u] = ld_stream(sb + band + (uint64_t)(w1_0 + pin) * g.s_panel +
                            (uint64_t)hin * g.upr + k);
-          doff[u] = (uint64_t)h * g.Wu + col;
+          doff[u] = (uint64_t)h * g.nd_row + col;
           ok[u] = true;
         }
       }
@@ -153,7 +154,7 @@ __global__ void __launch_bounds__(kThreads) nz_smem_kernel(uint4 *__restrict__ d
       if (j % 8) continue;
       if (kToFrac) {
         const uint32_t h = hb * g.BH + (j >> row_shift), col = pg * g.PG * upr + (j & row_mask);
-        if (h < g.H && col < g.Wu) prefetch_l2(sb + (uint64_t)h * g.Wu + col);
+        if (h < g.H && col < g.Wu) prefetch_l2(sb + (uint64_t)h * g.nd_row + col);
       } else {
         const uint32_t pin = j >> panel_shift;
         if (pg * g.PG + pin < g.W1)
@@ -182,7 +183,7 @@ __global__ void __launch_bounds__(kThreads) nz_smem_kernel(uint4 *__restrict__ d
       if (kToFrac) {  // ND order [row][unit]
         const uint32_t hin = j >> row_shift, uin = j & row_mask;
         const uint32_t h = h_0 + hin, col = w1_0 * upr + uin;
-        if (h < g.H && col < g.Wu) v[u] = ld_stream(sb + (uint64_t)h * g.Wu + col);
+        if (h < g.H && col < g.Wu) v[u] = ld_stream(sb + (uint64_t)h * g.nd_row + col);
       } else {  // tiled order [block][row][unit]
         const uint32_t pin = j >> panel_shift, rem = j & (panel_units - 1);
         if (w1_0 + pin < g.W1)
@@ -219,7 +220,7 @@ __global__ void __launch_bounds__(kThreads) nz_smem_kernel(uint4 *__restrict__ d
         const uint32_t pin = uin >> upr_shift;
         const uint32_t rem = (hin << upr_shift) + (uin & (upr - 1));
         if (h < g.H && col < g.Wu)
-          db[(uint64_t)h * g.Wu + col] = tile[pin * panel_units + (rem ^ ((pin << upr_shift) & 7))];
+          db[(uint64_t)h * g.nd_row + col] = tile[pin * panel_units + (rem ^ ((pin << upr_shift) & 7))];
       }
     }
     __syncthreads();
@@ -346,9 +347,62 @@ int launch_frac(void *dst, const void *src, const FracGeom &g, uint32_t ntiles, 
 
 }  // namespace
 
+int frac_launch(const FracPlan &p, void *dst, const void *src, bool to_frac,
+                dcopy_stream_t stream, const char *name) {
+  const int eb = p.elem_bytes;
+  // Unit: the widest power of two <= 16 bytes dividing every row, pitch and
+  // stride on both sides and both base addresses.
+  const uint64_t key = (uint64_t)(p.w0 * eb) | (uint64_t)(p.W * eb) | (uint64_t)(p.nd_row * eb) |
+                       (uint64_t)(p.nd_batch * eb) | (uint64_t)(p.s_band * eb) |
+                       (uint64_t)(p.s_panel * eb) | (uint64_t)(p.fr_batch * eb) |
+                       (uintptr_t)dst | (uintptr_t)src;
+  uint32_t us = 16;
+  while (us > (uint32_t)eb && key % us) us >>= 1;
+  if (key % us)
+    return set_error(DCOPY_ERR_PARAM_INVALID, "buffers must be aligned to the element size");
+  const uint64_t upr = (uint64_t)p.w0 * eb / us;
+  const uint64_t Wu = (uint64_t)p.W * eb / us;
+  if (p.times > 0xFFFFFFFFll || p.H1 * p.BH > (1ll << 30) || Wu > (1ull << 30) ||
+      upr > (1ull << 20) || p.W1 > (1ll << 30) || (uint64_t)p.BH * upr > (1ull << 24))
+    return set_error(DCOPY_ERR_UNSUPPORTED, "%s: shape beyond 32-bit tile indexing", name);
+  FracGeom g{};
+  g.H = (uint32_t)p.H;
+  g.Wu = (uint32_t)Wu;
+  g.upr = (uint32_t)upr;
+  g.BH = (uint32_t)p.BH;
+  g.W1 = (uint32_t)p.W1;
+  g.PG = (uint32_t)std::max<uint64_t>(1, kTileUnits / ((uint64_t)p.BH * upr));
+  g.hblocks = (uint32_t)p.H1;
+  g.pgroups = (g.W1 + g.PG - 1) / g.PG;
+  g.tile_units = g.BH * g.PG * g.upr;
+  g.f_upr = FastDiv(g.upr);
+  g.f_bh = FastDiv(g.BH);
+  g.f_pgu = FastDiv(g.PG * g.upr);
+  g.f_pgroups = FastDiv(std::max(1u, g.pgroups));
+  g.f_hblocks = FastDiv(std::max(1u, g.hblocks));
+  g.nd_row = (uint64_t)p.nd_row * eb / us;
+  g.nd_batch = (uint64_t)p.nd_batch * eb / us;
+  g.fr_batch = (uint64_t)p.fr_batch * eb / us;
+  g.s_band = (uint64_t)p.s_band * eb / us;
+  g.s_panel = (uint64_t)p.s_panel * eb / us;
+  const uint64_t ntiles = (uint64_t)p.times * g.hblocks * g.pgroups;
+  if (ntiles == 0) return DCOPY_OK;
+  if (ntiles > 0xFFFFFFFFull)
+    return set_error(DCOPY_ERR_UNSUPPORTED, "%s: %llu tiles exceed 32-bit indexing", name,
+                     (unsigned long long)ntiles);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (us) {
+    case 16: return launch_frac<uint4>(dst, src, g, (uint32_t)ntiles, to_frac, s);
+    case 8: return launch_frac<uint2>(dst, src, g, (uint32_t)ntiles, to_frac, s);
+    case 4: return launch_frac<uint32_t>(dst, src, g, (uint32_t)ntiles, to_frac, s);
+    case 2: return launch_frac<uint16_t>(dst, src, g, (uint32_t)ntiles, to_frac, s);
+    default: return launch_frac<uint8_t>(dst, src, g, (uint32_t)ntiles, to_frac, s);
+  }
+}
+
 int frac_transfer(FracKind kind, void *dst, const void *src, const int64_t *nd_shape, int rank,
                   int elem_bytes, int64_t w0, bool to_frac, dcopy_stream_t stream) {
-  const char *name = kind == FracKind::kNz ? "NZ" : "ZZ";
+  const char *name = kind == FracKind::kNz ? "ND<->NZ" : "ND<->ZZ";
   if (elem_bytes <= 0)
     return set_error(DCOPY_ERR_DATATYPE_INVALID, "elem_bytes %d: data type size must be > 0",
                      elem_bytes);
@@ -379,57 +433,22 @@ int frac_transfer(FracKind kind, void *dst, const void *src, const int64_t *nd_s
   if (!rc) rc = check_disjoint(src, src_bytes, dst, dst_bytes, to_frac ? "nd_to_frac" : "frac_to_nd");
   if (rc) return rc;
 
-  const int64_t times = hw[0], H = hw[1], W = hw[2];
-  const int64_t W1 = kind == FracKind::kNz ? fr[fr_rank - 4] : fr[fr_rank - 3];
-  const int64_t H1 = kind == FracKind::kNz ? fr[fr_rank - 3] : fr[fr_rank - 4];
-  const int64_t BH = fr[fr_rank - 2];
-  // Unit: the widest power of two <= 16 bytes dividing the block row, the ND
-  // row and both base addresses.
-  uint64_t key = (uint64_t)w0 * elem_bytes | (uint64_t)W * elem_bytes | (uintptr_t)dst |
-                 (uintptr_t)src;
-  if (W == 0) key = (uint64_t)w0 * elem_bytes | (uintptr_t)dst | (uintptr_t)src;
-  uint32_t us = 16;
-  while (us > (uint32_t)elem_bytes && key % us) us >>= 1;
-  if (key % us)
-    return set_error(DCOPY_ERR_PARAM_INVALID, "buffers must be aligned to the element size");
-  const uint64_t upr = (uint64_t)w0 * elem_bytes / us;
-  const uint64_t Wu = (uint64_t)W * elem_bytes / us;
-  if (times > 0xFFFFFFFFll || H1 * BH > (1ll << 30) || Wu > (1ull << 30) || upr > (1ull << 20) ||
-      W1 > (1ll << 30) || (uint64_t)BH * upr > (1ull << 24))
-    return set_error(DCOPY_ERR_UNSUPPORTED, "ND<->%s: shape beyond 32-bit tile indexing", name);
-  FracGeom g{};
-  g.H = (uint32_t)H;
-  g.Wu = (uint32_t)Wu;
-  g.upr = (uint32_t)upr;
-  g.BH = (uint32_t)BH;
-  g.W1 = (uint32_t)W1;
-  g.PG = (uint32_t)std::max<uint64_t>(1, kTileUnits / ((uint64_t)BH * upr));
-  g.hblocks = (uint32_t)H1;
-  g.pgroups = (g.W1 + g.PG - 1) / g.PG;
-  g.tile_units = g.BH * g.PG * g.upr;
-  g.f_upr = FastDiv(g.upr);
-  g.f_bh = FastDiv(g.BH);
-  g.f_pgu = FastDiv(g.PG * g.upr);
-  g.f_pgroups = FastDiv(std::max(1u, g.pgroups));
-  g.f_hblocks = FastDiv(std::max(1u, g.hblocks));
-  g.nd_batch = (uint64_t)H * Wu;
-  const uint64_t block = (uint64_t)BH * upr;
-  g.fr_batch = (uint64_t)H1 * W1 * block;
-  g.s_band = kind == FracKind::kNz ? block : (uint64_t)W1 * block;
-  g.s_panel = kind == FracKind::kNz ? (uint64_t)H1 * block : block;
-  const uint64_t ntiles = (uint64_t)times * g.hblocks * g.pgroups;
-  if (ntiles == 0) return DCOPY_OK;
-  if (ntiles > 0xFFFFFFFFull)
-    return set_error(DCOPY_ERR_UNSUPPORTED, "ND<->%s: %llu tiles exceed 32-bit indexing", name,
-                     (unsigned long long)ntiles);
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  switch (us) {
-    case 16: return launch_frac<uint4>(dst, src, g, (uint32_t)ntiles, to_frac, s);
-    case 8: return launch_frac<uint2>(dst, src, g, (uint32_t)ntiles, to_frac, s);
-    case 4: return launch_frac<uint32_t>(dst, src, g, (uint32_t)ntiles, to_frac, s);
-    case 2: return launch_frac<uint16_t>(dst, src, g, (uint32_t)ntiles, to_frac, s);
-    default: return launch_frac<uint8_t>(dst, src, g, (uint32_t)ntiles, to_frac, s);
-  }
+  FracPlan p{};
+  p.elem_bytes = elem_bytes;
+  p.times = hw[0];
+  p.H = hw[1];
+  p.W = hw[2];
+  p.nd_row = p.W;
+  p.nd_batch = p.H * p.W;
+  p.w0 = w0;
+  p.BH = fr[fr_rank - 2];
+  p.W1 = kind == FracKind::kNz ? fr[fr_rank - 4] : fr[fr_rank - 3];
+  p.H1 = kind == FracKind::kNz ? fr[fr_rank - 3] : fr[fr_rank - 4];
+  const int64_t block = p.BH * w0;
+  p.fr_batch = p.H1 * p.W1 * block;
+  p.s_band = kind == FracKind::kNz ? block : p.W1 * block;
+  p.s_panel = kind == FracKind::kNz ? p.H1 * block : block;
+  return frac_launch(p, dst, src, to_frac, stream, name);
 }
 
 int nz_transfer(void *dst, const void *src, const int64_t *nd_shape, int rank, int elem_bytes,

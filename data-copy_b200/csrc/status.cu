@@ -160,6 +160,7 @@ uint32_t dcopy_status_to_ge(int status) {
     case DCOPY_ERR_FORMAT_INVALID: return 145020u;
     case DCOPY_ERR_CUDA: return 245002u;     // ACL_ERROR_GE_DEVICE_MEMORY_OPERATE_FAILED
     case DCOPY_ERR_TIMEOUT: return 545601u;  // ACL_ERROR_GE_MODEL_EXECUTE_TIMEOUT
+    case DCOPY_ERR_FAILED: return 0xFFFFFFFFu;  // FAILED / GRAPH_FAILED
     default: return 545000u;                 // ACL_ERROR_GE_INTERNAL_ERROR
   }
 }

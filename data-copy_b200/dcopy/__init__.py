@@ -39,7 +39,9 @@ __all__ = [
     "signal", "wait_signal", "p2p_error", "DcopyDevCopy", "copy_ext_multi", "DcopyMemcpyInfo", "memcpy_async",
     "MEMCPY_KIND",
     "OK", "ERR_PARAM_INVALID", "ERR_SHAPE_INVALID", "ERR_DATATYPE_INVALID",
-    "ERR_FORMAT_INVALID", "ERR_CUDA", "ERR_TIMEOUT", "ERR_UNSUPPORTED",
+    "ERR_FORMAT_INVALID", "ERR_CUDA", "ERR_TIMEOUT", "ERR_UNSUPPORTED", "ERR_FAILED",
+    "fz_shape", "to_fractal_z", "from_fractal_z", "TRANSFER_FRACTAL_Z", "TRANSFER_FRACTAL_Z_TBE",
+    "TRANSFER_FRACZ_NCHW", "TRANSFER_FRACZ_HWCN", "TRANSFER_FRACZ_NHWC", "format_with_sub",
 ]
 
 OK = 0
@@ -50,6 +52,7 @@ ERR_FORMAT_INVALID = -4
 ERR_CUDA = -5
 ERR_TIMEOUT = -6
 ERR_UNSUPPORTED = -7
+ERR_FAILED = -8
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 # DCOPY_LIBRARY selects an alternative build of the same library (e.g. one built
@@ -87,12 +90,14 @@ class DcopyExtParams(ctypes.Structure):
 
 
 class DcopyTransArgs(ctypes.Structure):
-    """TransArgs (register_format_transfer.h:25-42) with device data and primary formats."""
+    """TransArgs (register_format_transfer.h:25-42) with device data; formats carry the
+    primary format in bits 0-7 and the sub format in bits 8-23."""
     _fields_ = [("data", ctypes.c_void_p), ("src_format", ctypes.c_int32),
                 ("dst_format", ctypes.c_int32), ("src_c0", ctypes.c_int64),
                 ("dst_c0", ctypes.c_int64), ("src_shape", ctypes.POINTER(ctypes.c_int64)),
                 ("src_rank", ctypes.c_int32), ("dst_shape", ctypes.POINTER(ctypes.c_int64)),
-                ("dst_rank", ctypes.c_int32), ("data_type", ctypes.c_int32)]
+                ("dst_rank", ctypes.c_int32), ("data_type", ctypes.c_int32),
+                ("src_sub_format", ctypes.c_int32), ("dst_sub_format", ctypes.c_int32)]
 
 
 # GE enum values (metadef graph/types.h; api/python/ge/ge/graph/types.py).
@@ -103,6 +108,13 @@ DATA_TYPE = {"FLOAT": 0, "FLOAT16": 1, "INT8": 2, "INT32": 3, "UINT8": 4, "INT16
              "STRING": 13, "COMPLEX64": 16, "COMPLEX128": 17, "BF16": 27, "UNDEFINED": 28}
 TRANSFER_FRACTAL_NZ, TRANSFER_FRACTAL_NZ_ND, TRANSFER_TRANSPOSE = 1, 2, 3
 TRANSFER_FRACTAL_ZZ, TRANSFER_FRACTAL_ZZ_ND = 4, 5
+TRANSFER_FRACTAL_Z, TRANSFER_FRACTAL_Z_TBE = 6, 7
+TRANSFER_FRACZ_NCHW, TRANSFER_FRACZ_HWCN, TRANSFER_FRACZ_NHWC = 8, 9, 10
+
+
+def format_with_sub(primary: int, sub: int) -> int:
+    """A GE Format value with a sub format (GetFormatFromSub): FRACTAL_Z groups."""
+    return (primary & 0xff) | ((sub & 0xffff) << 8)
 
 
 class DcopyMemcpyInfo(ctypes.Structure):
@@ -151,6 +163,12 @@ _SIGNATURES = {
                                       ctypes.c_int64, _vp]),
     "dcopy_nz_to_nd": (ctypes.c_int, [_vp, _vp, _i64p, ctypes.c_int, ctypes.c_int,
                                       ctypes.c_int64, _vp]),
+    "dcopy_fz_shape": (ctypes.c_int, [ctypes.c_int32, _i64p, ctypes.c_int, ctypes.c_int64,
+                                      ctypes.c_int64, _i64p]),
+    "dcopy_to_fractal_z": (ctypes.c_int, [_vp, _vp, ctypes.c_int32, _i64p, ctypes.c_int,
+                                          ctypes.c_int, ctypes.c_int64, ctypes.c_int64, _vp]),
+    "dcopy_from_fractal_z": (ctypes.c_int, [_vp, _vp, ctypes.c_int32, _i64p, ctypes.c_int,
+                                            ctypes.c_int, ctypes.c_int64, _vp]),
     "dcopy_zz_shape": (ctypes.c_int, [_i64p, ctypes.c_int, ctypes.c_int64, _i64p,
                                       ctypes.POINTER(ctypes.c_int), _i64p]),
     "dcopy_nd_to_zz": (ctypes.c_int, [_vp, _vp, _i64p, ctypes.c_int, ctypes.c_int,
@@ -357,6 +375,28 @@ def zz_to_nd(dst, src, nd_shape: Sequence[int], elem_bytes: int, c0: int, stream
            "dcopy_zz_to_nd")
 
 
+def fz_shape(src_format: int, src_shape: Sequence[int], c0: int, groups: int = 0):
+    """FRACTAL_Z TransShape: [C1*H*W, N1, 16, C0] of a NCHW/NHWC/HWCN/ND weight."""
+    arr, n = _shape_arg(src_shape)
+    out = (ctypes.c_int64 * 4)()
+    _check(lib().dcopy_fz_shape(src_format, arr, n, c0, groups, out), "dcopy_fz_shape")
+    return list(out)
+
+
+def to_fractal_z(dst, src, src_format: int, src_shape: Sequence[int], elem_bytes: int, c0: int,
+                 groups: int = 0, stream=None) -> None:
+    arr, n = _shape_arg(src_shape)
+    _check(lib().dcopy_to_fractal_z(_ptr(dst), _ptr(src), src_format, arr, n, elem_bytes, c0,
+                                    groups, _stream(stream)), "dcopy_to_fractal_z")
+
+
+def from_fractal_z(dst, src, dst_format: int, dst_shape: Sequence[int], elem_bytes: int,
+                   c0: int, stream=None) -> None:
+    arr, n = _shape_arg(dst_shape)
+    _check(lib().dcopy_from_fractal_z(_ptr(dst), _ptr(src), dst_format, arr, n, elem_bytes, c0,
+                                      _stream(stream)), "dcopy_from_fractal_z")
+
+
 # ---- GE TransData level -------------------------------------------------------------
 
 def data_type_size(data_type: int) -> int:
@@ -365,19 +405,21 @@ def data_type_size(data_type: int) -> int:
 
 
 def _trans_args(data, src_format, dst_format, src_shape, dst_shape, data_type, src_c0=16,
-                dst_c0=16):
+                dst_c0=16, src_sub=0, dst_sub=0):
     src = (ctypes.c_int64 * max(len(src_shape), 1))(*src_shape)
     dst = (ctypes.c_int64 * max(len(dst_shape), 1))(*dst_shape)
     a = DcopyTransArgs(_ptr(data), src_format, dst_format, src_c0, dst_c0, src, len(src_shape),
-                       dst, len(dst_shape), data_type)
+                       dst, len(dst_shape), data_type, src_sub, dst_sub)
     a._keep = (src, dst)
     return a
 
 
 def trans_data_format(dst, data, src_format, dst_format, src_shape, dst_shape, data_type,
-                      dst_capacity, src_c0=16, dst_c0=16, stream=None) -> int:
+                      dst_capacity, src_c0=16, dst_c0=16, stream=None, src_sub=0,
+                      dst_sub=0) -> int:
     """TransDataFormat (formats.cc:30-52) into `dst`; returns the result length in bytes."""
-    a = _trans_args(data, src_format, dst_format, src_shape, dst_shape, data_type, src_c0, dst_c0)
+    a = _trans_args(data, src_format, dst_format, src_shape, dst_shape, data_type, src_c0, dst_c0,
+                    src_sub, dst_sub)
     n = ctypes.c_uint64(0)
     _check(lib().dcopy_trans_data_format(ctypes.byref(a), _ptr(dst), dst_capacity,
                                          ctypes.byref(n), _stream(stream)),
@@ -386,9 +428,11 @@ def trans_data_format(dst, data, src_format, dst_format, src_shape, dst_shape, d
 
 
 def trans_format(transfer_class, dst, data, src_format, dst_format, src_shape, dst_shape,
-                 data_type, dst_capacity, src_c0=16, dst_c0=16, stream=None) -> int:
+                 data_type, dst_capacity, src_c0=16, dst_c0=16, stream=None, src_sub=0,
+                 dst_sub=0) -> int:
     """FormatTransfer<class>::TransFormat; returns the result length in bytes."""
-    a = _trans_args(data, src_format, dst_format, src_shape, dst_shape, data_type, src_c0, dst_c0)
+    a = _trans_args(data, src_format, dst_format, src_shape, dst_shape, data_type, src_c0, dst_c0,
+                    src_sub, dst_sub)
     n = ctypes.c_uint64(0)
     _check(lib().dcopy_trans_format(transfer_class, ctypes.byref(a), _ptr(dst), dst_capacity,
                                     ctypes.byref(n), _stream(stream)), "dcopy_trans_format")
@@ -396,10 +440,11 @@ def trans_format(transfer_class, dst, data, src_format, dst_format, src_shape, d
 
 
 def trans_format_check(transfer_class, data, src_format, dst_format, src_shape, dst_shape,
-                       data_type, src_c0=16, dst_c0=16) -> int:
+                       data_type, src_c0=16, dst_c0=16, src_sub=0, dst_sub=0) -> int:
     """Every check of TransDataFormat (class 0) or of one class's TransFormat, no data
     movement; returns the result length in bytes."""
-    a = _trans_args(data, src_format, dst_format, src_shape, dst_shape, data_type, src_c0, dst_c0)
+    a = _trans_args(data, src_format, dst_format, src_shape, dst_shape, data_type, src_c0, dst_c0,
+                    src_sub, dst_sub)
     n = ctypes.c_uint64(0)
     _check(lib().dcopy_trans_format_check(transfer_class, ctypes.byref(a), ctypes.byref(n)),
            "dcopy_trans_format_check")

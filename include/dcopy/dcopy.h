@@ -51,6 +51,7 @@ typedef struct CUstream_st *dcopy_stream_t;
 #define DCOPY_ERR_CUDA (-5)             /* a CUDA runtime/driver call failed */
 #define DCOPY_ERR_TIMEOUT (-6)          /* a bounded device-side wait gave up */
 #define DCOPY_ERR_UNSUPPORTED (-7)      /* valid request outside this build's limits */
+#define DCOPY_ERR_FAILED (-8)           /* GE's generic FAILED / GRAPH_FAILED 0xFFFFFFFF */
 
 /* Thread-local description of the last failure on this thread ("" if none). */
 const char *dcopy_last_error_message(void);
@@ -180,6 +181,38 @@ int dcopy_nd_to_zz(void *dst, const void *src, const int64_t *nd_shape, int rank
 int dcopy_zz_to_nd(void *dst, const void *src, const int64_t *nd_shape, int rank,
                    int elem_bytes, int64_t c0, dcopy_stream_t stream);
 
+/* ---- FRACTAL_Z (convolution weights) ---------------------------------------- */
+
+/* FRACTAL_Z is [C1*H*W, N1, 16, C0]: element (c1, h, w, n, c0) holds weight
+ * (n, c = c1*C0 + c0, h, w), zero where n >= N or c >= C.  Weight formats:
+ * NCHW (0), NHWC (1), HWCN (16), and ND (2) = a 2-D [C, N] weight.
+ *
+ * TransShape of FormatTransferFractalZ (format_transfer_fractal_z.cc:41-173,
+ * 571-604) and FormatTransferFractalZTbe (format_transfer_fractal_z_tbe.cc:
+ * 32-62, 131-146): fz_shape receives the 4 dims.  `groups` > 1 selects the
+ * group-convolution layout for NCHW and HWCN (GE takes it from the destination
+ * format's sub format).  Status as the reference: SHAPE_INVALID for a source
+ * that is not a valid 4-D shape, DATATYPE_INVALID for c0 < 0, FAILED when N /
+ * groups is 0 (and, where the reference divides by zero, for C == 0 or c0 == 0
+ * with groups) and for every ND failure. */
+int dcopy_fz_shape(int32_t src_format, const int64_t *src_shape, int rank, int64_t c0,
+                   int64_t groups, int64_t *fz_shape);
+
+/* NCHW / NHWC / HWCN / ND -> FRACTAL_Z on the GPU (the data movement of
+ * fractal_z.cc:175-537 and fractal_z_tbe.cc:64-114).  dst holds the whole
+ * FRACTAL_Z tensor, padding written as zeros.  groups > 1 is the HWCN group
+ * layout (fractal_z.cc:276-359) and is refused for the other formats. */
+int dcopy_to_fractal_z(void *dst, const void *src, int32_t src_format, const int64_t *src_shape,
+                       int rank, int elem_bytes, int64_t c0, int64_t groups,
+                       dcopy_stream_t stream);
+
+/* FRACTAL_Z -> NCHW / HWCN / NHWC on the GPU (format_transfer_fracz_nchw.cc,
+ * fracz_hwcn.cc, fracz_nhwc.cc): dst_shape is the weight's shape; padding is
+ * dropped. */
+int dcopy_from_fractal_z(void *dst, const void *src, int32_t dst_format,
+                         const int64_t *dst_shape, int rank, int elem_bytes, int64_t c0,
+                         dcopy_stream_t stream);
+
 /* ---- GE TransData level ------------------------------------------------------
  * The format-transfer registry of GE (base/formats/formats.cc:30-71,
  * register_format_transfer.h:25-95) on device buffers.  Formats and data types
@@ -188,11 +221,17 @@ int dcopy_zz_to_nd(void *dst, const void *src, const int64_t *nd_shape, int rank
  * C0 of each side given explicitly (TransArgs::src_c0_format/dst_c0_format).
  * Registered pairs: {ND, NCHW, NHWC} <-> FRACTAL_NZ
  * (format_transfer_fractal_nz.cc:459-464), {ND, NCHW, NHWC} <-> FRACTAL_ZZ
- * (format_transfer_fractal_zz.cc:494-499) and the 12 transposes among NCHW,
- * NHWC, HWCN, CHWN (format_transfer_transpose.cc:268-279). */
+ * (format_transfer_fractal_zz.cc:494-499), {NCHW, HWCN, NHWC, ND} ->
+ * FRACTAL_Z and FRACTAL_Z -> {NCHW, HWCN, NHWC} (fractal_z.cc:606-608,
+ * fractal_z_tbe.cc:147, fracz_{nchw,hwcn,nhwc}.cc) and the 12 transposes among NCHW, NHWC,
+ * HWCN, CHWN (format_transfer_transpose.cc:268-279).
+ * A format argument is a GE Format value: the primary format in bits 0-7, the
+ * sub format (GetSubFormat; FRACTAL_Z's group count) in bits 8-23.  Higher bits
+ * (GE's C0 field) are ignored: C0 is passed explicitly. */
 #define DCOPY_FORMAT_NCHW 0
 #define DCOPY_FORMAT_NHWC 1
 #define DCOPY_FORMAT_ND 2
+#define DCOPY_FORMAT_FRACTAL_Z 4
 #define DCOPY_FORMAT_CHWN 14
 #define DCOPY_FORMAT_HWCN 16
 #define DCOPY_FORMAT_FRACTAL_ZZ 28
@@ -204,12 +243,17 @@ int dcopy_zz_to_nd(void *dst, const void *src, const int64_t *nd_shape, int rank
 #define DCOPY_TRANSFER_TRANSPOSE 3     /* FormatTransferTranspose   (4-D permutes)       */
 #define DCOPY_TRANSFER_FRACTAL_ZZ 4    /* FormatTransferFractalZz   (ND/NCHW/NHWC -> ZZ) */
 #define DCOPY_TRANSFER_FRACTAL_ZZ_ND 5 /* FormatTransferFractalZzND (ZZ -> ND/NCHW/NHWC) */
+#define DCOPY_TRANSFER_FRACTAL_Z 6     /* FormatTransferFractalZ    (NCHW/HWCN/NHWC -> FZ) */
+#define DCOPY_TRANSFER_FRACTAL_Z_TBE 7 /* FormatTransferFractalZTbe (ND [C, N] -> FZ)     */
+#define DCOPY_TRANSFER_FRACZ_NCHW 8    /* FormatTransferFracZNchw   (FZ -> NCHW)          */
+#define DCOPY_TRANSFER_FRACZ_HWCN 9    /* FormatTransferFracZHwcn   (FZ -> HWCN)          */
+#define DCOPY_TRANSFER_FRACZ_NHWC 10   /* FormatTransferFracZNhwc   (FZ -> NHWC)          */
 
 /* TransArgs (register_format_transfer.h:25-42) with device data. */
 typedef struct DcopyTransArgs {
   const void *data;         /* source, device memory */
-  int32_t src_format;       /* primary GE Format of the source */
-  int32_t dst_format;       /* primary GE Format of the destination */
+  int32_t src_format;       /* GE Format of the source (primary + sub bits) */
+  int32_t dst_format;       /* GE Format of the destination (primary + sub bits) */
   int64_t src_c0;           /* C0 of the source format (used by NZ/ZZ -> ND) */
   int64_t dst_c0;           /* C0 of the destination format (used by ND -> NZ/ZZ) */
   const int64_t *src_shape;
@@ -217,6 +261,8 @@ typedef struct DcopyTransArgs {
   const int64_t *dst_shape; /* required by the transfers, as in the reference */
   int32_t dst_rank;
   int32_t data_type;        /* GE DataType */
+  int32_t src_sub_format;   /* TransArgs::src_sub_format (unused by these transfers) */
+  int32_t dst_sub_format;   /* TransArgs::dst_sub_format: HWCN -> FRACTAL_Z groups */
 } DcopyTransArgs;
 
 /* GetSizeByDataType: bytes of one element, or -1 for types without a fixed

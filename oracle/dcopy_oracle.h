@@ -10,9 +10,10 @@
  *   - tiling planner and RunTiles address model: fixtures generated from the
  *     reference's own Python twin (standalone_datacopy/profile.py:88-99,
  *     test_address_model.py:13-34) by tests/golden/make_golden.py;
- *   - ND<->FRACTAL_NZ, ND<->FRACTAL_ZZ and N-D transpose: GE's golden vectors
- *     (tests/ge/ut/ge/common/format_transfer_fractal_nz_unittest.cc,
- *      format_transfer_fractal_zz_unittest.cc,
+ *   - ND<->FRACTAL_NZ, ND<->FRACTAL_ZZ, FRACTAL_Z and N-D transpose: GE's golden
+ *     vectors (tests/ge/ut/ge/common/format_transfer_fractal_nz_unittest.cc,
+ *      format_transfer_fractal_zz_unittest.cc, format_transfer_*fractalz_unittest.cc,
+ *      format_transfer_fracz_*_unittest.cc, format_transfer_fractal_z_tbe_unittest.cc,
  *      format_transfer_transpose_unittest.cc), parsed at test time.
  *   - DataCopyExt gap addressing: test_address_model.py:24 (pinned through the
  *     RunTiles model, which is a DataCopyExt gather with blockLen=4).
@@ -37,6 +38,7 @@ enum {
   ORACLE_ESHAPE = -2,   /* ACL_ERROR_GE_SHAPE_INVALID */
   ORACLE_EDTYPE = -3,   /* ACL_ERROR_GE_DATATYPE_INVALID */
   ORACLE_EFORMAT = -4,  /* ACL_ERROR_GE_FORMAT_INVALID */
+  ORACLE_EFAILED = -8,  /* GE's generic FAILED / GRAPH_FAILED */
 };
 
 /* ---- standalone_datacopy ------------------------------------------------ */
@@ -103,6 +105,26 @@ int oracle_nd_to_zz(void *dst, const void *src, const int64_t *nd_shape, int ran
 /* TransFormatFromFracZzToNd (:238-334). */
 int oracle_zz_to_nd(void *dst, const void *src, const int64_t *nd_shape, int rank,
                     int elem_bytes, int64_t c0);
+
+/* ---- FRACTAL_Z (convolution weights; fractal_z_oracle.c) ------------------- */
+
+/* TransShape of FormatTransferFractalZ (fractal_z.cc:41-173, src_format NCHW 0,
+ * NHWC 1, HWCN 16; groups = the destination format's sub format, used when > 1
+ * for NCHW/HWCN) and of FormatTransferFractalZTbe (fractal_z_tbe.cc:32-62,
+ * src_format ND 2 = [C, N]).  dst_shape receives [C1*H*W, N1, 16, C0]. */
+int oracle_fz_shape(int src_format, const int64_t *src_shape, int rank, int64_t c0,
+                    int64_t groups, int64_t *dst_shape, int *dst_rank);
+/* The data movement of FormatTransferFractalZ::TransFormat / FractalZTbe
+ * (groups = TransArgs::dst_sub_format, used for HWCN when > 1).  *out_elems
+ * receives the element count the reference writes. */
+int oracle_to_fz(void *dst, const void *src, int src_format, const int64_t *src_shape, int rank,
+                 int elem_bytes, int64_t c0, int64_t groups, int64_t *out_elems);
+/* CheckArgsForFracZTo{Nchw,Hwcn,Nhwc} (fracz_nchw.cc:28-79 and twins). */
+int oracle_from_fz_check(const int64_t *src_shape, int src_rank, int dst_format,
+                         const int64_t *dst_shape, int dst_rank, int64_t c0);
+/* GetDstDataAfterTransForFracZTo{Nchw,Hwcn,Nhwc}: FZ -> NCHW / HWCN / NHWC. */
+int oracle_from_fz(void *dst, const void *src, int dst_format, const int64_t *dst_shape,
+                   int rank, int elem_bytes, int64_t c0);
 
 /* ---- N-D transpose -------------------------------------------------------- */
 

@@ -19,7 +19,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_build", "liboracle.so")
 
-OK, EPARAM, ESHAPE, EDTYPE, EFORMAT = 0, -1, -2, -3, -4
+OK, EPARAM, ESHAPE, EDTYPE, EFORMAT, EFAILED = 0, -1, -2, -3, -4, -8
 
 
 class Tiling(ctypes.Structure):
@@ -57,6 +57,14 @@ def lib() -> ctypes.CDLL:
             "oracle_nz_shape": [_i64p, ctypes.c_int, ctypes.c_int64, _i64p,
                                 ctypes.POINTER(ctypes.c_int), _i64p],
             "oracle_nd_to_nz": [_vp, _vp, _i64p, ctypes.c_int, ctypes.c_int, ctypes.c_int64],
+            "oracle_fz_shape": [ctypes.c_int, _i64p, ctypes.c_int, ctypes.c_int64,
+                                ctypes.c_int64, _i64p, ctypes.POINTER(ctypes.c_int)],
+            "oracle_to_fz": [_vp, _vp, ctypes.c_int, _i64p, ctypes.c_int, ctypes.c_int,
+                             ctypes.c_int64, ctypes.c_int64, _i64p],
+            "oracle_from_fz_check": [_i64p, ctypes.c_int, ctypes.c_int, _i64p, ctypes.c_int,
+                                     ctypes.c_int64],
+            "oracle_from_fz": [_vp, _vp, ctypes.c_int, _i64p, ctypes.c_int, ctypes.c_int,
+                               ctypes.c_int64],
             "oracle_zz_shape": [_i64p, ctypes.c_int, ctypes.c_int64, _i64p,
                                 ctypes.POINTER(ctypes.c_int), _i64p],
             "oracle_nd_to_zz": [_vp, _vp, _i64p, ctypes.c_int, ctypes.c_int, ctypes.c_int64],
@@ -153,6 +161,49 @@ def nd_to_zz(dst, src, nd_shape, elem_bytes, c0) -> int:
 
 def zz_to_nd(dst, src, nd_shape, elem_bytes, c0) -> int:
     return lib().oracle_zz_to_nd(_p(dst), _p(src), _i64(nd_shape), len(nd_shape), elem_bytes, c0)
+
+
+# GE format enum values used by the FRACTAL_Z family.
+NCHW, NHWC, ND, HWCN, FRACTAL_Z = 0, 1, 2, 16, 4
+
+
+def fz_shape(src_format: int, shape: Sequence[int], c0: int, groups: int = 0):
+    out = (ctypes.c_int64 * 4)()
+    rank = ctypes.c_int(0)
+    rc = lib().oracle_fz_shape(src_format, _i64(shape), len(shape), c0, groups, out,
+                               ctypes.byref(rank))
+    return rc, [out[i] for i in range(rank.value)]
+
+
+def to_fz(src: np.ndarray, src_format: int, c0: int, groups: int = 0) -> np.ndarray:
+    """FormatTransferFractalZ / FractalZTbe data movement (groups = the
+    TransArgs dst_sub_format); returns the written elements, flat."""
+    n = ctypes.c_int64(0)
+    src = np.ascontiguousarray(src)
+    args = (src_format, _i64(src.shape), src.ndim, src.dtype.itemsize, c0, groups,
+            ctypes.byref(n))
+    rc = lib().oracle_to_fz(None, _p(src), *args)  # sizing call: nothing written
+    if rc:
+        raise ValueError(f"to_fz rc={rc}")
+    out = np.empty(max(n.value, 1), dtype=src.dtype)
+    rc = lib().oracle_to_fz(_p(out), _p(src), *args)
+    if rc:
+        raise ValueError(f"to_fz rc={rc}")
+    return out[:n.value]
+
+
+def from_fz_check(src_shape, dst_format, dst_shape, c0) -> int:
+    return lib().oracle_from_fz_check(_i64(src_shape), len(src_shape), dst_format,
+                                      _i64(dst_shape), len(dst_shape), c0)
+
+
+def from_fz(src: np.ndarray, dst_format: int, dst_shape, c0: int) -> np.ndarray:
+    out = np.empty(dst_shape, dtype=src.dtype)
+    rc = lib().oracle_from_fz(_p(out), _p(np.ascontiguousarray(src)), dst_format,
+                              _i64(dst_shape), len(dst_shape), src.dtype.itemsize, c0)
+    if rc:
+        raise ValueError(f"from_fz rc={rc}")
+    return out
 
 
 def transpose(dst, src, src_shape, perm, elem_bytes) -> int:

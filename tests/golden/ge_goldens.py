@@ -22,9 +22,18 @@ import numpy as np
 
 NZ_TEST = "ge-develop/tests/ge/ut/ge/common/format_transfer_fractal_nz_unittest.cc"
 ZZ_TEST = "ge-develop/tests/ge/ut/ge/common/format_transfer_fractal_zz_unittest.cc"
+FZ_TESTS = {
+    "hwcn_fz": "ge-develop/tests/ge/ut/ge/common/format_transfer_hwcn_fractalz_unittest.cc",
+    "nchw_fz": "ge-develop/tests/ge/ut/ge/common/format_transfer_nchw_fractalz_unittest.cc",
+    "nhwc_fz": "ge-develop/tests/ge/ut/ge/common/format_transfer_nhwc_fractalz_unittest.cc",
+    "nd_fz": "ge-develop/tests/ge/ut/ge/common/format_transfer_fractal_z_tbe_unittest.cc",
+    "fz_nchw": "ge-develop/tests/ge/ut/ge/common/format_transfer_fracz_nchw_unittest.cc",
+    "fz_hwcn": "ge-develop/tests/ge/ut/ge/common/format_transfer_fracz_hwcn_unittest.cc",
+    "fz_nhwc": "ge-develop/tests/ge/ut/ge/common/format_transfer_fracz_nhwc_unittest.cc",
+}
 TRANSPOSE_TEST = "ge-develop/tests/ge/ut/ge/common/format_transfer_transpose_unittest.cc"
 
-_CTYPES = {"uint8_t": np.uint8, "uint16_t": np.uint16, "float": np.float32,
+_CTYPES = {"uint8_t": np.uint8, "int8_t": np.int8, "uint16_t": np.uint16, "float": np.float32,
            "int32_t": np.int32, "int64_t": np.int64, "double": np.float64}
 
 # GE DataType enum values and sizes (api/python/ge/ge/graph/types.py:15-58 mirrors
@@ -35,7 +44,10 @@ DT = {"DT_FLOAT": 0, "DT_FLOAT16": 1, "DT_INT8": 2, "DT_INT32": 3, "DT_UINT8": 4
 FMT = {"FORMAT_NCHW": 0, "FORMAT_NHWC": 1, "FORMAT_ND": 2, "FORMAT_NC1HWC0": 3,
        "FORMAT_FRACTAL_Z": 4, "FORMAT_C1HWNC0": 9, "FORMAT_CHWN": 14, "FORMAT_HWCN": 16,
        "FORMAT_FRACTAL_ZZ": 28, "FORMAT_FRACTAL_NZ": 29, "FORMAT_RESERVED": 40}
-STATUS = {"SUCCESS": 0, "ACL_ERROR_GE_PARAM_INVALID": 145000,
+_FMT_NAME = {v: k for k, v in FMT.items()}
+# GE's generic FAILED and GRAPH_FAILED (external metadef headers): 0xFFFFFFFF.
+STATUS = {"SUCCESS": 0, "FAILED": 0xFFFFFFFF, "GRAPH_FAILED": 0xFFFFFFFF,
+          "ACL_ERROR_GE_PARAM_INVALID": 145000,
           "ACL_ERROR_GE_FORMAT_INVALID": 145020, "ACL_ERROR_GE_SHAPE_INVALID": 145021,
           "ACL_ERROR_GE_DATATYPE_INVALID": 145022}
 
@@ -44,12 +56,16 @@ STATUS = {"SUCCESS": 0, "ACL_ERROR_GE_PARAM_INVALID": 145000,
 class Args:
     name: str                 # variable name (args, args2, ...)
     data_var: Optional[str]   # array passed as data (None for nullptr)
-    src_format: str
+    src_format: str           # primary formats (TransArgs::src/dst_primary_format)
     dst_format: str
     src_shape: List[int]
     dst_shape: List[int]
     dtype: str
     c0: List[int] = field(default_factory=list)
+    src_sub: int = 0          # TransArgs::src_sub_format / dst_sub_format
+    dst_sub: int = 0
+    src_format_sub: int = 0   # sub format carried by the full src_format / dst_format
+    dst_format_sub: int = 0
 
 
 @dataclass
@@ -67,6 +83,8 @@ class Case:
     arrays: Dict[str, np.ndarray]
     args: Dict[str, Args]
     expects: List[Expect]
+    # TransArgs variable -> name of the array its result is compared with
+    outputs: Dict[str, str] = field(default_factory=dict)
 
 
 def _nums(text: str):
@@ -79,7 +97,7 @@ def _array_values(body: str, ctype: str) -> np.ndarray:
     if _CTYPES[ctype] in (np.float32, np.float64):
         # A C++ double literal converted to float: parse as double, then round.
         return np.array([float(t) for t in toks], dtype=np.float64).astype(_CTYPES[ctype])
-    return np.array([int(t) for t in toks], dtype=np.int64).astype(_CTYPES[ctype])
+    return np.array([int(t, 0) for t in toks], dtype=np.int64).astype(_CTYPES[ctype])
 
 
 def _split_tests(text: str):
@@ -87,6 +105,80 @@ def _split_tests(text: str):
     for i, m in enumerate(heads):
         end = heads[i + 1].start() if i + 1 < len(heads) else len(text)
         yield m.group(1), text[m.end():end]
+
+
+def _split_top(text: str) -> List[str]:
+    """Splits at commas outside (), {} and <>."""
+    out, depth, cur = [], 0, []
+    for ch in text:
+        if ch in "({<":
+            depth += 1
+        elif ch in ")}>":
+            depth -= 1
+        if ch == "," and depth == 0:
+            out.append("".join(cur).strip())
+            cur = []
+        else:
+            cur.append(ch)
+    if "".join(cur).strip():
+        out.append("".join(cur).strip())
+    return out
+
+
+def _symbols(body: str):
+    """Integer and Format variables of one test body, and the (primary, sub)
+    of every full format built with GetFormatFromSub / GetFormatFromSubAndC0."""
+    sym, full = {}, {}
+
+    def val(tok):
+        tok = tok.strip()
+        if tok in FMT:
+            return FMT[tok]
+        if re.fullmatch(r"-?\d+", tok):
+            return int(tok)
+        return sym.get(tok)
+
+    for line in body.split(";"):
+        line = " ".join(line.split())
+        m = re.search(r"\b(?:int32_t|int64_t|int)\s+(\w+)\s*=\s*(-?\d+)$", line)
+        if m:
+            sym[m.group(1)] = int(m.group(2))
+            continue
+        m = re.search(r"Format\s+(\w+)\s*=\s*(FORMAT_\w+)$", line)
+        if m:
+            sym[m.group(1)] = FMT.get(m.group(2))
+            continue
+        m = re.search(r"(\w+)\s*=.*GetFormatFromSubAndC0\(\s*(\w+)\s*,\s*(\w+)\s*,\s*(\d+)\s*\)", line)
+        if m:
+            full[m.group(1)] = (val(m.group(2)), val(m.group(3)))
+            continue
+        m = re.search(r"(\w+)\s*=.*GetFormatFromSub\(\s*(\w+)\s*,\s*(\w+)\s*\)", line)
+        if m:
+            full[m.group(1)] = (val(m.group(2)), val(m.group(3)))
+            continue
+        m = re.search(r"(\w+)\s*=.*Get(Sub|Primary)Format\(\s*(?:static_cast<int32_t>\()?\s*(\w+)", line)
+        if m and m.group(3) in full:
+            sym[m.group(1)] = full[m.group(3)][1 if m.group(2) == "Sub" else 0]
+    return sym, full, val
+
+
+def _parse_args_positional(var: str, body: str, test_body: str) -> Optional[Args]:
+    """TransArgs{data, src_format, dst_format, src_primary, dst_primary, src_sub,
+    dst_sub, src_c0, dst_c0, src_shape, dst_shape, data_type} by position."""
+    f = _split_top(body)
+    if len(f) != 12:
+        return None
+    sym, full, val = _symbols(test_body)
+    data = re.match(r"\s*(?:reinterpret_cast<uint8_t\s*\*>\(\s*(\w+)\s*\)|(\w+))", f[0])
+    data_var = (data.group(1) or data.group(2)) if data else None
+    prim = [val(f[3]), val(f[4])]
+    if None in prim:
+        return None
+    shapes = [_nums(re.search(r"\{([-\d,\s]*)\}", x).group(1)) for x in (f[9], f[10])]
+    subs = [val(f[5]) or 0, val(f[6]) or 0]
+    fsub = [full.get(f[1].strip(), (None, 0))[1] or 0, full.get(f[2].strip(), (None, 0))[1] or 0]
+    return Args(var, data_var, _FMT_NAME[prim[0]], _FMT_NAME[prim[1]], shapes[0], shapes[1],
+                f[11].strip(), [int(f[7]), int(f[8])], subs[0], subs[1], fsub[0], fsub[1])
 
 
 def _parse_args(var: str, body: str) -> Args:
@@ -110,8 +202,8 @@ def parse(path: Path) -> List[Case]:
     cases = []
     for name, body in _split_tests(text):
         arrays = {}
-        for m in re.finditer(r"\b(uint8_t|uint16_t|float|int32_t|int64_t|double)\s+(\w+)\s*"
-                             r"\[([^\]]*)\]\s*=\s*\{(.*?)\};", body, re.S):
+        for m in re.finditer(r"\b(uint8_t|int8_t|uint16_t|float|int32_t|int64_t|double)\s+(\w+)\s*"
+                             r"\[([^\]]*)\]\s*=?\s*\{(.*?)\};", body, re.S):
             values = _array_values(m.group(4), m.group(1))
             # A shorter initializer list leaves the remaining elements zero (C++
             # aggregate initialisation): pad to the declared extent when it is
@@ -124,10 +216,11 @@ def parse(path: Path) -> List[Case]:
             arrays[m.group(2)] = values
         args = {}
         for m in re.finditer(r"TransArgs\s+(\w+)\s*\{(.*?)\};", body, re.S):
-            args[m.group(1)] = _parse_args(m.group(1), m.group(2))
+            a = _parse_args_positional(m.group(1), m.group(2), body)
+            args[m.group(1)] = a if a is not None else _parse_args(m.group(1), m.group(2))
         var_class = {v: k for k, v in re.findall(r"\b(FormatTransfer\w+)\s+(\w+)\s*;", body)}
         expects = []
-        for m in re.finditer(r"EXPECT_EQ\(\s*((?:(?!EXPECT_EQ).)*?)\s*,\s*(SUCCESS|ACL_ERROR_GE_\w+)"
+        for m in re.finditer(r"EXPECT_EQ\(\s*((?:(?!EXPECT_EQ).)*?)\s*,\s*(SUCCESS|FAILED|GRAPH_FAILED|ACL_ERROR_GE_\w+)"
                              r"\s*\)\s*;", body, re.S):
             call, status = m.group(1), STATUS[m.group(2)]
             if call.startswith("TransDataFormat("):
@@ -158,10 +251,17 @@ def parse(path: Path) -> List[Case]:
                                       {"data": dm.group(1), "src_shape": _vector(vecs[0]),
                                        "dst_shape": _vector(vecs[1]), "perm": _vector(vecs[2]),
                                        "dtype": dt}))
-        cases.append(Case(name, arrays, args, expects))
+        result_of = {}
+        for m in re.finditer(r"(?:\.TransFormat|TransDataFormat)\(\s*(\w+)\s*,\s*(\w+)\s*\)", body):
+            result_of[m.group(2)] = m.group(1)
+        outputs = {}
+        for m in re.finditer(r"(\w+)\.data\.get\(\)\)\)\[i\]\s*,\s*(\w+)\[i\]", body):
+            if m.group(1) in result_of and m.group(2) in arrays:
+                outputs[result_of[m.group(1)]] = m.group(2)
+        cases.append(Case(name, arrays, args, expects, outputs))
     return cases
 
 
 def load(reference_root: Path, which: str) -> List[Case]:
-    rel = {"nz": NZ_TEST, "zz": ZZ_TEST, "transpose": TRANSPOSE_TEST}[which]
+    rel = {"nz": NZ_TEST, "zz": ZZ_TEST, "transpose": TRANSPOSE_TEST, **FZ_TESTS}[which]
     return parse(Path(reference_root) / rel)

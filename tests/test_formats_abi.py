@@ -13,7 +13,9 @@ import ge_goldens
 
 CLASS = {"FormatTransferFractalNz": 1, "FormatTransferFractalNzND": 2,
          "FormatTransferTranspose": 3, "FormatTransferFractalZz": 4,
-         "FormatTransferFractalZzND": 5}
+         "FormatTransferFractalZzND": 5, "FormatTransferFractalZ": 6,
+         "FormatTransferFractalZTbe": 7, "FormatTransferFracZNchw": 8,
+         "FormatTransferFracZHwcn": 9, "FormatTransferFracZNhwc": 10}
 
 
 def _fmt(name):
@@ -79,9 +81,11 @@ def test_trans_shape_results(dcopy):
     with pytest.raises(dcopy.DcopyError) as e:
         dcopy.trans_tensor_shape(f["FRACTAL_NZ"], [1, 1, 16, 16], 1, f["ND"], 16)
     assert e.value.code == dcopy.ERR_FORMAT_INVALID
-    with pytest.raises(dcopy.DcopyError) as e:
-        dcopy.trans_tensor_shape(f["ND"], [4, 4], 1, f["FRACTAL_Z"], 16)
+    with pytest.raises(dcopy.DcopyError) as e:  # not a registered pair
+        dcopy.trans_tensor_shape(f["ND"], [4, 4], 1, f["NC1HWC0"], 16)
     assert e.value.code == dcopy.ERR_FORMAT_INVALID
+    # ND -> FRACTAL_Z is the TBE transfer: a 2-D [C, N] weight.
+    assert dcopy.trans_tensor_shape(f["ND"], [17, 4], 1, f["FRACTAL_Z"], 16) == [2, 1, 16, 16]
 
 
 def test_data_type_sizes(dcopy):
@@ -124,3 +128,54 @@ def test_transpose_argument_checks(dcopy):
     with pytest.raises(dcopy.DcopyError) as e:  # unsized data type
         dcopy.transpose(0, 0x1000, [2, 2], [1, 0], d["STRING"])
     assert e.value.code == dcopy.ERR_PARAM_INVALID
+
+
+FZ_FILES = sorted(ge_goldens.FZ_TESTS)
+
+
+def _full(dcopy, name, sub):
+    """The test's full GE format: primary plus the sub format it was built with."""
+    return dcopy.format_with_sub(ge_goldens.FMT[name], sub)
+
+
+@pytest.mark.parametrize("which", FZ_FILES)
+def test_fractal_z_expectations(dcopy, reference_root, which):
+    """Every expectation of GE's FRACTAL_Z unit tests, through the C ABI without data
+    movement: failures by status, TransShape by its result, and data-moving
+    successes by the result length the transfer reports."""
+    checked = 0
+    for case in ge_goldens.load(reference_root, which):
+        for e in case.expects:
+            a = case.args.get(e.args) if e.args else None
+            if a is None:
+                continue
+            src_f = _full(dcopy, a.src_format, a.src_format_sub)
+            dst_f = _full(dcopy, a.dst_format, a.dst_format_sub)
+            if e.call == "TransShape":
+                try:
+                    got_shape = dcopy.trans_shape(CLASS[e.transfer_class], src_f, a.src_shape,
+                                                  ge_goldens.DT[a.dtype], dst_f, a.c0[1])
+                    got = 0
+                except dcopy.DcopyError as err:
+                    got = dcopy.status_to_ge(err.code)
+                assert got == e.status, (case.name, e)
+                if got == 0:
+                    assert got_shape == a.dst_shape, case.name
+            else:
+                cls = 0 if e.call == "TransDataFormat" else CLASS[e.transfer_class]
+                data = 0 if a.data_var not in case.arrays else 0x1000
+                try:
+                    n = dcopy.trans_format_check(cls, data, src_f, dst_f, a.src_shape,
+                                                 a.dst_shape, ge_goldens.DT[a.dtype],
+                                                 src_c0=a.c0[0], dst_c0=a.c0[1],
+                                                 src_sub=a.src_sub, dst_sub=a.dst_sub)
+                    got = 0
+                except dcopy.DcopyError as err:
+                    got = dcopy.status_to_ge(err.code)
+                assert got == e.status, (case.name, e, got)
+                out = case.outputs.get(e.args)
+                if got == 0 and out is not None:
+                    assert n == case.arrays[out].nbytes, (case.name, n)
+            checked += 1
+    assert checked == {"hwcn_fz": 8, "nchw_fz": 10, "nhwc_fz": 10, "nd_fz": 6, "fz_nchw": 20,
+                       "fz_hwcn": 17, "fz_nhwc": 14}[which]
