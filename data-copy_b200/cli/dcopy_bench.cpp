@@ -16,6 +16,10 @@
 //                  [--device D]
 //       fp16 ND -> FRACTAL_NZ -> ND (or FRACTAL_ZZ), round trip
 //       verified.
+//   dcopy_bench fz [--n N] [--c C] [--h H] [--w W] [--eb B] [--c0 C0] [--reps R]
+//                  [--device D] [--peak GBPS]
+//       Convolution weights: NCHW / NHWC / HWCN -> FRACTAL_Z -> back, each
+//       round trip verified; one JSON line per format.
 //   dcopy_bench p2p [--mib M] [--reps R] [--device D] [--peer P] [--peak GBPS]
 //       NVLink between two GPUs: dcopy_p2p_copy as a push (launched on the
 //       sending GPU) and as a pull (launched on the receiving GPU), and the copy
@@ -354,6 +358,64 @@ int run_nz(const Args &a) {
   return 0;
 }
 
+// ---- fz ---------------------------------------------------------------------------
+
+int run_fz(const Args &a) {
+  const int64_t n = int64_t(a.num("n", 2048)), c = int64_t(a.num("c", 2048));
+  const int64_t h = int64_t(a.num("h", 3)), w = int64_t(a.num("w", 3));
+  const int eb = int(a.num("eb", 2));
+  const int64_t c0 = int64_t(a.num("c0", 16));
+  const int reps = int(a.num("reps", 10));
+  const double peak = a.num("peak", 6543.4);
+  Check(cudaSetDevice(int(a.num("device", 0))), "cudaSetDevice");
+  cudaStream_t s;
+  Check(cudaStreamCreate(&s), "stream");
+  dcopy_stream_t ds = reinterpret_cast<dcopy_stream_t>(s);
+  const uint64_t wbytes = uint64_t(n * c * h * w) * eb;
+  std::vector<uint8_t> host(wbytes), host2(wbytes);
+  uint64_t x = 0x2545F4914F6CDD1Dull;  // xorshift64 bytes
+  for (auto &v : host) {
+    x ^= x << 13;
+    x ^= x >> 7;
+    x ^= x << 17;
+    v = uint8_t(x);
+  }
+  DevBuf src(wbytes), back(wbytes), flush(512ull << 20);
+  Check(cudaMemcpy(src.p, host.data(), wbytes, cudaMemcpyHostToDevice), "H2D");
+  const struct {
+    const char *name;
+    int32_t fmt;
+    std::vector<int64_t> shape;
+  } fmts[] = {{"NCHW", 0, {n, c, h, w}}, {"NHWC", 1, {n, h, w, c}}, {"HWCN", 16, {h, w, c, n}}};
+  for (const auto &f : fmts) {
+    int64_t fz[4];
+    CheckD(dcopy_fz_shape(f.fmt, f.shape.data(), 4, c0, 0, fz));
+    const uint64_t fbytes = uint64_t(fz[0] * fz[1] * fz[2] * fz[3]) * eb;
+    DevBuf z(fbytes);
+    CheckD(dcopy_to_fractal_z(z.p, src.p, f.fmt, f.shape.data(), 4, eb, c0, 0, ds));
+    CheckD(dcopy_from_fractal_z(back.p, z.p, f.fmt, f.shape.data(), 4, eb, c0, ds));
+    Check(cudaMemcpy(host2.data(), back.p, wbytes, cudaMemcpyDeviceToHost), "D2H");
+    if (std::memcmp(host.data(), host2.data(), wbytes) != 0)
+      throw std::runtime_error(std::string(f.name) + " -> FRACTAL_Z -> back differs");
+    auto t1 = time_reps(
+        [&] { CheckD(dcopy_to_fractal_z(z.p, src.p, f.fmt, f.shape.data(), 4, eb, c0, 0, ds)); },
+        reps, s, flush);
+    auto t2 = time_reps(
+        [&] { CheckD(dcopy_from_fractal_z(back.p, z.p, f.fmt, f.shape.data(), 4, eb, c0, ds)); },
+        reps, s, flush);
+    const double g1 = double(wbytes + fbytes) / (median(t1) * 1e3);
+    const double g2 = double(wbytes + fbytes) / (median(t2) * 1e3);
+    std::cout << "{\"fz\": \"" << f.name << "\", \"weight_nchw\": [" << n << ", " << c << ", "
+              << h << ", " << w << "], \"elem_bytes\": " << eb << ", \"c0\": " << c0
+              << ", \"to_fz_us\": " << median(t1) << ", \"to_fz_GBps\": " << g1
+              << ", \"from_fz_us\": " << median(t2) << ", \"from_fz_GBps\": " << g2
+              << ", \"frac_of_peak\": [" << g1 / peak << ", " << g2 / peak
+              << "], \"round_trip_bit_exact\": true}" << std::endl;
+  }
+  cudaStreamDestroy(s);
+  return 0;
+}
+
 // ---- p2p --------------------------------------------------------------------------
 
 int run_p2p(const Args &a) {
@@ -457,13 +519,14 @@ int run_p2p(const Args &a) {
 
 int main(int argc, char **argv) {
   try {
-    if (argc < 2) throw std::runtime_error("usage: dcopy_bench sweep|standalone|nz|p2p [options]");
+    if (argc < 2) throw std::runtime_error("usage: dcopy_bench sweep|standalone|nz|fz|p2p [options]");
     const std::string cmd = argv[1];
     Args a(argc, argv);
     if (cmd == "sweep") return run_sweep(a);
     if (cmd == "standalone") return run_standalone(a);
     if (cmd == "nz") return run_nz(a);
     if (cmd == "p2p") return run_p2p(a);
+    if (cmd == "fz") return run_fz(a);
     throw std::runtime_error("unknown command " + cmd);
   } catch (const std::exception &e) {
     std::cerr << "dcopy_bench: " << e.what() << '\n';
