@@ -18,6 +18,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstring>
 
 #include "common.cuh"
@@ -134,6 +135,160 @@ __global__ void __launch_bounds__(kThreads) fz_groups_kernel(T *__restrict__ dst
   }
 }
 
+// Vectorised NCHW / HWCN / ND <-> FRACTAL_Z for 1-, 2- and 4-byte elements when
+// C0 is a power of two and C0*eb a multiple of 16 bytes.  A tile is S source
+// segments of L contiguous elements, moved between global and shared memory in
+// 16-byte vectors:
+//   NCHW: tile (c1, n block of NB): segment = weight n's C0 channels of block c1,
+//         L = C0*HW; the FRACTAL_Z side is HW runs of NB*C0 elements (pitch N1*16*C0).
+//   HWCN / ND: tile (c1, hw, n block of KT): segment = one input channel's KT
+//         consecutive n, L = KT; the FRACTAL_Z side is one run of KT*C0 elements.
+// The FRACTAL_Z side moves V = 16/eb consecutive c0 values per 16-byte vector,
+// each gathered from (scattered into) shared memory at stride B.  Shared memory
+// rows have an odd pitch in 4-byte words, so both the row-wise and the strided
+// accesses spread over the banks.
+template <int EB>
+struct FzLane;
+template <>
+struct FzLane<1> {
+  using T = uint8_t;
+  static constexpr int V = 16;
+};
+template <>
+struct FzLane<2> {
+  using T = uint16_t;
+  static constexpr int V = 8;
+};
+template <>
+struct FzLane<4> {
+  using T = uint32_t;
+  static constexpr int V = 4;
+};
+
+struct FzSGeom {
+  uint32_t S, L, P;      // segments per tile, segment length, shared row pitch (elements)
+  uint32_t VPS;          // 16-byte vectors per segment
+  FastDiv f_vps;
+  uint32_t C, C0, lc0, N, N1N0, HW;
+  uint32_t lrv;          // log2 of the 16-byte vectors per FRACTAL_Z run (NB*C0/V or C0/V)
+  uint32_t NB, nblocks;  // NCHW: n per tile, n blocks
+  uint32_t KT, ktiles;   // HWCN: n per tile, n tiles
+  FastDiv f_nblocks, f_ktiles, f_hw;
+  uint64_t seg_stride;   // global elements between segments
+};
+
+template <int EB, bool kToFz, bool kNchw>
+__global__ void __launch_bounds__(kThreads) fz_vec_kernel(unsigned char *__restrict__ dst_b,
+                                                          const unsigned char *__restrict__ src_b,
+                                                          FzSGeom g, uint32_t ntiles) {
+  using T = typename FzLane<EB>::T;
+  constexpr int V = FzLane<EB>::V;
+  union Pack {
+    uint4 u;
+    T e[V];
+  };
+  extern __shared__ __align__(16) unsigned char fz_vsmem[];
+  T *tile = reinterpret_cast<T *>(fz_vsmem);
+  T *dst = reinterpret_cast<T *>(dst_b);
+  const T *src = reinterpret_cast<const T *>(src_b);
+  pdl_trigger_at_entry();
+  pdl_wait();
+  pdl_launch_dependents();
+  for (uint32_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
+    // ---- tile geometry
+    uint32_t c1, s_valid, l_valid, k_out, r_vecs;
+    uint64_t seg_base, fz_base, dk;
+    uint32_t A, B;  // shared index of FRACTAL_Z element (R, k): (R >> lc0)*A + (R & (C0-1))*B + k
+    if (kNchw) {
+      c1 = g.f_nblocks.div(t);
+      const uint32_t nb = t - c1 * g.nblocks, n0 = nb * g.NB;
+      const uint32_t rb_valid = min(g.C0, g.C - c1 * g.C0);
+      s_valid = n0 < g.N ? min(g.NB, g.N - n0) : 0;
+      l_valid = rb_valid * g.HW;
+      seg_base = (uint64_t)n0 * g.seg_stride + (uint64_t)c1 * g.C0 * g.HW;
+      fz_base = ((uint64_t)c1 * g.HW * g.N1N0 + n0) * g.C0;
+      dk = (uint64_t)g.N1N0 * g.C0;
+      k_out = g.HW;
+      r_vecs = g.NB * g.C0 / V;
+      A = g.P;
+      B = g.HW;
+    } else {
+      const uint32_t q = g.f_ktiles.div(t), kt = t - q * g.ktiles;
+      c1 = g.f_hw.div(q);
+      const uint32_t hw = q - c1 * g.HW, n0 = kt * g.KT;
+      s_valid = min(g.C0, g.C - c1 * g.C0);
+      l_valid = n0 < g.N ? min(g.KT, g.N - n0) : 0;
+      seg_base = ((uint64_t)hw * g.C + (uint64_t)c1 * g.C0) * g.N + n0;
+      fz_base = (((uint64_t)c1 * g.HW + hw) * g.N1N0 + n0) * g.C0;
+      dk = g.C0;
+      k_out = min(g.KT, g.N1N0 - n0);
+      r_vecs = g.C0 / V;
+      A = 0;
+      B = g.P;
+    }
+    const uint32_t n_seg_vec = g.S * g.VPS, n_fz_vec = k_out * r_vecs;
+    if (kToFz) {
+      // ---- weight -> shared memory, 16 bytes per step, zero past the valid range
+      for (uint32_t u = threadIdx.x; u < n_seg_vec; u += kThreads) {
+        const uint32_t sg = g.f_vps.div(u), f0 = (u - sg * g.VPS) * V;
+        const uint32_t lv = sg < s_valid ? l_valid : 0;
+        const T *sp = src + seg_base + (uint64_t)sg * g.seg_stride + f0;
+        Pack x;
+        if (f0 + V <= lv) {
+          x.u = ld_stream(reinterpret_cast<const uint4 *>(sp));
+        } else {
+#pragma unroll
+          for (int j = 0; j < V; ++j) x.e[j] = f0 + j < lv ? sp[j] : T(0);
+        }
+        uint32_t *w = reinterpret_cast<uint32_t *>(tile + sg * g.P + f0);
+        w[0] = x.u.x;
+        w[1] = x.u.y;
+        w[2] = x.u.z;
+        w[3] = x.u.w;
+      }
+      __syncthreads();
+      // ---- shared memory -> FRACTAL_Z, V consecutive c0 per 16-byte store
+      for (uint32_t u = threadIdx.x; u < n_fz_vec; u += kThreads) {
+        const uint32_t k = u >> g.lrv, r0 = (u & (r_vecs - 1)) * V;
+        const uint32_t base = (r0 >> g.lc0) * A + (r0 & (g.C0 - 1)) * B + k;
+        Pack x;
+#pragma unroll
+        for (int j = 0; j < V; ++j) x.e[j] = tile[base + j * B];
+        *reinterpret_cast<uint4 *>(dst + fz_base + (uint64_t)k * dk + r0) = x.u;
+      }
+    } else {
+      // ---- FRACTAL_Z -> shared memory
+      for (uint32_t u = threadIdx.x; u < n_fz_vec; u += kThreads) {
+        const uint32_t k = u >> g.lrv, r0 = (u & (r_vecs - 1)) * V;
+        const uint32_t base = (r0 >> g.lc0) * A + (r0 & (g.C0 - 1)) * B + k;
+        Pack x;
+        x.u = ld_stream(reinterpret_cast<const uint4 *>(src + fz_base + (uint64_t)k * dk + r0));
+#pragma unroll
+        for (int j = 0; j < V; ++j) tile[base + j * B] = x.e[j];
+      }
+      __syncthreads();
+      // ---- shared memory -> weight, valid range only
+      for (uint32_t u = threadIdx.x; u < n_seg_vec; u += kThreads) {
+        const uint32_t sg = g.f_vps.div(u), f0 = (u - sg * g.VPS) * V;
+        const uint32_t lv = sg < s_valid ? l_valid : 0;
+        if (f0 >= lv) continue;
+        const uint32_t *w = reinterpret_cast<const uint32_t *>(tile + sg * g.P + f0);
+        Pack x;
+        x.u = make_uint4(w[0], w[1], w[2], w[3]);
+        T *dp = dst + seg_base + (uint64_t)sg * g.seg_stride + f0;
+        if (f0 + V <= lv) {
+          *reinterpret_cast<uint4 *>(dp) = x.u;
+        } else {
+#pragma unroll
+          for (int j = 0; j < V; ++j)
+            if (f0 + j < lv) dp[j] = x.e[j];
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
 bool fz_dims(int32_t fmt, const int64_t *s, int rank, int64_t *n, int64_t *c, int64_t *h,
              int64_t *w) {
   if (!s) return false;
@@ -217,9 +372,114 @@ int launch_groups(void *dst, const void *src, const FzGGeom &g, cudaStream_t s) 
                 static_cast<T *>(dst), static_cast<const T *>(src), g);
 }
 
+constexpr size_t kVecSmemMax = 96 * 1024;  // shared memory of one vectorised tile
+
+uint32_t log2_of(uint64_t v) {
+  uint32_t l = 0;
+  while ((1ull << l) < v) ++l;
+  return l;
+}
+
+template <int EB>
+int launch_vec(bool nchw, bool to_fz, void *dst, const void *src, const FzSGeom &g,
+               uint32_t ntiles, size_t smem, cudaStream_t s) {
+  static std::atomic<bool> raised[4][128];  // per kernel, per device: 48 KiB+ opt-in done
+  const int dev = current_device();
+  const int which = (nchw ? 2 : 0) + (to_fz ? 1 : 0);
+  void (*k)(unsigned char *, const unsigned char *, FzSGeom, uint32_t) =
+      nchw ? (to_fz ? fz_vec_kernel<EB, true, true> : fz_vec_kernel<EB, false, true>)
+           : (to_fz ? fz_vec_kernel<EB, true, false> : fz_vec_kernel<EB, false, false>);
+  if (smem > 48 * 1024 && dev >= 0 && dev < 128 && !raised[which][dev].load()) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kVecSmemMax);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+    raised[which][dev] = true;
+  }
+  const uint32_t grid = std::max(1u, std::min<uint32_t>(ntiles, 0x7FFFFFFFu));
+  return launch(k, grid, dim3(kThreads), smem, s, "fz_vec_kernel",
+                static_cast<unsigned char *>(dst), static_cast<const unsigned char *>(src), g,
+                ntiles);
+}
+
+// The vectorised path when its conditions hold; *taken = false otherwise.
+int run_vec(int32_t fmt, void *dst, const void *src, int64_t n, int64_t c, int64_t h, int64_t w,
+            int eb, int64_t c0, bool to_fz, cudaStream_t s, bool *taken) {
+  *taken = false;
+  if (eb != 1 && eb != 2 && eb != 4) return DCOPY_OK;
+  if (c0 <= 0 || (c0 & (c0 - 1)) || (c0 * eb) % 16 || c0 > 4096) return DCOPY_OK;
+  if (((uintptr_t)dst | (uintptr_t)src) % 16) return DCOPY_OK;
+  const int64_t V = 16 / eb, hw = h * w, n1n0 = ge_ceil(n, kNi) * kNi, c1 = ge_ceil(c, c0);
+  if (n > 0x7FFFFFFFll || c > 0x7FFFFFFFll || hw > 0x7FFFFFFFll || n1n0 * c0 > 0x7FFFFFFFll)
+    return DCOPY_OK;
+  FzSGeom g{};
+  g.C = (uint32_t)c;
+  g.C0 = (uint32_t)c0;
+  g.lc0 = log2_of((uint64_t)c0);
+  g.N = (uint32_t)n;
+  g.N1N0 = (uint32_t)n1n0;
+  g.HW = (uint32_t)hw;
+  auto pitch = [&](int64_t L) {  // odd number of 4-byte words
+    int64_t words = (L * eb + 3) / 4;
+    if (words % 2 == 0) ++words;
+    return words * 4 / eb;
+  };
+  uint64_t ntiles;
+  size_t smem;
+  if (fmt == kNchw) {
+    if ((c * hw * eb) % 16) return DCOPY_OK;  // segment starts must be 16-byte aligned
+    int64_t nb = 16;
+    const int64_t L = c0 * hw, P = pitch(L);
+    while (nb > 1 && (size_t)(nb * P * eb) > kVecSmemMax) nb /= 2;
+    if ((size_t)(nb * P * eb) > kVecSmemMax) return DCOPY_OK;
+    g.S = (uint32_t)nb;
+    g.L = (uint32_t)L;
+    g.P = (uint32_t)P;
+    g.NB = (uint32_t)nb;
+    g.nblocks = (uint32_t)(n1n0 / nb);
+    g.lrv = log2_of((uint64_t)(nb * c0 / V));
+    g.seg_stride = (uint64_t)(c * hw);
+    ntiles = (uint64_t)c1 * g.nblocks;
+    smem = (size_t)(nb * P * eb);
+  } else {  // HWCN, and ND [C, N] as HWCN with H = W = 1
+    if ((n * eb) % 16) return DCOPY_OK;
+    int64_t kt = std::max<int64_t>(V, (4096 / c0) / V * V);
+    kt = std::min<int64_t>(kt, n1n0);
+    const int64_t P = pitch(kt);
+    if ((size_t)(c0 * P * eb) > kVecSmemMax) return DCOPY_OK;
+    g.S = (uint32_t)c0;
+    g.L = (uint32_t)kt;
+    g.P = (uint32_t)P;
+    g.KT = (uint32_t)kt;
+    g.ktiles = (uint32_t)ge_ceil(n1n0, kt);
+    g.lrv = log2_of((uint64_t)(c0 / V));
+    g.seg_stride = (uint64_t)n;
+    ntiles = (uint64_t)c1 * hw * g.ktiles;
+    smem = (size_t)(c0 * P * eb);
+  }
+  g.VPS = g.L / (uint32_t)V;
+  g.f_vps = FastDiv(g.VPS);
+  g.f_nblocks = FastDiv(std::max(1u, g.nblocks));
+  g.f_ktiles = FastDiv(std::max(1u, g.ktiles));
+  g.f_hw = FastDiv(std::max(1u, g.HW));
+  *taken = true;
+  if (ntiles == 0) return DCOPY_OK;
+  if (ntiles > 0xFFFFFFFFull)
+    return set_error(DCOPY_ERR_UNSUPPORTED, "FRACTAL_Z: %llu tiles exceed 32-bit indexing",
+                     (unsigned long long)ntiles);
+  const bool nchw = fmt == kNchw;
+  switch (eb) {
+    case 1: return launch_vec<1>(nchw, to_fz, dst, src, g, (uint32_t)ntiles, smem, s);
+    case 2: return launch_vec<2>(nchw, to_fz, dst, src, g, (uint32_t)ntiles, smem, s);
+    default: return launch_vec<4>(nchw, to_fz, dst, src, g, (uint32_t)ntiles, smem, s);
+  }
+}
+
 // The NCHW / HWCN / ND (both directions) transposing path.
 int run_transpose(int32_t fmt, void *dst, const void *src, int64_t n, int64_t c, int64_t h,
                   int64_t w, int eb, int64_t c0, bool to_fz, cudaStream_t s) {
+  bool taken = false;
+  const int vrc = run_vec(fmt, dst, src, n, c, h, w, eb, c0, to_fz, s, &taken);
+  if (taken || vrc) return vrc;
   const int64_t n1n0 = ge_ceil(n, kNi) * kNi, c1 = ge_ceil(c, c0), hw = h * w;
   FzTGeom g{};
   int64_t R_ext, K_ext, B2;

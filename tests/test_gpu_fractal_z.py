@@ -20,6 +20,7 @@ NCHW, NHWC, ND, HWCN = 0, 1, 2, 16
 WEIGHTS = [  # (N, C, H, W)
     (1, 1, 1, 1), (16, 16, 1, 1), (17, 5, 3, 3), (64, 64, 3, 3), (33, 70, 1, 1),
     (5, 40, 4, 7), (128, 3, 7, 7), (31, 17, 4, 4), (2, 300, 2, 2), (40, 33, 5, 5),
+    (20, 32, 11, 11), (20, 16, 15, 15), (48, 64, 1, 1),
 ]
 
 
