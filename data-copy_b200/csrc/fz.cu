@@ -171,11 +171,15 @@ struct FzSGeom {
   FastDiv f_vps;
   uint32_t C, C0, lc0, N, N1N0, HW;
   uint32_t lrv;          // log2 of the 16-byte vectors per FRACTAL_Z run (NB*C0/V or C0/V)
+  uint32_t C1, c1_fast;  // NCHW: channel blocks; 1 = tiles walk them first
+  FastDiv f_c1;
   uint32_t NB, nblocks;  // NCHW: n per tile, n blocks
   uint32_t KT, ktiles;   // HWCN: n per tile, n tiles
   FastDiv f_nblocks, f_ktiles, f_hw;
   uint64_t seg_stride;   // global elements between segments
 };
+
+constexpr int kLoadBatch = 4;
 
 template <int EB, bool kToFz, bool kNchw>
 __global__ void __launch_bounds__(kThreads) fz_vec_kernel(unsigned char *__restrict__ dst_b,
@@ -200,8 +204,15 @@ __global__ void __launch_bounds__(kThreads) fz_vec_kernel(unsigned char *__restr
     uint64_t seg_base, fz_base, dk;
     uint32_t A, B;  // shared index of FRACTAL_Z element (R, k): (R >> lc0)*A + (R & (C0-1))*B + k
     if (kNchw) {
-      c1 = g.f_nblocks.div(t);
-      const uint32_t nb = t - c1 * g.nblocks, n0 = nb * g.NB;
+      uint32_t nb;
+      if (g.c1_fast) {
+        nb = g.f_c1.div(t);
+        c1 = t - nb * g.C1;
+      } else {
+        c1 = g.f_nblocks.div(t);
+        nb = t - c1 * g.nblocks;
+      }
+      const uint32_t n0 = nb * g.NB;
       const uint32_t rb_valid = min(g.C0, g.C - c1 * g.C0);
       s_valid = n0 < g.N ? min(g.NB, g.N - n0) : 0;
       l_valid = rb_valid * g.HW;
@@ -229,22 +240,36 @@ __global__ void __launch_bounds__(kThreads) fz_vec_kernel(unsigned char *__restr
     const uint32_t n_seg_vec = g.S * g.VPS, n_fz_vec = k_out * r_vecs;
     if (kToFz) {
       // ---- weight -> shared memory, 16 bytes per step, zero past the valid range
-      for (uint32_t u = threadIdx.x; u < n_seg_vec; u += kThreads) {
-        const uint32_t sg = g.f_vps.div(u), f0 = (u - sg * g.VPS) * V;
-        const uint32_t lv = sg < s_valid ? l_valid : 0;
-        const T *sp = src + seg_base + (uint64_t)sg * g.seg_stride + f0;
-        Pack x;
-        if (f0 + V <= lv) {
-          x.u = ld_stream(reinterpret_cast<const uint4 *>(sp));
-        } else {
+      // kLoadBatch loads are issued before their shared-memory stores, so each
+      // thread keeps that many 16-byte reads in flight.
+      for (uint32_t ub = threadIdx.x; ub < n_seg_vec; ub += kLoadBatch * kThreads) {
+        Pack x[kLoadBatch];
+        uint32_t at[kLoadBatch];
 #pragma unroll
-          for (int j = 0; j < V; ++j) x.e[j] = f0 + j < lv ? sp[j] : T(0);
+        for (int b = 0; b < kLoadBatch; ++b) {
+          const uint32_t u = ub + b * kThreads;
+          at[b] = 0xFFFFFFFFu;
+          if (u >= n_seg_vec) continue;
+          const uint32_t sg = g.f_vps.div(u), f0 = (u - sg * g.VPS) * V;
+          const uint32_t lv = sg < s_valid ? l_valid : 0;
+          const T *sp = src + seg_base + (uint64_t)sg * g.seg_stride + f0;
+          if (f0 + V <= lv) {
+            x[b].u = ld_stream(reinterpret_cast<const uint4 *>(sp));
+          } else {
+#pragma unroll
+            for (int j = 0; j < V; ++j) x[b].e[j] = f0 + j < lv ? sp[j] : T(0);
+          }
+          at[b] = sg * g.P + f0;
         }
-        uint32_t *w = reinterpret_cast<uint32_t *>(tile + sg * g.P + f0);
-        w[0] = x.u.x;
-        w[1] = x.u.y;
-        w[2] = x.u.z;
-        w[3] = x.u.w;
+#pragma unroll
+        for (int b = 0; b < kLoadBatch; ++b) {
+          if (at[b] == 0xFFFFFFFFu) continue;
+          uint32_t *w = reinterpret_cast<uint32_t *>(tile + at[b]);
+          w[0] = x[b].u.x;
+          w[1] = x[b].u.y;
+          w[2] = x[b].u.z;
+          w[3] = x[b].u.w;
+        }
       }
       __syncthreads();
       // ---- shared memory -> FRACTAL_Z, V consecutive c0 per 16-byte store
@@ -257,14 +282,25 @@ __global__ void __launch_bounds__(kThreads) fz_vec_kernel(unsigned char *__restr
         *reinterpret_cast<uint4 *>(dst + fz_base + (uint64_t)k * dk + r0) = x.u;
       }
     } else {
-      // ---- FRACTAL_Z -> shared memory
-      for (uint32_t u = threadIdx.x; u < n_fz_vec; u += kThreads) {
-        const uint32_t k = u >> g.lrv, r0 = (u & (r_vecs - 1)) * V;
-        const uint32_t base = (r0 >> g.lc0) * A + (r0 & (g.C0 - 1)) * B + k;
-        Pack x;
-        x.u = ld_stream(reinterpret_cast<const uint4 *>(src + fz_base + (uint64_t)k * dk + r0));
+      // ---- FRACTAL_Z -> shared memory, kLoadBatch reads in flight per thread
+      for (uint32_t ub = threadIdx.x; ub < n_fz_vec; ub += kLoadBatch * kThreads) {
+        Pack x[kLoadBatch];
+        uint32_t at[kLoadBatch];
 #pragma unroll
-        for (int j = 0; j < V; ++j) tile[base + j * B] = x.e[j];
+        for (int b = 0; b < kLoadBatch; ++b) {
+          const uint32_t u = ub + b * kThreads;
+          at[b] = 0xFFFFFFFFu;
+          if (u >= n_fz_vec) continue;
+          const uint32_t k = u >> g.lrv, r0 = (u & (r_vecs - 1)) * V;
+          at[b] = (r0 >> g.lc0) * A + (r0 & (g.C0 - 1)) * B + k;
+          x[b].u = ld_stream(reinterpret_cast<const uint4 *>(src + fz_base + (uint64_t)k * dk + r0));
+        }
+#pragma unroll
+        for (int b = 0; b < kLoadBatch; ++b) {
+          if (at[b] == 0xFFFFFFFFu) continue;
+#pragma unroll
+          for (int j = 0; j < V; ++j) tile[at[b] + j * B] = x[b].e[j];
+        }
       }
       __syncthreads();
       // ---- shared memory -> weight, valid range only
@@ -373,6 +409,18 @@ int launch_groups(void *dst, const void *src, const FzGGeom &g, cudaStream_t s) 
 }
 
 constexpr size_t kVecSmemMax = 96 * 1024;  // shared memory of one vectorised tile
+#ifndef DCOPY_FZ_NCHW_NB
+#define DCOPY_FZ_NCHW_NB 64  // largest n block of an NCHW tile (a multiple of 16)
+#endif
+#ifndef DCOPY_FZ_NHWC_BATCH_FAST
+#define DCOPY_FZ_NHWC_BATCH_FAST 1  // NHWC tiles: walk (h, w) first
+#endif
+#ifndef DCOPY_FZ_C1_FAST
+#define DCOPY_FZ_C1_FAST 1  // NCHW tiles: walk the channel blocks first
+#endif
+#ifndef DCOPY_FZ_HWCN_ELEMS
+#define DCOPY_FZ_HWCN_ELEMS 8192  // elements of an HWCN tile (C0 rows x KT)
+#endif
 
 uint32_t log2_of(uint64_t v) {
   uint32_t l = 0;
@@ -427,7 +475,8 @@ int run_vec(int32_t fmt, void *dst, const void *src, int64_t n, int64_t c, int64
   size_t smem;
   if (fmt == kNchw) {
     if ((c * hw * eb) % 16) return DCOPY_OK;  // segment starts must be 16-byte aligned
-    int64_t nb = 16;
+    int64_t nb = DCOPY_FZ_NCHW_NB;
+    while (nb > 16 && n1n0 % nb) nb /= 2;  // whole blocks: the last one may not overrun N1*16
     const int64_t L = c0 * hw, P = pitch(L);
     while (nb > 1 && (size_t)(nb * P * eb) > kVecSmemMax) nb /= 2;
     if ((size_t)(nb * P * eb) > kVecSmemMax) return DCOPY_OK;
@@ -442,7 +491,7 @@ int run_vec(int32_t fmt, void *dst, const void *src, int64_t n, int64_t c, int64
     smem = (size_t)(nb * P * eb);
   } else {  // HWCN, and ND [C, N] as HWCN with H = W = 1
     if ((n * eb) % 16) return DCOPY_OK;
-    int64_t kt = std::max<int64_t>(V, (4096 / c0) / V * V);
+    int64_t kt = std::max<int64_t>(V, (DCOPY_FZ_HWCN_ELEMS / c0) / V * V);
     kt = std::min<int64_t>(kt, n1n0);
     const int64_t P = pitch(kt);
     if ((size_t)(c0 * P * eb) > kVecSmemMax) return DCOPY_OK;
@@ -456,6 +505,9 @@ int run_vec(int32_t fmt, void *dst, const void *src, int64_t n, int64_t c, int64
     ntiles = (uint64_t)c1 * hw * g.ktiles;
     smem = (size_t)(c0 * P * eb);
   }
+  g.C1 = (uint32_t)c1;
+  g.c1_fast = DCOPY_FZ_C1_FAST;
+  g.f_c1 = FastDiv(std::max(1u, g.C1));
   g.VPS = g.L / (uint32_t)V;
   g.f_vps = FastDiv(g.VPS);
   g.f_nblocks = FastDiv(std::max(1u, g.nblocks));
@@ -568,6 +620,7 @@ int run_nhwc(void *dst, const void *src, int64_t n, int64_t c, int64_t h, int64_
   p.s_band = kNi * c0;
   p.fr_batch = p.H1 * kNi * c0;
   p.s_panel = h * w * p.fr_batch;
+  p.batch_fast = DCOPY_FZ_NHWC_BATCH_FAST;
   return frac_launch(p, dst, src, to_fz, stream, "NHWC<->FRACTAL_Z");
 }
 

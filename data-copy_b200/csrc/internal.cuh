@@ -25,6 +25,7 @@ struct FracPlan {
   int64_t times, H, W, nd_row, nd_batch;
   int64_t BH, w0, H1, W1, s_band, s_panel, fr_batch;
   int elem_bytes;
+  bool batch_fast;  // order tiles batch-first (neighbouring batches are adjacent in memory)
 };
 // Launches the shared tiled-format kernels for a plan whose buffers the caller
 // has already checked.

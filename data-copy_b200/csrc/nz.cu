@@ -56,7 +56,27 @@ struct FracGeom {
   uint64_t fr_batch;    // units per tiled batch = H1 * W1 * BH * upr
   uint64_t s_band;      // units between row bands
   uint64_t s_panel;     // units between column blocks
+  uint32_t times;       // batches
+  uint32_t batch_fast;  // 1: consecutive tiles walk the batches first
+  FastDiv f_times;
 };
+
+// Tile index -> (batch t, row band hb, column-block group pg).
+__device__ __forceinline__ void frac_tile(const FracGeom &g, uint32_t tile, uint32_t &t,
+                                          uint32_t &hb, uint32_t &pg) {
+  if (g.batch_fast) {
+    const uint32_t rest = g.f_times.div(tile);
+    t = tile - rest * g.times;
+    const uint32_t q = g.f_pgroups.div(rest);
+    pg = rest - q * g.pgroups;
+    hb = q;
+  } else {
+    const uint32_t q = g.f_pgroups.div(tile);
+    pg = tile - q * g.pgroups;
+    t = g.f_hblocks.div(q);
+    hb = q - t * g.hblocks;
+  }
+}
 
 template <typename T, bool kToFrac>
 __global__ void __launch_bounds__(kThreads) nz_kernel(T *__restrict__ dst,
@@ -67,10 +87,8 @@ __global__ void __launch_bounds__(kThreads) nz_kernel(T *__restrict__ dst,
   pdl_wait();
   pdl_launch_dependents();
   for (uint32_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-    const uint32_t q = g.f_pgroups.div(tile);
-    const uint32_t pg = tile - q * g.pgroups;
-    const uint32_t t = g.f_hblocks.div(q);
-    const uint32_t hb = q - t * g.hblocks;
+    uint32_t t, hb, pg;
+    frac_tile(g, tile, t, hb, pg);
     const uint32_t w1_0 = pg * g.PG, h_0 = hb * g.BH;
     const T *sb = src + (uint64_t)t * (kToFrac ? g.nd_batch : g.fr_batch);
     T *db = dst + (uint64_t)t * (kToFrac ? g.fr_batch : g.nd_batch);
@@ -143,10 +161,8 @@ __global__ void __launch_bounds__(kThreads) nz_smem_kernel(uint4 *__restrict__ d
   const uint32_t panel_units = 1u << panel_shift;
   if (DCOPY_PREFETCH && prefetch && blockIdx.x < ntiles) {
     // L2-prefetch the first tile's source, one prefetch per 128-byte line.
-    const uint32_t q = g.f_pgroups.div(blockIdx.x);
-    const uint32_t pg = blockIdx.x - q * g.pgroups;
-    const uint32_t t = g.f_hblocks.div(q);
-    const uint32_t hb = q - t * g.hblocks;
+    uint32_t t, hb, pg;
+    frac_tile(g, blockIdx.x, t, hb, pg);
     const uint4 *sb = src + (uint64_t)t * (kToFrac ? g.nd_batch : g.fr_batch);
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -166,10 +182,8 @@ __global__ void __launch_bounds__(kThreads) nz_smem_kernel(uint4 *__restrict__ d
   pdl_wait();
   pdl_launch_dependents();
   for (uint32_t tile_id = blockIdx.x; tile_id < ntiles; tile_id += gridDim.x) {
-    const uint32_t q = g.f_pgroups.div(tile_id);
-    const uint32_t pg = tile_id - q * g.pgroups;
-    const uint32_t t = g.f_hblocks.div(q);
-    const uint32_t hb = q - t * g.hblocks;
+    uint32_t t, hb, pg;
+    frac_tile(g, tile_id, t, hb, pg);
     const uint32_t w1_0 = pg * g.PG, h_0 = hb * g.BH;
     const uint4 *sb = src + (uint64_t)t * (kToFrac ? g.nd_batch : g.fr_batch);
     uint4 *db = dst + (uint64_t)t * (kToFrac ? g.fr_batch : g.nd_batch);
@@ -385,6 +399,9 @@ int frac_launch(const FracPlan &p, void *dst, const void *src, bool to_frac,
   g.fr_batch = (uint64_t)p.fr_batch * eb / us;
   g.s_band = (uint64_t)p.s_band * eb / us;
   g.s_panel = (uint64_t)p.s_panel * eb / us;
+  g.times = (uint32_t)p.times;
+  g.batch_fast = p.batch_fast ? 1u : 0u;
+  g.f_times = FastDiv(std::max(1u, g.times));
   const uint64_t ntiles = (uint64_t)p.times * g.hblocks * g.pgroups;
   if (ntiles == 0) return DCOPY_OK;
   if (ntiles > 0xFFFFFFFFull)
