@@ -364,6 +364,29 @@ def run_secondary(torch, dcopy, dev):
     out["config4_nd_to_zz_GBps"] = round(2 * nbytes / (ms / 1e3) / 1e9, 1)
     out["config4_zz_to_nd_GBps"] = round(2 * nbytes / (ms2 / 1e3) / 1e9, 1)
     del nd, nz, zz
+    # FRACTAL_Z (convolution weights): fp16 [2048, 2048, 3, 3], 72 MiB each way; two
+    # weight/FRACTAL_Z pairs alternate so the working set (288 MiB) exceeds L2.
+    n, c, h, w = 2048, 2048, 3, 3
+    wts = [torch.empty(n * c * h * w, dtype=torch.float16, device=dev).normal_()
+           for _ in range(2)]
+    fzs = [torch.empty(c // 16 * h * w * n * 16, dtype=torch.float16, device=dev)
+           for _ in range(2)]
+    fzb = 2 * wts[0].numel() * 2
+    frz = {}
+    for name, fmt, shape in (("NCHW", 0, [n, c, h, w]), ("NHWC", 1, [n, h, w, c]),
+                             ("HWCN", 16, [h, w, c, n])):
+        def to_fz():
+            for i in range(2):
+                dcopy.to_fractal_z(fzs[i], wts[i], fmt, shape, 2, 16)
+
+        def from_fz():
+            for i in range(2):
+                dcopy.from_fractal_z(wts[i], fzs[i], fmt, shape, 2, 16)
+        ms = _time_graph(torch, to_fz, reps=10) / 2
+        ms2 = _time_graph(torch, from_fz, reps=10) / 2
+        frz[name] = [round(fzb / (ms / 1e3) / 1e9, 1), round(fzb / (ms2 / 1e3) / 1e9, 1)]
+    out["fractal_z_fp16_2048x2048x3x3_to_from_GBps"] = frz
+    del wts, fzs
     # Standalone transpose at the 64 MiB maximum (rows 4088 x cols 4104 int32).
     rows, cols = 4088, 4104
     x = torch.empty(rows * cols, dtype=torch.int32, device=dev)

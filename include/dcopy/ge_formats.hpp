@@ -14,7 +14,8 @@
 // Differences, all on purpose:
 //   * formats are the PRIMARY GE formats; C0 comes from TransArgs'
 //     src_c0_format / dst_c0_format fields (GE decodes it from the full format);
-//   * the registry holds {ND, NCHW, NHWC} <-> FRACTAL_NZ / FRACTAL_ZZ and the 12
+//   * the registry holds {ND, NCHW, NHWC} <-> FRACTAL_NZ / FRACTAL_ZZ, {NCHW, HWCN,
+//     NHWC, ND} -> FRACTAL_Z, FRACTAL_Z -> {NCHW, HWCN, NHWC} and the 12
 //     transposes among NCHW/NHWC/HWCN/CHWN; other pairs are
 //     ACL_ERROR_GE_FORMAT_INVALID;
 //   * device work runs on an internal stream and the call returns after the
@@ -42,6 +43,7 @@ constexpr Status ACL_ERROR_GE_SHAPE_INVALID = 145021U;
 constexpr Status ACL_ERROR_GE_DATATYPE_INVALID = 145022U;
 constexpr Status ACL_ERROR_GE_MEMORY_ALLOCATION = 245000U;
 constexpr Status ACL_ERROR_GE_MEMORY_OPERATE_FAILED = 245001U;
+constexpr Status FAILED = 0xFFFFFFFFU;  // GE's generic failure (and GRAPH_FAILED)
 
 // GE enum values (metadef graph/types.h; api/python/ge/ge/graph/types.py).
 enum Format : int32_t {
@@ -87,8 +89,12 @@ namespace detail {
 inline DcopyTransArgs c_args(const TransArgs &a, const void *data) {
   DcopyTransArgs c{};
   c.data = data;
-  c.src_format = a.src_primary_format;
-  c.dst_format = a.dst_primary_format;
+  // Primary formats from their own fields, sub formats (FRACTAL_Z groups) from
+  // the full formats, as GE's transfers read them.
+  c.src_format = (a.src_format & 0xffff00) | (a.src_primary_format & 0xff);
+  c.dst_format = (a.dst_format & 0xffff00) | (a.dst_primary_format & 0xff);
+  c.src_sub_format = a.src_sub_format;
+  c.dst_sub_format = a.dst_sub_format;
   c.src_c0 = a.src_c0_format;
   c.dst_c0 = a.dst_c0_format;
   c.src_shape = a.src_shape.data();
@@ -188,8 +194,9 @@ inline Status TransTensorShape(Format src_format, const std::vector<int64_t> &sr
 }
 
 // The FormatTransfer classes (format_transfer_fractal_nz.h:21-38,
-// format_transfer_fractal_zz.h, format_transfer_transpose.h): TransFormat runs
-// that class's own checks.
+// format_transfer_fractal_zz.h, format_transfer_fractal_z.h, format_transfer_fractal_z_tbe.h,
+// format_transfer_fracz_{nchw,hwcn,nhwc}.h, format_transfer_transpose.h): TransFormat
+// runs that class's own checks.
 template <int kClass>
 class FormatTransferClass {
  public:
@@ -213,6 +220,11 @@ using FormatTransferFractalNzND = FormatTransferClass<DCOPY_TRANSFER_FRACTAL_NZ_
 using FormatTransferTranspose = FormatTransferClass<DCOPY_TRANSFER_TRANSPOSE>;
 using FormatTransferFractalZz = FormatTransferClass<DCOPY_TRANSFER_FRACTAL_ZZ>;
 using FormatTransferFractalZzND = FormatTransferClass<DCOPY_TRANSFER_FRACTAL_ZZ_ND>;
+using FormatTransferFractalZ = FormatTransferClass<DCOPY_TRANSFER_FRACTAL_Z>;
+using FormatTransferFractalZTbe = FormatTransferClass<DCOPY_TRANSFER_FRACTAL_Z_TBE>;
+using FormatTransferFracZNchw = FormatTransferClass<DCOPY_TRANSFER_FRACZ_NCHW>;
+using FormatTransferFracZHwcn = FormatTransferClass<DCOPY_TRANSFER_FRACZ_HWCN>;
+using FormatTransferFracZNhwc = FormatTransferClass<DCOPY_TRANSFER_FRACZ_NHWC>;
 
 // format_transfer_transpose.cc:142-215 with host buffers.
 inline Status TransposeWithShapeCheck(const uint8_t *src, const std::vector<int64_t> &src_shape,

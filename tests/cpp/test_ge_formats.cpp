@@ -106,6 +106,39 @@ static void nd_zz_round_trip(Format src_fmt, const std::vector<int64_t> &nd, Dat
                                                 shape_out) == ACL_ERROR_GE_FORMAT_INVALID);
 }
 
+static void fractal_z_round_trip() {
+  // NCHW fp16 [31, 17, 4, 4] -> FRACTAL_Z [32, 2, 16, 16] (GE's fp16_2c_2n_pad shape) and back.
+  const std::vector<int64_t> nchw = {31, 17, 4, 4}, fz = {32, 2, 16, 16};
+  auto data = random_vec<uint16_t>(31 * 17 * 16, 21);
+  std::vector<uint16_t> expect(32 * 2 * 16 * 16);
+  int64_t written = 0;
+  EXPECT(oracle_to_fz(expect.data(), data.data(), FORMAT_NCHW, nchw.data(), 4, 2, 16, 0,
+                      &written) == 0 && written == (int64_t)expect.size());
+  TransArgs args{reinterpret_cast<uint8_t *>(data.data()), FORMAT_NCHW, FORMAT_FRACTAL_Z,
+                 FORMAT_NCHW, FORMAT_FRACTAL_Z, FORMAT_RESERVED, FORMAT_NCHW, 16, 16, nchw, fz,
+                 DT_FLOAT16};
+  TransResult result;
+  EXPECT(FormatTransferFractalZ().TransFormat(args, result) == SUCCESS);
+  EXPECT(result.length == expect.size() * 2 &&
+         std::memcmp(result.data.get(), expect.data(), result.length) == 0);
+  std::vector<int64_t> shape_out;
+  EXPECT(FormatTransferFractalZ().TransShape(FORMAT_NCHW, nchw, DT_FLOAT16, FORMAT_FRACTAL_Z,
+                                             shape_out) == SUCCESS && shape_out == fz);
+  TransArgs back{reinterpret_cast<uint8_t *>(expect.data()), FORMAT_FRACTAL_Z, FORMAT_NCHW,
+                 FORMAT_FRACTAL_Z, FORMAT_NCHW, FORMAT_RESERVED, FORMAT_RESERVED, 16, 16, fz, nchw,
+                 DT_FLOAT16};
+  TransResult result2;
+  EXPECT(TransDataFormat(back, result2) == SUCCESS);
+  EXPECT(result2.length == data.size() * 2 &&
+         std::memcmp(result2.data.get(), data.data(), result2.length) == 0);
+  // NCHW with the group count 40 in the destination format: N / groups = 0 -> FAILED.
+  TransArgs bad{reinterpret_cast<uint8_t *>(data.data()),
+                static_cast<Format>(FORMAT_NCHW), static_cast<Format>(FORMAT_FRACTAL_Z | (40 << 8)),
+                FORMAT_NCHW, FORMAT_FRACTAL_Z, FORMAT_RESERVED, FORMAT_RESERVED, 16, 16,
+                {1, 1, 1, 1}, {1, 1, 16, 16}, DT_FLOAT16};
+  EXPECT(FormatTransferFractalZ().TransFormat(bad, result) == FAILED);
+}
+
 static void transposes() {
   const struct {
     Format src, dst;
@@ -189,6 +222,7 @@ int main(int argc, char **argv) {
     nd_nz_round_trip(FORMAT_NCHW, {2, 2, 17, 4}, DT_FLOAT, 4, 3);
     nd_nz_round_trip(FORMAT_NHWC, {2, 2, 4, 17}, DT_FLOAT, 4, 4);
     nd_nz_round_trip(FORMAT_ND, {3, 100, 256}, DT_BF16, 2, 5);
+    fractal_z_round_trip();
     nd_zz_round_trip(FORMAT_ND, {2, 3, 4, 33}, DT_UINT8, 1, 32, 6);
     nd_zz_round_trip(FORMAT_NHWC, {2, 2, 17, 4}, DT_FLOAT, 4, 16, 7);
     nd_zz_round_trip(FORMAT_ND, {3, 100, 256}, DT_BF16, 2, 16, 8);
