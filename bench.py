@@ -571,10 +571,12 @@ def main():
         import datetime
         import torch
         import torch.distributed as dist
-        # NCCL's version banner goes to stdout at INFO/VERSION level; rank 0's stdout
-        # must carry exactly one JSON line.
+        # NCCL writes its debug output, the version banner included (printed at the
+        # VERSION and WARN levels), to stdout unless NCCL_DEBUG_FILE names a file;
+        # rank 0's stdout must carry exactly one JSON line.
         if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
             os.environ["NCCL_DEBUG"] = "WARN"
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
