@@ -481,7 +481,7 @@ def run_config5(args, rank, world, local_rank):
                 nonlocal seq
                 seq += 1
                 multi.ring_shift(send, shard, peer, seq)
-                multi.wait_ring(flags, seq, status, timeout_ns=20_000_000_000)
+                multi.wait_ring(flags, seq, status, timeout_ns=2_000_000_000)
 
             for _ in range(2):
                 exchange()

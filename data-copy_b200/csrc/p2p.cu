@@ -56,7 +56,10 @@ __global__ void wait_signal_kernel(const uint32_t *flag, uint32_t value, uint64_
   for (uint64_t it = 0; it < max_iters; ++it) {
     uint32_t v;
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
-    if (v == value) {
+    // Sequence numbers: a signaller may already have moved the flag past `value`
+    // (a ring neighbour one step ahead), which counts as arrived.  The signed
+    // difference keeps the test right across 2^32 wrap-around.
+    if ((int32_t)(v - value) >= 0) {
       result = 0;
       break;
     }

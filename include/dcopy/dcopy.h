@@ -399,11 +399,13 @@ int dcopy_ipc_close_handle(void *base_ptr);
 
 /* Completion flags.  dcopy_signal stores `value` to *flag with release
  * semantics at system scope after all earlier work on `stream` (the flag may
- * live on another GPU).  dcopy_wait_signal launches a one-thread kernel that
- * waits, with acquire loads, until *flag == value, at most timeout_ns
- * nanoseconds (and a fixed iteration bound), then writes 0 (seen) or 1 (timed
- * out) to *status (device memory) and returns; later work on `stream` runs
- * after it either way.  The wait must not run on the same GPU as the kernel
+ * live on another GPU).  Flag values are sequence numbers that only grow.
+ * dcopy_wait_signal launches a one-thread kernel that waits, with acquire
+ * loads, until *flag has reached or passed value ((int32_t)(*flag - value) >= 0,
+ * so a signaller already a step ahead counts), at most timeout_ns nanoseconds
+ * (and a fixed iteration bound), then writes 0 (seen) or 1 (timed out) to
+ * *status (device memory) and returns; later work on `stream` runs after it
+ * either way.  The wait must not run on the same GPU as the kernel
  * that sets the flag, unless that kernel is already complete. */
 int dcopy_signal(uint32_t *flag, uint32_t value, dcopy_stream_t stream);
 int dcopy_wait_signal(const uint32_t *flag, uint32_t value, uint64_t timeout_ns,

@@ -37,6 +37,27 @@ def test_wait_signal_bounded(torch_cuda, dcopy):
     assert status.item() == 0 and flag.item() == 1
 
 
+def test_wait_signal_counts_a_flag_already_past(torch_cuda, dcopy):
+    """A ring neighbour one step ahead has already moved the flag past the awaited
+    sequence number: the wait must see it as arrived (not spin to its timeout)."""
+    torch = torch_cuda
+    flag = torch.zeros(1, dtype=torch.int32, device="cuda")
+    status = torch.full((1,), 7, dtype=torch.int32, device="cuda")
+    dcopy.signal(flag, 6)
+    dcopy.wait_signal(flag, 5, 2_000_000_000, status)
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    # Across the 2^32 wrap: 0x00000001 is past 0xFFFFFFFF.
+    dcopy.signal(flag, 1)
+    dcopy.wait_signal(flag, 0xFFFFFFFF, 2_000_000_000, status)
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    # A flag behind the awaited value still times out (2 ms).
+    dcopy.wait_signal(flag, 3, 2_000_000, status)
+    torch.cuda.synchronize()
+    assert status.item() == 1
+
+
 def test_p2p_copy_same_device(torch_cuda, dcopy):
     torch = torch_cuda
     src = torch.randint(0, 255, (1 << 20,), dtype=torch.uint8, device="cuda")
