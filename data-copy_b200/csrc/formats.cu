@@ -269,8 +269,9 @@ int fractal_zz_nd_format(const DcopyTransArgs *a, void *dst, uint64_t cap, uint6
   return rc ? rc : store_length(len, bytes);
 }
 
-// Transpose (transpose.cc:142-197) as an N-D box copy: the destination is
-// contiguous and the source strides are the permuted row-major heads.
+// Transpose (transpose.cc:142-197) as a permuted copy (permute.cu): the
+// destination is contiguous and the source strides are the permuted row-major
+// heads.
 int transpose_impl(void *dst, const void *src, const int64_t *shape, const int64_t *perm,
                    int rank, int32_t data_type, uint64_t cap, uint64_t *len, dcopy_stream_t s) {
   const int32_t size = type_size(data_type);
@@ -323,7 +324,12 @@ int transpose_impl(void *dst, const void *src, const int64_t *shape, const int64
   }
   if (m > 5)
     return set_error(DCOPY_ERR_UNSUPPORTED, "Transpose: %d non-trivial dims (at most 5)", m);
-  const int rc = dcopy_copy_nd(dst, src, m, ms, mss, mds, (uint32_t)size, s);
+  int rc = check_device_span(src, bytes, "Transpose src");
+  if (!rc) rc = check_device_span(dst, bytes, "Transpose dst");
+  if (!rc) rc = check_disjoint(src, bytes, dst, bytes, "Transpose");
+  if (!rc && ((uintptr_t)src | (uintptr_t)dst) % (uint32_t)size)
+    rc = set_error(DCOPY_ERR_PARAM_INVALID, "Transpose: buffers must be aligned to the element");
+  if (!rc) rc = permute_copy(dst, src, m, ms, mss, mds, size, s);
   return rc ? rc : store_length(len, bytes);
 }
 

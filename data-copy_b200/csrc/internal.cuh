@@ -55,6 +55,12 @@ int from_fz_check(const int64_t *src_shape, int src_rank, int32_t fmt, const int
 int from_fz(void *dst, const void *src, int32_t fmt, const int64_t *dst_shape, int rank, int eb,
             int64_t c0, dcopy_stream_t stream);
 
+// dst (contiguous) = the m-D (m <= 5) strided view of src: sizes and strides in
+// elements of eb bytes, dst strides the row-major heads of `size`.  Buffers are
+// checked by the caller.
+int permute_copy(void *dst, const void *src, int m, const uint64_t *size, const int64_t *ss,
+                 const int64_t *ds, int eb, dcopy_stream_t stream);
+
 // The reference's pretranspose workflow (asc:144-146): x -> B with RunTiles<1>,
 // then B -> y with RunTiles<2>, through a B buffer of scratch_bytes bytes that
 // the caller of this function guarantees is device memory (it is not checked).
