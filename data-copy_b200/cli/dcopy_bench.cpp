@@ -20,13 +20,18 @@
 //                  [--device D] [--peak GBPS]
 //       Convolution weights: NCHW / NHWC / HWCN -> FRACTAL_Z -> back, each
 //       round trip verified; one JSON line per format.
+//   dcopy_bench transpose --shape A,B,C,D --perm P0,P1,P2,P3 [--eb B] [--reps R]
+//                         [--device D] [--peak GBPS]
+//       GE Transpose (dcopy_transpose) of a dense tensor, verified against a host
+//       restatement; one JSON line.
 //   dcopy_bench p2p [--mib M] [--reps R] [--device D] [--peer P] [--peak GBPS]
 //       NVLink between two GPUs: dcopy_p2p_copy as a push (launched on the
 //       sending GPU) and as a pull (launched on the receiving GPU), and the copy
 //       engine, each with both GPUs sending at once and with one sending.
 //
-// Timing: CUDA events around each launch; a 512 MiB write between reps flushes
-// the 126 MB L2, so every rep reads cold data.
+// Timing: CUDA events around each launch; a 512 MiB read between reps (load-only
+// mode, so L2 holds only clean lines) evicts the 126 MB L2: every rep reads cold
+// data and no flush write-back falls inside the timed region.
 #include <cuda_runtime.h>
 #include <sys/stat.h>
 
@@ -89,6 +94,19 @@ struct DevBuf {
   DevBuf &operator=(const DevBuf &) = delete;
 };
 
+// Evicts the measured buffers from L2 by reading `flush` (512 MiB) with the
+// library's load-only mode: the lines left in L2 are clean, so no write-back of
+// flush data lands inside the next timed region (a memset would leave ~126 MB of
+// dirty lines to be written back while the measured kernel runs).
+void read_flush(DevBuf &flush, cudaStream_t s) {
+  DataCopyTiling t{};  // the flush buffer's contents are never used
+  CheckD(dcopy_plan_tiling(4088, 4104, 240, 0, &t));  // 64 MiB of int32, load only
+  const size_t chunk = size_t(4088) * 4104 * 4;
+  for (size_t off = 0; off + chunk <= flush.n; off += size_t(64) << 20)
+    CheckD(dcopy_datacopy_contiguous(static_cast<char *>(flush.p) + off, nullptr, &t,
+                                     reinterpret_cast<dcopy_stream_t>(s)));
+}
+
 // Times `fn` (one or more launches on `s`) `reps` times with an L2 flush between reps.
 template <typename F>
 std::vector<double> time_reps(F fn, int reps, cudaStream_t s, DevBuf &flush) {
@@ -97,7 +115,7 @@ std::vector<double> time_reps(F fn, int reps, cudaStream_t s, DevBuf &flush) {
   Check(cudaEventCreate(&b), "event");
   std::vector<double> us;
   for (int r = 0; r < reps; ++r) {
-    Check(cudaMemsetAsync(flush.p, r & 0xFF, flush.n, s), "flush");
+    read_flush(flush, s);
     Check(cudaEventRecord(a, s), "record");
     fn();
     Check(cudaEventRecord(b, s), "record");
@@ -416,6 +434,70 @@ int run_fz(const Args &a) {
   return 0;
 }
 
+// ---- transpose -----------------------------------------------------------------------
+
+std::vector<int64_t> parse_list(const std::string &text) {
+  std::vector<int64_t> v;
+  std::stringstream ss(text);
+  std::string item;
+  while (std::getline(ss, item, ',')) v.push_back(std::stoll(item));
+  return v;
+}
+
+int run_transpose(const Args &a) {
+  const std::vector<int64_t> shape = parse_list(a.str("shape", "32,256,56,56"));
+  const std::vector<int64_t> perm = parse_list(a.str("perm", "0,2,3,1"));
+  const int eb = int(a.num("eb", 2));
+  const int reps = int(a.num("reps", 10));
+  const double peak = a.num("peak", 6543.4);
+  const int rank = int(shape.size());
+  if (perm.size() != shape.size()) throw std::runtime_error("--perm and --shape differ in rank");
+  const int32_t dt = eb == 1 ? 4 : eb == 2 ? 1 : eb == 4 ? 0 : eb == 8 ? 9 : 17;
+  Check(cudaSetDevice(int(a.num("device", 0))), "cudaSetDevice");
+  cudaStream_t s;
+  Check(cudaStreamCreate(&s), "stream");
+  dcopy_stream_t ds = reinterpret_cast<dcopy_stream_t>(s);
+  uint64_t n = 1;
+  for (auto d : shape) n *= uint64_t(d);
+  const uint64_t bytes = n * eb;
+  std::vector<uint8_t> host(bytes), out(bytes), expect(bytes);
+  uint64_t x = 0x9E3779B97F4A7C15ull;
+  for (auto &v : host) {
+    x ^= x << 13;
+    x ^= x >> 7;
+    x ^= x << 17;
+    v = uint8_t(x);
+  }
+  // Host restatement: destination odometer over the permuted shape.
+  std::vector<int64_t> heads(rank), dshape(rank), idx(rank, 0);
+  for (int i = rank - 1; i >= 0; --i) heads[i] = i == rank - 1 ? 1 : shape[i + 1] * heads[i + 1];
+  for (int i = 0; i < rank; ++i) dshape[i] = shape[perm[i]];
+  for (uint64_t di = 0; di < n; ++di) {
+    int64_t off = 0;
+    for (int k = 0; k < rank; ++k) off += idx[k] * heads[perm[k]];
+    std::memcpy(&expect[di * eb], &host[off * eb], eb);
+    for (int k = rank - 1; k >= 0; --k) {
+      if (++idx[k] < dshape[k]) break;
+      idx[k] = 0;
+    }
+  }
+  DevBuf src(bytes), dst(bytes), flush(512ull << 20);
+  Check(cudaMemcpy(src.p, host.data(), bytes, cudaMemcpyHostToDevice), "H2D");
+  CheckD(dcopy_transpose(dst.p, src.p, shape.data(), perm.data(), rank, dt, ds));
+  Check(cudaMemcpy(out.data(), dst.p, bytes, cudaMemcpyDeviceToHost), "D2H");
+  if (out != expect) throw std::runtime_error("transpose result differs from the host restatement");
+  auto t = time_reps(
+      [&] { CheckD(dcopy_transpose(dst.p, src.p, shape.data(), perm.data(), rank, dt, ds)); },
+      reps, s, flush);
+  const double g = 2.0 * bytes / (median(t) * 1e3);
+  std::cout << "{\"transpose\": \"" << a.str("shape", "32,256,56,56") << " perm "
+            << a.str("perm", "0,2,3,1") << "\", \"elem_bytes\": " << eb
+            << ", \"us\": " << median(t) << ", \"GBps\": " << g
+            << ", \"frac_of_peak\": " << g / peak << ", \"verified\": true}" << std::endl;
+  cudaStreamDestroy(s);
+  return 0;
+}
+
 // ---- p2p --------------------------------------------------------------------------
 
 int run_p2p(const Args &a) {
@@ -519,7 +601,7 @@ int run_p2p(const Args &a) {
 
 int main(int argc, char **argv) {
   try {
-    if (argc < 2) throw std::runtime_error("usage: dcopy_bench sweep|standalone|nz|fz|p2p [options]");
+    if (argc < 2) throw std::runtime_error("usage: dcopy_bench sweep|standalone|nz|fz|transpose|p2p [options]");
     const std::string cmd = argv[1];
     Args a(argc, argv);
     if (cmd == "sweep") return run_sweep(a);
@@ -527,6 +609,7 @@ int main(int argc, char **argv) {
     if (cmd == "nz") return run_nz(a);
     if (cmd == "p2p") return run_p2p(a);
     if (cmd == "fz") return run_fz(a);
+    if (cmd == "transpose") return run_transpose(a);
     throw std::runtime_error("unknown command " + cmd);
   } catch (const std::exception &e) {
     std::cerr << "dcopy_bench: " << e.what() << '\n';
