@@ -29,6 +29,15 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kMaxBatch = 3;
 constexpr int kMaxRowDims = 4;
+#ifndef DCOPY_PERM_PACKED
+#define DCOPY_PERM_PACKED 1  // aligned tiles: packed [e][d] shared layout (0: element gather)
+#endif
+#ifndef DCOPY_PERM_TD2
+#define DCOPY_PERM_TD2 64  // 2-byte elements: tile rows (destination axis)
+#endif
+#ifndef DCOPY_PERM_TE2
+#define DCOPY_PERM_TE2 64  // 2-byte elements: tile columns (source axis)
+#endif
 
 // ---- rows ----------------------------------------------------------------------
 
@@ -184,6 +193,118 @@ __global__ void __launch_bounds__(kThreads) perm_tile_kernel(T *__restrict__ dst
   }
 }
 
+// Aligned tiles: G = 4/eb source rows (eb <= 4) are read as 16-byte vectors
+// along e and interleaved with byte permutes into 32-bit words, so shared memory
+// holds the tile already transposed, [e][d] with d contiguous, and each 16-byte
+// destination vector is one shared-memory load.  A warp reads 8 consecutive
+// e-vectors (128 contiguous bytes) of 4 row groups; the 16-byte chunks of each
+// shared row are XOR-swizzled with the row's e-vector index, so the word stores
+// of those 32 lanes hit 32 distinct banks and the chunk loads stay conflict-free.
+template <typename T, int V, int G, int TD, int TE>
+__global__ void __launch_bounds__(kThreads) perm_tile_packed_kernel(T *__restrict__ dst,
+                                                                    const T *__restrict__ src,
+                                                                    PermTGeom g,
+                                                                    uint32_t ntiles) {
+  static_assert(V * sizeof(T) == 16, "16-byte vectors");
+  static_assert(G * sizeof(T) == 4 || G == 1, "a row group fills one 32-bit word");
+  constexpr uint32_t kGroups = TD / G, kEv = TE / V, kDv = TD / V;
+  static_assert(kEv % 8 == 0 && kGroups % 4 == 0 && (kDv & (kDv - 1)) == 0, "tile shape");
+  union Vec {
+    uint4 u;
+    uint32_t w[4];
+    T e[V];
+  };
+  extern __shared__ __align__(16) unsigned char perm_smem[];
+  T *tile = reinterpret_cast<T *>(perm_smem);
+  // Element offset of (row r of the [e][d] tile, column d): chunk-swizzled.
+  auto at = [](uint32_t r, uint32_t d) {
+    return r * TD + (((d / V) ^ ((r / V) & (kDv - 1))) * V) + d % V;
+  };
+  pdl_trigger_at_entry();
+  pdl_wait();
+  pdl_launch_dependents();
+  for (uint32_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
+    const uint32_t q = g.f_etiles.div(t), et = t - q * g.etiles;
+    uint32_t b = g.f_dtiles.div(q);
+    const uint32_t dt = q - b * g.dtiles;
+    uint64_t sb = 0, db = 0;
+#pragma unroll
+    for (int k = kMaxBatch - 1; k >= 0; --k) {
+      if (k < (int)g.nb) {
+        const uint32_t qq = g.f_bsize[k].div(b);
+        const uint32_t idx = b - qq * g.bsize[k];
+        sb += (uint64_t)idx * g.bss[k];
+        db += (uint64_t)idx * g.bds[k];
+        b = qq;
+      }
+    }
+    const uint32_t d0 = dt * TD, e0 = et * TE;
+    const uint32_t dw = min((uint32_t)TD, g.D - d0), ew = min((uint32_t)TE, g.E - e0);
+    // ---- G source rows x V elements -> V words (or elements) of the [e][d] tile
+    for (uint32_t u = threadIdx.x; u < kGroups * kEv; u += kThreads) {
+      const uint32_t lane = u & 31, wu = u >> 5;
+      const uint32_t ev = (wu % (kEv / 8)) * 8 + (lane & 7);
+      const uint32_t dg = (wu / (kEv / 8)) * 4 + (lane >> 3);
+      const uint32_t e = ev * V, d = dg * G;
+      if (e >= ew || d >= dw) continue;
+      Vec x[G];
+#pragma unroll
+      for (int k = 0; k < G; ++k) {
+        if (d + k < dw) {
+          const T *sp = src + sb + (uint64_t)(d0 + d + k) * g.s_d + e0 + e;
+          if (e + V <= ew) {
+            x[k].u = ld_stream(reinterpret_cast<const uint4 *>(sp));
+          } else {
+#pragma unroll
+            for (int j = 0; j < V; ++j) x[k].e[j] = e + j < ew ? sp[j] : T();
+          }
+        } else {
+          x[k].u = make_uint4(0, 0, 0, 0);
+        }
+      }
+      if (G == 1) {
+#pragma unroll
+        for (int j = 0; j < V; ++j) tile[at(e + j, d)] = x[0].e[j];
+      } else if (G == 2) {  // 2-byte elements: word = (row d, row d+1) of column e+j
+#pragma unroll
+        for (int j = 0; j < V; ++j)
+          *reinterpret_cast<uint32_t *>(tile + at(e + j, d)) =
+              __byte_perm(x[0].w[j / 2], x[1].w[j / 2], (j & 1) ? 0x7632 : 0x5410);
+      } else {  // 1-byte elements: word = byte j of rows d..d+3
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t lo01 = __byte_perm(x[0].w[i], x[1].w[i], 0x5140);
+          const uint32_t hi01 = __byte_perm(x[0].w[i], x[1].w[i], 0x7362);
+          const uint32_t lo23 = __byte_perm(x[2].w[i], x[3].w[i], 0x5140);
+          const uint32_t hi23 = __byte_perm(x[2].w[i], x[3].w[i], 0x7362);
+          const uint32_t r = e + 4 * i;
+          *reinterpret_cast<uint32_t *>(tile + at(r, d)) = __byte_perm(lo01, lo23, 0x5410);
+          *reinterpret_cast<uint32_t *>(tile + at(r + 1, d)) = __byte_perm(lo01, lo23, 0x7632);
+          *reinterpret_cast<uint32_t *>(tile + at(r + 2, d)) = __byte_perm(hi01, hi23, 0x5410);
+          *reinterpret_cast<uint32_t *>(tile + at(r + 3, d)) = __byte_perm(hi01, hi23, 0x7632);
+        }
+      }
+    }
+    __syncthreads();
+    // ---- [e][d] tile -> destination rows along d, one 16-byte load per vector
+    for (uint32_t u = threadIdx.x; u < TE * kDv; u += kThreads) {
+      const uint32_t c = u / kDv, d = (u - c * kDv) * V;
+      if (c >= ew || d >= dw) continue;
+      Vec x;
+      x.u = *reinterpret_cast<const uint4 *>(tile + at(c, d));
+      T *dp = dst + db + (uint64_t)(e0 + c) * g.t_e + d0 + d;
+      if (d + V <= dw) {
+        *reinterpret_cast<uint4 *>(dp) = x.u;
+      } else {
+#pragma unroll
+        for (int j = 0; j < V; ++j)
+          if (d + j < dw) dp[j] = x.e[j];
+      }
+    }
+    __syncthreads();
+  }
+}
+
 template <typename T>
 int launch_rows(void *dst, const void *src, const PermRGeom &g0, uint64_t outer_ss,
                 cudaStream_t s) {
@@ -263,19 +384,54 @@ int run_rows(void *dst, const void *src, int m, const uint64_t *size, const int6
   }
 }
 
-template <typename T, int V>
-int run_tiles_t(void *dst, const void *src, int m, const uint64_t *size, const int64_t *ss,
-                const int64_t *ds, int e, cudaStream_t s) {
-  constexpr int eb = sizeof(T);
+// Tile geometry shared by both tile kernels; *ntiles = 0 when there is nothing to do.
+int tile_geometry(int m, const uint64_t *size, const int64_t *ss, const int64_t *ds, int e,
+                  uint32_t TD, uint32_t TE, PermTGeom *g, uint64_t *ntiles) {
   const int d = m - 1;
-  PermTGeom g{};
+  *g = PermTGeom{};
   if (size[d] > 0x7FFFFFFFull || size[e] > 0x7FFFFFFFull)
     return set_error(DCOPY_ERR_UNSUPPORTED, "transpose: dims beyond 32-bit tile indexing");
-  g.D = (uint32_t)size[d];
-  g.E = (uint32_t)size[e];
+  g->D = (uint32_t)size[d];
+  g->E = (uint32_t)size[e];
+  g->TD = TD;
+  g->TE = TE;
+  g->dtiles = (g->D + TD - 1) / TD;
+  g->etiles = (g->E + TE - 1) / TE;
+  g->f_dtiles = FastDiv(std::max(1u, g->dtiles));
+  g->f_etiles = FastDiv(std::max(1u, g->etiles));
+  g->s_d = (uint64_t)ss[d];
+  g->t_e = (uint64_t)ds[e];
+  uint64_t batches = 1;
+  int nb = 0;
+  for (int k = 0; k < m; ++k) {
+    if (k == d || k == e) continue;
+    if (size[k] > 0xFFFFFFFFull || nb == kMaxBatch)
+      return set_error(DCOPY_ERR_UNSUPPORTED, "transpose: too many or too large batch dims");
+    g->bsize[nb] = (uint32_t)size[k];
+    g->f_bsize[nb] = FastDiv(g->bsize[nb]);
+    g->bss[nb] = (uint64_t)ss[k];
+    g->bds[nb] = (uint64_t)ds[k];
+    batches *= size[k];
+    ++nb;
+  }
+  g->nb = (uint32_t)nb;
+  *ntiles = batches * g->dtiles * g->etiles;
+  if (*ntiles > 0xFFFFFFFFull)
+    return set_error(DCOPY_ERR_UNSUPPORTED, "transpose: %llu tiles exceed 32-bit indexing",
+                     (unsigned long long)*ntiles);
+  return DCOPY_OK;
+}
+
+// Element-access tiles (unaligned rows, 16-byte elements).
+template <typename T>
+int run_tiles_elem(void *dst, const void *src, int m, const uint64_t *size, const int64_t *ss,
+                   const int64_t *ds, int e, cudaStream_t s) {
+  constexpr int eb = sizeof(T);
   const uint32_t edge = PermEdge<T>::value;
-  g.TD = edge;
-  g.TE = edge;
+  PermTGeom g;
+  uint64_t ntiles = 0;
+  int rc = tile_geometry(m, size, ss, ds, e, edge, edge, &g, &ntiles);
+  if (rc || ntiles == 0) return rc;
   if (eb >= 4) {
     g.P = edge + 1;  // odd element pitch
   } else {           // odd word pitch, whole words per row
@@ -283,32 +439,44 @@ int run_tiles_t(void *dst, const void *src, int m, const uint64_t *size, const i
     if (words % 2 == 0) ++words;
     g.P = (uint32_t)(words * 4 / eb);
   }
-  g.dtiles = (g.D + g.TD - 1) / g.TD;
-  g.etiles = (g.E + g.TE - 1) / g.TE;
-  g.f_dtiles = FastDiv(g.dtiles);
-  g.f_etiles = FastDiv(g.etiles);
-  g.s_d = (uint64_t)ss[d];
-  g.t_e = (uint64_t)ds[e];
-  uint64_t batches = 1;
-  int nb = 0;
-  for (int k = 0; k < m; ++k) {
-    if (k == d || k == e) continue;
-    if (size[k] > 0xFFFFFFFFull || nb == kMaxBatch)
-      return set_error(DCOPY_ERR_UNSUPPORTED, "transpose: too many or too large batch dims");
-    g.bsize[nb] = (uint32_t)size[k];
-    g.f_bsize[nb] = FastDiv(g.bsize[nb]);
-    g.bss[nb] = (uint64_t)ss[k];
-    g.bds[nb] = (uint64_t)ds[k];
-    batches *= size[k];
-    ++nb;
+  return launch_tiles<T, 1>(dst, src, g, (uint32_t)ntiles, s);
+}
+
+// 16-byte-vector tiles gathering element by element from shared memory.
+template <typename T, int V>
+int run_tiles_vec(void *dst, const void *src, int m, const uint64_t *size, const int64_t *ss,
+                  const int64_t *ds, int e, cudaStream_t s) {
+  constexpr int eb = sizeof(T);
+  const uint32_t edge = PermEdge<T>::value;
+  PermTGeom g;
+  uint64_t ntiles = 0;
+  int rc = tile_geometry(m, size, ss, ds, e, edge, edge, &g, &ntiles);
+  if (rc || ntiles == 0) return rc;
+  if (eb >= 4) {
+    g.P = edge + 1;
+  } else {
+    int64_t words = ((int64_t)edge * eb + 3) / 4;
+    if (words % 2 == 0) ++words;
+    g.P = (uint32_t)(words * 4 / eb);
   }
-  g.nb = (uint32_t)nb;
-  const uint64_t ntiles = batches * g.dtiles * g.etiles;
-  if (ntiles == 0) return DCOPY_OK;
-  if (ntiles > 0xFFFFFFFFull)
-    return set_error(DCOPY_ERR_UNSUPPORTED, "transpose: %llu tiles exceed 32-bit indexing",
-                     (unsigned long long)ntiles);
   return launch_tiles<T, V>(dst, src, g, (uint32_t)ntiles, s);
+}
+
+// 16-byte-vector tiles with rows packed into words in shared memory.
+template <typename T, int TD, int TE>
+int run_tiles_packed(void *dst, const void *src, int m, const uint64_t *size, const int64_t *ss,
+                     const int64_t *ds, int e, cudaStream_t s) {
+  constexpr int V = 16 / sizeof(T);
+  constexpr int G = sizeof(T) >= 4 ? 1 : 4 / sizeof(T);
+  PermTGeom g;
+  uint64_t ntiles = 0;
+  int rc = tile_geometry(m, size, ss, ds, e, TD, TE, &g, &ntiles);
+  if (rc || ntiles == 0) return rc;
+  const size_t smem = (size_t)TD * TE * sizeof(T);
+  const uint32_t grid = std::max(1u, std::min<uint32_t>((uint32_t)ntiles, 0x7FFFFFFFu));
+  return launch(perm_tile_packed_kernel<T, V, G, TD, TE>, grid, dim3(kThreads), smem, s,
+                "perm_tile_packed_kernel", static_cast<T *>(dst), static_cast<const T *>(src), g,
+                (uint32_t)ntiles);
 }
 
 }  // namespace
@@ -329,20 +497,30 @@ int permute_copy(void *dst, const void *src, int m, const uint64_t *size, const 
   for (int k = 0; k < m; ++k)
     if (k != m - 1 && k != e) key |= (uint64_t)ss[k] * eb | (uint64_t)ds[k] * eb;
   const bool vec = key % 16 == 0 && eb <= 16;
+  if (!DCOPY_PERM_PACKED && vec) {
+    switch (eb) {
+      case 1: return run_tiles_vec<uint8_t, 16>(dst, src, m, size, ss, ds, e, s);
+      case 2: return run_tiles_vec<uint16_t, 8>(dst, src, m, size, ss, ds, e, s);
+      case 4: return run_tiles_vec<uint32_t, 4>(dst, src, m, size, ss, ds, e, s);
+      case 8: return run_tiles_vec<uint2, 2>(dst, src, m, size, ss, ds, e, s);
+      default: break;
+    }
+  }
   switch (eb) {
     case 1:
-      return vec ? run_tiles_t<uint8_t, 16>(dst, src, m, size, ss, ds, e, s)
-                 : run_tiles_t<uint8_t, 1>(dst, src, m, size, ss, ds, e, s);
+      return vec ? run_tiles_packed<uint8_t, 128, 128>(dst, src, m, size, ss, ds, e, s)
+                 : run_tiles_elem<uint8_t>(dst, src, m, size, ss, ds, e, s);
     case 2:
-      return vec ? run_tiles_t<uint16_t, 8>(dst, src, m, size, ss, ds, e, s)
-                 : run_tiles_t<uint16_t, 1>(dst, src, m, size, ss, ds, e, s);
+      return vec ? run_tiles_packed<uint16_t, DCOPY_PERM_TD2, DCOPY_PERM_TE2>(dst, src, m, size,
+                                                                             ss, ds, e, s)
+                 : run_tiles_elem<uint16_t>(dst, src, m, size, ss, ds, e, s);
     case 4:
-      return vec ? run_tiles_t<uint32_t, 4>(dst, src, m, size, ss, ds, e, s)
-                 : run_tiles_t<uint32_t, 1>(dst, src, m, size, ss, ds, e, s);
+      return vec ? run_tiles_packed<uint32_t, 64, 64>(dst, src, m, size, ss, ds, e, s)
+                 : run_tiles_elem<uint32_t>(dst, src, m, size, ss, ds, e, s);
     case 8:
-      return vec ? run_tiles_t<uint2, 2>(dst, src, m, size, ss, ds, e, s)
-                 : run_tiles_t<uint2, 1>(dst, src, m, size, ss, ds, e, s);
-    case 16: return run_tiles_t<uint4, 1>(dst, src, m, size, ss, ds, e, s);
+      return vec ? run_tiles_packed<uint2, 32, 32>(dst, src, m, size, ss, ds, e, s)
+                 : run_tiles_elem<uint2>(dst, src, m, size, ss, ds, e, s);
+    case 16: return run_tiles_elem<uint4>(dst, src, m, size, ss, ds, e, s);
     default:
       return set_error(DCOPY_ERR_DATATYPE_INVALID, "transpose: element of %d bytes", eb);
   }
