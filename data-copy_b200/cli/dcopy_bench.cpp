@@ -24,6 +24,10 @@
 //                         [--device D] [--peak GBPS]
 //       GE Transpose (dcopy_transpose) of a dense tensor, verified against a host
 //       restatement; one JSON line.
+//   dcopy_bench nd [--sizes A,B,C[,D,E]] [--eb B] [--src-pad P] [--dst-pad Q] [--reps R]
+//                  [--device D] [--peak GBPS]
+//       DataCopyNddma box (dcopy_copy_nd) between padded views, verified; one JSON
+//       line.  DCOPY_ND_TMA=0 in the environment selects the load/store kernels.
 //   dcopy_bench p2p [--mib M] [--reps R] [--device D] [--peer P] [--peak GBPS]
 //       NVLink between two GPUs: dcopy_p2p_copy as a push (launched on the
 //       sending GPU) and as a pull (launched on the receiving GPU), and the copy
@@ -498,6 +502,77 @@ int run_transpose(const Args &a) {
   return 0;
 }
 
+// ---- nd -----------------------------------------------------------------------------
+
+// A DataCopyNddma box (dcopy_copy_nd): `sizes` elements, source and destination
+// strides from extents padded by --src-pad / --dst-pad elements on every axis but
+// the outermost.  Verified element by element (box and untouched gaps).
+int run_nd(const Args &a) {
+  const std::vector<int64_t> sz = parse_list(a.str("sizes", "64,1024,1024"));
+  const int eb = int(a.num("eb", 2));
+  const int64_t sp = int64_t(a.num("src-pad", 8)), dp = int64_t(a.num("dst-pad", 0));
+  const int reps = int(a.num("reps", 10));
+  const double peak = a.num("peak", 6543.4);
+  const int nd = int(sz.size());
+  std::vector<uint64_t> sizes(sz.begin(), sz.end());
+  std::vector<int64_t> ss(nd), ds(nd);
+  ss[nd - 1] = ds[nd - 1] = 1;
+  for (int k = nd - 2; k >= 0; --k) {
+    ss[k] = ss[k + 1] * (sz[k + 1] + sp);
+    ds[k] = ds[k + 1] * (sz[k + 1] + dp);
+  }
+  const uint64_t src_n = uint64_t(ss[0]) * sz[0], dst_n = uint64_t(ds[0]) * sz[0];
+  uint64_t n = 1;
+  for (auto d : sz) n *= uint64_t(d);
+  Check(cudaSetDevice(int(a.num("device", 0))), "cudaSetDevice");
+  cudaStream_t s;
+  Check(cudaStreamCreate(&s), "stream");
+  dcopy_stream_t dsm = reinterpret_cast<dcopy_stream_t>(s);
+  std::vector<uint8_t> host(src_n * eb), out(dst_n * eb);
+  uint64_t x = 0x9E3779B97F4A7C15ull;
+  for (auto &v : host) {
+    x ^= x << 13;
+    x ^= x >> 7;
+    x ^= x << 17;
+    v = uint8_t(x);
+  }
+  DevBuf src(src_n * eb), dst(dst_n * eb), flush(512ull << 20);
+  Check(cudaMemcpy(src.p, host.data(), host.size(), cudaMemcpyHostToDevice), "H2D");
+  Check(cudaMemset(dst.p, 0xA5, dst_n * eb), "memset");
+  CheckD(dcopy_copy_nd(dst.p, src.p, nd, sizes.data(), ss.data(), ds.data(), eb, dsm));
+  Check(cudaMemcpy(out.data(), dst.p, out.size(), cudaMemcpyDeviceToHost), "D2H");
+  std::vector<uint8_t> expect(dst_n * eb, 0xA5);
+  std::vector<int64_t> idx(nd, 0);
+  for (uint64_t e = 0; e < n; ++e) {
+    int64_t so = 0, doff = 0;
+    for (int k = 0; k < nd; ++k) {
+      so += idx[k] * ss[k];
+      doff += idx[k] * ds[k];
+    }
+    std::memcpy(&expect[doff * eb], &host[so * eb], eb);
+    for (int k = nd - 1; k >= 0; --k) {
+      if (++idx[k] < sz[k]) break;
+      idx[k] = 0;
+    }
+  }
+  if (out != expect) throw std::runtime_error("copy_nd result differs from the host restatement");
+  auto t = time_reps(
+      [&] { CheckD(dcopy_copy_nd(dst.p, src.p, nd, sizes.data(), ss.data(), ds.data(), eb, dsm)); },
+      reps, s, flush);
+  uint32_t tma_err = 0;
+  CheckD(dcopy_tma_error(&tma_err));
+  if (tma_err) throw std::runtime_error("TMA box copy gave up a wait");
+  const double g = 2.0 * n * eb / (median(t) * 1e3);
+  const char *sel = std::getenv("DCOPY_ND_TMA");
+  std::cout << "{\"nd\": \"" << a.str("sizes", "64,1024,1024") << "\", \"src_pad\": " << sp
+            << ", \"dst_pad\": " << dp << ", \"elem_bytes\": " << eb
+            << ", \"tma_allowed\": " << ((!sel || std::atoi(sel)) ? "true" : "false")
+            << ", \"us\": " << median(t) << ", \"GBps\": " << g
+            << ", \"frac_of_peak\": " << g / peak << ", \"verified\": true}" << std::endl;
+  cudaStreamDestroy(s);
+  return 0;
+}
+
 // ---- p2p --------------------------------------------------------------------------
 
 int run_p2p(const Args &a) {
@@ -601,7 +676,7 @@ int run_p2p(const Args &a) {
 
 int main(int argc, char **argv) {
   try {
-    if (argc < 2) throw std::runtime_error("usage: dcopy_bench sweep|standalone|nz|fz|transpose|p2p [options]");
+    if (argc < 2) throw std::runtime_error("usage: dcopy_bench sweep|standalone|nz|fz|transpose|nd|p2p [options]");
     const std::string cmd = argv[1];
     Args a(argc, argv);
     if (cmd == "sweep") return run_sweep(a);
@@ -610,6 +685,7 @@ int main(int argc, char **argv) {
     if (cmd == "p2p") return run_p2p(a);
     if (cmd == "fz") return run_fz(a);
     if (cmd == "transpose") return run_transpose(a);
+    if (cmd == "nd") return run_nd(a);
     throw std::runtime_error("unknown command " + cmd);
   } catch (const std::exception &e) {
     std::cerr << "dcopy_bench: " << e.what() << '\n';

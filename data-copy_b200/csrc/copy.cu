@@ -17,6 +17,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "internal.cuh"
 #include "copy.cuh"
 #include "launch.cuh"
 
@@ -449,6 +450,14 @@ extern "C" int dcopy_copy_nd(void *dst, const void *src, int ndim, const uint64_
     const uint64_t dp = ndim == 2 ? (uint64_t)dst_strides[0] * elem_bytes : row_bytes;
     if (sp >= row_bytes && dp >= row_bytes)
       return copy2d(dst, src, rows, row_bytes, sp, dp, s);
+  }
+  // 3- to 5-D boxes with a contiguous innermost axis and 16-byte strides: TMA
+  // tensor copies (nd_tma.cu); anything else takes the element kernel below.
+  if (ndim >= 3) {
+    bool taken = false;
+    const int trc = nd_copy_tma(dst, src, ndim, sizes, src_strides, dst_strides, elem_bytes,
+                                stream, &taken);
+    if (taken || trc) return trc;
   }
   NdDesc d{};
   d.ndim = ndim;

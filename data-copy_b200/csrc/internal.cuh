@@ -61,6 +61,13 @@ int from_fz(void *dst, const void *src, int32_t fmt, const int64_t *dst_shape, i
 int permute_copy(void *dst, const void *src, int m, const uint64_t *size, const int64_t *ss,
                  const int64_t *ds, int eb, dcopy_stream_t stream);
 
+// A 3- to 5-D box copy through TMA tensor maps when both views allow it
+// (*taken = true); otherwise nothing is launched and *taken = false.  Sizes and
+// strides outermost first, in elements.  Buffers are checked by the caller.
+int nd_copy_tma(void *dst, const void *src, int ndim, const uint64_t *sizes,
+                const int64_t *src_strides, const int64_t *dst_strides, uint32_t eb,
+                dcopy_stream_t stream, bool *taken);
+
 // The reference's pretranspose workflow (asc:144-146): x -> B with RunTiles<1>,
 // then B -> y with RunTiles<2>, through a B buffer of scratch_bytes bytes that
 // the caller of this function guarantees is device memory (it is not checked).

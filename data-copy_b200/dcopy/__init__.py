@@ -36,7 +36,7 @@ __all__ = [
     "transpose_with_shape_check", "FORMAT", "DATA_TYPE", "TRANSFER_FRACTAL_NZ",
     "TRANSFER_FRACTAL_NZ_ND", "TRANSFER_TRANSPOSE", "shard_range", "enable_peer_access",
     "p2p_copy", "p2p_ring_shift", "ipc_get_handle", "ipc_open_handle", "ipc_close_handle",
-    "signal", "wait_signal", "p2p_error", "DcopyDevCopy", "copy_ext_multi", "DcopyMemcpyInfo", "memcpy_async",
+    "signal", "wait_signal", "p2p_error", "tma_error", "DcopyDevCopy", "copy_ext_multi", "DcopyMemcpyInfo", "memcpy_async",
     "MEMCPY_KIND",
     "OK", "ERR_PARAM_INVALID", "ERR_SHAPE_INVALID", "ERR_DATATYPE_INVALID",
     "ERR_FORMAT_INVALID", "ERR_CUDA", "ERR_TIMEOUT", "ERR_UNSUPPORTED", "ERR_FAILED",
@@ -209,6 +209,7 @@ _SIGNATURES = {
     "dcopy_p2p_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32)]),
     "dcopy_signal": (ctypes.c_int, [_vp, ctypes.c_uint32, _vp]),
     "dcopy_wait_signal": (ctypes.c_int, [_vp, ctypes.c_uint32, ctypes.c_uint64, _vp, _vp]),
+    "dcopy_tma_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32)]),
 }
 
 
@@ -535,6 +536,13 @@ def p2p_ring_shift(devices, srcs, dsts, nbytes: int, streams=None) -> None:
     if streams is not None:
         st = (ctypes.c_void_p * n)(*[_stream(x) for x in streams])
     _check(lib().dcopy_p2p_ring_shift(devs, s, d, st, n, nbytes), "dcopy_p2p_ring_shift")
+
+
+def tma_error() -> int:
+    """Reads and clears the device's TMA box-copy error word (1 = a copy gave up)."""
+    v = ctypes.c_uint32(0)
+    _check(lib().dcopy_tma_error(ctypes.byref(v)), "dcopy_tma_error")
+    return v.value
 
 
 def p2p_error() -> int:

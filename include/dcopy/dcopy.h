@@ -137,10 +137,21 @@ int dcopy_copy_ext_32b(void *dst, const void *src, uint32_t blockCount, uint32_t
 /* DataCopyNddma<T, dim> (v35/ascendc/api_regbase/datacopy_nddma.h:15-29): an
  * N-D box copy, 1 <= ndim <= 5.  sizes, src_strides and dst_strides are
  * outermost-first (like its output_dims argument) and strides count elements
- * of elem_bytes (1, 2, 4, 8 or 16) bytes.  Negative strides are refused. */
+ * of elem_bytes (1, 2, 4, 8 or 16) bytes.  Negative strides are refused.
+ * 3- to 5-D boxes whose innermost axis is contiguous on both sides and a
+ * multiple of 16 bytes, with 16-byte aligned bases and 16-byte multiple
+ * strides, run as TMA tensor copies
+ * (cp.async.bulk.tensor through two tensor maps); other boxes run on
+ * load/store kernels. */
 int dcopy_copy_nd(void *dst, const void *src, int ndim, const uint64_t *sizes,
                   const int64_t *src_strides, const int64_t *dst_strides, uint32_t elem_bytes,
                   dcopy_stream_t stream);
+
+/* Reads and clears the current device's TMA box-copy error word: 1 when a
+ * dcopy_copy_nd launch that took the tensor-copy path gave up waiting on one of
+ * its own loads (that copy is then incomplete), else 0.  Synchronises the
+ * device.  No counterpart in the reference. */
+int dcopy_tma_error(uint32_t *flag);
 
 /* ---- ND <-> FRACTAL_NZ ------------------------------------------------------ */
 
