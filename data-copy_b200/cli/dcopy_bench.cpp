@@ -2,8 +2,8 @@
 // msprof harness standalone_datacopy/profile.py and its host address model
 // test_address_model.py).  Every result is verified on the host before it is timed.
 //
-//   dcopy_bench sweep [--moved-mib M] [--reps R] [--device D]
-//       blockLen x gap sweep of dcopy_copy_ext on an int32
+//   dcopy_bench sweep [--moved-mib M] [--blens L,...] [--gaps G,...] [--reps R] [--device D]
+//       blockLen x gap sweep (gaps as multiples of blockLen) of dcopy_copy_ext on an int32
 //       element-index source; one JSON line per point with measured GB/s, the
 //       fraction of the copy peak and a DRAM-atom model of the achievable rate.
 //   dcopy_bench standalone ROWS COLS SMALL_KIB LARGE_KIB [--trials N] [--device D]
@@ -139,6 +139,8 @@ double median(std::vector<double> v) {
   return n % 2 ? v[n / 2] : 0.5 * (v[n / 2 - 1] + v[n / 2]);
 }
 
+std::vector<int64_t> parse_list(const std::string &text);
+
 // ---- sweep ---------------------------------------------------------------------
 
 // DRAM-atom model: HBM moves 64-byte atoms, so a burst of blen bytes that starts
@@ -164,8 +166,11 @@ int run_sweep(const Args &a) {
     Check(cudaMemcpy(src.p, host.data(), src_bytes, cudaMemcpyHostToDevice), "H2D");
   }
   std::vector<int32_t> out(moved / 4);
-  for (uint64_t blen : {32ull, 64ull, 128ull, 512ull, 4096ull, 65536ull}) {
-    for (uint64_t gx : {0ull, 1ull, 4ull, 16ull}) {
+  for (int64_t blen_ : parse_list(a.str("blens", "32,64,128,512,4096,65536"))) {
+    for (int64_t gx_ : parse_list(a.str("gaps", "0,1,4,16"))) {
+      const uint64_t blen = uint64_t(blen_), gx = uint64_t(gx_);
+      if (blen < 4 || blen % 4 || moved % blen || gx > 16)
+        throw std::runtime_error("sweep: blens must divide the moved bytes, gaps 0..16");
       const uint64_t gap = gx * blen, count = moved / blen;
       DcopyExtParams p{uint32_t(count), uint32_t(blen), gap, 0};
       Check(cudaMemsetAsync(dst.p, 0xA5, moved, s), "memset");
@@ -679,6 +684,16 @@ int main(int argc, char **argv) {
     if (argc < 2) throw std::runtime_error("usage: dcopy_bench sweep|standalone|nz|fz|transpose|nd|p2p [options]");
     const std::string cmd = argv[1];
     Args a(argc, argv);
+    // --l2-fetch B: the context's L2 fetch-granularity hint (cudaLimitMaxL2FetchGranularity,
+    // 0..128 bytes) for every command; it lasts as long as this process.
+    if (a.opt.count("l2-fetch")) {
+      Check(cudaSetDevice(int(a.num("device", 0))), "cudaSetDevice");
+      Check(cudaDeviceSetLimit(cudaLimitMaxL2FetchGranularity, size_t(a.num("l2-fetch", 64))),
+            "cudaDeviceSetLimit");
+      size_t got = 0;
+      Check(cudaDeviceGetLimit(&got, cudaLimitMaxL2FetchGranularity), "cudaDeviceGetLimit");
+      std::cerr << "L2 fetch granularity limit: " << got << " bytes\n";
+    }
     if (cmd == "sweep") return run_sweep(a);
     if (cmd == "standalone") return run_standalone(a);
     if (cmd == "nz") return run_nz(a);

@@ -104,6 +104,47 @@ __device__ __forceinline__ uint8_t ld_stream<uint8_t>(const uint8_t *p) {
   return (uint8_t)v;
 }
 
+// The same streaming loads with the `.L2::64B` size qualifier: the L2 fills the
+// 64-byte half line the load touches instead of the whole 128-byte line.  For
+// bursts that end inside a line with a gap behind them this halves the DRAM read
+// (measured on B200: 32 B bursts with a 128 B gap 2648 -> 3542 GB/s, 64 B bursts
+// with a 64 B gap 4443 -> 5242 GB/s); bursts of whole lines are unchanged.
+template <typename T>
+__device__ __forceinline__ T ld_stream_half_line(const T *p);
+
+template <>
+__device__ __forceinline__ uint4 ld_stream_half_line<uint4>(const uint4 *p) {
+  uint4 v;
+  asm("ld.global.nc.L1::no_allocate.L2::64B.v4.u32 {%0, %1, %2, %3}, [%4];"
+      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+      : "l"(p));
+  return v;
+}
+template <>
+__device__ __forceinline__ uint2 ld_stream_half_line<uint2>(const uint2 *p) {
+  uint2 v;
+  asm("ld.global.nc.L1::no_allocate.L2::64B.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+  return v;
+}
+template <>
+__device__ __forceinline__ uint32_t ld_stream_half_line<uint32_t>(const uint32_t *p) {
+  uint32_t v;
+  asm("ld.global.nc.L1::no_allocate.L2::64B.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+template <>
+__device__ __forceinline__ uint16_t ld_stream_half_line<uint16_t>(const uint16_t *p) {
+  uint16_t v;
+  asm("ld.global.nc.L1::no_allocate.L2::64B.u16 %0, [%1];" : "=h"(v) : "l"(p));
+  return v;
+}
+template <>
+__device__ __forceinline__ uint8_t ld_stream_half_line<uint8_t>(const uint8_t *p) {
+  uint16_t v;
+  asm("ld.global.nc.L1::no_allocate.L2::64B.u8 %0, [%1];" : "=h"(v) : "l"(p));
+  return (uint8_t)v;
+}
+
 // L2 prefetch hint for the line holding p.  Kernels issue these for their source
 // before waiting on the previous kernel of the stream (programmatic dependent
 // launch): a prefetch returns no data to the SM and has no effect on memory

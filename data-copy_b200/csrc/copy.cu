@@ -134,8 +134,10 @@ __global__ void __launch_bounds__(kThreads) linear_load_kernel(const uint8_t *__
 
 // Strided copy: element i of the flat [rows x epr] index space moves from
 // src + row*src_pitch + col*sizeof(T) to dst + row*dst_pitch + col*sizeof(T).
-// CTA b handles elements [b*per_cta, min((b+1)*per_cta, total)).
-template <typename T, int U>
+// CTA b handles elements [b*per_cta, min((b+1)*per_cta, total)).  kHalfLine:
+// source loads fill 64-byte half lines of L2 (bursts that start or end inside a
+// 128-byte line, with gaps between them).
+template <typename T, int U, bool kHalfLine>
 __global__ void __launch_bounds__(kThreads, Unroll<T>::strided_min_ctas)
     strided_copy_kernel(uint8_t *__restrict__ dst, const uint8_t *__restrict__ src,
                         uint32_t total, uint32_t per_cta, FastDiv epr, uint64_t src_pitch,
@@ -163,7 +165,11 @@ __global__ void __launch_bounds__(kThreads, Unroll<T>::strided_min_ctas)
       const uint32_t i = base + u * kThreads;
       if (i < end) {
         const uint32_t r = epr.div(i);
-        v[u] = ld_stream(reinterpret_cast<const T *>(src + (uint64_t)r * src_pitch) + (i - r * epr.d));
+        const T *p = reinterpret_cast<const T *>(src + (uint64_t)r * src_pitch) + (i - r * epr.d);
+        if constexpr (kHalfLine)
+          v[u] = ld_stream_half_line(p);
+        else
+          v[u] = ld_stream(p);
       }
     }
     // Destination addresses are recomputed (one multiply-high each) rather than
@@ -240,10 +246,13 @@ int launch_strided(uint8_t *dst, const uint8_t *src, uint64_t rows, uint64_t row
   const uint64_t max_rows = std::max<uint64_t>(1, (uint64_t(1) << 30) / epr);
   const FastDiv div((uint32_t)epr);
   const bool prefetch = is_local_device_memory(src);
+  // Gapped bursts that do not cover whole 128-byte lines: half-line L2 fills.
+  const bool half_line =
+      src_pitch != row_bytes && ((uintptr_t)src % 128 || row_bytes % 128 || src_pitch % 128);
   for (uint64_t r0 = 0; r0 < rows; r0 += max_rows) {
     const uint64_t nr = std::min(max_rows, rows - r0);
     const uint32_t total = (uint32_t)(nr * epr);
-    auto kernel = strided_copy_kernel<T, U>;
+    auto kernel = half_line ? strided_copy_kernel<T, U, true> : strided_copy_kernel<T, U, false>;
     const Split sp = split_work(kernel, total, U);
     int rc = launch(kernel, sp.grid, dim3(kThreads), 0, s, "strided_copy_kernel",
                     dst + r0 * dst_pitch, src + r0 * src_pitch, total, (uint32_t)sp.per_cta, div,
