@@ -24,10 +24,12 @@
 //                         [--device D] [--peak GBPS]
 //       GE Transpose (dcopy_transpose) of a dense tensor, verified against a host
 //       restatement; one JSON line.
-//   dcopy_bench nd [--sizes A,B,C[,D,E]] [--eb B] [--src-pad P] [--dst-pad Q] [--reps R]
-//                  [--device D] [--peak GBPS]
+//   dcopy_bench nd [--sizes A,B,C[,D,E]] [--eb B] [--src-pad P] [--dst-pad Q] [--tma 0|1]
+//                  [--reps R] [--device D] [--peak GBPS]
 //       DataCopyNddma box (dcopy_copy_nd) between padded views, verified; one JSON
-//       line.  DCOPY_ND_TMA=0 in the environment selects the load/store kernels.
+//       line: event time around the call, the same call replayed as a CUDA graph,
+//       and the host time of one call.  --tma 1 selects the TMA tensor-copy path
+//       (dcopy_set_nd_tma) for boxes that qualify.
 //   dcopy_bench p2p [--mib M] [--reps R] [--device D] [--peer P] [--peak GBPS]
 //       NVLink between two GPUs: dcopy_p2p_copy as a push (launched on the
 //       sending GPU) and as a pull (launched on the receiving GPU), and the copy
@@ -40,6 +42,7 @@
 #include <sys/stat.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
@@ -131,6 +134,36 @@ std::vector<double> time_reps(F fn, int reps, cudaStream_t s, DevBuf &flush) {
   cudaEventDestroy(a);
   cudaEventDestroy(b);
   return us;
+}
+
+// The same, with `fn` captured once into a CUDA graph and the graph replayed
+// between the events: device time without the host work of the call.
+template <typename F>
+std::vector<double> time_graph_reps(F fn, int reps, cudaStream_t s, DevBuf &flush) {
+  cudaGraph_t graph;
+  cudaGraphExec_t exec;
+  Check(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "begin capture");
+  fn();
+  Check(cudaStreamEndCapture(s, &graph), "end capture");
+  Check(cudaGraphInstantiate(&exec, graph, 0), "instantiate");
+  auto us = time_reps([&] { Check(cudaGraphLaunch(exec, s), "graph launch"); }, reps, s, flush);
+  cudaGraphExecDestroy(exec);
+  cudaGraphDestroy(graph);
+  return us;
+}
+
+// Host time of one call of `fn` (asynchronous launches; the stream drains after).
+template <typename F>
+double host_us_per_call(F fn, int reps, cudaStream_t s) {
+  double total = 0;
+  for (int r = 0; r < reps; ++r) {
+    const auto t0 = std::chrono::steady_clock::now();
+    fn();
+    const auto t1 = std::chrono::steady_clock::now();
+    total += std::chrono::duration<double, std::micro>(t1 - t0).count();
+    Check(cudaStreamSynchronize(s), "sync");
+  }
+  return total / reps;
 }
 
 double median(std::vector<double> v) {
@@ -519,6 +552,8 @@ int run_nd(const Args &a) {
   const int reps = int(a.num("reps", 10));
   const double peak = a.num("peak", 6543.4);
   const int nd = int(sz.size());
+  const int tma = int(a.num("tma", 0));
+  CheckD(dcopy_set_nd_tma(tma, nullptr));
   std::vector<uint64_t> sizes(sz.begin(), sz.end());
   std::vector<int64_t> ss(nd), ds(nd);
   ss[nd - 1] = ds[nd - 1] = 1;
@@ -561,19 +596,23 @@ int run_nd(const Args &a) {
     }
   }
   if (out != expect) throw std::runtime_error("copy_nd result differs from the host restatement");
-  auto t = time_reps(
-      [&] { CheckD(dcopy_copy_nd(dst.p, src.p, nd, sizes.data(), ss.data(), ds.data(), eb, dsm)); },
-      reps, s, flush);
+  auto call = [&] {
+    CheckD(dcopy_copy_nd(dst.p, src.p, nd, sizes.data(), ss.data(), ds.data(), eb, dsm));
+  };
+  auto t = time_reps(call, reps, s, flush);
+  auto tg = time_graph_reps(call, reps, s, flush);
+  const double host_call_us = host_us_per_call(call, reps, s);
   uint32_t tma_err = 0;
   CheckD(dcopy_tma_error(&tma_err));
   if (tma_err) throw std::runtime_error("TMA box copy gave up a wait");
   const double g = 2.0 * n * eb / (median(t) * 1e3);
-  const char *sel = std::getenv("DCOPY_ND_TMA");
   std::cout << "{\"nd\": \"" << a.str("sizes", "64,1024,1024") << "\", \"src_pad\": " << sp
             << ", \"dst_pad\": " << dp << ", \"elem_bytes\": " << eb
-            << ", \"tma_allowed\": " << ((!sel || std::atoi(sel)) ? "true" : "false")
+            << ", \"tma_selected\": " << (tma ? "true" : "false")
             << ", \"us\": " << median(t) << ", \"GBps\": " << g
-            << ", \"frac_of_peak\": " << g / peak << ", \"verified\": true}" << std::endl;
+            << ", \"frac_of_peak\": " << g / peak << ", \"graph_us\": " << median(tg)
+            << ", \"graph_GBps\": " << 2.0 * n * eb / (median(tg) * 1e3)
+            << ", \"host_us_per_call\": " << host_call_us << ", \"verified\": true}" << std::endl;
   cudaStreamDestroy(s);
   return 0;
 }

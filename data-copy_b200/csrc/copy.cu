@@ -460,13 +460,21 @@ extern "C" int dcopy_copy_nd(void *dst, const void *src, int ndim, const uint64_
     if (sp >= row_bytes && dp >= row_bytes)
       return copy2d(dst, src, rows, row_bytes, sp, dp, s);
   }
-  // 3- to 5-D boxes with a contiguous innermost axis and 16-byte strides: TMA
-  // tensor copies (nd_tma.cu); anything else takes the element kernel below.
+  // With the TMA path selected: 3- to 5-D boxes with 16-byte rows and strides
+  // as TMA tensor copies (nd_tma.cu).
   if (ndim >= 3) {
     bool taken = false;
     const int trc = nd_copy_tma(dst, src, ndim, sizes, src_strides, dst_strides, elem_bytes,
                                 stream, &taken);
     if (taken || trc) return trc;
+  }
+  // Other boxes with a contiguous innermost axis: rows in the widest unit that
+  // divides the row length, both bases and every stride (permute.cu).
+  {
+    bool taken = false;
+    const int rrc = rows_copy(dst, src, ndim, sizes, src_strides, dst_strides, (int)elem_bytes,
+                              stream, &taken);
+    if (taken || rrc) return rrc;
   }
   NdDesc d{};
   d.ndim = ndim;

@@ -64,6 +64,17 @@ int permute_copy(void *dst, const void *src, int m, const uint64_t *size, const 
 // A 3- to 5-D box copy through TMA tensor maps when both views allow it
 // (*taken = true); otherwise nothing is launched and *taken = false.  Sizes and
 // strides outermost first, in elements.  Buffers are checked by the caller.
+// Rows of size[m-1] elements, m <= 5, whose length, bases or strides are not
+// 16-byte multiples: aligned 16-byte destination vectors assembled with funnel
+// shifts (rows.cu).  ds == NULL: contiguous destination.
+int rows_shift(void *dst, const void *src, int m, const uint64_t *size, const int64_t *ss,
+               const int64_t *ds, int eb, cudaStream_t s);
+
+// Rows of a <=5-D box whose innermost axis is contiguous on both sides
+// (permute.cu); *taken = false when the row kernel does not apply.
+int rows_copy(void *dst, const void *src, int m, const uint64_t *size, const int64_t *ss,
+              const int64_t *ds, int eb, dcopy_stream_t stream, bool *taken);
+
 int nd_copy_tma(void *dst, const void *src, int ndim, const uint64_t *sizes,
                 const int64_t *src_strides, const int64_t *dst_strides, uint32_t eb,
                 dcopy_stream_t stream, bool *taken);

@@ -1,4 +1,7 @@
 // DataCopyNddma boxes through TMA tensor maps (cp.async.bulk.tensor) on sm_100a.
+// Selected with dcopy_set_nd_tma (or DCOPY_ND_TMA=1); off by default, because on
+// B200 the load/store row kernel measured as fast or faster on every box tried
+// (TMA 3.3-5.9 TB/s against 3.4-6.4 TB/s).
 //
 // A 3- to 5-D box copy (v35/ascendc/api_regbase/datacopy_nddma.h:15-29) whose
 // innermost axis is contiguous on both sides and whose other strides are
@@ -37,6 +40,9 @@ namespace {
 #endif
 #ifndef DCOPY_TMA_CTAS_PER_SM
 #define DCOPY_TMA_CTAS_PER_SM 3
+#endif
+#ifndef DCOPY_TMA_UNIT
+#define DCOPY_TMA_UNIT 8  // TMA element: 0 the library element, 8 always 8-byte units
 #endif
 constexpr int kStages = DCOPY_TMA_STAGES;
 constexpr uint32_t kStageBytes = DCOPY_TMA_STAGE_KIB * 1024;
@@ -248,18 +254,31 @@ int launch_rank(const CUtensorMap &sm, const CUtensorMap &dm, const TmaGeom &g, 
                 "nd_tma_kernel", sm, dm, g);
 }
 
+// Process-wide path selection: -1 until first read (then DCOPY_ND_TMA, default 0).
+std::atomic<int> g_tma_selected{-1};
+
+int initial_selection() {
+  const char *e = std::getenv("DCOPY_ND_TMA");
+  return e && std::atoi(e) != 0 ? 1 : 0;
+}
+
+bool tma_selected() {
+  int v = g_tma_selected.load(std::memory_order_relaxed);
+  if (v < 0) {
+    int expected = -1;
+    g_tma_selected.compare_exchange_strong(expected, initial_selection());
+    v = g_tma_selected.load(std::memory_order_relaxed);
+  }
+  return v != 0;
+}
+
 }  // namespace
 
 int nd_copy_tma(void *dst, const void *src, int ndim, const uint64_t *sizes,
                 const int64_t *src_strides, const int64_t *dst_strides, uint32_t eb,
                 dcopy_stream_t stream, bool *taken) {
   *taken = false;
-  // DCOPY_ND_TMA=0 selects the load/store kernels for every box (path comparison).
-  static const bool enabled = [] {
-    const char *e = std::getenv("DCOPY_ND_TMA");
-    return !e || std::atoi(e) != 0;
-  }();
-  if (!enabled) return DCOPY_OK;
+  if (!tma_selected()) return DCOPY_OK;
   // Conditions of a tiled tensor copy on both views (checked, else the caller
   // takes its load/store kernels): 16-byte aligned bases, unit innermost stride,
   // 16-byte multiple strides, rows of whole 16-byte granules, local memory.
@@ -282,8 +301,8 @@ int nd_copy_tma(void *dst, const void *src, int ndim, const uint64_t *sizes,
   if (!encode) return DCOPY_OK;
 
   // TMA element: the library element, or 8-byte halves of a 16-byte element.
-  const uint32_t te = eb == 16 ? 8 : eb;
-  const uint32_t scale = eb / te;
+  // Rows are whole 16-byte granules, so 8-byte units always tile them.
+  const uint32_t te = DCOPY_TMA_UNIT == 8 ? 8 : (eb == 16 ? 8 : eb);
   const CUtensorMapDataType dtype = te == 1   ? CU_TENSOR_MAP_DATA_TYPE_UINT8
                                     : te == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16
                                     : te == 4 ? CU_TENSOR_MAP_DATA_TYPE_UINT32
@@ -295,7 +314,7 @@ int nd_copy_tma(void *dst, const void *src, int ndim, const uint64_t *sizes,
   g.rank = (uint32_t)R;
   for (int d = 0; d < R; ++d) {  // d = 0 innermost
     const int k = ndim - 1 - d;
-    gdim[d] = sizes[k] * (d == 0 ? scale : 1);
+    gdim[d] = d == 0 ? sizes[k] * eb / te : sizes[k];
     if (d > 0) {
       sstride[d - 1] = (cuuint64_t)src_strides[k] * eb;
       dstride[d - 1] = (cuuint64_t)dst_strides[k] * eb;
@@ -354,6 +373,15 @@ int nd_copy_tma(void *dst, const void *src, int ndim, const uint64_t *sizes,
 }  // namespace dcopy
 
 using namespace dcopy;
+
+extern "C" int dcopy_set_nd_tma(int enable, int *previous) {
+  DCOPY_API_BEGIN
+  const int was = tma_selected() ? 1 : 0;
+  g_tma_selected.store(enable ? 1 : 0);
+  if (previous) *previous = was;
+  return DCOPY_OK;
+  DCOPY_API_END
+}
 
 extern "C" int dcopy_tma_error(uint32_t *flag) {
   DCOPY_API_BEGIN

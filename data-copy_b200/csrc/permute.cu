@@ -1,6 +1,7 @@
 // Permuted copy into a contiguous destination (GE's Transpose after dimension
 // merging): dst[i] = src[sum_k idx_k * src_stride_k] over the destination
 // odometer, sizes and strides in elements, at most 5 dims, dst contiguous.
+// The row kernel also serves strided destinations (rows_copy: NDDMA boxes).
 //
 // Two kernels, by where the source's contiguous axis lands:
 //   * perm_rows_kernel: the innermost axis is contiguous on both sides, so the
@@ -32,6 +33,9 @@ constexpr int kMaxRowDims = 4;
 #ifndef DCOPY_PERM_PACKED
 #define DCOPY_PERM_PACKED 1  // aligned tiles: packed [e][d] shared layout (0: element gather)
 #endif
+#ifndef DCOPY_ROWS_SHIFT_BELOW
+#define DCOPY_ROWS_SHIFT_BELOW 8  // rows whose widest unit is below this many bytes: rows_shift
+#endif
 #ifndef DCOPY_PERM_TD2
 #define DCOPY_PERM_TD2 64  // 2-byte elements: tile rows (destination axis)
 #endif
@@ -48,10 +52,14 @@ struct PermRGeom {
   uint32_t size[kMaxRowDims];
   FastDiv f_size[kMaxRowDims];
   uint64_t ss[kMaxRowDims];   // source stride of each row dim, in units
+  uint64_t ds[kMaxRowDims];   // destination stride of each row dim, in units (strided rows)
   uint64_t total;             // units (per launch below 2^31)
 };
 
-template <typename T>
+// kStridedDst: destination rows follow their own strides (NDDMA boxes); else the
+// destination is contiguous and unit i lands at dst[i].  kHalfLine: source loads
+// fill 64-byte half lines of L2 (gapped rows that do not cover whole lines).
+template <typename T, bool kStridedDst, bool kHalfLine>
 __global__ void __launch_bounds__(kThreads) perm_rows_kernel(T *__restrict__ dst,
                                                              const T *__restrict__ src,
                                                              PermRGeom g) {
@@ -63,29 +71,34 @@ __global__ void __launch_bounds__(kThreads) perm_rows_kernel(T *__restrict__ dst
   for (uint32_t base = blockIdx.x * kThreads * U + threadIdx.x; base < total;
        base += gridDim.x * kThreads * U) {
     T v[U];
-    uint32_t at[U];
+    uint64_t at[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const uint32_t i = base + u * kThreads;
-      at[u] = 0xFFFFFFFFu;
+      at[u] = ~0ull;
       if (i >= total) continue;
       uint32_t rem = g.f_vpr.div(i);
       const uint32_t col = i - rem * g.vpr;
-      uint64_t so = col;
+      uint64_t so = col, dof = col;
 #pragma unroll
       for (int k = kMaxRowDims - 1; k >= 0; --k) {
         if (k < (int)g.nd) {
           const uint32_t q = g.f_size[k].div(rem);
-          so += (uint64_t)(rem - q * g.size[k]) * g.ss[k];
+          const uint64_t idx = rem - q * g.size[k];
+          so += idx * g.ss[k];
+          if constexpr (kStridedDst) dof += idx * g.ds[k];
           rem = q;
         }
       }
-      v[u] = ld_stream(src + so);
-      at[u] = i;
+      if constexpr (kHalfLine)
+        v[u] = ld_stream_half_line(src + so);
+      else
+        v[u] = ld_stream(src + so);
+      at[u] = kStridedDst ? dof : i;
     }
 #pragma unroll
     for (int u = 0; u < U; ++u)
-      if (at[u] != 0xFFFFFFFFu) dst[at[u]] = v[u];
+      if (at[u] != ~0ull) dst[at[u]] = v[u];
   }
 }
 
@@ -305,9 +318,9 @@ __global__ void __launch_bounds__(kThreads) perm_tile_packed_kernel(T *__restric
   }
 }
 
-template <typename T>
+template <typename T, bool kStridedDst>
 int launch_rows(void *dst, const void *src, const PermRGeom &g0, uint64_t outer_ss,
-                cudaStream_t s) {
+                uint64_t outer_ds, bool half_line, cudaStream_t s) {
   // Chunk the outermost row dim so that one launch covers fewer than 2^31 units.
   uint64_t inner_units = g0.vpr;
   for (uint32_t k = 1; k < g0.nd; ++k) inner_units *= g0.size[k];
@@ -326,8 +339,10 @@ int launch_rows(void *dst, const void *src, const PermRGeom &g0, uint64_t outer_
     g.total = n * inner_units;
     const uint64_t per_cta = (uint64_t)kThreads * 4;
     const uint32_t grid = (uint32_t)std::max<uint64_t>(1, (g.total + per_cta - 1) / per_cta);
-    const int rc = launch(perm_rows_kernel<T>, grid, dim3(kThreads), 0, s, "perm_rows_kernel",
-                          static_cast<T *>(dst) + o0 * inner_units,
+    auto kernel = half_line ? perm_rows_kernel<T, kStridedDst, true>
+                            : perm_rows_kernel<T, kStridedDst, false>;
+    const int rc = launch(kernel, grid, dim3(kThreads), 0, s, "perm_rows_kernel",
+                          static_cast<T *>(dst) + o0 * (kStridedDst ? outer_ds : inner_units),
                           static_cast<const T *>(src) + o0 * outer_ss, g);
     if (rc) return rc;
   }
@@ -349,12 +364,14 @@ uint32_t unit_for(uint64_t key, int eb) {
   return us;
 }
 
-int run_rows(void *dst, const void *src, int m, const uint64_t *size, const int64_t *ss, int eb,
-             cudaStream_t s) {
+// Rows of size[m-1] elements; ds == NULL: contiguous destination.
+int run_rows(void *dst, const void *src, int m, const uint64_t *size, const int64_t *ss,
+             const int64_t *ds, int eb, cudaStream_t s) {
   const uint64_t L = size[m - 1];
   uint64_t key = L * eb | (uintptr_t)dst | (uintptr_t)src;
-  for (int k = 0; k < m - 1; ++k) key |= (uint64_t)ss[k] * eb;
+  for (int k = 0; k < m - 1; ++k) key |= (uint64_t)ss[k] * eb | (ds ? (uint64_t)ds[k] * eb : 0);
   const uint32_t us = unit_for(key, eb);
+  if (us < DCOPY_ROWS_SHIFT_BELOW && L * eb >= 16) return rows_shift(dst, src, m, size, ss, ds, eb, s);
   PermRGeom g{};
   g.vpr = (uint32_t)(L * eb / us);
   if ((uint64_t)g.vpr != L * eb / us)
@@ -370,17 +387,35 @@ int run_rows(void *dst, const void *src, int m, const uint64_t *size, const int6
     g.size[k] = (uint32_t)size[k];
     g.f_size[k] = FastDiv(g.size[k]);
     g.ss[k] = (uint64_t)ss[k] * eb / us;
+    g.ds[k] = ds ? (uint64_t)ds[k] * eb / us : 0;
     rows *= size[k];
   }
   g.total = rows * g.vpr;
   if (g.total == 0) return DCOPY_OK;
-  const uint64_t outer_ss = g.nd ? g.ss[0] : 0;
+  const uint64_t outer_ss = g.nd ? g.ss[0] : 0, outer_ds = g.nd ? g.ds[0] : 0;
+  // NDDMA boxes whose source rows have gaps behind them and do not cover whole
+  // 128-byte lines: half-line L2 fills (transposes read every line whole).
+  bool half_line = false;
+  if (ds && m >= 2 && (uint64_t)ss[m - 2] != L) {
+    uint64_t lines = L * eb | (uintptr_t)src;
+    for (int k = 0; k < m - 1; ++k) lines |= (uint64_t)ss[k] * eb;
+    half_line = lines % 128 != 0;
+  }
+  if (ds) {
+    switch (us) {
+      case 16: return launch_rows<uint4, true>(dst, src, g, outer_ss, outer_ds, half_line, s);
+      case 8: return launch_rows<uint2, true>(dst, src, g, outer_ss, outer_ds, half_line, s);
+      case 4: return launch_rows<uint32_t, true>(dst, src, g, outer_ss, outer_ds, half_line, s);
+      case 2: return launch_rows<uint16_t, true>(dst, src, g, outer_ss, outer_ds, half_line, s);
+      default: return launch_rows<uint8_t, true>(dst, src, g, outer_ss, outer_ds, half_line, s);
+    }
+  }
   switch (us) {
-    case 16: return launch_rows<uint4>(dst, src, g, outer_ss, s);
-    case 8: return launch_rows<uint2>(dst, src, g, outer_ss, s);
-    case 4: return launch_rows<uint32_t>(dst, src, g, outer_ss, s);
-    case 2: return launch_rows<uint16_t>(dst, src, g, outer_ss, s);
-    default: return launch_rows<uint8_t>(dst, src, g, outer_ss, s);
+    case 16: return launch_rows<uint4, false>(dst, src, g, outer_ss, 0, half_line, s);
+    case 8: return launch_rows<uint2, false>(dst, src, g, outer_ss, 0, half_line, s);
+    case 4: return launch_rows<uint32_t, false>(dst, src, g, outer_ss, 0, half_line, s);
+    case 2: return launch_rows<uint16_t, false>(dst, src, g, outer_ss, 0, half_line, s);
+    default: return launch_rows<uint8_t, false>(dst, src, g, outer_ss, 0, half_line, s);
   }
 }
 
@@ -486,7 +521,7 @@ int permute_copy(void *dst, const void *src, int m, const uint64_t *size, const 
   if (m < 1 || m > 5)
     return set_error(DCOPY_ERR_UNSUPPORTED, "transpose: %d non-trivial dims (at most 5)", m);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (ss[m - 1] == 1) return run_rows(dst, src, m, size, ss, eb, s);
+  if (ss[m - 1] == 1) return run_rows(dst, src, m, size, ss, nullptr, eb, s);
   int e = -1;
   for (int k = 0; k < m - 1; ++k)
     if (ss[k] == 1) e = k;
@@ -524,6 +559,20 @@ int permute_copy(void *dst, const void *src, int m, const uint64_t *size, const 
     default:
       return set_error(DCOPY_ERR_DATATYPE_INVALID, "transpose: element of %d bytes", eb);
   }
+}
+
+// Strided rows (dcopy_copy_nd boxes whose innermost axis is contiguous on both
+// sides): m <= 5 dims, row dims outermost first.  *taken = false when the box
+// does not fit the row kernel's 32-bit unit indexing.
+int rows_copy(void *dst, const void *src, int m, const uint64_t *size, const int64_t *ss,
+              const int64_t *ds, int eb, dcopy_stream_t stream, bool *taken) {
+  *taken = false;
+  if (m < 2 || m > kMaxRowDims + 1 || ss[m - 1] != 1 || ds[m - 1] != 1) return DCOPY_OK;
+  uint64_t inner = size[m - 1];  // elements per outer index, bounded like launch_rows
+  for (int k = 1; k < m - 1; ++k) inner *= size[k];
+  if (inner >= (1ull << 31)) return DCOPY_OK;
+  *taken = true;
+  return run_rows(dst, src, m, size, ss, ds, eb, reinterpret_cast<cudaStream_t>(stream));
 }
 
 }  // namespace dcopy

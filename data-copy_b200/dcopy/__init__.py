@@ -210,6 +210,7 @@ _SIGNATURES = {
     "dcopy_signal": (ctypes.c_int, [_vp, ctypes.c_uint32, _vp]),
     "dcopy_wait_signal": (ctypes.c_int, [_vp, ctypes.c_uint32, ctypes.c_uint64, _vp, _vp]),
     "dcopy_tma_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32)]),
+    "dcopy_set_nd_tma": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
 }
 
 
@@ -536,6 +537,13 @@ def p2p_ring_shift(devices, srcs, dsts, nbytes: int, streams=None) -> None:
     if streams is not None:
         st = (ctypes.c_void_p * n)(*[_stream(x) for x in streams])
     _check(lib().dcopy_p2p_ring_shift(devs, s, d, st, n, nbytes), "dcopy_p2p_ring_shift")
+
+
+def set_nd_tma(enable: bool) -> bool:
+    """Selects the TMA tensor-copy path of copy_nd (process-wide); returns the former setting."""
+    prev = ctypes.c_int(0)
+    _check(lib().dcopy_set_nd_tma(1 if enable else 0, ctypes.byref(prev)), "dcopy_set_nd_tma")
+    return bool(prev.value)
 
 
 def tma_error() -> int:

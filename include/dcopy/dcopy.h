@@ -138,14 +138,22 @@ int dcopy_copy_ext_32b(void *dst, const void *src, uint32_t blockCount, uint32_t
  * N-D box copy, 1 <= ndim <= 5.  sizes, src_strides and dst_strides are
  * outermost-first (like its output_dims argument) and strides count elements
  * of elem_bytes (1, 2, 4, 8 or 16) bytes.  Negative strides are refused.
- * 3- to 5-D boxes whose innermost axis is contiguous on both sides and a
- * multiple of 16 bytes, with 16-byte aligned bases and 16-byte multiple
- * strides, run as TMA tensor copies
- * (cp.async.bulk.tensor through two tensor maps); other boxes run on
- * load/store kernels. */
+ * Boxes whose innermost axis is contiguous on both sides run as rows in the
+ * widest unit (<= 16 bytes) dividing the row, both bases and every stride;
+ * other boxes run element by element.  With the TMA path selected
+ * (dcopy_set_nd_tma), 3- to 5-D boxes whose rows are whole 16-byte granules,
+ * with 16-byte aligned bases and 16-byte multiple strides, run as TMA tensor
+ * copies (cp.async.bulk.tensor through two tensor maps) instead. */
 int dcopy_copy_nd(void *dst, const void *src, int ndim, const uint64_t *sizes,
                   const int64_t *src_strides, const int64_t *dst_strides, uint32_t elem_bytes,
                   dcopy_stream_t stream);
+
+/* Selects (enable = 1) or deselects (0) the TMA tensor-copy path of
+ * dcopy_copy_nd for the whole process; *previous (may be NULL) receives the
+ * former setting.  The initial setting is DCOPY_ND_TMA from the environment
+ * (unset: 0).  Off by default: on B200 the row kernel measured as fast or faster
+ * on every box tried.  No counterpart in the reference. */
+int dcopy_set_nd_tma(int enable, int *previous);
 
 /* Reads and clears the current device's TMA box-copy error word: 1 when a
  * dcopy_copy_nd launch that took the tensor-copy path gave up waiting on one of

@@ -146,3 +146,10 @@ def test_error_message_is_thread_local(dcopy):
     t.join()
     assert seen == [b""]
     assert b"rows" in dcopy.lib().dcopy_last_error_message()
+
+
+def test_nd_tma_selection_round_trips(dcopy):
+    """dcopy_set_nd_tma is host state only: it reports the former setting."""
+    first = dcopy.set_nd_tma(True)
+    assert dcopy.set_nd_tma(False) is True
+    assert dcopy.set_nd_tma(first) is False

@@ -33,6 +33,7 @@ def _case(torch, dcopy, oracle, shape, perm, eb, seed):
     ([8, 16, 24, 32], [0, 2, 3, 1]), ([8, 24, 32, 16], [0, 3, 1, 2]), ([5, 7, 9, 11], [3, 2, 1, 0]),
     ([16, 16, 16, 16], [0, 2, 1, 3]), ([4, 6, 8, 10, 12], [4, 0, 3, 1, 2]),
     ([2, 3, 5, 7, 64], [1, 3, 0, 2, 4]), ([33, 65, 2], [2, 1, 0]), ([256, 256, 3, 3], [2, 3, 1, 0]),
+    ([5, 7, 37], [1, 0, 2]), ([3, 4, 5, 33], [2, 0, 1, 3]),  # odd rows kept innermost
 ])
 def test_permutes(torch_cuda, dcopy, oracle, eb, shape, perm):
     _case(torch_cuda, dcopy, oracle, shape, perm, eb, sum(shape) + eb)
