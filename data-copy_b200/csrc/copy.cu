@@ -46,6 +46,9 @@ constexpr int kCtasPerSm = 8;
 #ifndef DCOPY_PREFETCH
 #define DCOPY_PREFETCH 1  // L2-prefetch the source while waiting on the previous kernel
 #endif
+#ifndef DCOPY_COPY2D_SHIFT
+#define DCOPY_COPY2D_SHIFT 1  // bursts of 1/2/4-byte units through the funnel-shift row kernel
+#endif
 #ifndef DCOPY_STRIDED_U
 #define DCOPY_STRIDED_U 4  // elements in flight per thread (strided copy)
 #endif
@@ -304,6 +307,16 @@ int copy2d(void *dst, const void *src, uint64_t rows, uint64_t row_bytes, uint64
       if (rc) return rc;
     }
     return DCOPY_OK;
+  }
+  // Bursts only 1- or 2-byte units tile, and long bursts of 4-byte units:
+  // aligned 16-byte destination vectors assembled by funnel shifts (rows.cu).
+  // Measured on B200: 30 B bursts in 2-byte units 2213 -> 2363 GB/s, 4092 B in
+  // 4-byte units 3401 -> 5236; 36 B and 100 B bursts stay faster in 4-byte units.
+  if (DCOPY_COPY2D_SHIFT && shift_rows_pay(w, row_bytes) && row_bytes < (uint64_t(1) << 30) &&
+      rows <= 0xFFFFFFFFull) {
+    const uint64_t size[2] = {rows, row_bytes};
+    const int64_t ss[2] = {(int64_t)src_pitch, 1}, ds[2] = {(int64_t)dst_pitch, 1};
+    return rows_shift(dst, src, 2, size, ss, ds, 1, s);
   }
   switch (w) {
     case 16: return launch_strided<uint4>(d, sp, rows, row_bytes, src_pitch, dst_pitch, s);

@@ -69,6 +69,12 @@ int permute_copy(void *dst, const void *src, int m, const uint64_t *size, const 
 // shifts (rows.cu).  ds == NULL: contiguous destination.
 int rows_shift(void *dst, const void *src, int m, const uint64_t *size, const int64_t *ss,
                const int64_t *ds, int eb, cudaStream_t s);
+// Whether rows of row_bytes whose widest common unit is `unit` bytes move faster
+// through rows_shift than in units: 1- and 2-byte units always, 4-byte units
+// from 256-byte rows on.
+inline bool shift_rows_pay(uint32_t unit, uint64_t row_bytes) {
+  return row_bytes >= 16 && (unit <= 2 || (unit == 4 && row_bytes >= 256));
+}
 
 // Rows of a <=5-D box whose innermost axis is contiguous on both sides
 // (permute.cu); *taken = false when the row kernel does not apply.

@@ -238,8 +238,11 @@ def _ptr(x) -> Optional[int]:
     if isinstance(x, int):
         return x
     if hasattr(x, "data_ptr"):
-        if getattr(x, "is_cuda", True) is False:
-            raise ValueError("dcopy kernels need CUDA tensors (got a CPU tensor)")
+        if getattr(x, "is_cuda", True) is False and not x.is_pinned():
+            # Pinned host memory is GPU-addressable (the kernels read and write it over
+            # PCIe); pageable host memory is not.
+            raise ValueError("dcopy kernels need CUDA or pinned host tensors (got a pageable "
+                             "CPU tensor)")
         return x.data_ptr()
     raise TypeError(f"expected a CUDA tensor or a device address, got {type(x).__name__}")
 

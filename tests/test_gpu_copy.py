@@ -28,6 +28,8 @@ CASES = [  # (blockCount, blockLen, srcGap, dstGap, src_offset, dst_offset)
     (1023, 128, 512, 0, 0, 0), (64, 512, 2048, 512, 0, 0), (17, 4096, 12288, 0, 0, 0),
     (5, 65536, 65536, 32, 0, 0), (3, 1 << 20, 1 << 16, 0, 0, 0), (1, 1 << 22, 0, 0, 3, 7),
     (4096, 4, 4092, 0, 0, 0), (65536, 2, 6, 0, 2, 0),
+    (2000, 77, 13, 5, 3, 9), (500, 1000, 24, 8, 6, 2), (4096, 20, 12, 0, 0, 4),
+    (129, 4099, 1, 3, 1, 0), (3000, 18, 0, 14, 15, 1),  # bursts of 1/2/4-byte units
 ]
 
 
@@ -159,3 +161,29 @@ def test_copy_nd_matches_oracle(torch_cuda, dcopy, oracle, case):
     dcopy.copy_nd(dst, src, sizes, ss, ds, eb)
     torch.cuda.synchronize()
     assert dst.cpu().numpy().tobytes() == dst_np.tobytes()
+
+
+def test_pinned_host_buffers(torch_cuda, dcopy, oracle):
+    """Source and destination in pinned host memory: the kernels read and write them
+    over PCIe (the end-to-end path of the bench); pageable tensors are refused."""
+    torch = torch_cuda
+    count, blen, sgap = 300, 4096, 12288
+    src_np = _rand_bytes(count * (blen + sgap), seed=11)
+    expect = np.full(count * blen, CANARY, dtype=np.uint8)
+    oracle.copy_ext(expect, src_np, count, blen, sgap, 0)
+    h_src = torch.from_numpy(src_np).pin_memory()
+    h_dst = torch.full((count * blen,), CANARY, dtype=torch.uint8).pin_memory()
+    dcopy.copy_ext(h_dst, h_src, count, blen, sgap, 0)
+    torch.cuda.synchronize()
+    assert h_dst.numpy().tobytes() == expect.tobytes()
+    # An NDDMA box from device memory into a pinned host buffer (odd rows: shift kernel).
+    sizes, ss, ds = [4, 9, 55], [9 * 60, 60, 1], [9 * 55, 55, 1]
+    box_np = _rand_bytes(4 * 9 * 60 * 2, seed=12)
+    box_exp = np.full(4 * 9 * 55 * 2, CANARY, dtype=np.uint8)
+    assert oracle.copy_nd(box_exp, box_np, sizes, ss, ds, 2) == 0
+    h_box = torch.full((box_exp.size,), CANARY, dtype=torch.uint8).pin_memory()
+    dcopy.copy_nd(h_box, torch.from_numpy(box_np).cuda(), sizes, ss, ds, 2)
+    torch.cuda.synchronize()
+    assert h_box.numpy().tobytes() == box_exp.tobytes()
+    with pytest.raises(ValueError):
+        dcopy.copy_ext(torch.empty(16, dtype=torch.uint8), h_src, 1, 16, 0, 0)
