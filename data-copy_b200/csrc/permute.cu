@@ -36,6 +36,14 @@ constexpr int kMaxRowDims = 4;
 #ifndef DCOPY_ROWS_SHIFT
 #define DCOPY_ROWS_SHIFT 1  // rows of 1/2/4-byte units through rows_shift (shift_rows_pay)
 #endif
+#ifndef DCOPY_PERM_MINB1
+#define DCOPY_PERM_MINB1 7  // 1-byte packed tiles: resident CTAs per SM the registers must allow
+                            // (measured: 59 registers, 4 CTAs/SM 4445-4780 GB/s; 32, 7 CTAs/SM
+                            // 5578-5966 on B200)
+#endif
+#ifndef DCOPY_PERM_MINB
+#define DCOPY_PERM_MINB 8  // wider packed tiles: resident CTAs per SM the registers must allow
+#endif
 #ifndef DCOPY_PERM_TD2
 #define DCOPY_PERM_TD2 64  // 2-byte elements: tile rows (destination axis)
 #endif
@@ -214,7 +222,8 @@ __global__ void __launch_bounds__(kThreads) perm_tile_kernel(T *__restrict__ dst
 // shared row are XOR-swizzled with the row's e-vector index, so the word stores
 // of those 32 lanes hit 32 distinct banks and the chunk loads stay conflict-free.
 template <typename T, int V, int G, int TD, int TE>
-__global__ void __launch_bounds__(kThreads) perm_tile_packed_kernel(T *__restrict__ dst,
+__global__ void __launch_bounds__(kThreads, sizeof(T) == 1 ? DCOPY_PERM_MINB1 : DCOPY_PERM_MINB)
+    perm_tile_packed_kernel(T *__restrict__ dst,
                                                                     const T *__restrict__ src,
                                                                     PermTGeom g,
                                                                     uint32_t ntiles) {
