@@ -415,6 +415,26 @@ def run_secondary(torch, dcopy, dev):
             dcopy.copy_ext_32b(b[i], a[i], 128, 128, 0, 0)
     ms = _time_graph(torch, sixteen, reps=50) / 16
     out["config1_contiguous_512KiB_us"] = round(ms * 1e3, 2)
+    # Config 1 with the reference's own structure: 8 cores x 16 tiles, one 4 KiB
+    # DataCopy per tile -- 128 calls, or one dcopy_copy_ext_batch of 128 copies.
+    x, y = a[0], b[0]
+    tiles = [(y[i * 2048:], x[i * 2048:], 1, 4096, 0, 0) for i in range(128)]
+
+    def per_tile():
+        for (d, s, n_, l_, g1, g2) in tiles:
+            dcopy.copy_ext(d, s, n_, l_, g1, g2)
+    out["config1_128_tile_calls_us"] = round(_time_graph(torch, per_tile, reps=20) * 1e3, 2)
+    out["config1_128_tiles_one_batch_us"] = round(
+        _time_graph(torch, lambda: dcopy.copy_ext_batch(tiles), reps=50) * 1e3, 2)
+    del a, b
+    # Config 2's 16 gathers of one step as a single batch (one launch instead of 16).
+    base = torch.empty(ROWS, COLS, device=dev)
+    srcs = [torch.empty_like(base) for _ in range(SETS)]
+    dsts = [torch.empty(ROWS, C1 - C0, device=dev) for _ in range(SETS)]
+    gathers = [(dsts[i], srcs[i][:, C0:], ROWS, BLOCK_LEN, SRC_GAP, 0) for i in range(SETS)]
+    ms = _time_graph(torch, lambda: dcopy.copy_ext_batch(gathers), reps=20)
+    out["config2_16_gathers_one_batch_GBps"] = round(
+        BYTES_PER_GATHER * SETS / (ms / 1e3) / 1e9, 1)
     return out
 
 

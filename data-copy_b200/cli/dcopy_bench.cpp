@@ -35,7 +35,8 @@
 //       sending GPU) and as a pull (launched on the receiving GPU), and the copy
 //       engine, each with both GPUs sending at once and with one sending.
 //
-// Timing: CUDA events around each launch; a 512 MiB read between reps (load-only
+// Timing: 3 untimed warm-up calls, then CUDA events around each launch (median of
+// 20 reps by default); a 512 MiB read between reps (load-only
 // mode, so L2 holds only clean lines) evicts the 126 MB L2: every rep reads cold
 // data and no flush write-back falls inside the timed region.
 #include <cuda_runtime.h>
@@ -114,12 +115,17 @@ void read_flush(DevBuf &flush, cudaStream_t s) {
                                      reinterpret_cast<dcopy_stream_t>(s)));
 }
 
-// Times `fn` (one or more launches on `s`) `reps` times with an L2 flush between reps.
+constexpr int kWarmupReps = 3;
+
+// Times `fn` (one or more launches on `s`) `reps` times with an L2 flush between reps,
+// after kWarmupReps untimed calls.
 template <typename F>
 std::vector<double> time_reps(F fn, int reps, cudaStream_t s, DevBuf &flush) {
   cudaEvent_t a, b;
   Check(cudaEventCreate(&a), "event");
   Check(cudaEventCreate(&b), "event");
+  for (int r = 0; r < kWarmupReps; ++r) fn();  // untimed warm-up
+  Check(cudaStreamSynchronize(s), "sync");
   std::vector<double> us;
   for (int r = 0; r < reps; ++r) {
     read_flush(flush, s);
@@ -186,7 +192,7 @@ double model_gbps(double peak, uint64_t blen, uint64_t gap) {
 
 int run_sweep(const Args &a) {
   const uint64_t moved = uint64_t(a.num("moved-mib", 256)) << 20;
-  const int reps = int(a.num("reps", 10));
+  const int reps = int(a.num("reps", 20));
   const double peak = a.num("peak", 6543.4);
   Check(cudaSetDevice(int(a.num("device", 0))), "cudaSetDevice");
   cudaStream_t s;
@@ -370,7 +376,7 @@ int run_standalone(const Args &a) {
 int run_nz(const Args &a) {
   const int64_t shape[3] = {int64_t(a.num("batch", 16)), int64_t(a.num("h", 4096)),
                             int64_t(a.num("w", 4096))};
-  const int reps = int(a.num("reps", 10));
+  const int reps = int(a.num("reps", 20));
   const double peak = a.num("peak", 6543.4);
   const int64_t c0 = int64_t(a.num("c0", 16));
   const bool zz_format = a.str("format", "nz") == "zz";
@@ -425,7 +431,7 @@ int run_fz(const Args &a) {
   const int64_t h = int64_t(a.num("h", 3)), w = int64_t(a.num("w", 3));
   const int eb = int(a.num("eb", 2));
   const int64_t c0 = int64_t(a.num("c0", 16));
-  const int reps = int(a.num("reps", 10));
+  const int reps = int(a.num("reps", 20));
   const double peak = a.num("peak", 6543.4);
   Check(cudaSetDevice(int(a.num("device", 0))), "cudaSetDevice");
   cudaStream_t s;
@@ -490,7 +496,7 @@ int run_transpose(const Args &a) {
   const std::vector<int64_t> shape = parse_list(a.str("shape", "32,256,56,56"));
   const std::vector<int64_t> perm = parse_list(a.str("perm", "0,2,3,1"));
   const int eb = int(a.num("eb", 2));
-  const int reps = int(a.num("reps", 10));
+  const int reps = int(a.num("reps", 20));
   const double peak = a.num("peak", 6543.4);
   const int rank = int(shape.size());
   if (perm.size() != shape.size()) throw std::runtime_error("--perm and --shape differ in rank");
@@ -549,7 +555,7 @@ int run_nd(const Args &a) {
   const std::vector<int64_t> sz = parse_list(a.str("sizes", "64,1024,1024"));
   const int eb = int(a.num("eb", 2));
   const int64_t sp = int64_t(a.num("src-pad", 8)), dp = int64_t(a.num("dst-pad", 0));
-  const int reps = int(a.num("reps", 10));
+  const int reps = int(a.num("reps", 20));
   const double peak = a.num("peak", 6543.4);
   const int nd = int(sz.size());
   const int tma = int(a.num("tma", 0));

@@ -211,6 +211,7 @@ _SIGNATURES = {
     "dcopy_wait_signal": (ctypes.c_int, [_vp, ctypes.c_uint32, ctypes.c_uint64, _vp, _vp]),
     "dcopy_tma_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32)]),
     "dcopy_set_nd_tma": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
+    "dcopy_copy_ext_batch": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p]),
 }
 
 
@@ -303,6 +304,22 @@ def datacopy_contiguous(b, y, tiling: DataCopyTiling, stream=None) -> None:
 def datacopy_pretranspose_noalloc(x, y, tiling: DataCopyTiling, stream=None) -> None:
     """x -> B -> y without any allocation (B lives in the library's 16 MiB device array)."""
     _datacopy("dcopy_datacopy_pretranspose_noalloc", x, y, tiling, stream)
+
+
+class DcopyExtCopy(ctypes.Structure):
+    _fields_ = [("dst", ctypes.c_void_p), ("src", ctypes.c_void_p), ("params", DcopyExtParams)]
+
+
+def copy_ext_batch(copies, stream=None) -> None:
+    """Independent copies (dst, src, block_count, block_len, src_stride, dst_stride) in one
+    batch: one launch per 256 copies; destinations may not overlap other copies' spans."""
+    arr = (DcopyExtCopy * max(len(copies), 1))()
+    for i, (dst, src, count, blen, sgap, dgap) in enumerate(copies):
+        arr[i].dst = _ptr(dst)
+        arr[i].src = _ptr(src)
+        arr[i].params = DcopyExtParams(count, blen, sgap, dgap)
+    _check(lib().dcopy_copy_ext_batch(arr if copies else None, len(copies), _stream(stream)),
+           "dcopy_copy_ext_batch")
 
 
 def copy_ext(dst, src, block_count: int, block_len: int, src_stride: int = 0,

@@ -129,6 +129,23 @@ typedef struct DcopyExtParams {
 int dcopy_copy_ext(void *dst, const void *src, const DcopyExtParams *params,
                    dcopy_stream_t stream);
 
+/* One copy of a batch: dcopy_copy_ext(dst, src, &params) as a record. */
+typedef struct DcopyExtCopy {
+  void *dst;
+  const void *src;
+  DcopyExtParams params;
+} DcopyExtCopy;
+
+/* `count` independent dcopy_copy_ext copies in as few launches as possible (one
+ * per 256 copies; copies above 2^30 elements launch on their own).  An Ascend C
+ * kernel issues many DataCopy calls per launch (the standalone kernel moves
+ * each tile with one, datacopy_data_collection.asc:16-62); this is that shape
+ * for a host ABI.  Every copy is validated as dcopy_copy_ext validates it, and
+ * because the copies run concurrently no destination may overlap another
+ * copy's destination or source (DCOPY_ERR_PARAM_INVALID, nothing launched).
+ * No counterpart in the reference's host API. */
+int dcopy_copy_ext_batch(const DcopyExtCopy *copies, uint32_t count, dcopy_stream_t stream);
+
 /* Same copy with blockLen and both gaps in 32-byte units (AscendC DataCopyParams
  * units; BASELINE expresses configs 1, 2, 3 and 5 this way). */
 int dcopy_copy_ext_32b(void *dst, const void *src, uint32_t blockCount, uint32_t blockLen32,
@@ -433,6 +450,7 @@ int dcopy_wait_signal(const uint32_t *flag, uint32_t value, uint64_t timeout_ns,
 #ifdef __cplusplus
 }  /* extern "C" */
 static_assert(sizeof(DcopyExtParams) == 24, "DcopyExtParams layout");
+static_assert(sizeof(DcopyExtCopy) == 40, "DcopyExtCopy layout");
 #endif
 
 #endif /* DCOPY_DCOPY_H_ */

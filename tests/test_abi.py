@@ -153,3 +153,10 @@ def test_nd_tma_selection_round_trips(dcopy):
     first = dcopy.set_nd_tma(True)
     assert dcopy.set_nd_tma(False) is True
     assert dcopy.set_nd_tma(first) is False
+
+
+def test_copy_ext_batch_argument_checks(dcopy):
+    """Decided on the host before any device work: an empty batch is a no-op, a NULL
+    array with a count is refused."""
+    dcopy.copy_ext_batch([])
+    assert dcopy.lib().dcopy_copy_ext_batch(None, 3, None) == dcopy.ERR_PARAM_INVALID

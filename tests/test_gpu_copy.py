@@ -187,3 +187,54 @@ def test_pinned_host_buffers(torch_cuda, dcopy, oracle):
     assert h_box.numpy().tobytes() == box_exp.tobytes()
     with pytest.raises(ValueError):
         dcopy.copy_ext(torch.empty(16, dtype=torch.uint8), h_src, 1, 16, 0, 0)
+
+
+@pytest.mark.parametrize("n_copies", [1, 7, 128, 300])
+def test_copy_ext_batch_matches_oracle(torch_cuda, dcopy, oracle, n_copies):
+    """Independent copies of random shapes (aligned and unaligned) in one batch; 300
+    copies take two launches.  Each destination region is checked with the oracle and
+    the bytes between regions must keep their canary."""
+    torch = torch_cuda
+    rng = np.random.default_rng(n_copies)
+    src_np = _rand_bytes(1 << 22, seed=n_copies + 1)
+    src = torch.from_numpy(src_np).cuda()
+    expect = np.full(1 << 23, CANARY, dtype=np.uint8)
+    dst = _canary(torch, expect.size)
+    copies, at = [], 0
+    for _ in range(n_copies):
+        count = int(rng.integers(1, 40))
+        blen = int(rng.choice([int(rng.integers(1, 200)), 16 * int(rng.integers(1, 40))]))
+        sgap, dgap = int(rng.integers(0, 100)), int(rng.integers(0, 20))
+        src_span = (count - 1) * (blen + sgap) + blen
+        dst_span = (count - 1) * (blen + dgap) + blen
+        soff = int(rng.integers(0, src_np.size - src_span))
+        at += int(rng.integers(0, 40))
+        oracle.copy_ext(expect[at:], src_np[soff:], count, blen, sgap, dgap)
+        copies.append((dst.data_ptr() + at, src.data_ptr() + soff, count, blen, sgap, dgap))
+        at += dst_span
+    assert at < expect.size
+    dcopy.copy_ext_batch(copies)
+    torch.cuda.synchronize()
+    assert dst.cpu().numpy().tobytes() == expect.tobytes()
+
+
+def test_copy_ext_batch_refuses_overlaps(torch_cuda, dcopy):
+    torch = torch_cuda
+    a = _canary(torch, 1 << 16)
+    b = torch.zeros(1 << 16, dtype=torch.uint8, device="cuda")
+    base_a, base_b = a.data_ptr(), b.data_ptr()
+    # Two destinations overlapping: refused, nothing written.
+    with pytest.raises(dcopy.DcopyError) as e:
+        dcopy.copy_ext_batch([(base_a, base_b, 1, 256, 0, 0), (base_a + 128, base_b + 4096, 1, 256, 0, 0)])
+    assert e.value.code == dcopy.ERR_PARAM_INVALID
+    # A destination overlapping another copy's source: refused.
+    with pytest.raises(dcopy.DcopyError) as e:
+        dcopy.copy_ext_batch([(base_a, base_b, 1, 256, 0, 0), (base_b + 8192, base_a + 64, 1, 64, 0, 0)])
+    assert e.value.code == dcopy.ERR_PARAM_INVALID
+    torch.cuda.synchronize()
+    assert (a.cpu().numpy() == CANARY).all()
+    # Sources may overlap each other.
+    dcopy.copy_ext_batch([(base_a, base_b, 4, 64, 0, 0), (base_a + 1024, base_b + 32, 4, 64, 0, 0)])
+    torch.cuda.synchronize()
+    out = a.cpu().numpy()
+    assert (out[:256] == 0).all() and (out[1024:1280] == 0).all() and (out[256:1024] == CANARY).all()
