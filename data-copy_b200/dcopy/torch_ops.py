@@ -13,6 +13,13 @@ as operators in the ``dcopy`` namespace, on CUDA tensors:
                                                       DataCopyExt gather into a packed tensor
   torch.ops.dcopy.copy_ext_(dst, src, count, block_len, src_gap, dst_gap)
                                                       DataCopyExt in place (mutates dst)
+  torch.ops.dcopy.box(x, sizes, strides, offset)      DataCopyNddma: the strided box of x
+                                                      (element strides/offset) packed
+  torch.ops.dcopy.nd_to_zz(x, c0) / zz_to_nd(x_zz, nd_shape, c0)
+                                                      ND <-> FRACTAL_ZZ
+  torch.ops.dcopy.to_fractal_z(w, src_format, c0)     NCHW / NHWC / HWCN / ND weight -> FRACTAL_Z
+  torch.ops.dcopy.from_fractal_z(w_fz, dst_format, dst_shape, c0)
+                                                      FRACTAL_Z -> NCHW / NHWC / HWCN
 
 Lengths and gaps of the DataCopyExt operators count ELEMENTS of the tensors'
 dtype (as DataCopyPadExtend's arguments do, datacopy.h:14-40).  Each operator
@@ -132,3 +139,98 @@ def copy_ext_(dst: torch.Tensor, src: torch.Tensor, count: int, block_len: int, 
 @copy_ext_.register_fake
 def _copy_ext_fake(dst, src, count, block_len, src_gap, dst_gap):
     return None
+
+
+@custom_op("dcopy::box", mutates_args=(), device_types="cuda")
+def box(x: torch.Tensor, sizes: List[int], strides: List[int], offset: int = 0) -> torch.Tensor:
+    """torch.as_strided(x, sizes, strides, offset).contiguous(), moved by dcopy_copy_nd."""
+    _require_cuda(x)
+    if len(sizes) != len(strides) or not 1 <= len(sizes) <= 5:
+        raise ValueError("box: sizes and strides must have the same rank, 1..5")
+    x = x.contiguous()
+    last = offset + sum((n - 1) * st for n, st in zip(sizes, strides) if n > 0)
+    if offset < 0 or min(strides) < 0 or (all(n > 0 for n in sizes) and last >= x.numel()):
+        raise ValueError("box: the box runs outside x")
+    out = torch.empty(list(sizes), dtype=x.dtype, device=x.device)
+    if out.numel():
+        dense = [1] * len(sizes)
+        for k in range(len(sizes) - 2, -1, -1):
+            dense[k] = dense[k + 1] * sizes[k + 1]
+        dcopy.copy_nd(out, x.data_ptr() + offset * x.element_size(), list(sizes), list(strides),
+                      dense, x.element_size())
+    return out
+
+
+@box.register_fake
+def _box_fake(x, sizes, strides, offset=0):
+    return x.new_empty(list(sizes))
+
+
+@custom_op("dcopy::nd_to_zz", mutates_args=(), device_types="cuda")
+def nd_to_zz(x: torch.Tensor, c0: int = 16) -> torch.Tensor:
+    _require_cuda(x)
+    x = x.contiguous()
+    zz, _ = dcopy.zz_shape(list(x.shape), c0)
+    out = torch.empty(zz, dtype=x.dtype, device=x.device)
+    dcopy.nd_to_zz(out, x, list(x.shape), x.element_size(), c0)
+    return out
+
+
+@nd_to_zz.register_fake
+def _nd_to_zz_fake(x, c0=16):
+    zz, _ = dcopy.zz_shape(list(x.shape), c0)
+    return x.new_empty(zz)
+
+
+@custom_op("dcopy::zz_to_nd", mutates_args=(), device_types="cuda")
+def zz_to_nd(x: torch.Tensor, nd_shape: List[int], c0: int = 16) -> torch.Tensor:
+    _require_cuda(x)
+    zz, _ = dcopy.zz_shape(list(nd_shape), c0)
+    if list(x.shape) != zz:
+        raise ValueError(f"ZZ tensor shape {list(x.shape)} is not the ZZ shape {zz} of {nd_shape}")
+    x = x.contiguous()
+    out = torch.empty(list(nd_shape), dtype=x.dtype, device=x.device)
+    dcopy.zz_to_nd(out, x, list(nd_shape), x.element_size(), c0)
+    return out
+
+
+@zz_to_nd.register_fake
+def _zz_to_nd_fake(x, nd_shape, c0=16):
+    return x.new_empty(list(nd_shape))
+
+
+def _weight_format(name: str) -> int:
+    if name not in ("NCHW", "NHWC", "HWCN", "ND"):
+        raise ValueError(f"FRACTAL_Z weights are NCHW, NHWC, HWCN or ND, not {name}")
+    return dcopy.FORMAT[name]
+
+
+@custom_op("dcopy::to_fractal_z", mutates_args=(), device_types="cuda")
+def to_fractal_z(w: torch.Tensor, src_format: str, c0: int = 16) -> torch.Tensor:
+    _require_cuda(w)
+    fmt = _weight_format(src_format)
+    w = w.contiguous()
+    out = torch.empty(dcopy.fz_shape(fmt, list(w.shape), c0), dtype=w.dtype, device=w.device)
+    dcopy.to_fractal_z(out, w, fmt, list(w.shape), w.element_size(), c0)
+    return out
+
+
+@to_fractal_z.register_fake
+def _to_fractal_z_fake(w, src_format, c0=16):
+    return w.new_empty(dcopy.fz_shape(_weight_format(src_format), list(w.shape), c0))
+
+
+@custom_op("dcopy::from_fractal_z", mutates_args=(), device_types="cuda")
+def from_fractal_z(w: torch.Tensor, dst_format: str, dst_shape: List[int],
+                   c0: int = 16) -> torch.Tensor:
+    _require_cuda(w)
+    fmt = _weight_format(dst_format)
+    w = w.contiguous()
+    out = torch.empty(list(dst_shape), dtype=w.dtype, device=w.device)
+    dcopy.from_fractal_z(out, w, fmt, list(dst_shape), w.element_size(), c0)
+    return out
+
+
+@from_fractal_z.register_fake
+def _from_fractal_z_fake(w, dst_format, dst_shape, c0=16):
+    return w.new_empty(list(dst_shape))
