@@ -25,7 +25,7 @@
 //       GE Transpose (dcopy_transpose) of a dense tensor, verified against a host
 //       restatement; one JSON line.
 //   dcopy_bench nd [--sizes A,B,C[,D,E]] [--eb B] [--src-pad P] [--dst-pad Q] [--tma 0|1]
-//                  [--reps R] [--device D] [--peak GBPS]
+//                  [--src-order O0,O1,..] [--reps R] [--device D] [--peak GBPS]
 //       DataCopyNddma box (dcopy_copy_nd) between padded views, verified; one JSON
 //       line: event time around the call, the same call replayed as a CUDA graph,
 //       and the host time of one call.  --tma 1 selects the TMA tensor-copy path
@@ -567,7 +567,19 @@ int run_nd(const Args &a) {
     ss[k] = ss[k + 1] * (sz[k + 1] + sp);
     ds[k] = ds[k + 1] * (sz[k + 1] + dp);
   }
-  const uint64_t src_n = uint64_t(ss[0]) * sz[0], dst_n = uint64_t(ds[0]) * sz[0];
+  // --src-order: the box axes in the source's memory order, outermost first (an
+  // NHWC box of an NCHW tensor is 0,3,1,2); pads apply as above.
+  if (a.opt.count("src-order")) {
+    const std::vector<int64_t> order = parse_list(a.str("src-order", ""));
+    if ((int)order.size() != nd) throw std::runtime_error("--src-order needs one entry per axis");
+    int64_t step = 1;
+    for (int i = nd - 1; i >= 0; --i) {
+      ss[order[i]] = step;
+      step *= sz[order[i]] + (i == nd - 1 ? 0 : sp);
+    }
+  }
+  uint64_t src_n = 1, dst_n = uint64_t(ds[0]) * sz[0];
+  for (int k = 0; k < nd; ++k) src_n += uint64_t(sz[k] - 1) * ss[k];
   uint64_t n = 1;
   for (auto d : sz) n *= uint64_t(d);
   Check(cudaSetDevice(int(a.num("device", 0))), "cudaSetDevice");
