@@ -489,18 +489,14 @@ extern "C" int dcopy_copy_nd(void *dst, const void *src, int ndim, const uint64_
                               stream, &taken);
     if (taken || rrc) return rrc;
   }
-  // A packed destination read from a source whose unit-stride axis is another
-  // one (an NCHW tensor read as an NHWC box): the Transpose tile kernels.
+  // A destination with contiguous rows read through a source whose unit-stride
+  // axis is another one (an NCHW tensor read as an NHWC box): the Transpose tile
+  // kernels, which take any destination strides but the innermost.
   {
-    bool packed = dst_strides[ndim - 1] == 1, unit_src = false;
-    uint64_t want = sizes[ndim - 1];
-    for (int k = ndim - 2; k >= 0; --k) {
-      if ((uint64_t)dst_strides[k] != want) packed = false;
-      want *= sizes[k];
-    }
+    bool rows = dst_strides[ndim - 1] == 1, unit_src = false;
     for (int k = 0; k < ndim - 1; ++k) unit_src = unit_src || src_strides[k] == 1;
-    for (int k = 0; k < ndim; ++k) packed = packed && sizes[k] <= 0x7FFFFFFFull;
-    if (packed && unit_src && src_strides[ndim - 1] != 1)
+    for (int k = 0; k < ndim; ++k) rows = rows && sizes[k] <= 0x7FFFFFFFull;
+    if (rows && unit_src && src_strides[ndim - 1] != 1)
       return permute_copy(dst, src, ndim, sizes, src_strides, dst_strides, (int)elem_bytes,
                           stream);
   }

@@ -147,3 +147,36 @@ def test_shifted_rows_match_oracle(torch_cuda, dcopy, oracle, seed):
     dcopy.copy_nd(dst.data_ptr() + doff, src.data_ptr() + soff, sizes, ss, ds, eb)
     torch.cuda.synchronize()
     assert dst.cpu().numpy().tobytes() == expect.tobytes()
+
+
+PERMUTED = [  # (sizes, src memory order outermost first, src pad, dst pad, elem bytes)
+    ([4, 14, 14, 40], [0, 3, 1, 2], 0, 0, 2), ([4, 14, 14, 40], [0, 3, 1, 2], 3, 5, 2),
+    ([30, 70], [1, 0], 2, 3, 4), ([3, 33, 65], [0, 2, 1], 1, 0, 1), ([5, 6, 7, 8, 9], [4, 3, 2, 1, 0], 0, 2, 8),
+    ([2, 3, 40, 24], [1, 0, 3, 2], 4, 1, 16),
+]
+
+
+@pytest.mark.parametrize("case", PERMUTED, ids=lambda c: f"{c[0]}-{c[1]}-e{c[4]}")
+def test_permuted_source_boxes(torch_cuda, dcopy, oracle, case):
+    """Boxes whose source's unit-stride axis is not the innermost box axis and whose
+    destination rows are contiguous (packed or padded): the Transpose tile kernels."""
+    torch = torch_cuda
+    sizes, order, sp, dp, eb = case
+    m = len(sizes)
+    ss = [0] * m
+    step = 1
+    for i in range(m - 1, -1, -1):
+        ss[order[i]] = step
+        step *= sizes[order[i]] + (sp if i < m - 1 else 0)
+    ds = _strides(sizes, dp)
+    src_elems = sum((s - 1) * st for s, st in zip(sizes, ss)) + 1
+    dst_elems = sum((s - 1) * st for s, st in zip(sizes, ds)) + 1
+    src_np = np.random.default_rng(sum(sizes) * eb).integers(0, 256, size=src_elems * eb,
+                                                             dtype=np.uint8)
+    expect = np.full(dst_elems * eb, CANARY, dtype=np.uint8)
+    assert oracle.copy_nd(expect, src_np, sizes, ss, ds, eb) == 0
+    src = torch.from_numpy(src_np).cuda()
+    dst = torch.full((dst_elems * eb,), CANARY, dtype=torch.uint8, device="cuda")
+    dcopy.copy_nd(dst, src, sizes, ss, ds, eb)
+    torch.cuda.synchronize()
+    assert dst.cpu().numpy().tobytes() == expect.tobytes()
