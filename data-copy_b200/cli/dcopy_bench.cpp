@@ -25,7 +25,8 @@
 //       GE Transpose (dcopy_transpose) of a dense tensor, verified against a host
 //       restatement; one JSON line.
 //   dcopy_bench nd [--sizes A,B,C[,D,E]] [--eb B] [--src-pad P] [--dst-pad Q] [--tma 0|1]
-//                  [--src-order O0,O1,..] [--reps R] [--device D] [--peak GBPS]
+//                  [--src-order O0,O1,..] [--dst-order O0,O1,..] [--reps R] [--device D]
+//                  [--peak GBPS]
 //       DataCopyNddma box (dcopy_copy_nd) between padded views, verified; one JSON
 //       line: event time around the call, the same call replayed as a CUDA graph,
 //       and the host time of one call.  --tma 1 selects the TMA tensor-copy path
@@ -578,8 +579,20 @@ int run_nd(const Args &a) {
       step *= sz[order[i]] + (i == nd - 1 ? 0 : sp);
     }
   }
-  uint64_t src_n = 1, dst_n = uint64_t(ds[0]) * sz[0];
-  for (int k = 0; k < nd; ++k) src_n += uint64_t(sz[k] - 1) * ss[k];
+  if (a.opt.count("dst-order")) {  // the same for the destination
+    const std::vector<int64_t> order = parse_list(a.str("dst-order", ""));
+    if ((int)order.size() != nd) throw std::runtime_error("--dst-order needs one entry per axis");
+    int64_t step = 1;
+    for (int i = nd - 1; i >= 0; --i) {
+      ds[order[i]] = step;
+      step *= sz[order[i]] + (i == nd - 1 ? 0 : dp);
+    }
+  }
+  uint64_t src_n = 1, dst_n = 1;
+  for (int k = 0; k < nd; ++k) {
+    src_n += uint64_t(sz[k] - 1) * ss[k];
+    dst_n += uint64_t(sz[k] - 1) * ds[k];
+  }
   uint64_t n = 1;
   for (auto d : sz) n *= uint64_t(d);
   Check(cudaSetDevice(int(a.num("device", 0))), "cudaSetDevice");

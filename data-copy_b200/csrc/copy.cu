@@ -464,6 +464,44 @@ extern "C" int dcopy_copy_nd(void *dst, const void *src, int ndim, const uint64_
     return set_error(DCOPY_ERR_PARAM_INVALID, "copy_nd: buffers not aligned to elem_bytes %u",
                      elem_bytes);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // The box is the same for any order of its axes: drop axes of size 1 and put
+  // the destination's unit-stride axis last, so that the row and tile kernels
+  // below see every box that has a unit-stride axis on each side.
+  uint64_t cz[kMaxNd];
+  int64_t cs[kMaxNd], cd[kMaxNd];
+  int cn = 0;
+  for (int k = 0; k < ndim; ++k)
+    if (sizes[k] > 1) {
+      cz[cn] = sizes[k];
+      cs[cn] = src_strides[k];
+      cd[cn] = dst_strides[k];
+      ++cn;
+    }
+  if (cn == 0) {  // a single element
+    cz[0] = 1;
+    cs[0] = cd[0] = 1;
+    cn = 1;
+  }
+  if (cd[cn - 1] != 1) {
+    for (int k = cn - 2; k >= 0; --k)
+      if (cd[k] == 1) {
+        const uint64_t z = cz[k];
+        const int64_t a = cs[k], b = cd[k];
+        for (int j = k; j < cn - 1; ++j) {
+          cz[j] = cz[j + 1];
+          cs[j] = cs[j + 1];
+          cd[j] = cd[j + 1];
+        }
+        cz[cn - 1] = z;
+        cs[cn - 1] = a;
+        cd[cn - 1] = b;
+        break;
+      }
+  }
+  ndim = cn;
+  sizes = cz;
+  src_strides = cs;
+  dst_strides = cd;
   // Unit-stride innermost dim with <= 2 dims total: a burst copy.
   if (ndim <= 2 && src_strides[ndim - 1] == 1 && dst_strides[ndim - 1] == 1) {
     const uint64_t rows = ndim == 2 ? sizes[0] : 1;
