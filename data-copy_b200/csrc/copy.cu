@@ -498,6 +498,22 @@ extern "C" int dcopy_copy_nd(void *dst, const void *src, int ndim, const uint64_
         break;
       }
   }
+  // Merge neighbours whose strides chain on both sides (axis k steps over a
+  // whole axis k+1): fewer axes, and packed boxes become plain copies.
+  for (int k = cn - 2; k >= 0; --k) {
+    const unsigned __int128 step_s = (unsigned __int128)(uint64_t)cs[k + 1] * cz[k + 1];
+    const unsigned __int128 step_d = (unsigned __int128)(uint64_t)cd[k + 1] * cz[k + 1];
+    if (step_s == (uint64_t)cs[k] && step_d == (uint64_t)cd[k] &&
+        (unsigned __int128)cz[k] * cz[k + 1] <= 0xFFFFFFFFull) {
+      cz[k + 1] *= cz[k];
+      for (int j = k; j < cn - 1; ++j) {
+        cz[j] = cz[j + 1];
+        cs[j] = cs[j + 1];
+        cd[j] = cd[j + 1];
+      }
+      --cn;
+    }
+  }
   ndim = cn;
   sizes = cz;
   src_strides = cs;
