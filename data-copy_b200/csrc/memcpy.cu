@@ -1,11 +1,17 @@
 // rtMemcpyAsyncWithCfg-shaped memcpy task on the library's copy kernel.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <vector>
+
 #include "common.cuh"
 #include "copy.cuh"
 
 namespace dcopy {
 namespace {
+
+constexpr uint64_t kEngineBytes = 8ull << 20;  // host-side tasks from here on: copy engine
+constexpr uint64_t kPieceBytes = 1ull << 30;
 
 bool is_device_memory(const void *p) {
   cudaPointerAttributes a{};
@@ -14,6 +20,16 @@ bool is_device_memory(const void *p) {
     return false;
   }
   return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+// Memory a kernel can address: device (this GPU, a peer, managed) or pinned host.
+bool gpu_addressable(const void *p) {
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return false;
+  }
+  return a.type != cudaMemoryTypeUnregistered;
 }
 
 int device_to_device(const DcopyMemcpyInfo *m, cudaStream_t s) {
@@ -59,6 +75,69 @@ extern "C" int dcopy_memcpy_async(const DcopyMemcpyInfo *info, int32_t kind,
     default: return set_error(DCOPY_ERR_PARAM_INVALID, "memcpy: unknown kind %d", kind);
   }
   DCOPY_CUDA_TRY(cudaMemcpyAsync(info->dst, info->src, info->cnt, k, s));
+  return DCOPY_OK;
+  DCOPY_API_END
+}
+
+// Tasks whose two buffers a kernel can address (device memory, or pinned host
+// memory read and written over PCIe) and that are small enough for the launch
+// cost to matter go to one dcopy_copy_ext_batch: one launch per 256 tasks
+// instead of one copy call each.  Larger host-side transfers and pageable
+// host memory take the copy engine, one cudaMemcpyAsync each.
+extern "C" int dcopy_memcpy_async_batch(const DcopyMemcpyInfo *infos, uint32_t count,
+                                        int32_t kind, dcopy_stream_t stream) {
+  DCOPY_API_BEGIN
+  if (!count) return DCOPY_OK;
+  if (!infos) return set_error(DCOPY_ERR_PARAM_INVALID, "memcpy_batch: infos is NULL");
+  if (kind == 5)
+    return set_error(DCOPY_ERR_UNSUPPORTED,
+                     "memcpy_batch: RT_MEMCPY_ADDR_DEVICE_TO_DEVICE has no CUDA counterpart");
+  if (kind < 0 || kind > 8)
+    return set_error(DCOPY_ERR_PARAM_INVALID, "memcpy_batch: unknown kind %d", kind);
+  for (uint32_t i = 0; i < count; ++i) {  // every task is checked before anything runs
+    const DcopyMemcpyInfo &m = infos[i];
+    if (m.cnt > m.destMax)
+      return set_error(DCOPY_ERR_PARAM_INVALID,
+                       "memcpy_batch: task %u: count %llu exceeds destMax %llu", i,
+                       (unsigned long long)m.cnt, (unsigned long long)m.destMax);
+    if (m.cnt && (!m.dst || !m.src))
+      return set_error(DCOPY_ERR_PARAM_INVALID, "memcpy_batch: task %u: NULL pointer", i);
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const bool host_side = kind != DCOPY_MEMCPY_DEVICE_TO_DEVICE;
+  std::vector<DcopyExtCopy> batch;
+  std::vector<const DcopyMemcpyInfo *> engine;
+  for (uint32_t i = 0; i < count; ++i) {
+    const DcopyMemcpyInfo &m = infos[i];
+    if (!m.cnt) continue;
+    const bool kernel = kind != DCOPY_MEMCPY_HOST_TO_HOST &&
+                        !(host_side && m.cnt >= kEngineBytes) && gpu_addressable(m.dst) &&
+                        gpu_addressable(m.src);
+    if (!kernel) {
+      engine.push_back(&m);
+      continue;
+    }
+    // Contiguous pieces of at most 1 GiB (blockLen is 32-bit).
+    for (uint64_t off = 0; off < m.cnt; off += kPieceBytes) {
+      const uint64_t n = std::min<uint64_t>(kPieceBytes, m.cnt - off);
+      batch.push_back(DcopyExtCopy{static_cast<uint8_t *>(m.dst) + off,
+                                   static_cast<const uint8_t *>(m.src) + off,
+                                   DcopyExtParams{1u, (uint32_t)n, 0, 0}});
+    }
+  }
+  if (!batch.empty()) {
+    const int rc = dcopy_copy_ext_batch(batch.data(), (uint32_t)batch.size(), stream);
+    if (rc) return rc;
+  }
+  for (const DcopyMemcpyInfo *m : engine) {
+    cudaMemcpyKind k = cudaMemcpyDefault;
+    if (kind == DCOPY_MEMCPY_HOST_TO_HOST) k = cudaMemcpyHostToHost;
+    if (kind == DCOPY_MEMCPY_HOST_TO_DEVICE || kind == DCOPY_MEMCPY_HOST_TO_DEVICE_EX)
+      k = cudaMemcpyHostToDevice;
+    if (kind == DCOPY_MEMCPY_DEVICE_TO_HOST || kind == DCOPY_MEMCPY_DEVICE_TO_HOST_EX)
+      k = cudaMemcpyDeviceToHost;
+    DCOPY_CUDA_TRY(cudaMemcpyAsync(m->dst, m->src, m->cnt, k, s));
+  }
   return DCOPY_OK;
   DCOPY_API_END
 }

@@ -212,6 +212,8 @@ _SIGNATURES = {
     "dcopy_tma_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32)]),
     "dcopy_set_nd_tma": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
     "dcopy_copy_ext_batch": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p]),
+    "dcopy_memcpy_async_batch": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_int32,
+                                                ctypes.c_void_p]),
 }
 
 
@@ -608,6 +610,25 @@ def wait_signal(flag, value: int, timeout_ns: int, status, stream=None) -> None:
     """Bounded device-side wait for *flag == value; writes 0 (seen) / 1 (timeout) to status."""
     _check(lib().dcopy_wait_signal(_ptr(flag), value, timeout_ns, _ptr(status), _stream(stream)),
            "dcopy_wait_signal")
+
+
+def memcpy_async_batch(tasks, kind, stream=None) -> None:
+    """Many memcpy tasks (dst, dst_max, src, count) of one kind; small tasks between
+    device or pinned host buffers run as one batched launch."""
+    if isinstance(kind, str):
+        kind = MEMCPY_KIND[kind]
+
+    def addr(x):
+        if hasattr(x, "data_ptr"):
+            return x.data_ptr()
+        if hasattr(x, "ctypes"):
+            return x.ctypes.data
+        return x
+    arr = (DcopyMemcpyInfo * max(len(tasks), 1))()
+    for i, (dst, dst_max, src, count) in enumerate(tasks):
+        arr[i] = DcopyMemcpyInfo(addr(dst), dst_max, addr(src), count)
+    _check(lib().dcopy_memcpy_async_batch(arr if tasks else None, len(tasks), kind,
+                                          _stream(stream)), "dcopy_memcpy_async_batch")
 
 
 def memcpy_async(dst, dst_max: int, src, count: int, kind, stream=None) -> None:

@@ -379,6 +379,17 @@ typedef struct DcopyMemcpyInfo {  /* MemcpyAsyncMemInfo */
  * cudaMemcpyAsync.  RT_MEMCPY_ADDR_DEVICE_TO_DEVICE (5) is UNSUPPORTED. */
 int dcopy_memcpy_async(const DcopyMemcpyInfo *info, int32_t kind, dcopy_stream_t stream);
 
+/* `count` memcpy tasks of one kind, each checked as dcopy_memcpy_async checks
+ * it (nothing runs if one fails).  Tasks whose buffers are device or pinned
+ * host memory, below 8 MiB when a host side is involved, run together on the
+ * batched copy kernel (one launch per 256 tasks; host buffers are read and
+ * written over PCIe); pageable host memory, larger host-side transfers and
+ * HOST_TO_HOST take cudaMemcpyAsync, one per task, after the batch.  Tasks run
+ * concurrently: a destination may not overlap another task's buffers.
+ * No counterpart in the reference (its tasks are issued one by one). */
+int dcopy_memcpy_async_batch(const DcopyMemcpyInfo *infos, uint32_t count, int32_t kind,
+                             dcopy_stream_t stream);
+
 /* ---- multi-GPU ----------------------------------------------------------------
  * No counterpart in the reference (single-core Ascend kernels; SURVEY row e).
  * Copies shard by splitting the blockCount range over devices with no
