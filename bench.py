@@ -58,8 +58,9 @@ def parse_args():
     ap.add_argument("--impl", choices=["dcopy", "reference"], default="dcopy")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the secondary measurements (sweep, NZ, transpose)")
-    ap.add_argument("--workload", choices=["config2", "config5"], default="config2",
-                    help="config2 (headline, default) or config5 (sharded copy + NVLink ring)")
+    ap.add_argument("--workload", choices=["config2", "config4", "config5"], default="config2",
+                    help="config2 (headline, default), config4 (ND<->NZ with batches split over "
+                         "ranks) or config5 (sharded copy + NVLink ring)")
     return ap.parse_args()
 
 
@@ -551,6 +552,83 @@ def run_config5(args, rank, world, local_rank):
             "p2p": p2p}
 
 
+# ---------------------------------------------------------------------------- config 4
+
+def run_config4(args, rank, world, local_rank):
+    """BASELINE config 4 on N GPUs: fp16 [16, 4096, 4096] ND -> FRACTAL_NZ -> ND, the 16
+    batches (the `times` axis, outermost on both sides) split over ranks with no
+    exchange (strong scaling); every rank times its own round trips, max over ranks."""
+    import torch
+    import dcopy
+    torch.cuda.set_device(local_rank)
+    dcopy.lib()
+    dev = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist_mod
+        dist = dist_mod
+    T, H, W = 16, 4096, 4096
+    b0, nb = dcopy.shard_range(T, rank, world)
+    batch_bytes = H * W * 2
+    # Enough buffer sets that each rank's working set exceeds L2 (>= 512 MiB).
+    sets = max(1, min(4, -(-(512 * MIB) // max(1, 2 * nb * batch_bytes))))
+    g = torch.Generator(device=dev).manual_seed(2)
+    nds = [torch.empty(nb, H, W, dtype=torch.float16, device=dev) for _ in range(sets)]
+    for x in nds:
+        x.normal_(generator=g)
+    nzs = [torch.empty(nb, W // 16, H // 16, 16, 16, dtype=torch.float16, device=dev)
+           for _ in range(sets)]
+    shape = [nb, H, W]
+
+    def barrier():
+        if dist is not None:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize()
+
+    def step():
+        for i in range(sets):
+            dcopy.nd_to_nz(nzs[i], nds[i], shape, 2, 16)
+        for i in range(sets):
+            dcopy.nz_to_nd(nds[i], nzs[i], shape, 2, 16)
+
+    if nb:
+        ref = nds[0].clone()
+        step()
+        torch.cuda.synchronize()
+        want = ref.view(nb, H // 16, 16, W // 16, 16).permute(0, 3, 1, 2, 4)
+        assert torch.equal(nzs[0].view(torch.int16), want.view(torch.int16)), "ND->NZ mismatch"
+        assert torch.equal(nds[0].view(torch.int16), ref.view(torch.int16)), "NZ->ND mismatch"
+        del ref, want
+        for _ in range(max(args.warmup, 3)):
+            step()
+    barrier()
+    steps = max(1, min(args.steps, 20))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps if nb else 0):
+        step()
+    e1.record()
+    e1.synchronize()
+    barrier()
+    t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    # All ranks together: every batch read and written once per direction per set.
+    total_bytes = 2 * 2 * T * batch_bytes * sets * steps
+    value = total_bytes / (float(t.item()) / 1e3) / 1e9
+    if rank != 0:
+        return None
+    return {"metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": steps, "warmup": args.warmup,
+            "ms_per_step": round(float(t.item()) / steps, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
+            "data": "synthetic (normal(0,1) fp16 from seed 2)",
+            "config": {"workload": "config4: fp16 [16,4096,4096] ND -> FRACTAL_NZ [16,256,256,16,16]"
+                                   " -> ND, batches split over ranks",
+                       "batches_per_rank0": nb, "buffer_sets": sets,
+                       "l2": "each rank's working set >= 512 MiB (rotating buffer sets)"}}
+
+
 # ---------------------------------------------------------------------------- reference arm
 
 def run_reference(args):
@@ -609,6 +687,8 @@ def main():
     try:
         if args.workload == "config5":
             line = run_config5(args, rank, world, local_rank)
+        elif args.workload == "config4":
+            line = run_config4(args, rank, world, local_rank)
         else:
             line = run_dcopy(args, rank, world, local_rank)
         if rank == 0:
