@@ -44,7 +44,7 @@ constexpr int kThreadsY = 8;
 template <bool kStore>
 __global__ void __launch_bounds__(kThreadsX *kThreadsY)
     transpose_i32_kernel(const uint32_t *__restrict__ a, uint32_t *__restrict__ b, uint32_t rows,
-                         uint32_t cols, uint32_t col_tiles, uint32_t tiles,
+                         uint32_t cols, uint32_t pitch, uint32_t col_tiles, uint32_t tiles,
                          uint32_t *__restrict__ sink) {
   __shared__ uint32_t tile[kTileCols][kTileRows + 1];
   pdl_trigger_at_entry();
@@ -56,7 +56,7 @@ __global__ void __launch_bounds__(kThreadsX *kThreadsY)
 #pragma unroll
     for (int k = 0; k < kTileRows / kThreadsY; ++k) {
       const uint32_t r = rt * kTileRows + ty + k * kThreadsY;
-      if (r < rows && c < cols) prefetch_l2(a + (uint64_t)r * cols + c);
+      if (r < rows && c < cols) prefetch_l2(a + (uint64_t)r * pitch + c);
     }
   }
   pdl_wait();
@@ -70,7 +70,7 @@ __global__ void __launch_bounds__(kThreadsX *kThreadsY)
     for (int k = 0; k < kTileRows / kThreadsY; ++k) {
       const uint32_t r = r0 + ty + k * kThreadsY;
       v[k] = 0;
-      if (r < rows && c < cols) v[k] = ld_stream(a + (uint64_t)r * cols + c);
+      if (r < rows && c < cols) v[k] = ld_stream(a + (uint64_t)r * pitch + c);
     }
     if constexpr (!kStore) {  // load-only: fold the tile into a value only a NULL sink receives
       uint32_t acc = 0;
@@ -98,8 +98,10 @@ __global__ void __launch_bounds__(kThreadsX *kThreadsY)
   }
 }
 
-int launch_transpose(const void *x, void *y, uint32_t rows, uint32_t cols, bool store,
-                     cudaStream_t s) {
+// B = A^T for A = rows x cols int32 with row pitch `pitch` elements (cols of a
+// wider A when a column range is run on its own).
+int launch_transpose(const void *x, void *y, uint32_t rows, uint32_t cols, uint32_t pitch,
+                     bool store, cudaStream_t s) {
   const uint32_t col_tiles = (cols + kTileCols - 1) / kTileCols;
   const uint32_t row_tiles = (rows + kTileRows - 1) / kTileRows;
   const uint32_t tiles = col_tiles * row_tiles;
@@ -111,9 +113,9 @@ int launch_transpose(const void *x, void *y, uint32_t rows, uint32_t cols, bool 
   uint32_t *no_sink = nullptr;
   if (store)
     return launch(transpose_i32_kernel<true>, grid, block, 0, s, "transpose_i32_kernel", a, b,
-                  rows, cols, col_tiles, tiles, no_sink);
+                  rows, cols, pitch, col_tiles, tiles, no_sink);
   return launch(transpose_i32_kernel<false>, grid, block, 0, s, "transpose_i32_kernel", a, b, rows,
-                cols, col_tiles, tiles, no_sink);
+                cols, pitch, col_tiles, tiles, no_sink);
 }
 
 // Fetches the caller's tiling (host or device pointer) and validates it the way
@@ -152,9 +154,11 @@ int fetch_tiling(const DataCopyTiling *p, cudaStream_t s, DataCopyTiling *t) {
   return DCOPY_OK;
 }
 
-// phase 0 = small/large, 1 = pretranspose, 2 = contiguous (RunTiles<phase>).
+// phase 0 = small/large, 1 = pretranspose, 2 = contiguous (RunTiles<phase>),
+// over the reference's tiles [tile_begin, tile_begin + tile_count) of
+// tiling->tile_cols columns each (all tiles: 0, UINT32_MAX).
 int run_tiles(int phase, const void *in, void *out, const DataCopyTiling *tp,
-              dcopy_stream_t stream) {
+              dcopy_stream_t stream, uint32_t tile_begin = 0, uint32_t tile_count = 0xFFFFFFFFu) {
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   DataCopyTiling t;
   int rc = fetch_tiling(tp, s, &t);
@@ -167,8 +171,24 @@ int run_tiles(int phase, const void *in, void *out, const DataCopyTiling *tp,
   if (rc) return rc;
   if ((uintptr_t)in % 4 || (store && (uintptr_t)out % 4))
     return set_error(DCOPY_ERR_PARAM_INVALID, "datacopy: int32 buffers must be 4-byte aligned");
-  if (phase == 2) return store ? copy_linear(out, in, bytes, s) : load_linear(in, bytes, s);
-  return launch_transpose(in, out, t.rows, t.cols, store, s);
+  // Columns of the requested tiles (asc:36: tile c0 covers [c0, min(c0 + tile_cols, cols))).
+  const uint32_t ntiles = (t.cols + t.tile_cols - 1) / t.tile_cols;
+  if (tile_begin > ntiles || (tile_count != 0xFFFFFFFFu && tile_count > ntiles - tile_begin))
+    return set_error(DCOPY_ERR_PARAM_INVALID, "datacopy: tiles [%u, +%u) outside the %u tiles",
+                     tile_begin, tile_count, ntiles);
+  const uint32_t c_lo = std::min(t.cols, tile_begin * t.tile_cols);
+  const uint32_t c_hi = tile_count == 0xFFFFFFFFu
+                            ? t.cols
+                            : (uint32_t)std::min<uint64_t>(
+                                  t.cols, (uint64_t)(tile_begin + tile_count) * t.tile_cols);
+  if (c_hi <= c_lo) return DCOPY_OK;
+  const uint64_t off = (uint64_t)c_lo * t.rows * 4u, part = (uint64_t)(c_hi - c_lo) * t.rows * 4u;
+  const uint8_t *ip = static_cast<const uint8_t *>(in);
+  uint8_t *op = static_cast<uint8_t *>(out);
+  if (phase == 2)  // B and y share the [cols, rows] layout: the tiles are one contiguous range
+    return store ? copy_linear(op + off, ip + off, part, s) : load_linear(ip + off, part, s);
+  return launch_transpose(ip + (uint64_t)c_lo * 4u, store ? op + off : nullptr, t.rows,
+                          c_hi - c_lo, t.cols, store, s);
 }
 
 }  // namespace
@@ -191,7 +211,7 @@ int run_pretranspose_workflow(const void *x, void *scratch, uint64_t scratch_byt
   if (rc) return rc;
   if ((uintptr_t)x % 4 || (t.store && (uintptr_t)y % 4))
     return set_error(DCOPY_ERR_PARAM_INVALID, "datacopy: int32 buffers must be 4-byte aligned");
-  rc = launch_transpose(x, scratch, t.rows, t.cols, true, s);  // RunTiles<1>: B always written
+  rc = launch_transpose(x, scratch, t.rows, t.cols, t.cols, true, s);  // RunTiles<1>: B written
   if (rc) return rc;
   return t.store ? copy_linear(y, scratch, bytes, s) : load_linear(scratch, bytes, s);
 }
@@ -250,5 +270,17 @@ extern "C" int dcopy_datacopy_contiguous(const void *b, void *y, const DataCopyT
                                          dcopy_stream_t stream) {
   DCOPY_API_BEGIN
   return run_tiles(2, b, y, tiling, stream);
+  DCOPY_API_END
+}
+
+extern "C" int dcopy_datacopy_tiles(int32_t phase, const void *in, void *out,
+                                    const DataCopyTiling *tiling, uint32_t tile_begin,
+                                    uint32_t tile_count, dcopy_stream_t stream) {
+  DCOPY_API_BEGIN
+  if (phase < 0 || phase > 2)
+    return set_error(DCOPY_ERR_PARAM_INVALID, "datacopy_tiles: phase %d is not 0, 1 or 2", phase);
+  if (tile_count == 0xFFFFFFFFu)
+    return set_error(DCOPY_ERR_PARAM_INVALID, "datacopy_tiles: tile_count out of range");
+  return run_tiles(phase, in, out, tiling, stream, tile_begin, tile_count);
   DCOPY_API_END
 }

@@ -151,6 +151,8 @@ _SIGNATURES = {
     "dcopy_datacopy_large": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(DataCopyTiling), _vp]),
     "dcopy_datacopy_pretranspose": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(DataCopyTiling), _vp]),
     "dcopy_datacopy_contiguous": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(DataCopyTiling), _vp]),
+    "dcopy_datacopy_tiles": (ctypes.c_int, [ctypes.c_int32, _vp, _vp, ctypes.POINTER(DataCopyTiling),
+                                            ctypes.c_uint32, ctypes.c_uint32, _vp]),
     "dcopy_datacopy_pretranspose_noalloc": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(DataCopyTiling),
                                                            _vp]),
     "dcopy_copy_ext": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(DcopyExtParams), _vp]),
@@ -301,6 +303,15 @@ def datacopy_pretranspose(x, b, tiling: DataCopyTiling, stream=None) -> None:
 
 def datacopy_contiguous(b, y, tiling: DataCopyTiling, stream=None) -> None:
     _datacopy("dcopy_datacopy_contiguous", b, y, tiling, stream)
+
+
+def datacopy_tiles(phase: int, inp, out, tiling: DataCopyTiling, tile_begin: int,
+                   tile_count: int, stream=None) -> None:
+    """RunTiles<phase> over the tiles [tile_begin, tile_begin + tile_count) only (one core's
+    or one GPU's share); in, out and tiling are those of the whole problem."""
+    _check(lib().dcopy_datacopy_tiles(phase, _ptr(inp), _ptr(out), ctypes.byref(tiling),
+                                      tile_begin, tile_count, _stream(stream)),
+           "dcopy_datacopy_tiles")
 
 
 def datacopy_pretranspose_noalloc(x, y, tiling: DataCopyTiling, stream=None) -> None:

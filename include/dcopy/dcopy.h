@@ -90,6 +90,17 @@ int dcopy_datacopy_pretranspose(const void *x, void *b, const DataCopyTiling *ti
 int dcopy_datacopy_contiguous(const void *b, void *y, const DataCopyTiling *tiling,
                               dcopy_stream_t stream);
 
+/* RunTiles<phase> (0 small/large, 1 pretranspose, 2 contiguous) over the
+ * reference's tiles [tile_begin, tile_begin + tile_count) only: tile k covers
+ * columns [k*tile_cols, min((k+1)*tile_cols, cols)) of x (asc:36) and writes
+ * out[c*rows + r] for those columns, a contiguous range of out.  In, out and
+ * tiling are those of the whole problem.  This is one Ascend core's share of
+ * the tiles, and how the transpose shards across GPUs (dcopy_shard_range over
+ * the tile count; each GPU writes a disjoint slice of y).  Tiles past the end
+ * are PARAM_INVALID; an empty range is a no-op. */
+int dcopy_datacopy_tiles(int32_t phase, const void *in, void *out, const DataCopyTiling *tiling,
+                         uint32_t tile_begin, uint32_t tile_count, dcopy_stream_t stream);
+
 /* The whole pretranspose workflow (x -> B -> y, as datacopy_pretranspose
  * followed by datacopy_contiguous) for callers that cannot allocate device
  * memory for B: a runtime that owns the whole device-memory budget, or a

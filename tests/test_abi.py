@@ -160,3 +160,11 @@ def test_copy_ext_batch_argument_checks(dcopy):
     array with a count is refused."""
     dcopy.copy_ext_batch([])
     assert dcopy.lib().dcopy_copy_ext_batch(None, 3, None) == dcopy.ERR_PARAM_INVALID
+
+
+def test_datacopy_tiles_argument_checks(dcopy):
+    t = dcopy.plan_tiling(256, 768, 8, 1)
+    for phase, count in ((3, 1), (-1, 1), (0, 0xFFFFFFFF)):
+        with pytest.raises(dcopy.DcopyError) as e:
+            dcopy.datacopy_tiles(phase, 0x1000, 0x2000, t, 0, count)
+        assert e.value.code == dcopy.ERR_PARAM_INVALID

@@ -156,3 +156,50 @@ def test_buffer_extent_checked(torch_cuda, dcopy, cuda_malloc):
     with pytest.raises(dcopy.DcopyError) as e:
         dcopy.datacopy_small(x, host.ctypes.data, t)
     assert e.value.code == dcopy.ERR_PARAM_INVALID
+
+
+@pytest.mark.parametrize("rows,cols,kib,parts", [(256, 768, 8, 3), (128, 513, 4, 5), (72, 33, 2, 2),
+                                                  (4088, 19, 240, 1), (16, 255, 3, 7)])
+def test_tile_ranges_compose(torch_cuda, dcopy, oracle, rows, cols, kib, parts):
+    """The tiles split over `parts` shards (dcopy_shard_range, as GPUs or cores would take
+    them), each run on its own: together they write exactly the whole result, for every
+    phase; store = 0 shards write nothing."""
+    torch = torch_cuda
+    a = oracle.fill_pattern(rows * cols)
+    x = _dev(torch, a)
+    t = dcopy.plan_tiling(rows, cols, kib, 1)
+    ntiles = -(-cols // t.tile_cols)
+    expect = a.reshape(rows, cols).T.copy()
+    y, b, y2 = _canary(torch, a.nbytes), _canary(torch, a.nbytes), _canary(torch, a.nbytes)
+    for r in range(parts):
+        begin, count = dcopy.shard_range(ntiles, r, parts)
+        dcopy.datacopy_tiles(0, x, y, t, begin, count)
+        dcopy.datacopy_tiles(1, x, b, t, begin, count)
+    torch.cuda.synchronize()
+    for r in reversed(range(parts)):
+        begin, count = dcopy.shard_range(ntiles, r, parts)
+        dcopy.datacopy_tiles(2, b, y2, t, begin, count)
+    torch.cuda.synchronize()
+    assert _host(y).tobytes() == expect.tobytes()
+    assert _host(b).tobytes() == expect.tobytes()
+    assert _host(y2).tobytes() == expect.tobytes()
+    # One shard alone writes exactly its own columns.
+    begin, count = dcopy.shard_range(ntiles, parts - 1, parts)
+    y3 = _canary(torch, a.nbytes)
+    dcopy.datacopy_tiles(0, x, y3, t, begin, count)
+    torch.cuda.synchronize()
+    c_lo = min(cols, begin * t.tile_cols)
+    c_hi = min(cols, (begin + count) * t.tile_cols)
+    got = _host(y3).view(np.int32).reshape(cols, rows)
+    assert got[c_lo:c_hi].tobytes() == expect[c_lo:c_hi].tobytes()
+    untouched = _host(_canary(torch, a.nbytes)).view(np.int32).reshape(cols, rows)
+    assert got[:c_lo].tobytes() == untouched[:c_lo].tobytes()
+    assert got[c_hi:].tobytes() == untouched[c_hi:].tobytes()
+    t0 = dcopy.plan_tiling(rows, cols, kib, 0)
+    y4 = _canary(torch, a.nbytes)
+    dcopy.datacopy_tiles(0, x, y4, t0, 0, ntiles)
+    torch.cuda.synchronize()
+    assert _host(y4).tobytes() == untouched.tobytes()
+    with pytest.raises(dcopy.DcopyError) as e:
+        dcopy.datacopy_tiles(0, x, y, t, ntiles, 1)
+    assert e.value.code == dcopy.ERR_PARAM_INVALID
