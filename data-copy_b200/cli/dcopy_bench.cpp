@@ -31,6 +31,9 @@
 //       line: event time around the call, the same call replayed as a CUDA graph,
 //       and the host time of one call.  --tma 1 selects the TMA tensor-copy path
 //       (dcopy_set_nd_tma) for boxes that qualify.
+//   dcopy_bench batch [--gathers G] [--reps R] [--device D] [--peak GBPS]
+//       G config-2 gathers as one dcopy_copy_ext_batch against G dcopy_copy_ext calls
+//       (both captured in a CUDA graph), verified; one JSON line.
 //   dcopy_bench p2p [--mib M] [--reps R] [--device D] [--peer P] [--peak GBPS]
 //       NVLink between two GPUs: dcopy_p2p_copy as a push (launched on the
 //       sending GPU) and as a pull (launched on the receiving GPU), and the copy
@@ -648,6 +651,62 @@ int run_nd(const Args &a) {
   return 0;
 }
 
+// ---- batch ----------------------------------------------------------------------------
+
+// BASELINE config 2's gather (fp32 [4096,4096] cols 1024..2047 -> [4096,1024]) on
+// `gathers` independent buffer pairs: one dcopy_copy_ext_batch against one
+// dcopy_copy_ext per gather, both verified.
+int run_batch(const Args &a) {
+  const int gathers = int(a.num("gathers", 16));
+  const int reps = int(a.num("reps", 20));
+  const double peak = a.num("peak", 6543.4);
+  if (gathers < 1 || gathers > 256) throw std::runtime_error("--gathers must be 1..256");
+  Check(cudaSetDevice(int(a.num("device", 0))), "cudaSetDevice");
+  cudaStream_t s;
+  Check(cudaStreamCreate(&s), "stream");
+  dcopy_stream_t ds = reinterpret_cast<dcopy_stream_t>(s);
+  const uint32_t rows = 4096, cols = 4096, c0 = 1024, width = 1024;
+  const size_t src_bytes = size_t(rows) * cols * 4, dst_bytes = size_t(rows) * width * 4;
+  std::vector<std::unique_ptr<DevBuf>> src, dst;
+  std::vector<uint32_t> host(size_t(rows) * cols);
+  for (size_t i = 0; i < host.size(); ++i) host[i] = uint32_t(i * 2654435761u);
+  std::vector<DcopyExtCopy> copies;
+  for (int g = 0; g < gathers; ++g) {
+    src.push_back(std::make_unique<DevBuf>(src_bytes));
+    dst.push_back(std::make_unique<DevBuf>(dst_bytes));
+    Check(cudaMemcpy(src.back()->p, host.data(), src_bytes, cudaMemcpyHostToDevice), "H2D");
+    Check(cudaMemset(dst.back()->p, 0xA5, dst_bytes), "memset");
+    copies.push_back(DcopyExtCopy{dst.back()->p, static_cast<char *>(src.back()->p) + c0 * 4,
+                                  DcopyExtParams{rows, width * 4, uint64_t(cols - width) * 4, 0}});
+  }
+  DevBuf flush(512ull << 20);
+  CheckD(dcopy_copy_ext_batch(copies.data(), uint32_t(copies.size()), ds));
+  std::vector<uint32_t> out(size_t(rows) * width);
+  for (int g = 0; g < gathers; ++g) {
+    Check(cudaMemcpy(out.data(), dst[g]->p, dst_bytes, cudaMemcpyDeviceToHost), "D2H");
+    for (uint32_t r = 0; r < rows; ++r)
+      for (uint32_t c = 0; c < width; ++c)
+        if (out[size_t(r) * width + c] != host[size_t(r) * cols + c0 + c])
+          throw std::runtime_error("batch gather mismatch");
+  }
+  auto tb = time_graph_reps([&] { CheckD(dcopy_copy_ext_batch(copies.data(), uint32_t(copies.size()), ds)); },
+                            reps, s, flush);
+  auto tc = time_graph_reps(
+      [&] {
+        for (auto &c : copies) CheckD(dcopy_copy_ext(c.dst, c.src, &c.params, ds));
+      },
+      reps, s, flush);
+  const double bytes = 2.0 * dst_bytes * gathers;
+  const double gb = bytes / (median(tb) * 1e3), gc = bytes / (median(tc) * 1e3);
+  std::cout << "{\"batch\": \"config2 gathers\", \"gathers\": " << gathers
+            << ", \"batch_us\": " << median(tb) << ", \"batch_GBps\": " << gb
+            << ", \"batch_frac_of_peak\": " << gb / peak << ", \"calls_us\": " << median(tc)
+            << ", \"calls_GBps\": " << gc << ", \"calls_frac_of_peak\": " << gc / peak
+            << ", \"verified\": true}" << std::endl;
+  cudaStreamDestroy(s);
+  return 0;
+}
+
 // ---- p2p --------------------------------------------------------------------------
 
 int run_p2p(const Args &a) {
@@ -751,7 +810,7 @@ int run_p2p(const Args &a) {
 
 int main(int argc, char **argv) {
   try {
-    if (argc < 2) throw std::runtime_error("usage: dcopy_bench sweep|standalone|nz|fz|transpose|nd|p2p [options]");
+    if (argc < 2) throw std::runtime_error("usage: dcopy_bench sweep|standalone|nz|fz|transpose|nd|batch|p2p [options]");
     const std::string cmd = argv[1];
     Args a(argc, argv);
     // --l2-fetch B: the context's L2 fetch-granularity hint (cudaLimitMaxL2FetchGranularity,
@@ -771,6 +830,7 @@ int main(int argc, char **argv) {
     if (cmd == "fz") return run_fz(a);
     if (cmd == "transpose") return run_transpose(a);
     if (cmd == "nd") return run_nd(a);
+    if (cmd == "batch") return run_batch(a);
     throw std::runtime_error("unknown command " + cmd);
   } catch (const std::exception &e) {
     std::cerr << "dcopy_bench: " << e.what() << '\n';
