@@ -49,6 +49,9 @@ constexpr int kCtasPerSm = 8;
 #ifndef DCOPY_COPY2D_SHIFT
 #define DCOPY_COPY2D_SHIFT 1  // bursts of 1/2/4-byte units through the funnel-shift row kernel
 #endif
+#ifndef DCOPY_HALF_LINE_NO_PREFETCH
+#define DCOPY_HALF_LINE_NO_PREFETCH 1
+#endif
 #ifndef DCOPY_STRIDED_U
 #define DCOPY_STRIDED_U 4  // elements in flight per thread (strided copy)
 #endif
@@ -249,9 +252,11 @@ int launch_strided(uint8_t *dst, const uint8_t *src, uint64_t rows, uint64_t row
   const uint64_t max_rows = std::max<uint64_t>(1, (uint64_t(1) << 30) / epr);
   const FastDiv div((uint32_t)epr);
   const bool prefetch = is_local_device_memory(src);
-  // Gapped bursts that do not cover whole 128-byte lines: half-line L2 fills.
+  // Gapped bursts that do not cover whole 128-byte lines: half-line L2 fills,
+  // and no L2 prefetch (a prefetch fills the whole line of every 8th element).
   const bool half_line =
       src_pitch != row_bytes && ((uintptr_t)src % 128 || row_bytes % 128 || src_pitch % 128);
+  const bool prefetch_src = prefetch && !(half_line && DCOPY_HALF_LINE_NO_PREFETCH);
   for (uint64_t r0 = 0; r0 < rows; r0 += max_rows) {
     const uint64_t nr = std::min(max_rows, rows - r0);
     const uint32_t total = (uint32_t)(nr * epr);
@@ -259,7 +264,7 @@ int launch_strided(uint8_t *dst, const uint8_t *src, uint64_t rows, uint64_t row
     const Split sp = split_work(kernel, total, U);
     int rc = launch(kernel, sp.grid, dim3(kThreads), 0, s, "strided_copy_kernel",
                     dst + r0 * dst_pitch, src + r0 * src_pitch, total, (uint32_t)sp.per_cta, div,
-                    src_pitch, dst_pitch, prefetch);
+                    src_pitch, dst_pitch, prefetch_src);
     if (rc) return rc;
   }
   return DCOPY_OK;
