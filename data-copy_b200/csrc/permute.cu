@@ -44,6 +44,12 @@ constexpr int kMaxRowDims = 4;
 #ifndef DCOPY_PERM_MINB
 #define DCOPY_PERM_MINB 8  // wider packed tiles: resident CTAs per SM the registers must allow
 #endif
+#ifndef DCOPY_PERM_TD4
+#define DCOPY_PERM_TD4 64  // 4-byte elements: tile rows (destination axis)
+#endif
+#ifndef DCOPY_PERM_TE4
+#define DCOPY_PERM_TE4 64  // 4-byte elements: tile columns (source axis)
+#endif
 #ifndef DCOPY_PERM_TD2
 #define DCOPY_PERM_TD2 64  // 2-byte elements: tile rows (destination axis)
 #endif
@@ -560,7 +566,8 @@ int permute_copy(void *dst, const void *src, int m, const uint64_t *size, const 
                                                                              ss, ds, e, s)
                  : run_tiles_elem<uint16_t>(dst, src, m, size, ss, ds, e, s);
     case 4:
-      return vec ? run_tiles_packed<uint32_t, 64, 64>(dst, src, m, size, ss, ds, e, s)
+      return vec ? run_tiles_packed<uint32_t, DCOPY_PERM_TD4, DCOPY_PERM_TE4>(dst, src, m, size,
+                                                                             ss, ds, e, s)
                  : run_tiles_elem<uint32_t>(dst, src, m, size, ss, ds, e, s);
     case 8:
       return vec ? run_tiles_packed<uint2, 32, 32>(dst, src, m, size, ss, ds, e, s)
