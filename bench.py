@@ -277,8 +277,10 @@ def run_dcopy(args, rank, world, local_rank):
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_value = BYTES_PER_GATHER * e2e_steps * world / (float(te.item()) / 1e3) / 1e9
 
+    # The other configs are single-GPU measurements: taken on the N=1 run only, so
+    # multi-GPU runs do not hold N GPUs while rank 0 alone measures them.
     secondary = None
-    if not args.no_secondary and rank == 0:
+    if not args.no_secondary and world == 1:
         secondary = run_secondary(torch, dcopy, dev)
 
     line = None
