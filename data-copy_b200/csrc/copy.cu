@@ -432,6 +432,25 @@ extern "C" int dcopy_copy_ext_32b(void *dst, const void *src, uint32_t blockCoun
   return dcopy_copy_ext(dst, src, &p, stream);
 }
 
+extern "C" int dcopy_copy_ext_loop(void *dst, const void *src, const DcopyExtParams *p,
+                                   const DcopyLoopModeParams *loop, dcopy_stream_t stream) {
+  DCOPY_API_BEGIN
+  if (!p || !loop) return set_error(DCOPY_ERR_PARAM_INVALID, "copy_ext_loop: params is NULL");
+  if (p->srcStride > (1ull << 48) || p->dstStride > (1ull << 48) ||
+      loop->loop1SrcStride > (1ull << 48) || loop->loop1DstStride > (1ull << 48) ||
+      loop->loop2SrcStride > (1ull << 48) || loop->loop2DstStride > (1ull << 48))
+    return set_error(DCOPY_ERR_PARAM_INVALID, "copy_ext_loop: stride beyond 2^48 bytes");
+  // [loop2][loop1][blockCount][blockLen] bytes; the box copy validates spans and
+  // overlap and picks the kernel.
+  const uint64_t sizes[4] = {loop->loop2Size, loop->loop1Size, p->blockCount, p->blockLen};
+  const int64_t ss[4] = {(int64_t)loop->loop2SrcStride, (int64_t)loop->loop1SrcStride,
+                         (int64_t)(p->blockLen + p->srcStride), 1};
+  const int64_t ds[4] = {(int64_t)loop->loop2DstStride, (int64_t)loop->loop1DstStride,
+                         (int64_t)(p->blockLen + p->dstStride), 1};
+  return dcopy_copy_nd(dst, src, 4, sizes, ss, ds, 1, stream);
+  DCOPY_API_END
+}
+
 extern "C" int dcopy_copy_nd(void *dst, const void *src, int ndim, const uint64_t *sizes,
                              const int64_t *src_strides, const int64_t *dst_strides,
                              uint32_t elem_bytes, dcopy_stream_t stream) {

@@ -214,6 +214,8 @@ _SIGNATURES = {
     "dcopy_tma_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32)]),
     "dcopy_set_nd_tma": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
     "dcopy_copy_ext_batch": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p]),
+    "dcopy_copy_ext_loop": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                           ctypes.c_void_p, ctypes.c_void_p]),
     "dcopy_memcpy_async_batch": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_int32,
                                                 ctypes.c_void_p]),
 }
@@ -317,6 +319,23 @@ def datacopy_tiles(phase: int, inp, out, tiling: DataCopyTiling, tile_begin: int
 def datacopy_pretranspose_noalloc(x, y, tiling: DataCopyTiling, stream=None) -> None:
     """x -> B -> y without any allocation (B lives in the library's 16 MiB device array)."""
     _datacopy("dcopy_datacopy_pretranspose_noalloc", x, y, tiling, stream)
+
+
+class DcopyLoopModeParams(ctypes.Structure):
+    """LoopModeParams: two outer loops around a DataCopyExt copy; strides in bytes."""
+    _fields_ = [("loop1Size", ctypes.c_uint32), ("loop2Size", ctypes.c_uint32),
+                ("loop1SrcStride", ctypes.c_uint64), ("loop1DstStride", ctypes.c_uint64),
+                ("loop2SrcStride", ctypes.c_uint64), ("loop2DstStride", ctypes.c_uint64)]
+
+
+def copy_ext_loop(dst, src, block_count: int, block_len: int, src_gap: int, dst_gap: int,
+                  loop1, loop2=(1, 0, 0), stream=None) -> None:
+    """DataCopyPadExtend with LoopModeParams: loop1/loop2 = (size, src stride, dst stride),
+    strides in bytes; the inner copy is copy_ext(block_count, block_len, gaps)."""
+    p = DcopyExtParams(block_count, block_len, src_gap, dst_gap)
+    lp = DcopyLoopModeParams(loop1[0], loop2[0], loop1[1], loop1[2], loop2[1], loop2[2])
+    _check(lib().dcopy_copy_ext_loop(_ptr(dst), _ptr(src), ctypes.byref(p), ctypes.byref(lp),
+                                     _stream(stream)), "dcopy_copy_ext_loop")
 
 
 class DcopyExtCopy(ctypes.Structure):

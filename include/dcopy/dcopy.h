@@ -140,6 +140,27 @@ typedef struct DcopyExtParams {
 int dcopy_copy_ext(void *dst, const void *src, const DcopyExtParams *params,
                    dcopy_stream_t stream);
 
+/* LoopModeParams of the v35 DataCopyPadExtend (v35/ascendc/api_regbase/datacopy.h:29-45,
+ * 60-72), field order as GE's codegen emits it (v35/codegen/reg_api_call/
+ * reg_api_call_utils.cpp:64-73); strides in bytes, absolute (not gaps). */
+typedef struct DcopyLoopModeParams {
+  uint32_t loop1Size;
+  uint32_t loop2Size;
+  uint64_t loop1SrcStride;
+  uint64_t loop1DstStride;
+  uint64_t loop2SrcStride;
+  uint64_t loop2DstStride;
+} DcopyLoopModeParams;
+
+/* The DataCopyExt copy inside two outer loops (reg_api_call_utils.h:17-25):
+ *   for i < loop2Size, j < loop1Size:
+ *     dcopy_copy_ext(dst + i*loop2DstStride + j*loop1DstStride,
+ *                    src + i*loop2SrcStride + j*loop1SrcStride, params)
+ * run as one N-D box.  Destinations of different (i, j) must not overlap
+ * (a zero destination stride with a loop size above 1 is PARAM_INVALID). */
+int dcopy_copy_ext_loop(void *dst, const void *src, const DcopyExtParams *params,
+                        const DcopyLoopModeParams *loop, dcopy_stream_t stream);
+
 /* One copy of a batch: dcopy_copy_ext(dst, src, &params) as a record. */
 typedef struct DcopyExtCopy {
   void *dst;
@@ -473,6 +494,7 @@ int dcopy_wait_signal(const uint32_t *flag, uint32_t value, uint64_t timeout_ns,
 }  /* extern "C" */
 static_assert(sizeof(DcopyExtParams) == 24, "DcopyExtParams layout");
 static_assert(sizeof(DcopyExtCopy) == 40, "DcopyExtCopy layout");
+static_assert(sizeof(DcopyLoopModeParams) == 40, "DcopyLoopModeParams layout");
 #endif
 
 #endif /* DCOPY_DCOPY_H_ */

@@ -168,3 +168,14 @@ def test_datacopy_tiles_argument_checks(dcopy):
         with pytest.raises(dcopy.DcopyError) as e:
             dcopy.datacopy_tiles(phase, 0x1000, 0x2000, t, 0, count)
         assert e.value.code == dcopy.ERR_PARAM_INVALID
+
+
+def test_copy_ext_loop_argument_checks(dcopy):
+    import ctypes
+    p = dcopy.DcopyExtParams(1, 16, 0, 0)
+    assert dcopy.lib().dcopy_copy_ext_loop(None, None, ctypes.byref(p), None, None) == \
+        dcopy.ERR_PARAM_INVALID
+    with pytest.raises(dcopy.DcopyError) as e:
+        dcopy.copy_ext_loop(0x1000, 0x2000, 1, 16, 0, 0, (2, 1 << 50, 64))
+    assert e.value.code == dcopy.ERR_PARAM_INVALID
+    dcopy.copy_ext_loop(0x1000, 0x2000, 0, 16, 0, 0, (2, 64, 64))  # nothing to copy
