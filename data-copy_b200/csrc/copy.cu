@@ -314,10 +314,9 @@ int copy2d(void *dst, const void *src, uint64_t rows, uint64_t row_bytes, uint64
     return DCOPY_OK;
   }
   // Bursts only 1- or 2-byte units tile, and long bursts of 4-byte units:
-  // aligned 16-byte destination vectors assembled by funnel shifts (rows.cu).
-  // Measured on B200: 30 B bursts in 2-byte units 2213 -> 2363 GB/s, 4092 B in
-  // 4-byte units 3401 -> 5236; 36 B and 100 B bursts stay faster in 4-byte units.
-  if (DCOPY_COPY2D_SHIFT && shift_rows_pay(w, row_bytes) && row_bytes < (uint64_t(1) << 30) &&
+  // aligned 16-byte destination vectors assembled by funnel shifts (rows.cu;
+  // the measured thresholds are in shift_rows_pay).
+  if (DCOPY_COPY2D_SHIFT && shift_rows_pay(w, row_bytes, false) && row_bytes < (uint64_t(1) << 30) &&
       rows <= 0xFFFFFFFFull) {
     const uint64_t size[2] = {rows, row_bytes};
     const int64_t ss[2] = {(int64_t)src_pitch, 1}, ds[2] = {(int64_t)dst_pitch, 1};

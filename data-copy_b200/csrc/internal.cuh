@@ -70,10 +70,14 @@ int permute_copy(void *dst, const void *src, int m, const uint64_t *size, const 
 int rows_shift(void *dst, const void *src, int m, const uint64_t *size, const int64_t *ss,
                const int64_t *ds, int eb, cudaStream_t s);
 // Whether rows of row_bytes whose widest common unit is `unit` bytes move faster
-// through rows_shift than in units: 1- and 2-byte units always, 4-byte units
-// from 256-byte rows on.
-inline bool shift_rows_pay(uint32_t unit, uint64_t row_bytes) {
-  return row_bytes >= 16 && (unit <= 2 || (unit == 4 && row_bytes >= 256));
+// through rows_shift than in units (measured on B200).  N-D rows (the row kernel
+// with an odometer per unit): 1-, 2- and 4-byte units (112-byte rows in 4-byte
+// units: 2358 -> 4978 GB/s).  2-D bursts (the strided kernel, one division per
+// unit): 1- and 2-byte units, and 4-byte units from 256-byte bursts on (36-byte
+// bursts stay faster in units: 4608 against 3880 GB/s).  8-byte units never.
+inline bool shift_rows_pay(uint32_t unit, uint64_t row_bytes, bool nd_rows) {
+  if (row_bytes < 16 || unit >= 8) return false;
+  return unit <= 2 || nd_rows || row_bytes >= 256;
 }
 
 // Rows of a <=5-D box whose innermost axis is contiguous on both sides

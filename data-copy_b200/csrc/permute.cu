@@ -34,7 +34,7 @@ constexpr int kMaxRowDims = 4;
 #define DCOPY_PERM_PACKED 1  // aligned tiles: packed [e][d] shared layout (0: element gather)
 #endif
 #ifndef DCOPY_ROWS_SHIFT
-#define DCOPY_ROWS_SHIFT 1  // rows of 1/2/4-byte units through rows_shift (shift_rows_pay)
+#define DCOPY_ROWS_SHIFT 1  // rows of narrow units through rows_shift (shift_rows_pay)
 #endif
 #ifndef DCOPY_PERM_MINB1
 #define DCOPY_PERM_MINB1 7  // 1-byte packed tiles: resident CTAs per SM the registers must allow
@@ -386,7 +386,7 @@ int run_rows(void *dst, const void *src, int m, const uint64_t *size, const int6
   uint64_t key = L * eb | (uintptr_t)dst | (uintptr_t)src;
   for (int k = 0; k < m - 1; ++k) key |= (uint64_t)ss[k] * eb | (ds ? (uint64_t)ds[k] * eb : 0);
   const uint32_t us = unit_for(key, eb);
-  if (DCOPY_ROWS_SHIFT && shift_rows_pay(us, L * eb))
+  if (DCOPY_ROWS_SHIFT && shift_rows_pay(us, L * eb, true))
     return rows_shift(dst, src, m, size, ss, ds, eb, s);
   PermRGeom g{};
   g.vpr = (uint32_t)(L * eb / us);

@@ -5,13 +5,14 @@
 // 16-byte source blocks that hold its bytes.  The element kernels would move
 // such rows in 1- or 2-byte units.
 //
-// Thread slot (r, k): the k-th aligned 16-byte vector of destination row r,
-// k in [0, slots) with slots = ceil(row_bytes / 16) + 1 (the extra slot covers
-// a row that straddles one more vector than its length needs; empty slots do
-// nothing).  Bytes of a slot outside the row are neither read nor written: the
-// vector's two partial ends are stored byte by byte, and a source block is
-// only loaded when it holds a byte the slot needs, so every load stays inside
-// the page of a byte the caller owns.
+// A thread moves a run of kRun consecutive aligned 16-byte vectors of one
+// destination row (a row spans at most ceil(row_bytes / 16) + 1 vectors; runs
+// past its end do nothing).  All vectors of a row share one shift against the
+// source's aligned blocks, so a run loads kRun + 1 blocks for kRun vectors and
+// computes the row's odometer once.  Bytes outside the row are neither read
+// nor written: the vector at each end of a row is stored in aligned pieces, and
+// a source block is only loaded when it holds a byte the run needs, so every
+// load stays inside the page of a byte the caller owns.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -25,11 +26,11 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kRowDims = 4;  // row dims (outermost first) besides the row itself
-constexpr int kSlotsInFlight = 2;
+constexpr int kRun = 4;  // destination vectors per thread (one row, consecutive)
 
 struct ShiftGeom {
   uint32_t row_bytes;
-  uint32_t slots;  // vectors per row slot range
+  uint32_t slots;  // runs of kRun destination vectors per row
   FastDiv f_slots;
   uint32_t nd;
   uint32_t size[kRowDims];
@@ -86,6 +87,22 @@ __device__ __forceinline__ void store_partial(uint8_t *v, uint4 x, uint32_t lo, 
     }
 }
 
+// Source blocks of a run: neighbouring lanes read the two halves of a 32-byte
+// sector one instruction apart, so these loads allocate in L1.
+template <bool kHalfLine>
+__device__ __forceinline__ uint4 load_block_l1(const uint8_t *p) {
+  uint4 v;
+  if constexpr (kHalfLine)
+    asm("ld.global.nc.L2::64B.v4.u32 {%0, %1, %2, %3}, [%4];"
+        : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+        : "l"(p));
+  else
+    asm("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+        : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+        : "l"(p));
+  return v;
+}
+
 template <bool kHalfLine>
 __device__ __forceinline__ uint4 load_block(const uint8_t *p) {
   if constexpr (kHalfLine)
@@ -101,55 +118,51 @@ __global__ void __launch_bounds__(kThreads) rows_shift_kernel(uint8_t *__restric
   pdl_trigger_at_entry();
   pdl_wait();
   pdl_launch_dependents();
-  for (uint32_t base = blockIdx.x * kThreads * kSlotsInFlight + threadIdx.x; base < g.total;
-       base += gridDim.x * kThreads * kSlotsInFlight) {
-    uint4 out[kSlotsInFlight];
-    uint8_t *vec[kSlotsInFlight];
-    uint32_t lo[kSlotsInFlight], hi[kSlotsInFlight];  // written byte range within the vector
+  for (uint32_t i = blockIdx.x * kThreads + threadIdx.x; i < g.total; i += gridDim.x * kThreads) {
+    uint32_t r = g.f_slots.div(i);
+    const uint32_t k0 = (i - r * g.slots) * kRun;
+    uint64_t so = 0, dof = 0;
 #pragma unroll
-    for (int u = 0; u < kSlotsInFlight; ++u) {
-      const uint32_t i = base + u * kThreads;
-      lo[u] = hi[u] = 0;
-      vec[u] = nullptr;
-      if (i >= g.total) continue;
-      uint32_t r = g.f_slots.div(i);
-      const uint32_t k = i - r * g.slots;
-      uint64_t so = 0, dof = 0;
-#pragma unroll
-      for (int d = kRowDims - 1; d >= 0; --d) {
-        if (d < (int)g.nd) {
-          const uint32_t q = g.f_size[d].div(r);
-          const uint64_t idx = r - q * g.size[d];
-          so += idx * g.ss[d];
-          dof += idx * g.ds[d];
-          r = q;
-        }
+    for (int d = kRowDims - 1; d >= 0; --d) {
+      if (d < (int)g.nd) {
+        const uint32_t q = g.f_size[d].div(r);
+        const uint64_t idx = r - q * g.size[d];
+        so += idx * g.ss[d];
+        dof += idx * g.ds[d];
+        r = q;
       }
-      const uintptr_t drow = reinterpret_cast<uintptr_t>(dst) + dof;
-      const uintptr_t v = (drow & ~(uintptr_t)15) + 16u * k;
-      const uintptr_t b_lo = v > drow ? v : drow;
-      const uintptr_t b_hi = v + 16 < drow + g.row_bytes ? v + 16 : drow + g.row_bytes;
-      if (b_lo >= b_hi) continue;
-      // Source address of the vector's first byte (which may precede the row).
-      const uintptr_t sa = reinterpret_cast<uintptr_t>(src) + so + (v - drow);
-      const uintptr_t blk = sa & ~(uintptr_t)15;
-      const uint32_t sh = (uint32_t)(sa & 15);
-      const uintptr_t need_lo = sa + (b_lo - v), need_hi = sa + (b_hi - v);
-      uint4 a = make_uint4(0, 0, 0, 0), b = make_uint4(0, 0, 0, 0);
-      if (need_lo < blk + 16) a = load_block<kHalfLine>(reinterpret_cast<const uint8_t *>(blk));
-      if (need_hi > blk + 16) b = load_block<kHalfLine>(reinterpret_cast<const uint8_t *>(blk + 16));
-      out[u] = shift_pair(a, b, sh);
-      vec[u] = reinterpret_cast<uint8_t *>(v);
-      lo[u] = (uint32_t)(b_lo - v);
-      hi[u] = (uint32_t)(b_hi - v);
+    }
+    const uintptr_t drow = reinterpret_cast<uintptr_t>(dst) + dof;
+    const uintptr_t drow_end = drow + g.row_bytes;
+    const uintptr_t v0 = (drow & ~(uintptr_t)15) + 16u * k0;
+    if (v0 >= drow_end) continue;
+    // Source address of the run's first destination byte (which may precede the
+    // row); every vector of the run has the same shift against the source blocks.
+    const uintptr_t sa0 = reinterpret_cast<uintptr_t>(src) + so + (v0 - drow);
+    const uintptr_t blk0 = sa0 & ~(uintptr_t)15;
+    const uint32_t sh = (uint32_t)(sa0 & 15);
+    const uintptr_t run_end = v0 + 16u * kRun < drow_end ? v0 + 16u * kRun : drow_end;
+    const uintptr_t need_lo = sa0 + ((v0 > drow ? v0 : drow) - v0), need_hi = sa0 + (run_end - v0);
+    uint4 blk[kRun + 1];
+#pragma unroll
+    for (int j = 0; j <= kRun; ++j) {  // only blocks that hold a byte the run needs
+      const uintptr_t b = blk0 + 16u * j;
+      blk[j] = make_uint4(0, 0, 0, 0);
+      if (b < need_hi && b + 16 > need_lo)
+        blk[j] = load_block_l1<kHalfLine>(reinterpret_cast<const uint8_t *>(b));
     }
 #pragma unroll
-    for (int u = 0; u < kSlotsInFlight; ++u) {
-      if (lo[u] >= hi[u]) continue;
-      if (lo[u] == 0 && hi[u] == 16)
-        *reinterpret_cast<uint4 *>(vec[u]) = out[u];
+    for (int j = 0; j < kRun; ++j) {
+      const uintptr_t v = v0 + 16u * j;
+      const uintptr_t b_lo = v > drow ? v : drow;
+      const uintptr_t b_hi = v + 16 < drow_end ? v + 16 : drow_end;
+      if (b_lo >= b_hi) continue;
+      const uint4 out = shift_pair(blk[j], blk[j + 1], sh);
+      const uint32_t lo = (uint32_t)(b_lo - v), hi = (uint32_t)(b_hi - v);
+      if (lo == 0 && hi == 16)
+        *reinterpret_cast<uint4 *>(v) = out;
       else
-        store_partial(vec[u], out[u], lo[u], hi[u]);
+        store_partial(reinterpret_cast<uint8_t *>(v), out, lo, hi);
     }
   }
 }
@@ -167,7 +180,7 @@ int rows_shift(void *dst, const void *src, int m, const uint64_t *size, const in
                      (unsigned long long)row_bytes);
   ShiftGeom g{};
   g.row_bytes = (uint32_t)row_bytes;
-  g.slots = (uint32_t)((row_bytes + 15) / 16 + 1);
+  g.slots = (uint32_t)(((row_bytes + 15) / 16 + 1 + kRun - 1) / kRun);
   g.f_slots = FastDiv(g.slots);
   g.nd = (uint32_t)(m - 1);
   // Destination byte strides: given, or those of a contiguous destination.
@@ -207,7 +220,7 @@ int rows_shift(void *dst, const void *src, int m, const uint64_t *size, const in
       c.f_size[0] = FastDiv(c.size[0]);
     }
     c.total = (uint32_t)(n * inner);
-    const uint64_t per_cta = (uint64_t)kThreads * kSlotsInFlight;
+    const uint64_t per_cta = (uint64_t)kThreads;
     const uint32_t grid = (uint32_t)std::max<uint64_t>(1, (c.total + per_cta - 1) / per_cta);
     const uint64_t s_off = m >= 2 ? o0 * g.ss[0] : 0, d_off = m >= 2 ? o0 * g.ds[0] : 0;
     const int rc = launch(kernel, grid, dim3(kThreads), 0, s, "rows_shift_kernel",
