@@ -216,6 +216,9 @@ _SIGNATURES = {
     "dcopy_copy_ext_batch": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p]),
     "dcopy_copy_ext_loop": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                            ctypes.c_void_p, ctypes.c_void_p]),
+    "dcopy_copy_ext_staged": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                             ctypes.c_void_p, ctypes.c_uint64, ctypes.c_int32,
+                                             ctypes.c_void_p]),
     "dcopy_memcpy_async_batch": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_int32,
                                                 ctypes.c_void_p]),
 }
@@ -326,6 +329,30 @@ class DcopyLoopModeParams(ctypes.Structure):
     _fields_ = [("loop1Size", ctypes.c_uint32), ("loop2Size", ctypes.c_uint32),
                 ("loop1SrcStride", ctypes.c_uint64), ("loop1DstStride", ctypes.c_uint64),
                 ("loop2SrcStride", ctypes.c_uint64), ("loop2DstStride", ctypes.c_uint64)]
+
+
+STAGED_COPY_ENGINE_RETURN = 1
+
+
+def copy_ext_staged(dst, src, block_count: int, block_len: int, src_gap: int, dst_gap: int,
+                    staging, staging_bytes: int = None, flags: int = 0, stream=None) -> None:
+    """DataCopyExt between host buffers through a device staging buffer (copy-engine
+    gather host -> device, return write overlapped on a second stream)."""
+    if staging_bytes is None:
+        staging_bytes = staging.numel() * staging.element_size()
+    p = DcopyExtParams(block_count, block_len, src_gap, dst_gap)
+    _check(lib().dcopy_copy_ext_staged(_host_or_dev(dst), _host_or_dev(src), ctypes.byref(p),
+                                       _ptr(staging), staging_bytes, flags, _stream(stream)),
+           "dcopy_copy_ext_staged")
+
+
+def _host_or_dev(x):
+    """Address of a tensor in any memory (pageable host included), a numpy array or an int."""
+    if hasattr(x, "data_ptr"):
+        return x.data_ptr()
+    if hasattr(x, "ctypes"):
+        return x.ctypes.data
+    return x
 
 
 def copy_ext_loop(dst, src, block_count: int, block_len: int, src_gap: int, dst_gap: int,

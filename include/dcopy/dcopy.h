@@ -140,6 +140,21 @@ typedef struct DcopyExtParams {
 int dcopy_copy_ext(void *dst, const void *src, const DcopyExtParams *params,
                    dcopy_stream_t stream);
 
+/* DataCopyExt whose source and destination are host memory, through a device
+ * staging buffer the caller provides (`staging`, `staging_bytes`, memory of the
+ * current device; no allocation inside).  The copy engine gathers the bursts
+ * host -> device chunk by chunk on `stream` (a 2-D copy reads only the bursts);
+ * each staged chunk is written to dst, with its gaps, on the library's
+ * per-device return stream while the next chunk is gathered, so both PCIe
+ * directions are busy at once.  The return write is the copy kernel (dst must
+ * be pinned host memory) unless flags has DCOPY_STAGED_COPY_ENGINE_RETURN (any
+ * host memory).  `stream` waits for the last write: the call is ordered on it.
+ * Staging must hold at least two bursts; four chunks' worth keeps the pipeline
+ * full.  No counterpart in the reference. */
+#define DCOPY_STAGED_COPY_ENGINE_RETURN 1
+int dcopy_copy_ext_staged(void *dst, const void *src, const DcopyExtParams *params, void *staging,
+                          uint64_t staging_bytes, int32_t flags, dcopy_stream_t stream);
+
 /* LoopModeParams of the v35 DataCopyPadExtend (v35/ascendc/api_regbase/datacopy.h:29-45,
  * 60-72), field order as GE's codegen emits it (v35/codegen/reg_api_call/
  * reg_api_call_utils.cpp:64-73); strides in bytes, absolute (not gaps). */

@@ -179,3 +179,14 @@ def test_copy_ext_loop_argument_checks(dcopy):
         dcopy.copy_ext_loop(0x1000, 0x2000, 1, 16, 0, 0, (2, 1 << 50, 64))
     assert e.value.code == dcopy.ERR_PARAM_INVALID
     dcopy.copy_ext_loop(0x1000, 0x2000, 0, 16, 0, 0, (2, 64, 64))  # nothing to copy
+
+
+def test_copy_ext_staged_argument_checks(dcopy):
+    import ctypes
+    assert dcopy.lib().dcopy_copy_ext_staged(None, None, None, None, 0, 0, None) == \
+        dcopy.ERR_PARAM_INVALID
+    p = dcopy.DcopyExtParams(4, 64, 0, 0)
+    assert dcopy.lib().dcopy_copy_ext_staged(0x1000, 0x2000, ctypes.byref(p), 0x3000, 1 << 20, 6,
+                                             None) == dcopy.ERR_PARAM_INVALID  # unknown flags
+    assert dcopy.lib().dcopy_copy_ext_staged(0x1000, 0x2000, ctypes.byref(p), None, 1 << 20, 0,
+                                             None) == dcopy.ERR_PARAM_INVALID  # no staging

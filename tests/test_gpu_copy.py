@@ -268,3 +268,47 @@ def test_copy_ext_loop_matches_oracle(torch_cuda, dcopy, oracle, seed):
                         (l1, l1s, l1d), (l2, l2s, l2d))
     torch.cuda.synchronize()
     assert dst.cpu().numpy().tobytes() == expect.tobytes()
+
+
+@pytest.mark.parametrize("ce_return", [False, True])
+@pytest.mark.parametrize("staging_bursts", [1000, 3, 7])
+def test_copy_ext_staged_matches_oracle(torch_cuda, dcopy, oracle, ce_return, staging_bursts):
+    """Host -> host DataCopyExt through a device staging buffer: the copy engine gathers
+    chunks, the kernel (or the copy engine) writes them back; a staging buffer of a few
+    bursts runs as a ring of two slots."""
+    torch = torch_cuda
+    count, blen, sgap, dgap = 300, 96, 160, 32
+    src_np = _rand_bytes((count - 1) * (blen + sgap) + blen, seed=21)
+    expect = np.full((count - 1) * (blen + dgap) + blen + 16, CANARY, dtype=np.uint8)
+    oracle.copy_ext(expect, src_np, count, blen, sgap, dgap)
+    h_src = torch.from_numpy(src_np).pin_memory()
+    h_dst = torch.full((expect.size,), CANARY, dtype=torch.uint8).pin_memory()
+    staging = torch.empty(staging_bursts * blen, dtype=torch.uint8, device="cuda")
+    flags = dcopy.STAGED_COPY_ENGINE_RETURN if ce_return else 0
+    dcopy.copy_ext_staged(h_dst, h_src, count, blen, sgap, dgap, staging, flags=flags)
+    torch.cuda.current_stream().synchronize()
+    assert h_dst.numpy().tobytes() == expect.tobytes()
+
+
+def test_copy_ext_staged_pageable_and_refusals(torch_cuda, dcopy, oracle):
+    torch = torch_cuda
+    count, blen, sgap = 64, 4096, 12288
+    src_np = _rand_bytes((count - 1) * (blen + sgap) + blen, seed=22)
+    expect = np.zeros(count * blen, dtype=np.uint8)
+    oracle.copy_ext(expect, src_np, count, blen, sgap, 0)
+    staging = torch.empty(1 << 20, dtype=torch.uint8, device="cuda")
+    pageable = np.zeros(count * blen, dtype=np.uint8)
+    # Pageable host memory both ways: the copy engine writes the result back.
+    dcopy.copy_ext_staged(pageable, src_np, count, blen, sgap, 0, staging,
+                          flags=dcopy.STAGED_COPY_ENGINE_RETURN)
+    torch.cuda.current_stream().synchronize()
+    assert pageable.tobytes() == expect.tobytes()
+    # The kernel cannot write pageable memory: refused before anything runs.
+    with pytest.raises(dcopy.DcopyError) as e:
+        dcopy.copy_ext_staged(np.zeros(count * blen, dtype=np.uint8), src_np, count, blen, sgap,
+                              0, staging)
+    assert e.value.code == dcopy.ERR_PARAM_INVALID
+    with pytest.raises(dcopy.DcopyError) as e:  # staging smaller than two bursts
+        dcopy.copy_ext_staged(pageable, src_np, count, blen, sgap, 0, staging, staging_bytes=blen,
+                              flags=dcopy.STAGED_COPY_ENGINE_RETURN)
+    assert e.value.code == dcopy.ERR_PARAM_INVALID
