@@ -126,9 +126,10 @@ extern "C" int dcopy_copy_ext_batch(const DcopyExtCopy *copies, uint32_t count,
     if (c.params.srcStride > (1ull << 48) || c.params.dstStride > (1ull << 48))
       return set_error(DCOPY_ERR_PARAM_INVALID, "copy_ext_batch: copy %u: stride beyond 2^48 bytes",
                        k);
-    const uint64_t src_span = (n - 1) * (len + c.params.srcStride) + len;
-    const uint64_t dst_span = (n - 1) * (len + c.params.dstStride) + len;
-    int rc = check_device_span(c.src, src_span, "copy_ext_batch src");
+    uint64_t src_span = 0, dst_span = 0;
+    int rc = block_span(n, len + c.params.srcStride, len, &src_span, "copy_ext_batch src");
+    if (!rc) rc = block_span(n, len + c.params.dstStride, len, &dst_span, "copy_ext_batch dst");
+    if (!rc) rc = check_device_span(c.src, src_span, "copy_ext_batch src");
     if (!rc) rc = check_device_span(c.dst, dst_span, "copy_ext_batch dst");
     if (!rc) rc = check_disjoint(c.src, src_span, c.dst, dst_span, "copy_ext_batch");
     if (rc) return rc;

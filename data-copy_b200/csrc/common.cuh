@@ -36,6 +36,10 @@ bool is_local_device_memory(const void *ptr);
 uint64_t allocation_base(const void *ptr);
 // 0 when the byte ranges [a, a+an) and [b, b+bn) are disjoint, else PARAM_INVALID.
 int check_disjoint(const void *a, uint64_t an, const void *b, uint64_t bn, const char *what);
+// Bytes spanned by `count` (>= 1) blocks of `len` bytes, `pitch` bytes apart:
+// (count - 1) * pitch + len, computed without wrapping.  0 (OK) with *span set,
+// or PARAM_INVALID (`what` in the message) when the span reaches 2^62 bytes.
+int block_span(uint64_t count, uint64_t pitch, uint64_t len, uint64_t *span, const char *what);
 
 // Streaming multiprocessors of the current device (cached per device).
 int sm_count();

@@ -408,8 +408,10 @@ extern "C" int dcopy_copy_ext(void *dst, const void *src, const DcopyExtParams *
   const uint64_t sp = len + p->srcStride, dp = len + p->dstStride;
   if (p->srcStride > (1ull << 48) || p->dstStride > (1ull << 48))
     return set_error(DCOPY_ERR_PARAM_INVALID, "copy_ext: stride beyond 2^48 bytes");
-  const uint64_t src_span = (count - 1) * sp + len, dst_span = (count - 1) * dp + len;
-  int rc = check_device_span(src, src_span, "copy_ext src");
+  uint64_t src_span = 0, dst_span = 0;
+  int rc = block_span(count, sp, len, &src_span, "copy_ext src");
+  if (!rc) rc = block_span(count, dp, len, &dst_span, "copy_ext dst");
+  if (!rc) rc = check_device_span(src, src_span, "copy_ext src");
   if (!rc) rc = check_device_span(dst, dst_span, "copy_ext dst");
   if (!rc) rc = check_disjoint(src, src_span, dst, dst_span, "copy_ext");
   if (rc) return rc;
@@ -462,7 +464,7 @@ extern "C" int dcopy_copy_nd(void *dst, const void *src, int ndim, const uint64_
     return set_error(DCOPY_ERR_DATATYPE_INVALID, "copy_nd: elem_bytes %u not in {1,2,4,8,16}",
                      elem_bytes);
   uint64_t total = 1;
-  uint64_t src_last = 0, dst_last = 0;  // element offset of the last element
+  unsigned __int128 src_last = 0, dst_last = 0;  // element offset of the last element
   for (int k = 0; k < ndim; ++k) {
     if (src_strides[k] < 0 || dst_strides[k] < 0)
       return set_error(DCOPY_ERR_PARAM_INVALID, "copy_nd: negative stride in dim %d", k);
@@ -473,12 +475,16 @@ extern "C" int dcopy_copy_nd(void *dst, const void *src, int ndim, const uint64_
       return set_error(DCOPY_ERR_UNSUPPORTED, "copy_nd: dim %d size beyond 2^32", k);
     total *= sizes[k];
     if (sizes[k]) {
-      src_last += (sizes[k] - 1) * (uint64_t)src_strides[k];
-      dst_last += (sizes[k] - 1) * (uint64_t)dst_strides[k];
+      src_last += (unsigned __int128)(sizes[k] - 1) * (uint64_t)src_strides[k];
+      dst_last += (unsigned __int128)(sizes[k] - 1) * (uint64_t)dst_strides[k];
     }
   }
   if (!total) return DCOPY_OK;
-  const uint64_t src_span = (src_last + 1) * elem_bytes, dst_span = (dst_last + 1) * elem_bytes;
+  if ((src_last + 1) * elem_bytes >= ((unsigned __int128)1 << 62) ||
+      (dst_last + 1) * elem_bytes >= ((unsigned __int128)1 << 62))
+    return set_error(DCOPY_ERR_PARAM_INVALID, "copy_nd: the box spans 2^62 bytes or more");
+  const uint64_t src_span = (uint64_t)((src_last + 1) * elem_bytes);
+  const uint64_t dst_span = (uint64_t)((dst_last + 1) * elem_bytes);
   int rc = check_device_span(src, src_span, "copy_nd src");
   if (!rc) rc = check_device_span(dst, dst_span, "copy_nd dst");
   if (!rc) rc = check_disjoint(src, src_span, dst, dst_span, "copy_nd");

@@ -281,6 +281,14 @@ int transpose_impl(void *dst, const void *src, const int64_t *shape, const int64
                      data_type);
   if (!shape_arg_valid(shape, rank, perm, rank))
     return set_error(DCOPY_ERR_PARAM_INVALID, "Transpose: invalid shape or perm");
+  {  // the element count and its bytes must not wrap (GE would fail the allocation)
+    unsigned __int128 items = 1;
+    for (int i = 0; i < rank && items; ++i) {
+      items *= (uint64_t)shape[i];
+      if (items * (uint64_t)(size ? size : 1) >= ((unsigned __int128)1 << 62))
+        return set_error(DCOPY_ERR_PARAM_INVALID, "Transpose: the tensor spans 2^62 bytes or more");
+    }
+  }
   int64_t heads[kMaxRank];
   for (int i = rank - 1; i >= 0; --i) heads[i] = (i == rank - 1) ? 1 : shape[i + 1] * heads[i + 1];
   uint64_t sizes[kMaxRank];

@@ -82,11 +82,14 @@ extern "C" int dcopy_copy_ext_staged(void *dst, const void *src, const DcopyExtP
   if (!dst || !src || !staging)
     return set_error(DCOPY_ERR_PARAM_INVALID, "copy_ext_staged: NULL buffer");
   const uint64_t sp = len + p->srcStride, dp = len + p->dstStride;
-  const uint64_t src_span = (rows - 1) * sp + len, dst_span = (rows - 1) * dp + len;
+  uint64_t src_span = 0, dst_span = 0;
+  int rc = block_span(rows, sp, len, &src_span, "copy_ext_staged src");
+  if (!rc) rc = block_span(rows, dp, len, &dst_span, "copy_ext_staged dst");
+  if (rc) return rc;
   // The staging buffer is device memory of the current device; the destination
   // must be pinned for the kernel to write it (the copy engine takes any).
-  int rc = check_device_span(staging, std::min<uint64_t>(staging_bytes, rows * len),
-                             "copy_ext_staged staging");
+  rc = check_device_span(staging, std::min<uint64_t>(staging_bytes, rows * len),
+                         "copy_ext_staged staging");
   if (rc) return rc;
   if (!is_local_device_memory(staging))
     return set_error(DCOPY_ERR_PARAM_INVALID,

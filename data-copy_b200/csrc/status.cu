@@ -117,6 +117,14 @@ uint64_t allocation_base(const void *ptr) {
   return (uint64_t)start;
 }
 
+int block_span(uint64_t count, uint64_t pitch, uint64_t len, uint64_t *span, const char *what) {
+  const unsigned __int128 s = (unsigned __int128)(count ? count - 1 : 0) * pitch + len;
+  if (s >= ((unsigned __int128)1 << 62))
+    return set_error(DCOPY_ERR_PARAM_INVALID, "%s: the copy spans 2^62 bytes or more", what);
+  *span = (uint64_t)s;
+  return DCOPY_OK;
+}
+
 int check_disjoint(const void *a, uint64_t an, const void *b, uint64_t bn, const char *what) {
   if (!an || !bn) return DCOPY_OK;
   const uint64_t pa = (uint64_t)(uintptr_t)a, pb = (uint64_t)(uintptr_t)b;

@@ -190,3 +190,22 @@ def test_copy_ext_staged_argument_checks(dcopy):
                                              None) == dcopy.ERR_PARAM_INVALID  # unknown flags
     assert dcopy.lib().dcopy_copy_ext_staged(0x1000, 0x2000, ctypes.byref(p), None, 1 << 20, 0,
                                              None) == dcopy.ERR_PARAM_INVALID  # no staging
+
+
+def test_spans_that_would_wrap_are_refused(dcopy):
+    """Spans are computed without wrapping: a copy whose span reaches 2^62 bytes is
+    refused on the host before any pointer is looked at."""
+    big_count, big_gap = 0xFFFFFFFF, 1 << 48
+    with pytest.raises(dcopy.DcopyError) as e:
+        dcopy.copy_ext(0x1000, 0x2000, big_count, 16, big_gap, 0)
+    assert e.value.code == dcopy.ERR_PARAM_INVALID and "2^62" in str(e.value)
+    with pytest.raises(dcopy.DcopyError) as e:
+        dcopy.copy_ext_batch([(0x1000, 0x2000, big_count, 16, big_gap, 0)])
+    assert e.value.code == dcopy.ERR_PARAM_INVALID
+    with pytest.raises(dcopy.DcopyError) as e:
+        dcopy.copy_nd(0x1000, 0x2000, [0xFFFFFFFF, 0xFFFFFFFF, 4], [1 << 40, 1 << 20, 1],
+                      [1 << 24, 4, 1], 4)
+    assert e.value.code == dcopy.ERR_PARAM_INVALID
+    with pytest.raises(dcopy.DcopyError) as e:
+        dcopy.transpose(0x1000, 0x2000, [1 << 31, 1 << 31, 1 << 10], [2, 1, 0], 0)
+    assert e.value.code == dcopy.ERR_PARAM_INVALID
