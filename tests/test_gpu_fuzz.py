@@ -17,7 +17,7 @@ def _bytes(n, rng):
     return rng.integers(0, 256, size=n, dtype=np.uint8)
 
 
-@pytest.mark.parametrize("seed", range(40))
+@pytest.mark.parametrize("seed", range(80))
 def test_transpose_random(torch_cuda, dcopy, oracle, seed):
     torch = torch_cuda
     rng = np.random.default_rng(5000 + seed)
@@ -41,7 +41,7 @@ def test_transpose_random(torch_cuda, dcopy, oracle, seed):
     assert (out[:off_d] == CANARY).all() and (out[off_d + n:] == CANARY).all()
 
 
-@pytest.mark.parametrize("seed", range(40))
+@pytest.mark.parametrize("seed", range(80))
 def test_copy_ext_random(torch_cuda, dcopy, oracle, seed):
     torch = torch_cuda
     rng = np.random.default_rng(6000 + seed)
@@ -61,7 +61,7 @@ def test_copy_ext_random(torch_cuda, dcopy, oracle, seed):
     assert dst.cpu().numpy().tobytes() == expect.tobytes(), (count, blen, sgap, dgap, soff, doff)
 
 
-@pytest.mark.parametrize("seed", range(40))
+@pytest.mark.parametrize("seed", range(80))
 def test_copy_nd_random(torch_cuda, dcopy, oracle, seed):
     """Random boxes: destination strides are a padded dense layout in a random axis
     order (no two elements share a destination), source strides are arbitrary
@@ -103,7 +103,7 @@ def test_copy_nd_random(torch_cuda, dcopy, oracle, seed):
 NZ_KINDS = [(2, 16), (1, 32), (4, 16), (4, 8), (8, 16), (2, 8)]  # (element bytes, W0 / C0)
 
 
-@pytest.mark.parametrize("seed", range(24))
+@pytest.mark.parametrize("seed", range(40))
 def test_nz_zz_random(torch_cuda, dcopy, oracle, seed):
     torch = torch_cuda
     rng = np.random.default_rng(8000 + seed)
@@ -139,7 +139,7 @@ NCHW, NHWC, HWCN = 0, 1, 16
 FZ_KINDS = [(2, 16), (1, 32), (4, 16), (4, 8)]
 
 
-@pytest.mark.parametrize("seed", range(24))
+@pytest.mark.parametrize("seed", range(40))
 def test_fractal_z_random(torch_cuda, dcopy, oracle, seed):
     torch = torch_cuda
     rng = np.random.default_rng(9000 + seed)
