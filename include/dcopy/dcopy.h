@@ -438,7 +438,7 @@ int dcopy_memcpy_async_batch(const DcopyMemcpyInfo *infos, uint32_t count, int32
                              dcopy_stream_t stream);
 
 /* ---- multi-GPU ----------------------------------------------------------------
- * No counterpart in the reference (single-core Ascend kernels; SURVEY row e).
+ * No counterpart in the reference (its kernels run on one device).
  * Copies shard by splitting the blockCount range over devices with no
  * exchange; the separate ring shift moves each device's shard to the next
  * device with in-kernel stores over NVLink.  No TMA multicast is used. */
