@@ -150,7 +150,9 @@ int dcopy_copy_ext(void *dst, const void *src, const DcopyExtParams *params,
  * be pinned host memory) unless flags has DCOPY_STAGED_COPY_ENGINE_RETURN (any
  * host memory).  `stream` waits for the last write: the call is ordered on it.
  * Staging must hold at least two bursts; four chunks' worth keeps the pipeline
- * full.  No counterpart in the reference. */
+ * full.  Calls on one device share the return stream (they serialise there);
+ * capturing one in a CUDA graph while another thread issues staged copies on
+ * the same device is not supported.  No counterpart in the reference. */
 #define DCOPY_STAGED_COPY_ENGINE_RETURN 1
 int dcopy_copy_ext_staged(void *dst, const void *src, const DcopyExtParams *params, void *staging,
                           uint64_t staging_bytes, int32_t flags, dcopy_stream_t stream);
