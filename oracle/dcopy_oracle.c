@@ -101,6 +101,18 @@ void oracle_copy_ext(void *dst, const void *src, uint64_t block_count, uint64_t 
   for (uint64_t i = 0; i < block_count; ++i) memcpy(d + i * dp, s + i * sp, block_len);
 }
 
+void oracle_copy_ext_loop(void *dst, const void *src, uint64_t block_count, uint64_t block_len,
+                          uint64_t src_gap, uint64_t dst_gap, uint64_t loop1_size,
+                          uint64_t loop2_size, uint64_t loop1_src, uint64_t loop1_dst,
+                          uint64_t loop2_src, uint64_t loop2_dst) {
+  const uint8_t *s = (const uint8_t *)src;
+  uint8_t *d = (uint8_t *)dst;
+  for (uint64_t i = 0; i < loop2_size; ++i)
+    for (uint64_t j = 0; j < loop1_size; ++j)
+      oracle_copy_ext(d + i * loop2_dst + j * loop1_dst, s + i * loop2_src + j * loop1_src,
+                      block_count, block_len, src_gap, dst_gap);
+}
+
 typedef struct {
   uint8_t *dst;
   const uint8_t *src;

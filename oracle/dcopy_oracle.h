@@ -66,6 +66,16 @@ void oracle_fill_pattern(int32_t *dst, uint64_t n);
  * Regions must not overlap. */
 void oracle_copy_ext(void *dst, const void *src, uint64_t block_count, uint64_t block_len,
                      uint64_t src_gap, uint64_t dst_gap);
+/* The gap copy inside LoopModeParams' two outer loops, as GE's codegen writes
+ * the loop nest (v35/codegen/reg_api_call/reg_api_call_utils.h:17-25):
+ *   for i < loop2_size, j < loop1_size: copy_ext(dst + i*loop2_dst + j*loop1_dst,
+ *                                                src + i*loop2_src + j*loop1_src)
+ * loop strides in bytes (reg_api_call_utils.cpp:64-73 multiplies by the
+ * element size). */
+void oracle_copy_ext_loop(void *dst, const void *src, uint64_t block_count, uint64_t block_len,
+                          uint64_t src_gap, uint64_t dst_gap, uint64_t loop1_size,
+                          uint64_t loop2_size, uint64_t loop1_src, uint64_t loop1_dst,
+                          uint64_t loop2_src, uint64_t loop2_dst);
 /* Same, blockCount range split over `nthreads` pthreads (CPU baseline). */
 int oracle_copy_ext_mt(void *dst, const void *src, uint64_t block_count, uint64_t block_len,
                        uint64_t src_gap, uint64_t dst_gap, int nthreads);

@@ -52,6 +52,7 @@ def lib() -> ctypes.CDLL:
             "oracle_run_tiles": [ctypes.c_int, _vp, _vp, ctypes.POINTER(Tiling)],
             "oracle_fill_pattern": [_vp, ctypes.c_uint64],
             "oracle_copy_ext": [_vp, _vp] + [ctypes.c_uint64] * 4,
+            "oracle_copy_ext_loop": [_vp, _vp] + [ctypes.c_uint64] * 10,
             "oracle_copy_ext_mt": [_vp, _vp] + [ctypes.c_uint64] * 4 + [ctypes.c_int],
             "oracle_copy_nd": [_vp, _vp, ctypes.c_int, _u64p, _i64p, _i64p, ctypes.c_uint32],
             "oracle_nz_shape": [_i64p, ctypes.c_int, ctypes.c_int64, _i64p,
@@ -79,7 +80,8 @@ def lib() -> ctypes.CDLL:
         for name, args in sig.items():
             fn = getattr(h, name)
             fn.argtypes = args
-            fn.restype = None if name in ("oracle_fill_pattern", "oracle_copy_ext") else ctypes.c_int
+            fn.restype = (None if name in ("oracle_fill_pattern", "oracle_copy_ext",
+                                           "oracle_copy_ext_loop") else ctypes.c_int)
         _lib = h
     return _lib
 
@@ -117,6 +119,13 @@ def copy_ext(dst: np.ndarray, src: np.ndarray, count, blen, sgap=0, dgap=0, thre
         lib().oracle_copy_ext_mt(_p(dst), _p(src), count, blen, sgap, dgap, threads)
     else:
         lib().oracle_copy_ext(_p(dst), _p(src), count, blen, sgap, dgap)
+
+
+def copy_ext_loop(dst: np.ndarray, src: np.ndarray, count, blen, sgap, dgap, loop1,
+                  loop2=(1, 0, 0)) -> None:
+    """LoopModeParams around the gap copy; loop1/loop2 = (size, src stride, dst stride) bytes."""
+    lib().oracle_copy_ext_loop(_p(dst), _p(src), count, blen, sgap, dgap, loop1[0], loop2[0],
+                               loop1[1], loop1[2], loop2[1], loop2[2])
 
 
 def copy_nd(dst, src, sizes, src_strides, dst_strides, elem_bytes) -> int:

@@ -243,7 +243,7 @@ def test_copy_ext_batch_refuses_overlaps(torch_cuda, dcopy):
 @pytest.mark.parametrize("seed", range(12))
 def test_copy_ext_loop_matches_oracle(torch_cuda, dcopy, oracle, seed):
     """LoopModeParams: the DataCopyExt copy inside two outer loops
-    (reg_api_call_utils.h:17-25), composed on the host from the oracle's copy_ext."""
+    (reg_api_call_utils.h:17-25), against the oracle's restatement of the loop nest."""
     torch = torch_cuda
     rng = np.random.default_rng(300 + seed)
     count, blen = int(rng.integers(1, 20)), int(rng.choice([int(rng.integers(1, 90)), 64, 256]))
@@ -258,10 +258,8 @@ def test_copy_ext_loop_matches_oracle(torch_cuda, dcopy, oracle, seed):
     soff, doff = int(rng.integers(0, 16)), int(rng.integers(0, 16))
     src_np = _rand_bytes((l2 - 1) * l2s + (l1 - 1) * l1s + inner_src + soff, seed=seed)
     expect = np.full((l2 - 1) * l2d + (l1 - 1) * l1d + inner_dst + doff + 32, CANARY, dtype=np.uint8)
-    for i in range(l2):
-        for j in range(l1):
-            d0, s0 = doff + i * l2d + j * l1d, soff + i * l2s + j * l1s
-            oracle.copy_ext(expect[d0:], src_np[s0:], count, blen, sgap, dgap)
+    oracle.copy_ext_loop(expect[doff:], src_np[soff:], count, blen, sgap, dgap, (l1, l1s, l1d),
+                         (l2, l2s, l2d))
     src = torch.from_numpy(src_np).cuda()
     dst = _canary(torch, expect.size)
     dcopy.copy_ext_loop(dst.data_ptr() + doff, src.data_ptr() + soff, count, blen, sgap, dgap,

@@ -179,3 +179,23 @@ def test_copy_nd_matches_numpy(oracle):
     d_strides = [42, 7, 1]
     assert oracle.copy_nd(dst, src, sizes, s_strides, d_strides, 4) == 0
     assert (dst == np.transpose(src, (2, 0, 1))).all()
+
+
+def test_copy_ext_loop_is_the_loop_nest(oracle):
+    """oracle_copy_ext_loop equals GE codegen's documented loop nest around the gap copy,
+    checked against a numpy restatement of the same addresses."""
+    rng = np.random.default_rng(77)
+    count, blen, sgap, dgap = 5, 24, 8, 4
+    l1, l1s, l1d = 3, 200, 150
+    l2, l2s, l2d = 2, 700, 500
+    src = rng.integers(0, 256, size=2000, dtype=np.uint8)
+    got = np.zeros(1200, dtype=np.uint8)
+    oracle.copy_ext_loop(got, src, count, blen, sgap, dgap, (l1, l1s, l1d), (l2, l2s, l2d))
+    want = np.zeros_like(got)
+    for i in range(l2):
+        for j in range(l1):
+            for b in range(count):
+                s0 = i * l2s + j * l1s + b * (blen + sgap)
+                d0 = i * l2d + j * l1d + b * (blen + dgap)
+                want[d0:d0 + blen] = src[s0:s0 + blen]
+    assert got.tobytes() == want.tobytes()
