@@ -10,8 +10,10 @@ for p in (ROOT, ROOT / "data-copy_b200", ROOT / "tests" / "golden"):
     if str(p) not in sys.path:
         sys.path.insert(0, str(p))
 
-# Reference checkout (only present where the golden vectors can be re-read).
-REFERENCE = Path(os.environ.get("DCOPY_REFERENCE", "/root/reference"))
+# Reference checkout, only present where the golden vectors can be re-read: the
+# directory DCOPY_REFERENCE names, else a checkout called `reference` beside this
+# repository.  Tests that need it skip when neither exists.
+REFERENCE = Path(os.environ.get("DCOPY_REFERENCE") or (ROOT.parent / "reference"))
 GOLDEN = ROOT / "tests" / "golden"
 
 

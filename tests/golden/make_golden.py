@@ -29,7 +29,8 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-DEFAULT_REFERENCE = os.environ.get("DCOPY_REFERENCE", "/root/reference")
+# The reference checkout: DCOPY_REFERENCE, else `reference` beside this repository.
+DEFAULT_REFERENCE = os.environ.get("DCOPY_REFERENCE") or str(HERE.parents[2] / "reference")
 
 
 def load_reference(ref_root: Path):
