@@ -1,16 +1,26 @@
-// demo_datacopy: the standalone_datacopy host driver on a B200, through the dcopy C ABI.
+// demo_datacopy: runs one standalone_datacopy mode on a B200 through the dcopy C ABI
+// and checks the transpose on the host.
 //
-// Same command line, validation, input pattern, canary, verification and report
-// file as the reference host (standalone_datacopy/datacopy_data_collection.asc:73-181):
 //   demo_datacopy small|large|pretranspose ROWS COLS TILE_KIB STORE(0|1) DEVICE_ID
 //                 [VERIFICATION_FILE]
-// The summary line keeps the reference's keys and appends the device time of
-// the kernels (CUDA events) and the resulting GB/s (read + write).
+//
+// The command line, the error texts, the input pattern (word i holds i*17+3),
+// the 0xA5 canary in y and the one-line report file follow the reference's
+// host program (standalone_datacopy/datacopy_data_collection.asc:97-181), so
+// scripts written for it (profile.py) drive this tool unchanged.  The tiling
+// itself is validated by dcopy_plan_tiling, whose messages are the reference's.
+// The summary line keeps the reference's keys and adds the device time of the
+// timed launch (CUDA events) and the GB/s it moved.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <cctype>
 #include <cstdint>
+#include <cstdlib>
 #include <fstream>
 #include <iostream>
+#include <memory>
+#include <sstream>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -19,145 +29,182 @@
 
 namespace {
 
-void Check(cudaError_t e) {
-  if (e != cudaSuccess) throw std::runtime_error(std::string("CUDA error ") + cudaGetErrorName(e));
-}
-
-void CheckD(int rc) {
-  if (rc != DCOPY_OK) throw std::runtime_error(dcopy_last_error_message());
-}
-
-// Device allocation that waits for pending work on its stream before freeing,
-// also while an exception unwinds (asc:76-87).
-struct DeviceBuffer {
-  void *data = nullptr;
-  cudaStream_t stream;
-  DeviceBuffer(size_t bytes, cudaStream_t s) : stream(s) { Check(cudaMalloc(&data, bytes)); }
-  ~DeviceBuffer() {
-    if (data) {
-      cudaStreamSynchronize(stream);
-      cudaFree(data);
-    }
-  }
-  DeviceBuffer(const DeviceBuffer &) = delete;
-  DeviceBuffer &operator=(const DeviceBuffer &) = delete;
+struct Failure : std::runtime_error {
+  using std::runtime_error::runtime_error;
 };
 
-uint32_t Number(const char *s) {  // asc:89-96
-  std::string value(s);
-  if (value.empty() || value.find_first_not_of("0123456789") != std::string::npos)
-    throw std::runtime_error("Expected a nonnegative integer");
-  const auto n = std::stoull(value);
-  if (n > UINT32_MAX) throw std::runtime_error("Integer overflow");
-  return static_cast<uint32_t>(n);
+void cuda_ok(cudaError_t e, const char *what) {
+  if (e != cudaSuccess) throw Failure(std::string(what) + ": " + cudaGetErrorName(e));
+}
+void dcopy_ok(int rc) {
+  if (rc != DCOPY_OK) throw Failure(dcopy_last_error_message());
+}
+
+// ---- command line ----------------------------------------------------------------
+
+enum class Mode { kSmall, kLarge, kPretranspose };
+
+struct Options {
+  Mode mode;
+  std::string mode_name;
+  uint32_t rows, cols, tile_kib, store, device;
+  const char *report = nullptr;  // VERIFICATION_FILE, only with STORE=1
+};
+
+// A decimal u32: digits only (no sign, no blank), at most 4294967295.
+uint32_t parse_u32(const std::string &text) {
+  const bool digits = !text.empty() && std::all_of(text.begin(), text.end(), [](unsigned char ch) {
+    return std::isdigit(ch) != 0;
+  });
+  if (!digits) throw Failure("Expected a nonnegative integer");
+  uint64_t v = 0;
+  for (char ch : text) {
+    v = v * 10 + uint64_t(ch - '0');
+    if (v > 0xFFFFFFFFull) throw Failure("Integer overflow");
+  }
+  return uint32_t(v);
+}
+
+Options parse(int argc, char **argv) {
+  if (argc < 7 || argc > 8)
+    throw Failure(
+        "Usage: demo_datacopy small|large|pretranspose ROWS COLS TILE_KIB STORE(0|1) DEVICE_ID "
+        "[VERIFICATION_FILE]");
+  static const std::pair<const char *, Mode> kModes[] = {
+      {"small", Mode::kSmall}, {"large", Mode::kLarge}, {"pretranspose", Mode::kPretranspose}};
+  Options o{};
+  o.mode_name = argv[1];
+  const auto *hit = std::find_if(std::begin(kModes), std::end(kModes),
+                                 [&](const auto &m) { return o.mode_name == m.first; });
+  if (hit == std::end(kModes)) throw Failure("Unknown mode");
+  o.mode = hit->second;
+  uint32_t *fields[] = {&o.rows, &o.cols, &o.tile_kib, &o.store, &o.device};
+  for (int i = 0; i < 5; ++i) *fields[i] = parse_u32(argv[2 + i]);
+  if (argc == 8) {
+    if (o.store != 1) throw Failure("VERIFICATION_FILE requires STORE=1");
+    o.report = argv[7];
+  }
+  return o;
+}
+
+// ---- device buffers -------------------------------------------------------------
+
+// Owns the run's stream and device buffers.  The destructor drains the stream
+// before anything is freed, on success and on every error path alike.
+class Session {
+ public:
+  explicit Session(int device) {
+    cuda_ok(cudaSetDevice(device), "cudaSetDevice");
+    cuda_ok(cudaStreamCreate(&stream_), "cudaStreamCreate");
+  }
+  ~Session() {
+    cudaStreamSynchronize(stream_);
+    for (void *p : owned_) cudaFree(p);
+    cudaStreamDestroy(stream_);
+  }
+  Session(const Session &) = delete;
+  Session &operator=(const Session &) = delete;
+
+  void *alloc(size_t bytes) {
+    void *p = nullptr;
+    cuda_ok(cudaMalloc(&p, bytes), "cudaMalloc");
+    owned_.push_back(p);
+    return p;
+  }
+  cudaStream_t stream() const { return stream_; }
+  dcopy_stream_t handle() const { return reinterpret_cast<dcopy_stream_t>(stream_); }
+
+ private:
+  cudaStream_t stream_ = nullptr;
+  std::vector<void *> owned_;
+};
+
+// ---- the run ----------------------------------------------------------------------
+
+// The mode's kernels in stream order: pretranspose writes B, then copies B to y.
+void launch_mode(Mode mode, const void *x, void *y, void *b, const DataCopyTiling *t,
+                 dcopy_stream_t s) {
+  switch (mode) {
+    case Mode::kSmall: dcopy_ok(dcopy_datacopy_small(x, y, t, s)); break;
+    case Mode::kLarge: dcopy_ok(dcopy_datacopy_large(x, y, t, s)); break;
+    case Mode::kPretranspose:
+      dcopy_ok(dcopy_datacopy_pretranspose(x, b, t, s));
+      dcopy_ok(dcopy_datacopy_contiguous(b, y, t, s));
+      break;
+  }
+}
+
+std::string run(const Options &o) {
+  DataCopyTiling tiling{};
+  dcopy_ok(dcopy_plan_tiling(o.rows, o.cols, o.tile_kib, o.store, &tiling));
+  if (o.device > 255) throw Failure("device: 0..255");
+  const size_t words = size_t(tiling.rows) * tiling.cols, bytes = words * 4;
+  // Word i of the input is i*17+3 (wrapping in 32 bits), as the reference fills it.
+  std::vector<uint32_t> host(words);
+  for (size_t i = 0; i < words; ++i) host[i] = uint32_t(i) * 17u + 3u;
+
+  Session dev(int(o.device));
+  const bool two_pass = o.mode == Mode::kPretranspose;
+  void *x = dev.alloc(bytes), *y = dev.alloc(bytes), *b = dev.alloc(two_pass ? bytes : 16);
+  auto *tiling_dev = static_cast<DataCopyTiling *>(dev.alloc(sizeof(tiling)));
+  cuda_ok(cudaMemcpy(x, host.data(), bytes, cudaMemcpyHostToDevice), "input upload");
+  cuda_ok(cudaMemcpy(tiling_dev, &tiling, sizeof(tiling), cudaMemcpyHostToDevice), "tiling upload");
+
+  // First launch with the tiling in device memory, as the reference hands it to
+  // its kernels; it also loads the kernels' module, so the timed launch below
+  // (host tiling: no synchronising read) measures the copy alone.
+  launch_mode(o.mode, x, y, b, tiling_dev, dev.handle());
+  if (tiling.store) cuda_ok(cudaMemsetAsync(y, 0xA5, bytes, dev.stream()), "canary");
+  cudaEvent_t ev[2];
+  for (cudaEvent_t &e : ev) cuda_ok(cudaEventCreate(&e), "cudaEventCreate");
+  cuda_ok(cudaEventRecord(ev[0], dev.stream()), "cudaEventRecord");
+  launch_mode(o.mode, x, y, b, &tiling, dev.handle());
+  cuda_ok(cudaEventRecord(ev[1], dev.stream()), "cudaEventRecord");
+  cuda_ok(cudaStreamSynchronize(dev.stream()), "cudaStreamSynchronize");
+  float ms = 0.f;
+  cuda_ok(cudaEventElapsedTime(&ms, ev[0], ev[1]), "cudaEventElapsedTime");
+  for (cudaEvent_t e : ev) cudaEventDestroy(e);
+
+  if (tiling.store) {
+    // y = x transposed: y word (c, r) must hold the input value of word r*cols + c.
+    cuda_ok(cudaMemcpy(host.data(), y, bytes, cudaMemcpyDeviceToHost), "result download");
+    for (size_t j = 0; j < words; ++j) {
+      const size_t c = j / tiling.rows, r = j % tiling.rows;
+      if (host[j] != uint32_t(r * tiling.cols + c) * 17u + 3u)
+        throw Failure("Transpose verification failed at " + std::to_string(r) + "," +
+                      std::to_string(c));
+    }
+  }
+  // Device bytes per launch sequence: x read, plus y (and B) written when stored.
+  const double moved = double(bytes) * (two_pass ? 4.0 : (tiling.store ? 2.0 : 1.0));
+  std::ostringstream line;
+  line << "mode=" << o.mode_name << " rows=" << tiling.rows << " cols=" << tiling.cols
+       << " input_bytes=" << bytes << " tile_cols=" << tiling.tile_cols
+       << " tile_count=" << (tiling.cols + tiling.tile_cols - 1) / tiling.tile_cols
+       << " ub_bytes=" << tiling.ub_bytes
+       << " verification=" << (tiling.store ? "PASS" : "not_requested")
+       << " kernel_us=" << ms * 1e3 << " gbps=" << moved / (double(ms) * 1e6);
+  return line.str();
 }
 
 }  // namespace
 
 int main(int argc, char **argv) {
-  cudaStream_t stream = nullptr;
-  int result = 0;
+  Options opts{};
   try {
-    if (argc != 7 && argc != 8)
-      throw std::runtime_error(
-          "Usage: demo_datacopy small|large|pretranspose ROWS COLS TILE_KIB STORE(0|1) DEVICE_ID "
-          "[VERIFICATION_FILE]");
-    const std::string mode(argv[1]);
-    if (mode != "small" && mode != "large" && mode != "pretranspose")
-      throw std::runtime_error("Unknown mode");
-    const uint32_t rows = Number(argv[2]), cols = Number(argv[3]), tile_kib = Number(argv[4]);
-    const uint32_t store = Number(argv[5]);
-    if (argc == 8 && store != 1) throw std::runtime_error("VERIFICATION_FILE requires STORE=1");
-    const uint32_t device = Number(argv[6]);
-    if (!rows || rows > 4095 || rows % 8 || !cols || cols > 65535 || !tile_kib || tile_kib > 240 ||
-        store > 1 || device > 255)
-      throw std::runtime_error(
-          "rows: 8..4088 multiple of 8; cols: 1..65535; tile: 1..240 KiB; store: 0/1; device: "
-          "0..255");
-    DataCopyTiling t{};
-    CheckD(dcopy_plan_tiling(rows, cols, tile_kib, store, &t));  // asc:119-123
-    const size_t bytes = size_t(rows) * cols * 4;
-    std::vector<int32_t> input(bytes / 4), output(t.store ? bytes / 4 : 0);
-    for (size_t i = 0; i < input.size(); ++i) input[i] = static_cast<int32_t>(i * 17 + 3);
-    Check(cudaSetDevice(static_cast<int>(device)));
-    Check(cudaStreamCreate(&stream));
-    float kernel_ms = 0.f;
-    {
-      DeviceBuffer x(bytes, stream), y(bytes, stream);
-      DeviceBuffer b(mode == "pretranspose" ? bytes : 32, stream), td(sizeof(t), stream);
-      Check(cudaMemcpy(x.data, input.data(), bytes, cudaMemcpyHostToDevice));
-      Check(cudaMemcpy(td.data, &t, sizeof(t), cudaMemcpyHostToDevice));  // tiling in device GM
-      if (t.store) Check(cudaMemset(y.data, 0xA5, bytes));                 // asc:134 canary
-      const auto *gt = static_cast<const DataCopyTiling *>(td.data);
-      cudaEvent_t e0, e1;
-      Check(cudaEventCreate(&e0));
-      Check(cudaEventCreate(&e1));
-      // The tiling lives in device memory as in the reference (asc:133).  Reading
-      // it costs the library one synchronising 20-byte copy, so the timed launch
-      // below uses a host copy of it.
-      DataCopyTiling check{};
-      Check(cudaMemcpy(&check, gt, sizeof(check), cudaMemcpyDeviceToHost));
-      dcopy_stream_t s = reinterpret_cast<dcopy_stream_t>(stream);
-      // One untimed launch first, with the tiling read from device memory as the
-      // reference passes it: CUDA loads a kernel's module on its first launch,
-      // which would otherwise dominate the single timed run.
-      if (mode == "pretranspose")
-        CheckD(dcopy_datacopy_pretranspose(x.data, b.data, gt, s));
-      else
-        CheckD(dcopy_datacopy_small(x.data, y.data, gt, s));
-      if (t.store) Check(cudaMemsetAsync(y.data, 0xA5, bytes, stream));
-      Check(cudaEventRecord(e0, stream));
-      if (mode == "small") {
-        CheckD(dcopy_datacopy_small(x.data, y.data, &check, s));
-      } else if (mode == "large") {
-        CheckD(dcopy_datacopy_large(x.data, y.data, &check, s));
-      } else {  // two launches on one stream: stream order is the dependency (asc:144-146)
-        CheckD(dcopy_datacopy_pretranspose(x.data, b.data, &check, s));
-        CheckD(dcopy_datacopy_contiguous(b.data, y.data, &check, s));
-      }
-      Check(cudaEventRecord(e1, stream));
-      Check(cudaStreamSynchronize(stream));
-      Check(cudaEventElapsedTime(&kernel_ms, e0, e1));
-      cudaEventDestroy(e0);
-      cudaEventDestroy(e1);
-      if (t.store) {  // asc:149-155
-        Check(cudaMemcpy(output.data(), y.data, bytes, cudaMemcpyDeviceToHost));
-        for (uint32_t c = 0; c < t.cols; ++c)
-          for (uint32_t r = 0; r < t.rows; ++r)
-            if (output[size_t(c) * t.rows + r] != input[size_t(r) * t.cols + c])
-              throw std::runtime_error("Transpose verification failed at " + std::to_string(r) +
-                                       "," + std::to_string(c));
-      }
-      // Bytes moved on the device: x read (and y / b written) per kernel.
-      const double passes = mode == "pretranspose" ? 2.0 : 1.0;
-      const double moved = passes * double(bytes) * (mode == "pretranspose" || t.store ? 2 : 1);
-      std::cout << "mode=" << mode << " rows=" << t.rows << " cols=" << t.cols
-                << " input_bytes=" << bytes << " tile_cols=" << t.tile_cols
-                << " tile_count=" << (t.cols + t.tile_cols - 1) / t.tile_cols
-                << " ub_bytes=" << t.ub_bytes
-                << " verification=" << (t.store ? "PASS" : "not_requested")
-                << " kernel_us=" << kernel_ms * 1e3 << " gbps=" << moved / (kernel_ms * 1e6)
-                << '\n';
-    }
-    if (cudaStreamDestroy(stream) != cudaSuccess) result = 1;
-    stream = nullptr;
+    opts = parse(argc, argv);
+    std::cout << run(opts) << '\n';  // every device resource is released by now
   } catch (const std::exception &e) {
     std::cerr << e.what() << '\n';
-    result = 1;
-    if (stream) {
-      cudaStreamSynchronize(stream);
-      cudaStreamDestroy(stream);
+    return 1;
+  }
+  if (opts.report) {  // written only once the run and its cleanup have succeeded
+    std::ofstream out(opts.report);
+    out << "verification=PASS\n";
+    if (!out.flush()) {
+      std::cerr << "Cannot write verification report: " << opts.report << '\n';
+      return 1;
     }
   }
-  // The report is written only after every check and all cleanup succeeded (asc:172-179).
-  if (result == 0 && argc == 8) {
-    std::ofstream report(argv[7]);
-    report << "verification=PASS\n";
-    report.close();
-    if (!report) {
-      std::cerr << "Cannot write verification report: " << argv[7] << '\n';
-      result = 1;
-    }
-  }
-  return result;
+  return 0;
 }
