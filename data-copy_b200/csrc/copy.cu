@@ -55,6 +55,22 @@ constexpr int kCtasPerSm = 8;
 #ifndef DCOPY_STRIDED_U
 #define DCOPY_STRIDED_U 4  // elements in flight per thread (strided copy)
 #endif
+#ifndef DCOPY_SPREAD_PROBE
+// 1: before the dependent-launch wait, each CTA of a strided copy also
+// prefetches one source and one destination line at a row spread over the
+// whole copy (a Weyl sequence over the rows), so that the CTAs resident early
+// touch every page of both spans while the previous kernel drains.
+#define DCOPY_SPREAD_PROBE 0
+#endif
+#ifndef DCOPY_L2_SPAN256
+#define DCOPY_L2_SPAN256 0  // 1: 16-byte loads of bursts of whole 256-byte spans fetch 256 bytes
+#endif
+#ifndef DCOPY_STRIDED_CPC
+// Chunks of kThreads x U elements per CTA of a strided copy.  Above 1 the grid
+// covers a fraction of the CTA slots, so the next launch on the stream can be
+// resident (and L2-prefetch its whole range, see below) while this one drains.
+#define DCOPY_STRIDED_CPC 1
+#endif
 
 template <typename T>
 struct Unroll {
@@ -151,10 +167,16 @@ __global__ void __launch_bounds__(kThreads, Unroll<T>::strided_min_ctas)
   pdl_trigger_at_entry();
   const uint32_t begin = blockIdx.x * per_cta;
   const uint32_t end = begin + per_cta < total ? begin + per_cta : total;
-  if (DCOPY_PREFETCH && prefetch) {  // first U elements, one prefetch per 128-byte line
+  if (DCOPY_SPREAD_PROBE && prefetch && threadIdx.x == 0) {
+    const uint32_t rows = total / epr.d;
+    const uint32_t r = __umulhi(blockIdx.x * 0x9E3779B9u, rows);  // frac(b * golden ratio) * rows
+    prefetch_l2(src + (uint64_t)r * src_pitch);
+    prefetch_l2(dst + (uint64_t)r * dst_pitch);
+  }
+  if (DCOPY_PREFETCH && prefetch) {  // the CTA's range, one prefetch per 128-byte line
     constexpr uint32_t per_line = 128 / sizeof(T) > 0 ? 128 / sizeof(T) : 1;
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
+    for (int u = 0; u < U * DCOPY_STRIDED_CPC; ++u) {
       const uint32_t i = begin + threadIdx.x + u * kThreads;
       if (i < end && (threadIdx.x % per_line == 0 || i == begin)) {
         const uint32_t r = epr.div(i);
@@ -174,6 +196,8 @@ __global__ void __launch_bounds__(kThreads, Unroll<T>::strided_min_ctas)
         const T *p = reinterpret_cast<const T *>(src + (uint64_t)r * src_pitch) + (i - r * epr.d);
         if constexpr (kHalfLine)
           v[u] = ld_stream_half_line(p);
+        else if constexpr (DCOPY_L2_SPAN256 && sizeof(T) == 16)
+          v[u] = ld_stream_span256(p);
         else
           v[u] = ld_stream(p);
       }
@@ -261,7 +285,7 @@ int launch_strided(uint8_t *dst, const uint8_t *src, uint64_t rows, uint64_t row
     const uint64_t nr = std::min(max_rows, rows - r0);
     const uint32_t total = (uint32_t)(nr * epr);
     auto kernel = half_line ? strided_copy_kernel<T, U, true> : strided_copy_kernel<T, U, false>;
-    const Split sp = split_work(kernel, total, U);
+    const Split sp = split_work(kernel, total, U * DCOPY_STRIDED_CPC);
     int rc = launch(kernel, sp.grid, dim3(kThreads), 0, s, "strided_copy_kernel",
                     dst + r0 * dst_pitch, src + r0 * src_pitch, total, (uint32_t)sp.per_cta, div,
                     src_pitch, dst_pitch, prefetch_src);
@@ -312,6 +336,16 @@ int copy2d(void *dst, const void *src, uint64_t rows, uint64_t row_bytes, uint64
       if (rc) return rc;
     }
     return DCOPY_OK;
+  }
+  // Bursts of whole 16-byte granules from DCOPY_BULK_MIN_BURST bytes in this
+  // GPU's memory: bulk copies through shared memory (bulk.cu).
+  {
+    bool taken = false;
+    const int brc = bulk_bursts(dst, src, rows, row_bytes, src_pitch, dst_pitch, s, &taken);
+    if (taken || brc) return brc;
+    // Short gapped bursts (16 to 112 bytes): 2-D tensor copies (nd_tma.cu).
+    const int trc = tma_short_bursts(dst, src, rows, row_bytes, src_pitch, dst_pitch, s, &taken);
+    if (taken || trc) return trc;
   }
   // Bursts only 1- or 2-byte units tile, and long bursts of 4-byte units:
   // aligned 16-byte destination vectors assembled by funnel shifts (rows.cu;
@@ -480,6 +514,29 @@ extern "C" int dcopy_copy_nd(void *dst, const void *src, int ndim, const uint64_
     }
   }
   if (!total) return DCOPY_OK;
+  // The kernels write every element of the box concurrently, so no two box
+  // elements may share a destination.  Sorted by stride, each destination axis
+  // must step past everything the axes below it cover (a layout that does not
+  // interleave: dense, padded or permuted boxes).  Rarer injective interleavings
+  // are refused as well.
+  {
+    int order[kMaxNd], m = 0;
+    for (int k = 0; k < ndim; ++k)
+      if (sizes[k] > 1) order[m++] = k;
+    for (int j = 1; j < m; ++j)  // insertion sort by destination stride (m <= 5)
+      for (int i = j; i > 0 && dst_strides[order[i]] < dst_strides[order[i - 1]]; --i)
+        std::swap(order[i], order[i - 1]);
+    unsigned __int128 covered = 1;  // elements from the first to the last offset so far
+    for (int j = 0; j < m; ++j) {
+      const int k = order[j];
+      if ((unsigned __int128)(uint64_t)dst_strides[k] < covered)
+        return set_error(DCOPY_ERR_PARAM_INVALID,
+                         "copy_nd: dst stride %lld of dim %d is inside the %llu elements the "
+                         "smaller-stride dims cover: destinations would repeat",
+                         (long long)dst_strides[k], k, (unsigned long long)covered);
+      covered += (unsigned __int128)(sizes[k] - 1) * (uint64_t)dst_strides[k];
+    }
+  }
   if ((src_last + 1) * elem_bytes >= ((unsigned __int128)1 << 62) ||
       (dst_last + 1) * elem_bytes >= ((unsigned __int128)1 << 62))
     return set_error(DCOPY_ERR_PARAM_INVALID, "copy_nd: the box spans 2^62 bytes or more");

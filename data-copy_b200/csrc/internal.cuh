@@ -1,6 +1,7 @@
 // Host-side helpers shared between translation units of libdcopy.
 #pragma once
 
+#include <cuda_runtime.h>
 #include <stdint.h>
 
 #include "dcopy/dcopy.h"
@@ -88,6 +89,23 @@ int rows_copy(void *dst, const void *src, int m, const uint64_t *size, const int
 int nd_copy_tma(void *dst, const void *src, int ndim, const uint64_t *sizes,
                 const int64_t *src_strides, const int64_t *dst_strides, uint32_t eb,
                 dcopy_stream_t stream, bool *taken);
+
+// With the TMA paths selected: a 2-D strided copy through shared memory with
+// the bulk-copy engine (bulk.cu) when its bursts are 16-byte granules of at
+// least DCOPY_BULK_MIN_BURST bytes in this GPU's memory (*taken = true);
+// otherwise nothing is launched.
+int bulk_bursts(void *dst, const void *src, uint64_t rows, uint64_t row_bytes,
+                uint64_t src_pitch, uint64_t dst_pitch, cudaStream_t s, bool *taken);
+// Whether the TMA paths are selected (dcopy_set_nd_tma / DCOPY_ND_TMA): the
+// tensor-copy box kernel and the bulk-copy and tensor-copy 2-D burst kernels.
+bool tma_paths_selected();
+// With the TMA paths selected: gapped 2-D bursts of whole 16-byte granules
+// shorter than 128 bytes as 2-D tensor copies (nd_tma.cu; *taken = true), else
+// nothing is launched.
+int tma_short_bursts(void *dst, const void *src, uint64_t rows, uint64_t row_bytes,
+                     uint64_t src_pitch, uint64_t dst_pitch, cudaStream_t s, bool *taken);
+// ORs the bulk-copy kernel's give-up flag into *flag and clears it.
+int bulk_error_take(uint32_t *flag);
 
 // The reference's pretranspose workflow (asc:144-146): x -> B with RunTiles<1>,
 // then B -> y with RunTiles<2>, through a B buffer of scratch_bytes bytes that

@@ -81,9 +81,32 @@ extern "C" int dcopy_memcpy_async(const DcopyMemcpyInfo *info, int32_t kind,
 
 // Tasks whose two buffers a kernel can address (device memory, or pinned host
 // memory read and written over PCIe) and that are small enough for the launch
-// cost to matter go to one dcopy_copy_ext_batch: one launch per 256 tasks
-// instead of one copy call each.  Larger host-side transfers and pageable
-// host memory take the copy engine, one cudaMemcpyAsync each.
+// cost to matter run as dcopy_copy_ext_batch launches: one launch for a run of
+// such tasks instead of one copy call each.  Larger host-side transfers and
+// pageable host memory take the copy engine, one cudaMemcpyAsync each.
+//
+// Task order is kept: the tasks of one launch run concurrently, so a run ends
+// (its launch is issued) before a copy-engine task and before a task whose
+// buffers overlap a buffer of a task already in the run.
+namespace {
+
+struct Span {
+  uintptr_t lo, hi;  // [lo, hi)
+  bool overlaps(const Span &o) const { return lo < o.hi && o.lo < hi; }
+};
+
+// Whether task m reads or writes memory that a task of the pending run writes,
+// or writes memory that one of them reads.
+bool conflicts(const std::vector<std::pair<Span, Span>> &run, const DcopyMemcpyInfo &m) {
+  const Span d{(uintptr_t)m.dst, (uintptr_t)m.dst + m.cnt};
+  const Span s{(uintptr_t)m.src, (uintptr_t)m.src + m.cnt};
+  for (const auto &t : run)  // t.first: destination, t.second: source
+    if (d.overlaps(t.first) || d.overlaps(t.second) || s.overlaps(t.first)) return true;
+  return false;
+}
+
+}  // namespace
+
 extern "C" int dcopy_memcpy_async_batch(const DcopyMemcpyInfo *infos, uint32_t count,
                                         int32_t kind, dcopy_stream_t stream) {
   DCOPY_API_BEGIN
@@ -94,29 +117,57 @@ extern "C" int dcopy_memcpy_async_batch(const DcopyMemcpyInfo *infos, uint32_t c
                      "memcpy_batch: RT_MEMCPY_ADDR_DEVICE_TO_DEVICE has no CUDA counterpart");
   if (kind < 0 || kind > 8)
     return set_error(DCOPY_ERR_PARAM_INVALID, "memcpy_batch: unknown kind %d", kind);
-  for (uint32_t i = 0; i < count; ++i) {  // every task is checked before anything runs
+  const bool host_side = kind != DCOPY_MEMCPY_DEVICE_TO_DEVICE;
+  // Every task is checked before anything runs; `kernel` marks the tasks that
+  // run on the batched copy kernel.
+  std::vector<char> kernel(count, 0);
+  for (uint32_t i = 0; i < count; ++i) {
     const DcopyMemcpyInfo &m = infos[i];
     if (m.cnt > m.destMax)
       return set_error(DCOPY_ERR_PARAM_INVALID,
                        "memcpy_batch: task %u: count %llu exceeds destMax %llu", i,
                        (unsigned long long)m.cnt, (unsigned long long)m.destMax);
-    if (m.cnt && (!m.dst || !m.src))
+    if (!m.cnt) continue;
+    if (!m.dst || !m.src)
       return set_error(DCOPY_ERR_PARAM_INVALID, "memcpy_batch: task %u: NULL pointer", i);
+    kernel[i] = kind != DCOPY_MEMCPY_HOST_TO_HOST && !(host_side && m.cnt >= kEngineBytes) &&
+                gpu_addressable(m.dst) && gpu_addressable(m.src);
+    if (kernel[i]) {
+      int rc = check_device_span(m.src, m.cnt, "memcpy_batch src");
+      if (!rc) rc = check_device_span(m.dst, m.cnt, "memcpy_batch dst");
+      if (!rc) rc = check_disjoint(m.src, m.cnt, m.dst, m.cnt, "memcpy_batch");
+      if (rc) return rc;
+    }
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const bool host_side = kind != DCOPY_MEMCPY_DEVICE_TO_DEVICE;
   std::vector<DcopyExtCopy> batch;
-  std::vector<const DcopyMemcpyInfo *> engine;
+  std::vector<std::pair<Span, Span>> run;
+  auto flush = [&]() -> int {
+    if (batch.empty()) return DCOPY_OK;
+    const int rc = dcopy_copy_ext_batch(batch.data(), (uint32_t)batch.size(), stream);
+    batch.clear();
+    run.clear();
+    return rc;
+  };
   for (uint32_t i = 0; i < count; ++i) {
     const DcopyMemcpyInfo &m = infos[i];
     if (!m.cnt) continue;
-    const bool kernel = kind != DCOPY_MEMCPY_HOST_TO_HOST &&
-                        !(host_side && m.cnt >= kEngineBytes) && gpu_addressable(m.dst) &&
-                        gpu_addressable(m.src);
-    if (!kernel) {
-      engine.push_back(&m);
+    if (!kernel[i] || conflicts(run, m)) {
+      const int rc = flush();
+      if (rc) return rc;
+    }
+    if (!kernel[i]) {
+      cudaMemcpyKind k = cudaMemcpyDefault;
+      if (kind == DCOPY_MEMCPY_HOST_TO_HOST) k = cudaMemcpyHostToHost;
+      if (kind == DCOPY_MEMCPY_HOST_TO_DEVICE || kind == DCOPY_MEMCPY_HOST_TO_DEVICE_EX)
+        k = cudaMemcpyHostToDevice;
+      if (kind == DCOPY_MEMCPY_DEVICE_TO_HOST || kind == DCOPY_MEMCPY_DEVICE_TO_HOST_EX)
+        k = cudaMemcpyDeviceToHost;
+      DCOPY_CUDA_TRY(cudaMemcpyAsync(m.dst, m.src, m.cnt, k, s));
       continue;
     }
+    run.push_back({Span{(uintptr_t)m.dst, (uintptr_t)m.dst + m.cnt},
+                   Span{(uintptr_t)m.src, (uintptr_t)m.src + m.cnt}});
     // Contiguous pieces of at most 1 GiB (blockLen is 32-bit).
     for (uint64_t off = 0; off < m.cnt; off += kPieceBytes) {
       const uint64_t n = std::min<uint64_t>(kPieceBytes, m.cnt - off);
@@ -125,19 +176,6 @@ extern "C" int dcopy_memcpy_async_batch(const DcopyMemcpyInfo *infos, uint32_t c
                                    DcopyExtParams{1u, (uint32_t)n, 0, 0}});
     }
   }
-  if (!batch.empty()) {
-    const int rc = dcopy_copy_ext_batch(batch.data(), (uint32_t)batch.size(), stream);
-    if (rc) return rc;
-  }
-  for (const DcopyMemcpyInfo *m : engine) {
-    cudaMemcpyKind k = cudaMemcpyDefault;
-    if (kind == DCOPY_MEMCPY_HOST_TO_HOST) k = cudaMemcpyHostToHost;
-    if (kind == DCOPY_MEMCPY_HOST_TO_DEVICE || kind == DCOPY_MEMCPY_HOST_TO_DEVICE_EX)
-      k = cudaMemcpyHostToDevice;
-    if (kind == DCOPY_MEMCPY_DEVICE_TO_HOST || kind == DCOPY_MEMCPY_DEVICE_TO_HOST_EX)
-      k = cudaMemcpyDeviceToHost;
-    DCOPY_CUDA_TRY(cudaMemcpyAsync(m->dst, m->src, m->cnt, k, s));
-  }
-  return DCOPY_OK;
+  return flush();
   DCOPY_API_END
 }

@@ -44,6 +44,18 @@ namespace {
 #ifndef DCOPY_TMA_UNIT
 #define DCOPY_TMA_UNIT 8  // TMA element: 0 the library element, 8 always 8-byte units
 #endif
+#ifndef DCOPY_TMA_SHORT_BURSTS
+// 1: with the TMA paths selected, gapped 2-D bursts of 16 to 112 bytes (whole
+// 16-byte granules) move as 2-D tensor copies.  Measured on B200 (256 MiB moved,
+// against the load/store kernel): 32 B bursts with 4x / 16x gaps +5 % / +4 %,
+// 32 B with 1x gaps and every 64 B point -4 to -6 %; so it is not the default.
+#define DCOPY_TMA_SHORT_BURSTS 1
+#endif
+#ifndef DCOPY_TMA_SHORT_PROMOTION
+// L2 promotion of those loads: 64 (half lines).  No promotion measured 25-30 %
+// slower on 32 B bursts with 4x / 16x gaps.
+#define DCOPY_TMA_SHORT_PROMOTION 64
+#endif
 constexpr int kStages = DCOPY_TMA_STAGES;
 constexpr uint32_t kStageBytes = DCOPY_TMA_STAGE_KIB * 1024;
 constexpr uint32_t kWaitIters = 1u << 22;  // try_wait suspends ~us per call: seconds in total
@@ -274,11 +286,14 @@ bool tma_selected() {
 
 }  // namespace
 
-int nd_copy_tma(void *dst, const void *src, int ndim, const uint64_t *sizes,
-                const int64_t *src_strides, const int64_t *dst_strides, uint32_t eb,
-                dcopy_stream_t stream, bool *taken) {
+namespace {
+
+// The tensor-copy path for one box whose views allow it (*taken = true), with
+// the L2 promotion of short rows given by short_promotion.
+int tma_box_copy(void *dst, const void *src, int ndim, const uint64_t *sizes,
+                 const int64_t *src_strides, const int64_t *dst_strides, uint32_t eb,
+                 dcopy_stream_t stream, CUtensorMapL2promotion short_promotion, bool *taken) {
   *taken = false;
-  if (!tma_selected()) return DCOPY_OK;
   // Conditions of a tiled tensor copy on both views (checked, else the caller
   // takes its load/store kernels): 16-byte aligned bases, unit innermost stride,
   // 16-byte multiple strides, rows of whole 16-byte granules, local memory.
@@ -348,9 +363,8 @@ int nd_copy_tma(void *dst, const void *src, int ndim, const uint64_t *sizes,
   // L2 sector promotion: rows shorter than a 128-byte line fill 64-byte half
   // lines (measured on B200: 64 B rows with 64 B gaps 3970 -> 5140 GB/s); longer
   // rows fill 256-byte spans.
-  const CUtensorMapL2promotion kPromotion = sizes[ndim - 1] * eb < 128
-                                                ? CU_TENSOR_MAP_L2_PROMOTION_L2_64B
-                                                : CU_TENSOR_MAP_L2_PROMOTION_L2_256B;
+  const CUtensorMapL2promotion kPromotion =
+      sizes[ndim - 1] * eb < 128 ? short_promotion : CU_TENSOR_MAP_L2_PROMOTION_L2_256B;
   CUtensorMap sm, dm;
   if (encode(&sm, dtype, (cuuint32_t)R, const_cast<void *>(src), gdim, sstride, box, estride,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -368,6 +382,34 @@ int nd_copy_tma(void *dst, const void *src, int ndim, const uint64_t *sizes,
     case 4: return launch_rank<4>(sm, dm, g, s);
     default: return launch_rank<5>(sm, dm, g, s);
   }
+}
+
+}  // namespace
+
+bool tma_paths_selected() { return tma_selected(); }
+
+int nd_copy_tma(void *dst, const void *src, int ndim, const uint64_t *sizes,
+                const int64_t *src_strides, const int64_t *dst_strides, uint32_t eb,
+                dcopy_stream_t stream, bool *taken) {
+  *taken = false;
+  if (!tma_selected()) return DCOPY_OK;
+  return tma_box_copy(dst, src, ndim, sizes, src_strides, dst_strides, eb, stream,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_64B, taken);
+}
+
+int tma_short_bursts(void *dst, const void *src, uint64_t rows, uint64_t row_bytes,
+                     uint64_t src_pitch, uint64_t dst_pitch, cudaStream_t s, bool *taken) {
+  *taken = false;
+  if (!DCOPY_TMA_SHORT_BURSTS || !tma_selected() || row_bytes >= 128 || row_bytes % 16 ||
+      src_pitch == row_bytes)
+    return DCOPY_OK;
+  if (rows < 2 || rows > 0x7FFFFFFFull) return DCOPY_OK;
+  const uint64_t sizes[2] = {rows, row_bytes};
+  const int64_t ss[2] = {(int64_t)src_pitch, 1}, ds[2] = {(int64_t)dst_pitch, 1};
+  return tma_box_copy(dst, src, 2, sizes, ss, ds, 1, reinterpret_cast<dcopy_stream_t>(s),
+                      DCOPY_TMA_SHORT_PROMOTION == 0 ? CU_TENSOR_MAP_L2_PROMOTION_NONE
+                                                     : CU_TENSOR_MAP_L2_PROMOTION_L2_64B,
+                      taken);
 }
 
 }  // namespace dcopy
@@ -389,6 +431,6 @@ extern "C" int dcopy_tma_error(uint32_t *flag) {
   uint32_t zero = 0;
   DCOPY_CUDA_TRY(cudaMemcpyFromSymbol(flag, g_tma_error, sizeof(uint32_t)));
   DCOPY_CUDA_TRY(cudaMemcpyToSymbol(g_tma_error, &zero, sizeof(uint32_t)));
-  return DCOPY_OK;
+  return bulk_error_take(flag);
   DCOPY_API_END
 }

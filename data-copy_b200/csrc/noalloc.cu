@@ -41,25 +41,67 @@ namespace {
 
 constexpr int kMaxDevices = 128;
 std::mutex g_mutex;
-void *g_b_address[kMaxDevices] = {nullptr};
 
-// Device address of g_pretranspose_b on the current device, looked up once per
-// device (with that device current) and cached.
+// The array's address on one device, and the CUDA context it belongs to.  A
+// device reset (or a primary context released and created again) reloads the
+// module, which may place the array elsewhere: the address is then looked up
+// again in the new context.
+struct Slot {
+  void *address = nullptr;
+  unsigned long long context_id = 0;  // 0: not known
+};
+Slot g_slots[kMaxDevices];
+
+typedef int (*PfnCtxGetCurrent)(void **);
+typedef int (*PfnCtxGetId)(void *, unsigned long long *);
+
+// The unique id of the calling thread's current context (driver API, looked up
+// through the runtime, so the library needs no link against libcuda); false
+// when there is none or the driver lacks the call.
+bool current_context_id(unsigned long long *id) {
+  static PfnCtxGetCurrent get_current = nullptr;
+  static PfnCtxGetId get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<PfnCtxGetCurrent>(p);
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<PfnCtxGetId>(p);
+  });
+  void *ctx = nullptr;
+  if (!get_current || !get_id || get_current(&ctx) != 0 || !ctx) return false;
+  return get_id(ctx, id) == 0 && *id != 0;
+}
+
+// Device address of g_pretranspose_b on the current device.  Set-up, once per
+// device (and again after the device's context was replaced), with that device
+// current: cudaGetSymbolAddress, whose return code is checked.
 int b_address(void **out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if (dev < 0 || dev >= kMaxDevices)
     return set_error(DCOPY_ERR_UNSUPPORTED, "device ordinal %d beyond %d", dev, kMaxDevices);
+  unsigned long long ctx = 0;
+  bool known = current_context_id(&ctx);
   std::lock_guard<std::mutex> lock(g_mutex);
-  if (!g_b_address[dev]) {
+  Slot &slot = g_slots[dev];
+  if (!slot.address || !known || slot.context_id != ctx) {
     void *p = nullptr;
     e = cudaGetSymbolAddress(&p, g_pretranspose_b);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_pretranspose_b)");
     if (!p) return set_error(DCOPY_ERR_CUDA, "cudaGetSymbolAddress returned NULL");
-    g_b_address[dev] = p;
+    if (!known) known = current_context_id(&ctx);  // the look-up made the context current
+    slot.address = p;
+    slot.context_id = known ? ctx : 0;  // unknown: looked up again on the next call
   }
-  *out = g_b_address[dev];
+  *out = slot.address;
   return DCOPY_OK;
 }
 

@@ -31,6 +31,8 @@ __all__ = [
     "DataCopyTiling", "DcopyExtParams", "DcopyError", "DcopyUnavailable", "lib", "lib_path",
     "plan_tiling", "datacopy_small", "datacopy_large", "datacopy_pretranspose",
     "datacopy_contiguous", "datacopy_pretranspose_noalloc", "copy_ext", "copy_ext_32b", "copy_nd", "nz_shape", "nd_to_nz",
+    "DcopyPadParams", "PAD_NORMAL", "PAD_COMPACT", "copy_pad_gm_to_ub", "copy_pad_ub_to_gm",
+    "datacopy_pad_extend",
     "nz_to_nd", "zz_shape", "nd_to_zz", "zz_to_nd", "TRANSFER_FRACTAL_ZZ", "TRANSFER_FRACTAL_ZZ_ND", "status_to_ge", "DcopyTransArgs", "data_type_size", "trans_data_format",
     "trans_format", "trans_format_check", "trans_shape", "trans_tensor_shape", "transpose",
     "transpose_with_shape_check", "FORMAT", "DATA_TYPE", "TRANSFER_FRACTAL_NZ",
@@ -87,6 +89,17 @@ class DcopyExtParams(ctypes.Structure):
     """blockCount bursts of blockLen bytes; srcStride/dstStride are gaps in bytes."""
     _fields_ = [("blockCount", ctypes.c_uint32), ("blockLen", ctypes.c_uint32),
                 ("srcStride", ctypes.c_uint64), ("dstStride", ctypes.c_uint64)]
+
+
+class DcopyPadParams(ctypes.Structure):
+    """AscendC::DataCopyPadExtParams<T> with T given by its size (include/dcopy/dcopy.h)."""
+    _fields_ = [("isPad", ctypes.c_uint8), ("leftPadding", ctypes.c_uint8),
+                ("rightPadding", ctypes.c_uint8), ("reserved", ctypes.c_uint8),
+                ("elemBytes", ctypes.c_uint32), ("paddingValue", ctypes.c_uint64)]
+
+
+PAD_NORMAL = 0   # AscendC::PaddingMode::Normal
+PAD_COMPACT = 1  # AscendC::PaddingMode::Compact
 
 
 class DcopyTransArgs(ctypes.Structure):
@@ -157,6 +170,15 @@ _SIGNATURES = {
                                                            _vp]),
     "dcopy_copy_ext": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(DcopyExtParams), _vp]),
     "dcopy_copy_ext_32b": (ctypes.c_int, [_vp, _vp] + [ctypes.c_uint32] * 4 + [_vp]),
+    "dcopy_copy_pad_gm_to_ub": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(DcopyExtParams),
+                                               ctypes.POINTER(DcopyPadParams), ctypes.c_int32,
+                                               _vp]),
+    "dcopy_copy_pad_ub_to_gm": (ctypes.c_int, [_vp, _vp, ctypes.POINTER(DcopyExtParams),
+                                               ctypes.c_int32, _vp]),
+    "dcopy_datacopy_pad_extend_load": (ctypes.c_int, [_vp, _vp] + [ctypes.c_uint32] * 5 +
+                                       [ctypes.c_int32, _vp]),
+    "dcopy_datacopy_pad_extend_store": (ctypes.c_int, [_vp, _vp] + [ctypes.c_uint32] * 5 +
+                                        [ctypes.c_int32, _vp]),
     "dcopy_copy_nd": (ctypes.c_int, [_vp, _vp, ctypes.c_int, _u64p, _i64p, _i64p,
                                      ctypes.c_uint32, _vp]),
     "dcopy_nz_shape": (ctypes.c_int, [_i64p, ctypes.c_int, ctypes.c_int64, _i64p,
@@ -394,6 +416,36 @@ def copy_ext_32b(dst, src, block_count: int, block_len32: int, src_stride32: int
     _check(lib().dcopy_copy_ext_32b(_ptr(dst), _ptr(src), block_count, block_len32,
                                     src_stride32, dst_stride32, _stream(stream)),
            "dcopy_copy_ext_32b")
+
+
+def copy_pad_gm_to_ub(ub, gm, block_count: int, block_len: int, src_gap: int, dst_blocks: int,
+                      mode: int = PAD_NORMAL, pad=(True, 0, 0, 0), elem_bytes: int = 1,
+                      stream=None) -> None:
+    """DataCopyPad GM -> UB: blockLen and the GM gap in bytes, the UB gap in 32-byte
+    blocks; pad = DataCopyPadExtParams (isPad, leftPadding, rightPadding, paddingValue)
+    with paddingValue given as the element's bits."""
+    p = DcopyExtParams(block_count, block_len, src_gap, dst_blocks)
+    pp = DcopyPadParams(int(bool(pad[0])), pad[1], pad[2], 0, elem_bytes, pad[3])
+    _check(lib().dcopy_copy_pad_gm_to_ub(_ptr(ub), _ptr(gm), ctypes.byref(p), ctypes.byref(pp),
+                                         mode, _stream(stream)), "dcopy_copy_pad_gm_to_ub")
+
+
+def copy_pad_ub_to_gm(gm, ub, block_count: int, block_len: int, src_blocks: int, dst_gap: int,
+                      mode: int = PAD_NORMAL, stream=None) -> None:
+    """DataCopyPad UB -> GM: the UB gap in 32-byte blocks, the GM gap in bytes."""
+    p = DcopyExtParams(block_count, block_len, src_blocks, dst_gap)
+    _check(lib().dcopy_copy_pad_ub_to_gm(_ptr(gm), _ptr(ub), ctypes.byref(p), mode,
+                                         _stream(stream)), "dcopy_copy_pad_ub_to_gm")
+
+
+def datacopy_pad_extend(dst, src, elem_bytes: int, block_count: int, block_len: int,
+                        src_stride: int, dst_stride: int, to_ub: bool, mode: int = PAD_NORMAL,
+                        stream=None) -> None:
+    """DataCopyPadExtend (ascendc/api/datacopy.h:14-40) in elements of T: to_ub=True is
+    the GM -> UB overload (dst is the UB image), False the UB -> GM one."""
+    fn = lib().dcopy_datacopy_pad_extend_load if to_ub else lib().dcopy_datacopy_pad_extend_store
+    _check(fn(_ptr(dst), _ptr(src), elem_bytes, block_count, block_len, src_stride, dst_stride,
+              mode, _stream(stream)), "dcopy_datacopy_pad_extend")
 
 
 def copy_nd(dst, src, sizes: Sequence[int], src_strides: Sequence[int],

@@ -110,8 +110,9 @@ int dcopy_datacopy_tiles(int32_t phase, const void *in, void *out, const DataCop
  *     held by every GPU that loads this part of the library until exit.
  *     rows*cols*4 above 16 MiB is refused with DCOPY_ERR_PARAM_INVALID.
  *   - The first call on a device looks up the array's device address (with that
- *     device current) and caches it; make that first call before any stream
- *     capture on the device.
+ *     device current) and caches it for the device's current context; a call
+ *     after the context was replaced (cudaDeviceReset) looks it up again.  Make
+ *     the first call on a device before any stream capture on it.
  *   - Every call on a device shares the one array: calls whose work overlaps on
  *     the GPU (other streams, other threads) race on it.  B needs no clearing:
  *     each call overwrites all of the part it reads.
@@ -199,6 +200,64 @@ int dcopy_copy_ext_batch(const DcopyExtCopy *copies, uint32_t count, dcopy_strea
  * units; BASELINE expresses configs 1, 2, 3 and 5 this way). */
 int dcopy_copy_ext_32b(void *dst, const void *src, uint32_t blockCount, uint32_t blockLen32,
                        uint32_t srcStride32, uint32_t dstStride32, dcopy_stream_t stream);
+
+/* ---- DataCopyPad with the Unified-Buffer side conventions ------------------ */
+
+/* AscendC::DataCopyPadExtParams<T> {isPad, leftPadding, rightPadding,
+ * paddingValue} (the GM->UB padding of DataCopyPad, ascendc/api/datacopy.h:24),
+ * with T given by its size: paddingValue holds T's bits in its low elemBytes
+ * bytes; leftPadding / rightPadding count elements (at most 32 bytes each). */
+typedef struct DcopyPadParams {
+  uint8_t isPad;
+  uint8_t leftPadding;
+  uint8_t rightPadding;
+  uint8_t reserved;
+  uint32_t elemBytes;    /* sizeof(T): 1, 2, 4 or 8 */
+  uint64_t paddingValue;
+} DcopyPadParams;
+
+/* AscendC::PaddingMode (v35/ascendc/api_regbase/datacopy.h:13). */
+#define DCOPY_PAD_NORMAL 0  /* every UB block starts on a 32-byte boundary */
+#define DCOPY_PAD_COMPACT 1 /* UB blocks packed; the transfer's end rounded up to 32 bytes */
+
+/* DataCopyPad GM -> UB as DataCopyPadExtend drives it (ascendc/api/datacopy.h:
+ * 14-25; v35/ascendc/api_regbase/datacopy.h:14-25).  `ub` is a device buffer
+ * laid out as the Unified Buffer would hold the tile.  params->blockLen is in
+ * bytes, params->srcStride a GM gap in bytes, params->dstStride a UB gap in
+ * 32-BYTE BLOCKS.  Block i (blockLen bytes from gm + i*(blockLen + srcStride))
+ * fills UB slot i at ub + i*(slot + 32*dstStride), after leftPadding elements;
+ * slot = left*eb + blockLen + right*eb, rounded up to 32 bytes in Normal mode.
+ * With pad->isPad, every padding byte of a slot (and, in Compact mode, the bytes
+ * that round the transfer's end up to 32) holds paddingValue element by element;
+ * without it they are left untouched (their contents are unspecified on Ascend).
+ * blockLen must be a whole number of elements.  The padding bytes' exact
+ * hardware contents are unpinned (the reference holds no vectors for them). */
+int dcopy_copy_pad_gm_to_ub(void *ub, const void *gm, const DcopyExtParams *params,
+                            const DcopyPadParams *pad, int32_t mode, dcopy_stream_t stream);
+
+/* DataCopyPad UB -> GM (ascendc/api/datacopy.h:28-40): params->srcStride is a
+ * UB gap in 32-BYTE BLOCKS, params->dstStride a GM gap in bytes.  Block i of
+ * blockLen bytes goes from UB slot i at ub + i*(slot + 32*srcStride), slot =
+ * blockLen rounded up to 32 in Normal mode (blockLen in Compact mode), to
+ * gm + i*(blockLen + dstStride). */
+int dcopy_copy_pad_ub_to_gm(void *gm, const void *ub, const DcopyExtParams *params, int32_t mode,
+                            dcopy_stream_t stream);
+
+/* DataCopyPadExtend itself, arguments in elements of T exactly as GE's codegen
+ * emits them (e.g. `DataCopyPadExtend(local_1[0 + 0], local_0, 1, 1, 16 - 1, 0)`,
+ * tests/autofuse/ut/codegen/api_call/test_codegen_store_api_call.cpp:131):
+ *   load  (GM -> UB, datacopy.h:14-25): blockLen = block_len*eb, srcStride =
+ *         src_stride*eb bytes, dstStride = dst_stride / (32/eb) blocks (rounded
+ *         down), padding {true, 0, 0, 0};
+ *   store (UB -> GM, datacopy.h:28-40): blockLen = block_len*eb, srcStride =
+ *         src_stride / (32/eb) blocks, dstStride = dst_stride*eb bytes.
+ * block_len*eb must fit 32 bits (the reference truncates; here PARAM_INVALID). */
+int dcopy_datacopy_pad_extend_load(void *ub, const void *gm, uint32_t elem_bytes,
+                                   uint32_t block_count, uint32_t block_len, uint32_t src_stride,
+                                   uint32_t dst_stride, int32_t mode, dcopy_stream_t stream);
+int dcopy_datacopy_pad_extend_store(void *gm, const void *ub, uint32_t elem_bytes,
+                                    uint32_t block_count, uint32_t block_len, uint32_t src_stride,
+                                    uint32_t dst_stride, int32_t mode, dcopy_stream_t stream);
 
 /* DataCopyNddma<T, dim> (v35/ascendc/api_regbase/datacopy_nddma.h:15-29): an
  * N-D box copy, 1 <= ndim <= 5.  sizes, src_strides and dst_strides are
@@ -433,9 +492,13 @@ int dcopy_memcpy_async(const DcopyMemcpyInfo *info, int32_t kind, dcopy_stream_t
  * host memory, below 8 MiB when a host side is involved, run together on the
  * batched copy kernel (one launch per 256 tasks; host buffers are read and
  * written over PCIe); pageable host memory, larger host-side transfers and
- * HOST_TO_HOST take cudaMemcpyAsync, one per task, after the batch.  Tasks run
- * concurrently: a destination may not overlap another task's buffers.
- * No counterpart in the reference (its tasks are issued one by one). */
+ * HOST_TO_HOST take cudaMemcpyAsync, one per task.  The result is that of the
+ * tasks issued one by one in order: the tasks of one kernel launch run
+ * concurrently, so a launch is issued before each copy-engine task and before
+ * any task that reads or writes what a task already in the launch writes (or
+ * writes what one reads).  A task whose own source and destination overlap is
+ * PARAM_INVALID.  No counterpart in the reference (its tasks are issued one by
+ * one). */
 int dcopy_memcpy_async_batch(const DcopyMemcpyInfo *infos, uint32_t count, int32_t kind,
                              dcopy_stream_t stream);
 

@@ -113,6 +113,63 @@ void oracle_copy_ext_loop(void *dst, const void *src, uint64_t block_count, uint
                       block_count, block_len, src_gap, dst_gap);
 }
 
+/* ------------------------------------------------------------------------ */
+/* DataCopyPad with the UB-side conventions (ascendc/api/datacopy.h:14-40;    */
+/* v35/ascendc/api_regbase/datacopy.h:14-72)                                  */
+/* ------------------------------------------------------------------------ */
+
+static uint64_t round_up32(uint64_t x) { return (x + 31) / 32 * 32; }
+
+/* Bytes block i's UB slot occupies before the stride gap. */
+static uint64_t pad_slot(uint64_t block_len, int mode, uint32_t left, uint32_t right,
+                         uint32_t eb) {
+  const uint64_t used = (uint64_t)left * eb + block_len + (uint64_t)right * eb;
+  return mode == 0 ? round_up32(used) : used;
+}
+
+uint64_t oracle_pad_ub_span(uint64_t block_count, uint64_t block_len, uint64_t ub_blocks, int mode,
+                            uint32_t left, uint32_t right, uint32_t eb) {
+  if (!block_count) return 0;
+  const uint64_t slot = pad_slot(block_len, mode, left, right, eb);
+  const uint64_t end = (block_count - 1) * (slot + ub_blocks * 32) + slot;
+  return mode == 0 ? end : round_up32(end);
+}
+
+int oracle_copy_pad_gm_to_ub(void *ub, const void *gm, uint64_t block_count, uint64_t block_len,
+                             uint64_t src_gap, uint64_t dst_blocks, int mode, int is_pad,
+                             uint32_t left, uint32_t right, uint64_t value, uint32_t eb) {
+  if ((eb != 1 && eb != 2 && eb != 4 && eb != 8) || block_len % eb || (uint64_t)left * eb > 32 ||
+      (uint64_t)right * eb > 32 || (mode != 0 && mode != 1))
+    return ORACLE_EPARAM;
+  const uint8_t *s = (const uint8_t *)gm;
+  uint8_t *d = (uint8_t *)ub;
+  const uint64_t slot = pad_slot(block_len, mode, left, right, eb);
+  const uint64_t ub_pitch = slot + dst_blocks * 32, lead = (uint64_t)left * eb;
+  for (uint64_t i = 0; i < block_count; ++i) {
+    uint8_t *b = d + i * ub_pitch;
+    memcpy(b + lead, s + i * (block_len + src_gap), block_len);
+    if (is_pad) /* the element-aligned padding positions of the slot hold `value` */
+      for (uint64_t o = 0; o < slot; ++o)
+        if (o < lead || o >= lead + block_len) b[o] = (uint8_t)(value >> (8 * (o % eb)));
+  }
+  if (mode == 1 && is_pad && block_count) { /* Compact: round the whole transfer up to 32 B */
+    const uint64_t end = (block_count - 1) * ub_pitch + slot;
+    for (uint64_t o = end; o < round_up32(end); ++o) d[o] = (uint8_t)(value >> (8 * (o % eb)));
+  }
+  return ORACLE_OK;
+}
+
+int oracle_copy_pad_ub_to_gm(void *gm, const void *ub, uint64_t block_count, uint64_t block_len,
+                             uint64_t src_blocks, uint64_t dst_gap, int mode) {
+  if (mode != 0 && mode != 1) return ORACLE_EPARAM;
+  const uint8_t *s = (const uint8_t *)ub;
+  uint8_t *d = (uint8_t *)gm;
+  const uint64_t ub_pitch = pad_slot(block_len, mode, 0, 0, 1) + src_blocks * 32;
+  for (uint64_t i = 0; i < block_count; ++i)
+    memcpy(d + i * (block_len + dst_gap), s + i * ub_pitch, block_len);
+  return ORACLE_OK;
+}
+
 typedef struct {
   uint8_t *dst;
   const uint8_t *src;

@@ -80,6 +80,39 @@ void oracle_copy_ext_loop(void *dst, const void *src, uint64_t block_count, uint
 int oracle_copy_ext_mt(void *dst, const void *src, uint64_t block_count, uint64_t block_len,
                        uint64_t src_gap, uint64_t dst_gap, int nthreads);
 
+/* ---- DataCopyPad with the UB-side conventions ------------------------------ */
+
+/* The destination (GM -> UB) or source (UB -> GM) is laid out as the Unified
+ * Buffer holds it: its stride is a gap in 32-byte blocks (ascendc/api/
+ * datacopy.h:20-21 GM->UB dstStride = dst_stride / align_num, :36-37 UB->GM
+ * srcStride = src_stride / align_num, align_num = 32 / sizeof(T)).
+ *   mode 0 (PaddingMode::Normal): each UB block starts on a 32-byte boundary and
+ *     occupies round_up(left*eb + block_len + right*eb, 32) bytes;
+ *   mode 1 (PaddingMode::Compact, v35/ascendc/api_regbase/datacopy.h:14-25 and
+ *     standalone_datacopy/README.md: Compact packs UB without per-block 32-byte
+ *     padding): each UB block occupies left*eb + block_len + right*eb bytes,
+ *     and only the end of the whole transfer is rounded up to 32 bytes.
+ * GM -> UB (DataCopyPad(LocalTensor, GlobalTensor, DataCopyExtParams,
+ * DataCopyPadExtParams{is_pad, left, right, value})): block i of block_len
+ * bytes from gm + i*(block_len + src_gap) goes to ub + i*(slot + dst_blocks*32)
+ * + left*eb; when is_pad, the padding bytes (left, right and the round-up) hold
+ * `value` (the low eb bytes, element by element); otherwise they are untouched
+ * (the reference leaves their contents unspecified).
+ * UB -> GM (DataCopyPad(GlobalTensor, LocalTensor, DataCopyExtParams)): block i
+ * of block_len bytes from ub + i*(slot + src_blocks*32) (slot without padding
+ * elements) to gm + i*(block_len + dst_gap).
+ * Hardware results for the padding bytes are unpinned: the reference holds no
+ * vectors for them.  Returns ORACLE_EPARAM for eb not 1/2/4/8, block_len not a
+ * multiple of eb, or left/right padding above 32 bytes. */
+int oracle_copy_pad_gm_to_ub(void *ub, const void *gm, uint64_t block_count, uint64_t block_len,
+                             uint64_t src_gap, uint64_t dst_blocks, int mode, int is_pad,
+                             uint32_t left, uint32_t right, uint64_t value, uint32_t eb);
+int oracle_copy_pad_ub_to_gm(void *gm, const void *ub, uint64_t block_count, uint64_t block_len,
+                             uint64_t src_blocks, uint64_t dst_gap, int mode);
+/* Bytes a GM -> UB transfer spans in UB (first byte to the end of its last slot). */
+uint64_t oracle_pad_ub_span(uint64_t block_count, uint64_t block_len, uint64_t ub_blocks, int mode,
+                            uint32_t left, uint32_t right, uint32_t eb);
+
 /* DataCopyNddma (v35/ascendc/api_regbase/datacopy_nddma.h:15-29): an N-D box
  * copy.  sizes/strides are outermost-first, strides in elements. */
 int oracle_copy_nd(void *dst, const void *src, int ndim, const uint64_t *sizes,

@@ -55,6 +55,11 @@ def lib() -> ctypes.CDLL:
             "oracle_copy_ext_loop": [_vp, _vp] + [ctypes.c_uint64] * 10,
             "oracle_copy_ext_mt": [_vp, _vp] + [ctypes.c_uint64] * 4 + [ctypes.c_int],
             "oracle_copy_nd": [_vp, _vp, ctypes.c_int, _u64p, _i64p, _i64p, ctypes.c_uint32],
+            "oracle_copy_pad_gm_to_ub": [_vp, _vp] + [ctypes.c_uint64] * 4 +
+                                        [ctypes.c_int, ctypes.c_int, ctypes.c_uint32,
+                                         ctypes.c_uint32, ctypes.c_uint64, ctypes.c_uint32],
+            "oracle_copy_pad_ub_to_gm": [_vp, _vp] + [ctypes.c_uint64] * 4 + [ctypes.c_int],
+            "oracle_pad_ub_span": [ctypes.c_uint64] * 3 + [ctypes.c_int] + [ctypes.c_uint32] * 3,
             "oracle_nz_shape": [_i64p, ctypes.c_int, ctypes.c_int64, _i64p,
                                 ctypes.POINTER(ctypes.c_int), _i64p],
             "oracle_nd_to_nz": [_vp, _vp, _i64p, ctypes.c_int, ctypes.c_int, ctypes.c_int64],
@@ -81,7 +86,8 @@ def lib() -> ctypes.CDLL:
             fn = getattr(h, name)
             fn.argtypes = args
             fn.restype = (None if name in ("oracle_fill_pattern", "oracle_copy_ext",
-                                           "oracle_copy_ext_loop") else ctypes.c_int)
+                                           "oracle_copy_ext_loop") else
+                          ctypes.c_uint64 if name == "oracle_pad_ub_span" else ctypes.c_int)
         _lib = h
     return _lib
 
@@ -126,6 +132,22 @@ def copy_ext_loop(dst: np.ndarray, src: np.ndarray, count, blen, sgap, dgap, loo
     """LoopModeParams around the gap copy; loop1/loop2 = (size, src stride, dst stride) bytes."""
     lib().oracle_copy_ext_loop(_p(dst), _p(src), count, blen, sgap, dgap, loop1[0], loop2[0],
                                loop1[1], loop1[2], loop2[1], loop2[2])
+
+
+def copy_pad_gm_to_ub(ub: np.ndarray, gm: np.ndarray, count, blen, src_gap, dst_blocks, mode=0,
+                      pad=(True, 0, 0, 0), eb=1) -> int:
+    """DataCopyPad GM -> UB; pad = DataCopyPadExtParams (is_pad, left, right, value)."""
+    return lib().oracle_copy_pad_gm_to_ub(_p(ub), _p(gm), count, blen, src_gap, dst_blocks, mode,
+                                          int(bool(pad[0])), pad[1], pad[2], pad[3], eb)
+
+
+def copy_pad_ub_to_gm(gm: np.ndarray, ub: np.ndarray, count, blen, src_blocks, dst_gap,
+                      mode=0) -> int:
+    return lib().oracle_copy_pad_ub_to_gm(_p(gm), _p(ub), count, blen, src_blocks, dst_gap, mode)
+
+
+def pad_ub_span(count, blen, ub_blocks, mode=0, left=0, right=0, eb=1) -> int:
+    return lib().oracle_pad_ub_span(count, blen, ub_blocks, mode, left, right, eb)
 
 
 def copy_nd(dst, src, sizes, src_strides, dst_strides, elem_bytes) -> int:

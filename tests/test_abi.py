@@ -209,3 +209,17 @@ def test_spans_that_would_wrap_are_refused(dcopy):
     with pytest.raises(dcopy.DcopyError) as e:
         dcopy.transpose(0x1000, 0x2000, [1 << 31, 1 << 31, 1 << 10], [2, 1, 0], 0)
     assert e.value.code == dcopy.ERR_PARAM_INVALID
+
+
+@pytest.mark.parametrize("sizes,ds", [
+    ([2, 4], [1, 1]),          # two axes on the same stride
+    ([3, 4], [2, 1]),          # outer stride inside the inner axis's extent
+    ([2, 3, 8], [8, 24, 2]),   # a middle stride of 8 inside the 15 elements dim 2 covers
+])
+def test_copy_nd_refuses_repeating_destinations_on_host(dcopy, sizes, ds):
+    """Boxes whose destination elements repeat are refused before any device memory is
+    touched: the kernels write the box concurrently, so the result would not be that of
+    the reference's sequential loop."""
+    with pytest.raises(dcopy.DcopyError) as e:
+        dcopy.copy_nd(0x10000, 0x90000, sizes, [1] * len(sizes), ds, 1)
+    assert e.value.code == dcopy.ERR_PARAM_INVALID and "destinations would repeat" in str(e.value)

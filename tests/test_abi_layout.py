@@ -18,6 +18,8 @@ STRUCTS = {
     "DcopyLoopModeParams": ["loop1Size", "loop2Size", "loop1SrcStride", "loop1DstStride",
                             "loop2SrcStride", "loop2DstStride"],
     "DcopyMemcpyInfo": ["dst", "destMax", "src", "cnt"],
+    "DcopyPadParams": ["isPad", "leftPadding", "rightPadding", "reserved", "elemBytes",
+                       "paddingValue"],
     "DcopyDevCopy": ["device", "dst", "src", "params", "stream"],
     "DcopyTransArgs": ["data", "src_format", "dst_format", "src_c0", "dst_c0", "src_shape",
                        "src_rank", "dst_shape", "dst_rank", "data_type", "src_sub_format",

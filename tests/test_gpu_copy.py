@@ -33,8 +33,26 @@ CASES = [  # (blockCount, blockLen, srcGap, dstGap, src_offset, dst_offset)
 ]
 
 
-@pytest.mark.parametrize("case", CASES, ids=lambda c: "x".join(map(str, c)))
-def test_copy_ext_matches_oracle(torch_cuda, dcopy, oracle, case):
+@pytest.fixture(params=[False, True], ids=["lsu", "tma"])
+def burst_path(request, dcopy):
+    """False: the default load/store kernels.  True: the TMA paths selected
+    (set_nd_tma), under which 16-byte-granular bursts from 512 bytes take the
+    bulk-copy kernel and gapped granular bursts under 128 bytes the 2-D tensor copy."""
+    prev = dcopy.set_nd_tma(request.param)
+    yield request.param
+    dcopy.set_nd_tma(prev)
+
+
+TMA_BURST_CASES = [  # 16-byte granular: (blockCount, blockLen, srcGap, dstGap, soff, doff)
+    (100, 32, 32, 0, 0, 0), (1000, 64, 192, 0, 16, 0), (257, 48, 80, 16, 0, 0),
+    (4096, 16, 1008, 32, 0, 0), (300, 112, 16, 0, 0, 16),
+    (64, 512, 2048, 512, 0, 0), (17, 4096, 12288, 0, 0, 0), (5, 65536, 65536, 32, 0, 0),
+    (3, 1 << 20, 1 << 16, 0, 0, 0), (7, 16400, 16, 48, 32, 16), (1000, 528, 0, 16, 0, 0),
+]
+
+
+@pytest.mark.parametrize("case", CASES + TMA_BURST_CASES, ids=lambda c: "x".join(map(str, c)))
+def test_copy_ext_matches_oracle(torch_cuda, dcopy, oracle, case, burst_path):
     torch = torch_cuda
     count, blen, sgap, dgap, soff, doff = case
     src_span = (count - 1) * (blen + sgap) + blen
@@ -47,6 +65,8 @@ def test_copy_ext_matches_oracle(torch_cuda, dcopy, oracle, case):
     dcopy.copy_ext(dst.data_ptr() + doff, src.data_ptr() + soff, count, blen, sgap, dgap)
     torch.cuda.synchronize()
     assert dst.cpu().numpy().tobytes() == dst_np.tobytes()
+    if burst_path:
+        assert dcopy.tma_error() == 0  # no bounded wait gave up
 
 
 def test_copy_ext_32b_units(torch_cuda, dcopy):
@@ -310,3 +330,16 @@ def test_copy_ext_staged_pageable_and_refusals(torch_cuda, dcopy, oracle):
         dcopy.copy_ext_staged(pageable, src_np, count, blen, sgap, 0, staging, staging_bytes=blen,
                               flags=dcopy.STAGED_COPY_ENGINE_RETURN)
     assert e.value.code == dcopy.ERR_PARAM_INVALID
+
+
+@pytest.mark.parametrize("sizes,ds", [([2, 4], [1, 1]), ([3, 4], [2, 1]), ([4, 16], [8, 1])])
+def test_copy_nd_refuses_repeating_destinations(torch_cuda, dcopy, sizes, ds):
+    """A destination box whose elements repeat is PARAM_INVALID and leaves dst untouched."""
+    torch = torch_cuda
+    src = torch.arange(256, dtype=torch.uint8, device="cuda")
+    dst = _canary(torch, 256)
+    with pytest.raises(dcopy.DcopyError) as e:
+        dcopy.copy_nd(dst, src, sizes, [sizes[1], 1], ds, 1)
+    assert e.value.code == dcopy.ERR_PARAM_INVALID
+    torch.cuda.synchronize()
+    assert bool((dst == CANARY).all())

@@ -95,3 +95,32 @@ def test_memcpy_batch_kinds(torch_cuda, dcopy):
                               (small_dev, 100, big.data_ptr() + 7, 100)], "DEFAULT")
     torch.cuda.synchronize()
     assert torch.equal(big_dev.cpu(), big) and torch.equal(small_dev.cpu(), big[7:107])
+
+
+@pytest.mark.gpu
+def test_memcpy_batch_keeps_task_order(torch_cuda, dcopy):
+    """Tasks that depend on earlier tasks give the result of running them one by one:
+    a chain a -> b -> c of kernel tasks, a copy-engine task (pageable host) between
+    kernel tasks that reads what the first wrote, and a later kernel task that reads
+    what the engine task wrote."""
+    torch = torch_cuda
+    n = 4096
+    a = torch.randint(0, 255, (n,), dtype=torch.uint8, device="cuda")
+    b = torch.zeros_like(a)
+    c = torch.zeros_like(a)
+    dcopy.memcpy_async_batch([(b, n, a.data_ptr(), n), (c, n, b.data_ptr(), n)],
+                             "DEVICE_TO_DEVICE")
+    torch.cuda.synchronize()
+    assert torch.equal(b, a) and torch.equal(c, a)
+    pageable = np.zeros(n, dtype=np.uint8)
+    pinned = torch.zeros(n, dtype=torch.uint8).pin_memory()
+    d = torch.zeros_like(a)
+    e = torch.zeros_like(a)
+    dcopy.memcpy_async_batch([(pinned.data_ptr(), n, a.data_ptr(), n),        # kernel
+                              (pageable.ctypes.data, n, pinned.data_ptr(), n),  # engine
+                              (d, n, pinned.data_ptr(), n),                    # kernel
+                              (e, n, d.data_ptr(), n)], "DEFAULT")             # kernel, reads d
+    torch.cuda.synchronize()
+    want = a.cpu().numpy().tobytes()
+    assert pageable.tobytes() == want
+    assert d.cpu().numpy().tobytes() == want and e.cpu().numpy().tobytes() == want

@@ -60,3 +60,45 @@ def test_noalloc_refuses_shapes_beyond_its_array(torch_cuda, dcopy):
     y = torch.zeros_like(x)
     assert fn(x.data_ptr(), y.data_ptr(), ctypes.byref(t), None) == dcopy.ERR_PARAM_INVALID
     assert b"16777216-byte static B buffer" in dcopy.lib().dcopy_last_error_message()
+
+
+def test_noalloc_store0_leaves_y_untouched(torch_cuda, dcopy):
+    """With store = 0 the workflow writes only the library's array, never y (as
+    dcopy_datacopy_contiguous with store = 0); two calls in a row."""
+    torch = torch_cuda
+    fn = _noalloc(dcopy)
+    rows, cols = 256, 768
+    x = torch.arange(rows * cols, dtype=torch.int32, device="cuda")
+    t = dcopy.plan_tiling(rows, cols, 240, 0)
+    y = torch.full_like(x, -0x5A5A5A5B)
+    for _ in range(2):
+        assert fn(x.data_ptr(), y.data_ptr(), ctypes.byref(t), None) == 0
+        torch.cuda.synchronize()
+        assert bool((y == -0x5A5A5A5B).all())
+    # A store = 1 call right after still gives the transpose.
+    t1 = dcopy.plan_tiling(rows, cols, 240, 1)
+    assert fn(x.data_ptr(), y.data_ptr(), ctypes.byref(t1), None) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(y.view(cols, rows), x.view(rows, cols).t())
+
+
+def test_noalloc_on_a_second_device(torch_cuda, dcopy):
+    """Each device has its own copy of the array, looked up with that device current."""
+    torch = torch_cuda
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    fn = _noalloc(dcopy)
+    rows, cols = 128, 513
+    t = dcopy.plan_tiling(rows, cols, 4, 1)
+    outs = []
+    for dev in (1, 0, 1):
+        with torch.cuda.device(dev):
+            x = torch.arange(rows * cols, dtype=torch.int32, device=f"cuda:{dev}") * 7 + dev
+            y = torch.full_like(x, -1)
+            stream = torch.cuda.current_stream(dev).cuda_stream or None
+            assert fn(x.data_ptr(), y.data_ptr(), ctypes.byref(t), stream) == 0, \
+                dcopy.lib().dcopy_last_error_message()
+            torch.cuda.synchronize(dev)
+            assert torch.equal(y.view(cols, rows), x.view(rows, cols).t())
+            outs.append(y.cpu())
+    assert torch.equal(outs[0], outs[2])
