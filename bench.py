@@ -50,6 +50,16 @@ NVML_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_po
                 0x100: "display_clock_setting"}
 
 
+def workload_config(world: int) -> dict:
+    """The `config` object of both arms' JSON lines (the same keys and values)."""
+    return {"workload": WORKLOAD, "gathers_per_step": SETS,
+            "bytes_per_gather": BYTES_PER_GATHER,
+            "l2": "inputs larger than L2: 16 rotating buffer sets, 512 MiB touched per step "
+                  "vs 126 MB L2",
+            "timing": "CUDA graph of one step replayed K times between CUDA events",
+            "parallelism": f"independent per-GPU copies x{world} (no collective)"}
+
+
 def parse_args():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -245,25 +255,30 @@ def run_dcopy(args, rank, world, local_rank):
     launch_ms = ms / launches
     achieved = BYTES_PER_GATHER / (launch_ms / 1e3) / 1e9
     peak, peak_kind = load_peaks()
-    traffic = load_traffic().get("strided_copy_kernel/config2")
+    # DRAM bytes of one launch from an ncu capture of this bench's own launches
+    # (profiles/strided_copy_kernel_config2_traffic.md): a committed figure, since
+    # the counters cannot be read without the profiler.
+    traffic_rec = load_traffic().get("strided_copy_kernel/config2") or {}
+    traffic = traffic_rec.get("traffic_bytes_per_launch")
 
     # End to end through the public call with host buffers (pinned source and
     # destination, every step). dcopy_copy_ext_staged: the copy engine gathers the
     # 4 KiB bursts host -> device in chunks (16 MiB cross PCIe, not the 64 MiB
-    # source), and the gather kernel writes each staged chunk to the host
-    # destination while the next chunk is gathered, so both PCIe directions are
-    # busy. Measured on B200: the whole source in and the result out around a device
-    # gather 21.9 GB/s; the kernel reading and writing host memory directly
-    # (zero-copy, reported beside) 56-57 GB/s; this path 68-70 GB/s.
+    # source) into a 16 MiB staging ring, and the copy engine returns each staged
+    # chunk to the host destination on a second stream while the next chunk is
+    # gathered, so both PCIe directions are busy. Measured on B200: the whole
+    # source in and the result out around a device gather 21.9 GB/s; the kernel
+    # reading and writing host memory directly (zero-copy, reported beside) 50-57
+    # GB/s; this path 74.8 GB/s against a measured duplex ceiling of 87.2 GB/s.
     e2e_steps = max(3, min(args.steps, 30))
     h_src = base.cpu().pin_memory()
     h_dst = torch.empty(ROWS, C1 - C0).pin_memory()
-    staging = torch.empty(8 * MIB, dtype=torch.uint8, device=dev)
+    staging = torch.empty(16 * MIB, dtype=torch.uint8, device=dev)
     ref_host = h_src[:, C0:C1].contiguous().view(torch.int32)
 
     def staged_step():
         dcopy.copy_ext_staged(h_dst, h_src.data_ptr() + C0 * 4, ROWS, BLOCK_LEN, SRC_GAP, 0,
-                              staging)
+                              staging, flags=dcopy.STAGED_COPY_ENGINE_RETURN)
 
     def zero_copy_step():
         dcopy.copy_ext_32b(h_dst, h_src[:, C0:], ROWS, BLOCK_LEN // 32, SRC_GAP // 32, 0)
@@ -287,6 +302,13 @@ def run_dcopy(args, rank, world, local_rank):
 
     e2e_value = time_e2e(staged_step)
     zero_copy_value = time_e2e(zero_copy_step)
+    pcie = pcie_ceiling(torch, dev, barrier, dist, world)
+
+    # N > 1: BASELINE config 5's NVLink step as well -- every rank pushes a 1 GiB
+    # shard into rank (r + 1) mod N over NVLink, every received shard checked whole.
+    p2p = None
+    if world > 1:
+        p2p = ring_shift_measure(torch, dcopy, dev, rank, world, barrier, dist, args.steps)
 
     # The other configs are single-GPU measurements: taken on the N=1 run only, so
     # multi-GPU runs do not hold N GPUs while rank 0 alone measures them.
@@ -310,25 +332,32 @@ def run_dcopy(args, rank, world, local_rank):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 5),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
             "data": "synthetic (torch.rand fp32 from seed 1+rank; copies are value-agnostic)",
-            "config": {"workload": WORKLOAD, "gathers_per_step": SETS,
-                       "bytes_per_gather": BYTES_PER_GATHER,
-                       "l2": "inputs larger than L2: 16 rotating buffer sets, 512 MiB touched "
-                             "per step vs 126 MB L2",
-                       "timing": "CUDA graph of one step replayed K times between CUDA events",
-                       "parallelism": f"independent per-GPU copies x{world} (no collective)"},
+            "config": workload_config(world),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": traffic, "kernel": "strided_copy_kernel<uint4,4>",
+                         "algorithmic_bytes": BYTES_PER_GATHER,
+                         "traffic_read": traffic_rec.get("dram_read_bytes_per_launch"),
+                         "traffic_write": traffic_rec.get("dram_write_bytes_per_launch"),
+                         "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum per launch, "
+                                         "ncu --cache-control none over 8 consecutive launches of "
+                                         "this bench (writes land as later write-backs), no "
+                                         "scaling; from profiles/ncu_traffic.json",
                          "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)"},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 3), "unit": "GB/s",
                     "h2d_bytes_per_step": ROWS * (C1 - C0) * 4,
                     "d2h_bytes_per_step": ROWS * (C1 - C0) * 4,
                     "steps": e2e_steps,
-                    "path": "dcopy_copy_ext_staged on pinned host buffers, 8 MiB device "
+                    "path": "dcopy_copy_ext_staged on pinned host buffers, 16 MiB device "
                             "staging: copy-engine gather of the bursts host -> device in 4 "
-                            "chunks, the gather kernel writing each chunk to host memory while "
-                            "the next is gathered",
+                            "chunks, each chunk returned to host memory by the copy engine on "
+                            "a second stream while the next is gathered",
+                    "pcie_duplex_ceiling_GBps": pcie["duplex"],
+                    "pcie_h2d_GBps": pcie["h2d"], "pcie_d2h_GBps": pcie["d2h"],
+                    "frac_of_duplex_ceiling": round(e2e_value / world / pcie["duplex"], 4),
+                    "pcie_note": "ceiling = 16 MiB pinned H2D and D2H cudaMemcpyAsync on two "
+                                 "streams at once (per GPU); e2e moves the same bytes each way",
                     "zero_copy_value": round(zero_copy_value, 3),
                     "zero_copy_path": "dcopy_copy_ext_32b on the pinned host buffers: the kernel "
                                       "reads and writes host memory over PCIe"},
@@ -337,7 +366,132 @@ def run_dcopy(args, rank, world, local_rank):
         }
         if secondary is not None:
             line["secondary"] = secondary
+        if p2p is not None:
+            line["p2p"] = p2p
     return line
+
+
+def pcie_ceiling(torch, dev, barrier, dist, world):
+    """Per-GPU PCIe bandwidth of pinned 16 MiB cudaMemcpyAsync: host -> device alone,
+    device -> host alone, and both at once on two streams (the duplex ceiling of an
+    end-to-end copy, which moves the same bytes in each direction)."""
+    n = 16 * MIB
+    h_a = torch.empty(n, dtype=torch.uint8).pin_memory()
+    h_b = torch.empty(n, dtype=torch.uint8).pin_memory()
+    d_a = torch.empty(n, dtype=torch.uint8, device=dev)
+    d_b = torch.empty(n, dtype=torch.uint8, device=dev)
+    s1, s2 = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    main = torch.cuda.current_stream(dev)
+
+    def run(h2d, d2h, reps=16):
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(main)
+        s1.wait_event(a)
+        s2.wait_event(a)
+        for _ in range(reps):
+            if h2d:
+                with torch.cuda.stream(s1):
+                    d_a.copy_(h_a, non_blocking=True)
+            if d2h:
+                with torch.cuda.stream(s2):
+                    h_b.copy_(d_b, non_blocking=True)
+        main.wait_stream(s1)
+        main.wait_stream(s2)
+        b.record(main)
+        b.synchronize()
+        t = torch.tensor([a.elapsed_time(b)], dtype=torch.float64, device=dev)
+        if dist is not None:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return round(n * reps * (int(h2d) + int(d2h)) / (float(t.item()) / 1e3) / 1e9, 2)
+
+    run(True, True, reps=2)  # warm-up
+    return {"h2d": run(True, False), "d2h": run(False, True), "duplex": run(True, True)}
+
+
+def ring_shift_measure(torch, dcopy, dev, rank, world, barrier, dist, steps):
+    """BASELINE config 5's exchange step on N GPUs: rank r pushes a 1 GiB shard into
+    rank (r+1) mod N's receive buffer over NVLink (dcopy_p2p_copy into the CUDA IPC
+    mapping), release-stores a sequence number into that rank's flag, and waits for
+    its own flag with a bounded device-side wait.  Every received shard is compared
+    whole with the sender's data.  The same exchange with cudaMemcpyAsync (the copy
+    engine) in place of the kernel is timed on the same buffers as the comparator.
+    Timing: CUDA events on each rank's stream, max over ranks."""
+    from dcopy import multi
+    from cuda.bindings import runtime as cudart
+    shard = 1 << 30
+    words = shard // 4
+    prev = (rank - 1) % world
+
+    def pattern(r):  # the shard rank r sends: random words from seed 3 + r (BASELINE seed 3)
+        g = torch.Generator(device=dev).manual_seed(3 + r)
+        return torch.randint(-2**31, 2**31 - 1, (words,), dtype=torch.int32, device=dev,
+                             generator=g)
+
+    send = pattern(rank)
+    expect = pattern(prev)
+    recv = torch.zeros(words, dtype=torch.int32, device=dev)
+    flags = torch.zeros(4, dtype=torch.int32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    barrier()
+    peer = multi.map_next_peer(recv, flags, rank, world)
+    seq = 0
+    results = {}
+    try:
+        def exchange(engine):
+            nonlocal seq
+            seq += 1
+            if engine:
+                err, = cudart.cudaMemcpyAsync(peer.recv_ptr, send.data_ptr(), shard,
+                                              cudart.cudaMemcpyKind.cudaMemcpyDefault,
+                                              stream.cuda_stream)
+                if err != cudart.cudaError_t.cudaSuccess:
+                    raise RuntimeError(f"cudaMemcpyAsync to the peer failed: {err}")
+                dcopy.signal(peer.flag_ptr, seq, stream)
+            else:
+                multi.ring_shift(send, shard, peer, seq, stream)
+            multi.wait_ring(flags, seq, status, timeout_ns=2_000_000_000, stream=stream)
+
+        psteps = max(2, min(steps, 10))
+        for name, engine in (("kernel", False), ("copy_engine", True)):
+            recv.zero_()
+            barrier()
+            for _ in range(2):
+                exchange(engine)
+            torch.cuda.synchronize(dev)
+            ok = status.item() == 0 and torch.equal(recv, expect)
+            barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(psteps):
+                exchange(engine)
+            e1.record(stream)
+            e1.synchronize()
+            ok = ok and status.item() == 0
+            # The last exchange must also have delivered the whole shard.
+            barrier()
+            ok = ok and torch.equal(recv, expect)
+            t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+            good = torch.tensor([1 if ok else 0], dtype=torch.int32, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            dist.all_reduce(good, op=dist.ReduceOp.MIN)
+            results[name] = (shard * psteps / (float(t.item()) / 1e3) / 1e9, bool(good.item()))
+        err = dcopy.p2p_error()
+    finally:
+        barrier()
+        peer.release()
+    kern, ce = results["kernel"], results["copy_engine"]
+    return {"per_direction_GBps": round(kern[0], 1), "aggregate_GBps": round(kern[0] * world, 1),
+            "nominal_GBps": 900.0, "frac_of_nominal": round(kern[0] / 900.0, 4),
+            "measured_peer_copy_GBps": 770.0,
+            "frac_of_measured_peer_copy": round(kern[0] / 770.0, 4),
+            "flags_ok": kern[1] and ce[1] and err == 0, "shards_checked": "whole 1 GiB shard",
+            "copy_engine_per_direction_GBps": round(ce[0], 1),
+            "bytes_per_rank_per_step": shard, "steps": max(2, min(steps, 10)),
+            "path": "dcopy_p2p_copy (SM bulk-copy push) into the next rank's IPC-mapped "
+                    "buffer + release flag; bounded device-side wait on this rank's flag",
+            "comparator": "cudaMemcpyAsync into the same mapping, same flags"}
 
 
 def _time_graph(torch, fn, reps=10, warm=3):
@@ -464,7 +618,6 @@ def run_config5(args, rank, world, local_rank):
     1 GiB shard to rank (r+1) mod N over NVLink (CUDA IPC, in-kernel stores)."""
     import torch
     import dcopy
-    from dcopy import multi
     torch.cuda.set_device(local_rank)
     dcopy.lib()
     dev = torch.device("cuda", local_rank)
@@ -509,53 +662,8 @@ def run_config5(args, rank, world, local_rank):
     del src
 
     p2p = None
-    if world > 1:
-        shard = gib
-        send = torch.empty(shard, dtype=torch.uint8, device=dev)
-        send.fill_(rank + 1)
-        recv = torch.zeros(shard, dtype=torch.uint8, device=dev)
-        flags = torch.zeros(4, dtype=torch.int32, device=dev)
-        status = torch.zeros(1, dtype=torch.int32, device=dev)
-        barrier()
-        peer = multi.map_next_peer(recv, flags, rank, world)
-        try:
-            seq = 0
-
-            def exchange():
-                nonlocal seq
-                seq += 1
-                multi.ring_shift(send, shard, peer, seq)
-                multi.wait_ring(flags, seq, status, timeout_ns=2_000_000_000)
-
-            for _ in range(2):
-                exchange()
-            torch.cuda.synchronize()
-            assert status.item() == 0, "ring shift flag timed out"
-            assert torch.equal(recv[:4096], torch.full((4096,), ((rank - 1) % world) + 1,
-                                                       dtype=torch.uint8, device=dev))
-            barrier()
-            psteps = max(1, min(args.steps, 10))
-            p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            p0.record()
-            for _ in range(psteps):
-                exchange()
-            p1.record()
-            p1.synchronize()
-            ok = torch.tensor([status.item() == 0], dtype=torch.int32, device=dev)
-            pt = torch.tensor([p0.elapsed_time(p1)], dtype=torch.float64, device=dev)
-            barrier()
-            dist.all_reduce(pt, op=dist.ReduceOp.MAX)
-            dist.all_reduce(ok, op=dist.ReduceOp.MIN)
-            per_dir = shard * psteps / (float(pt.item()) / 1e3) / 1e9
-            p2p = {"per_direction_GBps": round(per_dir, 1),
-                   "aggregate_GBps": round(per_dir * world, 1),
-                   "reference_peak_GBps": 770.0, "frac_of_measured_peer_copy": round(per_dir / 770.0, 4),
-                   "bytes_per_rank_per_step": shard, "steps": psteps, "flags_ok": bool(ok.item()),
-                   "path": "dcopy_p2p_copy into the next rank's IPC-mapped buffer + release flag; "
-                           "bounded device-side wait on this rank's flag"}
-        finally:
-            barrier()
-            peer.release()
+    if world > 1:  # the ring shift, every received 1 GiB shard checked whole
+        p2p = ring_shift_measure(torch, dcopy, dev, rank, world, barrier, dist, args.steps)
     if rank != 0:
         return None
     return {"metric": METRIC, "value": round(local_value, 2), "unit": "GB/s", "n_gpus": world,
@@ -671,7 +779,7 @@ def run_reference(args):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(el * 1e3 / args.steps, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-        "config": {"workload": WORKLOAD},
+        "config": workload_config(args.gpus),
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads,
                          "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,

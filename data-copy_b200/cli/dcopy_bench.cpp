@@ -35,7 +35,8 @@
 //       G config-2 gathers as one dcopy_copy_ext_batch against G dcopy_copy_ext calls
 //       (both captured in a CUDA graph), verified; one JSON line.
 //   dcopy_bench p2p [--mib M] [--reps R] [--device D] [--peer P] [--peak GBPS]
-//       NVLink between two GPUs: dcopy_p2p_copy as a push (launched on the
+//       NVLink between two GPUs (push, pull, copy engine, and the two halves
+//       split SM push + copy engine or push + pull): dcopy_p2p_copy as a push (launched on the
 //       sending GPU) and as a pull (launched on the receiving GPU), and the copy
 //       engine, each with both GPUs sending at once and with one sending.
 //
@@ -717,27 +718,48 @@ int run_p2p(const Args &a) {
   CheckD(dcopy_enable_peer_access(dev[0], dev[1]));
   CheckD(dcopy_enable_peer_access(dev[1], dev[0]));
   std::unique_ptr<DevBuf> src[2], dst[2];
-  cudaStream_t s[2];
-  cudaEvent_t ev[2][2];
+  cudaStream_t s[2][2];  // [device][0: main, 1: second stream]
+  cudaEvent_t ev[2][2][2];
   for (int i = 0; i < 2; ++i) {
     Check(cudaSetDevice(dev[i]), "cudaSetDevice");
     src[i] = std::make_unique<DevBuf>(bytes);
     dst[i] = std::make_unique<DevBuf>(bytes);
     Check(cudaMemset(src[i]->p, 0x11 * (i + 1), bytes), "memset");
-    Check(cudaStreamCreateWithFlags(&s[i], cudaStreamNonBlocking), "stream");
-    Check(cudaEventCreate(&ev[i][0]), "event");
-    Check(cudaEventCreate(&ev[i][1]), "event");
+    for (int k = 0; k < 2; ++k) {
+      Check(cudaStreamCreateWithFlags(&s[i][k], cudaStreamNonBlocking), "stream");
+      Check(cudaEventCreate(&ev[i][k][0]), "event");
+      Check(cudaEventCreate(&ev[i][k][1]), "event");
+    }
   }
-  // GPU i sends src[i] to the other GPU's dst; a pull is launched on the receiver.
+  // GPU i sends src[i] to the other GPU's dst.  push: the SM kernel on the
+  // sender; pull: the load kernel on the receiver; ce: cudaMemcpyPeerAsync;
+  // split: SM push of the first half and the copy engine for the second half,
+  // on two streams of the sender; pushpull: SM push of the first half on the
+  // sender and a pull of the second half on the receiver.
+  const uint64_t half = bytes / 2 / 16 * 16;
+  auto push = [&](int on, void *d, const void *sp, uint64_t n, int k) {
+    Check(cudaSetDevice(dev[on]), "cudaSetDevice");
+    CheckD(dcopy_p2p_copy(d, sp, n, reinterpret_cast<dcopy_stream_t>(s[on][k])));
+  };
   auto issue = [&](const std::string &mode, int i) {
     const int peer = 1 - i;
-    const int launch_on = mode == "pull" ? peer : i;
-    Check(cudaSetDevice(dev[launch_on]), "cudaSetDevice");
-    dcopy_stream_t ds = reinterpret_cast<dcopy_stream_t>(s[launch_on]);
-    if (mode == "ce")
-      Check(cudaMemcpyPeerAsync(dst[peer]->p, dev[peer], src[i]->p, dev[i], bytes, s[i]), "peer");
-    else
-      CheckD(dcopy_p2p_copy(dst[peer]->p, src[i]->p, bytes, ds));
+    uint8_t *d = static_cast<uint8_t *>(dst[peer]->p);
+    const uint8_t *sp = static_cast<const uint8_t *>(src[i]->p);
+    if (mode == "push") {
+      push(i, d, sp, bytes, 0);
+    } else if (mode == "pull") {
+      push(peer, d, sp, bytes, 0);
+    } else if (mode == "ce") {
+      Check(cudaSetDevice(dev[i]), "cudaSetDevice");
+      Check(cudaMemcpyPeerAsync(d, dev[peer], sp, dev[i], bytes, s[i][0]), "peer");
+    } else if (mode == "split") {
+      push(i, d, sp, half, 0);
+      Check(cudaMemcpyPeerAsync(d + half, dev[peer], sp + half, dev[i], bytes - half, s[i][1]),
+            "peer");
+    } else {  // pushpull
+      push(i, d, sp, half, 0);
+      push(peer, d + half, sp + half, bytes - half, 1);
+    }
   };
   auto sync_all = [&] {
     for (int i = 0; i < 2; ++i) {
@@ -745,8 +767,14 @@ int run_p2p(const Args &a) {
       Check(cudaDeviceSynchronize(), "sync");
     }
   };
+  auto record_all = [&](int which) {
+    for (int i = 0; i < 2; ++i) {
+      Check(cudaSetDevice(dev[i]), "cudaSetDevice");
+      for (int k = 0; k < 2; ++k) Check(cudaEventRecord(ev[i][k][which], s[i][k]), "record");
+    }
+  };
   std::vector<uint8_t> host(bytes);
-  for (const std::string mode : {"push", "pull", "ce"}) {
+  for (const std::string mode : {"push", "pull", "ce", "split", "pushpull"}) {
     for (int senders = 2; senders >= 1; --senders) {
       for (int i = 0; i < 2; ++i) {
         Check(cudaSetDevice(dev[i]), "cudaSetDevice");
@@ -756,25 +784,20 @@ int run_p2p(const Args &a) {
       for (int w = 0; w < 2; ++w)
         for (int i = 0; i < senders; ++i) issue(mode, i);
       sync_all();
-      // The stream that carries sender i's copy: the receiver's for a pull.
-      auto stream_of = [&](int i) { return mode == "pull" ? 1 - i : i; };
-      for (int i = 0; i < senders; ++i) {
-        Check(cudaSetDevice(dev[stream_of(i)]), "cudaSetDevice");
-        Check(cudaEventRecord(ev[stream_of(i)][0], s[stream_of(i)]), "record");
-      }
+      // Every stream of both GPUs is idle here: the time of the exchange is the
+      // longest span between its start and end events.
+      record_all(0);
       for (int r = 0; r < reps; ++r)
         for (int i = 0; i < senders; ++i) issue(mode, i);
-      for (int i = 0; i < senders; ++i) {
-        Check(cudaSetDevice(dev[stream_of(i)]), "cudaSetDevice");
-        Check(cudaEventRecord(ev[stream_of(i)][1], s[stream_of(i)]), "record");
-      }
+      record_all(1);
       sync_all();
       double ms = 0;
-      for (int i = 0; i < senders; ++i) {
-        float m = 0;
-        Check(cudaEventElapsedTime(&m, ev[stream_of(i)][0], ev[stream_of(i)][1]), "elapsed");
-        ms = std::max(ms, double(m));
-      }
+      for (int i = 0; i < 2; ++i)
+        for (int k = 0; k < 2; ++k) {
+          float m = 0;
+          Check(cudaEventElapsedTime(&m, ev[i][k][0], ev[i][k][1]), "elapsed");
+          ms = std::max(ms, double(m));
+        }
       uint32_t gave_up = 0;
       for (int i = 0; i < 2; ++i) {
         Check(cudaSetDevice(dev[i]), "cudaSetDevice");
@@ -797,9 +820,11 @@ int run_p2p(const Args &a) {
   }
   for (int i = 0; i < 2; ++i) {
     Check(cudaSetDevice(dev[i]), "cudaSetDevice");
-    cudaEventDestroy(ev[i][0]);
-    cudaEventDestroy(ev[i][1]);
-    cudaStreamDestroy(s[i]);
+    for (int k = 0; k < 2; ++k) {
+      cudaEventDestroy(ev[i][k][0]);
+      cudaEventDestroy(ev[i][k][1]);
+      cudaStreamDestroy(s[i][k]);
+    }
     src[i].reset();
     dst[i].reset();
   }
