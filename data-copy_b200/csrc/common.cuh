@@ -149,16 +149,6 @@ __device__ __forceinline__ uint8_t ld_stream_half_line<uint8_t>(const uint8_t *p
   return (uint8_t)v;
 }
 
-// Streaming 16-byte load whose L2 miss fetches the 256-byte span around it (the
-// `.L2::256B` prefetch-size qualifier), for bursts that cover whole spans.
-__device__ __forceinline__ uint4 ld_stream_span256(const uint4 *p) {
-  uint4 v;
-  asm("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0, %1, %2, %3}, [%4];"
-      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-      : "l"(p));
-  return v;
-}
-
 // L2 prefetch hint for the line holding p.  Kernels issue these for their source
 // before waiting on the previous kernel of the stream (programmatic dependent
 // launch): a prefetch returns no data to the SM and has no effect on memory

@@ -55,22 +55,17 @@ constexpr int kCtasPerSm = 8;
 #ifndef DCOPY_STRIDED_U
 #define DCOPY_STRIDED_U 4  // elements in flight per thread (strided copy)
 #endif
-#ifndef DCOPY_SPREAD_PROBE
-// 1: before the dependent-launch wait, each CTA of a strided copy also
-// prefetches one source and one destination line at a row spread over the
-// whole copy (a Weyl sequence over the rows), so that the CTAs resident early
-// touch every page of both spans while the previous kernel drains.
-#define DCOPY_SPREAD_PROBE 0
+#ifndef DCOPY_STRIDED_THREADS
+// Threads per CTA of the strided copy over whole lines.  Measured on B200 (
+// 16 gathers per CUDA graph): 1024 -> 5535 GB/s, 512 -> 5389, 256 -> 5372, 128 -> 5458; the
+// 256 MiB sweep points unchanged.  Half-line copies (short gapped bursts) keep 256, where 1024
+// cost 2 % on 64 B bursts.
+#define DCOPY_STRIDED_THREADS 1024
 #endif
-#ifndef DCOPY_L2_SPAN256
-#define DCOPY_L2_SPAN256 0  // 1: 16-byte loads of bursts of whole 256-byte spans fetch 256 bytes
-#endif
-#ifndef DCOPY_STRIDED_CPC
-// Chunks of kThreads x U elements per CTA of a strided copy.  Above 1 the grid
-// covers a fraction of the CTA slots, so the next launch on the stream can be
-// resident (and L2-prefetch its whole range, see below) while this one drains.
-#define DCOPY_STRIDED_CPC 1
-#endif
+template <bool kHalfLine>
+struct StridedShape {
+  static constexpr int threads = kHalfLine ? kThreads : DCOPY_STRIDED_THREADS;
+};
 
 template <typename T>
 struct Unroll {
@@ -160,24 +155,20 @@ __global__ void __launch_bounds__(kThreads) linear_load_kernel(const uint8_t *__
 // source loads fill 64-byte half lines of L2 (bursts that start or end inside a
 // 128-byte line, with gaps between them).
 template <typename T, int U, bool kHalfLine>
-__global__ void __launch_bounds__(kThreads, Unroll<T>::strided_min_ctas)
+__global__ void __launch_bounds__(StridedShape<kHalfLine>::threads,
+                      Unroll<T>::strided_min_ctas * kThreads / StridedShape<kHalfLine>::threads)
     strided_copy_kernel(uint8_t *__restrict__ dst, const uint8_t *__restrict__ src,
                         uint32_t total, uint32_t per_cta, FastDiv epr, uint64_t src_pitch,
                         uint64_t dst_pitch, bool prefetch) {
+  constexpr uint32_t kSThreads = StridedShape<kHalfLine>::threads;
   pdl_trigger_at_entry();
   const uint32_t begin = blockIdx.x * per_cta;
   const uint32_t end = begin + per_cta < total ? begin + per_cta : total;
-  if (DCOPY_SPREAD_PROBE && prefetch && threadIdx.x == 0) {
-    const uint32_t rows = total / epr.d;
-    const uint32_t r = __umulhi(blockIdx.x * 0x9E3779B9u, rows);  // frac(b * golden ratio) * rows
-    prefetch_l2(src + (uint64_t)r * src_pitch);
-    prefetch_l2(dst + (uint64_t)r * dst_pitch);
-  }
-  if (DCOPY_PREFETCH && prefetch) {  // the CTA's range, one prefetch per 128-byte line
+  if (DCOPY_PREFETCH && prefetch) {  // first U elements, one prefetch per 128-byte line
     constexpr uint32_t per_line = 128 / sizeof(T) > 0 ? 128 / sizeof(T) : 1;
 #pragma unroll
-    for (int u = 0; u < U * DCOPY_STRIDED_CPC; ++u) {
-      const uint32_t i = begin + threadIdx.x + u * kThreads;
+    for (int u = 0; u < U; ++u) {
+      const uint32_t i = begin + threadIdx.x + u * kSThreads;
       if (i < end && (threadIdx.x % per_line == 0 || i == begin)) {
         const uint32_t r = epr.div(i);
         prefetch_l2(reinterpret_cast<const T *>(src + (uint64_t)r * src_pitch) + (i - r * epr.d));
@@ -186,18 +177,16 @@ __global__ void __launch_bounds__(kThreads, Unroll<T>::strided_min_ctas)
   }
   pdl_wait();
   pdl_launch_dependents();
-  for (uint32_t base = begin + threadIdx.x; base < end; base += kThreads * U) {
+  for (uint32_t base = begin + threadIdx.x; base < end; base += kSThreads * U) {
     T v[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const uint32_t i = base + u * kThreads;
+      const uint32_t i = base + u * kSThreads;
       if (i < end) {
         const uint32_t r = epr.div(i);
         const T *p = reinterpret_cast<const T *>(src + (uint64_t)r * src_pitch) + (i - r * epr.d);
         if constexpr (kHalfLine)
           v[u] = ld_stream_half_line(p);
-        else if constexpr (DCOPY_L2_SPAN256 && sizeof(T) == 16)
-          v[u] = ld_stream_span256(p);
         else
           v[u] = ld_stream(p);
       }
@@ -206,7 +195,7 @@ __global__ void __launch_bounds__(kThreads, Unroll<T>::strided_min_ctas)
     // kept live, which holds the kernel at 32 registers: 8 CTAs per SM.
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const uint32_t i = base + u * kThreads;
+      const uint32_t i = base + u * kSThreads;
       if (i < end) {
         const uint32_t r = epr.div(i);
         *(reinterpret_cast<T *>(dst + (uint64_t)r * dst_pitch) + (i - r * epr.d)) = v[u];
@@ -224,8 +213,8 @@ struct Split {
 };
 
 template <typename K>
-Split split_work(K kernel, uint64_t n, int U) {
-  const uint64_t chunk = (uint64_t)kThreads * U;
+Split split_work(K kernel, uint64_t n, int U, int threads = kThreads) {
+  const uint64_t chunk = (uint64_t)threads * U;
   uint64_t grid = (n + chunk - 1) / chunk;
 #if DCOPY_BALANCED
   grid = std::min<uint64_t>(grid, resident_ctas(kernel, kThreads, 0));
@@ -234,7 +223,7 @@ Split split_work(K kernel, uint64_t n, int U) {
 #endif
   grid = std::max<uint64_t>(grid, 1);
   uint64_t per = (n + grid - 1) / grid;
-  per = (per + kThreads - 1) / kThreads * kThreads;
+  per = (per + threads - 1) / threads * threads;
   grid = std::max<uint64_t>(1, (n + per - 1) / per);
   return {(unsigned)grid, per};
 }
@@ -285,8 +274,9 @@ int launch_strided(uint8_t *dst, const uint8_t *src, uint64_t rows, uint64_t row
     const uint64_t nr = std::min(max_rows, rows - r0);
     const uint32_t total = (uint32_t)(nr * epr);
     auto kernel = half_line ? strided_copy_kernel<T, U, true> : strided_copy_kernel<T, U, false>;
-    const Split sp = split_work(kernel, total, U * DCOPY_STRIDED_CPC);
-    int rc = launch(kernel, sp.grid, dim3(kThreads), 0, s, "strided_copy_kernel",
+    const int threads = half_line ? StridedShape<true>::threads : StridedShape<false>::threads;
+    const Split sp = split_work(kernel, total, U, threads);
+    int rc = launch(kernel, sp.grid, dim3(threads), 0, s, "strided_copy_kernel",
                     dst + r0 * dst_pitch, src + r0 * src_pitch, total, (uint32_t)sp.per_cta, div,
                     src_pitch, dst_pitch, prefetch_src);
     if (rc) return rc;
