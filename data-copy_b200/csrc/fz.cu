@@ -21,6 +21,7 @@
 #include <atomic>
 #include <cstring>
 
+#include "bulk.cuh"
 #include "common.cuh"
 #include "internal.cuh"
 #include "launch.cuh"
@@ -449,6 +450,212 @@ int launch_vec(bool nchw, bool to_fz, void *dst, const void *src, const FzSGeom 
                 ntiles);
 }
 
+// ---- NCHW -> FRACTAL_Z with bulk-copied, double-buffered tiles ----------------------
+//
+// A tile is NB weights (rows n) of one channel block c1: per row the C0*HW
+// contiguous source elements (c0, hw) of that block.  The rows arrive by
+// cp.async.bulk (one per row, this GPU's memory, no multicast) into one of two
+// shared stages while the other stage is turned into FRACTAL_Z, so the loads of
+// the next tile are in flight during the whole gather of this one and hold no
+// registers.  Gather mapping (lane = hw lo 2 bits | c0 vector q | row nl): a
+// warp builds the 16-byte FRACTAL_Z vectors (hw, n, q) of 4 consecutive hw x all
+// C0/V vectors x NL = 32/(4 C0/V) rows, reading element (n, q*V + j, hw) at
+// n*P + (q*V + j)*HW + hw.  The row pitch P (a multiple of 16 bytes, as bulk
+// copies need) has the word residue 32/NL mod 32: for odd HW every gather of a
+// warp then reads distinct banks (two lanes reading one word share it).  Each
+// warp writes 4 whole 128-byte-aligned runs of NL*C0 elements.  Rows of padding
+// weights (n >= N) are zero-filled by the threads.  The mbarrier waits are
+// bounded; a give-up is recorded (read through dcopy_tma_error) and the CTA
+// waits (bounded) for its own copies before returning.
+struct FzBGeom {
+  uint32_t N, HW, C0, NB, P, L;  // elements; L = C0*HW, P = row pitch
+  uint32_t lq, lnl, lnnb;        // log2(C0/V), log2(NL), log2(NB/NL)
+  uint32_t nblocks, ntiles, C1;
+  FastDiv f_nblocks;
+  uint64_t seg_stride, N1N0;     // global elements between weights; padded weight count
+};
+
+__device__ uint32_t g_fz_error;
+
+template <int EB>
+__global__ void __launch_bounds__(kThreads) fz_nchw_bulk_kernel(unsigned char *__restrict__ dst_b,
+                                                                const unsigned char *__restrict__ src_b,
+                                                                FzBGeom g) {
+  using T = typename FzLane<EB>::T;
+  constexpr int V = FzLane<EB>::V;
+  union Pack {
+    uint4 u;
+    T e[V];
+  };
+  extern __shared__ __align__(128) unsigned char fzb_smem[];
+  __shared__ __align__(8) uint64_t bars[2];
+  T *dst = reinterpret_cast<T *>(dst_b);
+  const T *src = reinterpret_cast<const T *>(src_b);
+  const uint32_t stage_elems = g.NB * g.P;
+  const uint32_t row_bytes = g.L * EB;
+  pdl_trigger_at_entry();
+  if (threadIdx.x == 0) {
+    bulk::mbar_init(&bars[0], 1);
+    bulk::mbar_init(&bars[1], 1);
+    bulk::mbar_init_fence();
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_launch_dependents();
+  // Tile t: channel block c1 = t / nblocks, weights n0 = (t % nblocks) * NB.
+  auto issue = [&](uint32_t t, int st) {
+    const uint32_t c1 = g.f_nblocks.div(t), n0 = (t - c1 * g.nblocks) * g.NB;
+    const uint32_t valid = n0 < g.N ? min(g.NB, g.N - n0) : 0;
+    T *stage = reinterpret_cast<T *>(fzb_smem) + st * stage_elems;
+    if (threadIdx.x < 32) {
+      if (threadIdx.x == 0)
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(
+                         bulk::smem_u32(&bars[st])),
+                     "r"(valid * row_bytes)
+                     : "memory");
+      __syncwarp();
+      const T *base = src + (uint64_t)n0 * g.seg_stride + (uint64_t)c1 * g.L;
+      for (uint32_t r = threadIdx.x; r < valid; r += 32)
+        asm volatile(
+            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, "
+            "[%3];" ::"r"(bulk::smem_u32(stage + r * g.P)),
+            "l"(base + (uint64_t)r * g.seg_stride), "r"(row_bytes), "r"(bulk::smem_u32(&bars[st]))
+            : "memory");
+    }
+    // Padding weights: zero rows, written by the threads (read after the
+    // __syncthreads that ends the current tile).
+    for (uint32_t i = threadIdx.x; i < (g.NB - valid) * (g.L / V); i += kThreads) {
+      const uint32_t r = valid + i / (g.L / V), f = (i % (g.L / V)) * V;
+      *reinterpret_cast<uint4 *>(stage + r * g.P + f) = make_uint4(0, 0, 0, 0);
+    }
+  };
+  uint32_t k = 0;  // tiles of this CTA so far
+  if (blockIdx.x < g.ntiles) issue(blockIdx.x, 0);
+  __syncthreads();  // the first tile's zero rows are visible to every thread
+  bool ok = true, next_issued = false;
+  for (uint32_t t = blockIdx.x; t < g.ntiles; t += gridDim.x, ++k) {
+    const int st = (int)(k & 1);
+    next_issued = t + gridDim.x < g.ntiles;
+    if (next_issued) issue(t + gridDim.x, st ^ 1);
+    // Every thread polls the barrier; the give-up decision is made for the
+    // whole CTA, so no thread leaves the loop while others wait at a barrier.
+    const bool arrived = bulk::mbar_wait_bounded(&bars[st], (k >> 1) & 1);
+    if (__syncthreads_or(!arrived)) {
+      ok = false;
+      break;
+    }
+    const uint32_t c1 = g.f_nblocks.div(t), n0 = (t - c1 * g.nblocks) * g.NB;
+    const T *stage = reinterpret_cast<const T *>(fzb_smem) + st * stage_elems;
+    T *out = dst + ((uint64_t)c1 * g.HW * g.N1N0 + n0) * g.C0;
+    const uint32_t lane = threadIdx.x & 31, q = (lane >> 2) & ((1u << g.lq) - 1);
+    const uint32_t units = ((g.HW + 3) >> 2) << g.lnnb;
+    for (uint32_t un = threadIdx.x >> 5; un < units; un += kThreads / 32) {
+      const uint32_t hw = ((un >> g.lnnb) << 2) + (lane & 3);
+      if (hw >= g.HW) continue;
+      const uint32_t n = ((un & ((1u << g.lnnb) - 1)) << g.lnl) + (lane >> (2 + g.lq));
+      const uint32_t at = n * g.P + q * V * g.HW + hw;
+      Pack x;
+#pragma unroll
+      for (int j = 0; j < V; ++j) x.e[j] = stage[at + j * g.HW];
+      *reinterpret_cast<uint4 *>(out + (uint64_t)hw * g.N1N0 * g.C0 + n * g.C0 + q * V) = x.u;
+    }
+    __syncthreads();  // every read of this stage is done before it is refilled
+  }
+  if (!ok) {
+    if (threadIdx.x == 0) atomicExch(&g_fz_error, 1u);
+    // Wait (bounded) for the copies still in flight into either stage before
+    // the CTA's shared memory is released.
+    (void)bulk::mbar_wait_bounded(&bars[k & 1], (k >> 1) & 1);
+    if (next_issued) (void)bulk::mbar_wait_bounded(&bars[(k + 1) & 1], ((k + 1) >> 1) & 1);
+  }
+}
+
+#ifndef DCOPY_FZ_NCHW_BULK
+#define DCOPY_FZ_NCHW_BULK 0  // opt-in until measured against fz_vec_kernel
+#endif
+#ifndef DCOPY_FZ_BULK_NB
+#define DCOPY_FZ_BULK_NB 64  // weights per tile (a power of two)
+#endif
+constexpr size_t kBulkSmemMax = 96 * 1024;  // both stages
+
+// NCHW -> FRACTAL_Z through fz_nchw_bulk_kernel when every channel block is
+// whole, rows are 16-byte granules and both buffers are this GPU's memory.
+int run_nchw_bulk(void *dst, const void *src, int64_t n, int64_t c, int64_t hw, int eb,
+                  int64_t c0, cudaStream_t s, bool *taken) {
+  *taken = false;
+  if (!DCOPY_FZ_NCHW_BULK || (eb != 1 && eb != 2 && eb != 4)) return DCOPY_OK;
+  const int64_t V = 16 / eb;
+  if (c0 <= 0 || (c0 & (c0 - 1)) || c0 % V || c % c0 || (c * hw * eb) % 16) return DCOPY_OK;
+  if (((uintptr_t)dst | (uintptr_t)src) % 16) return DCOPY_OK;
+  if (!is_local_device_memory(src) || !is_local_device_memory(dst)) return DCOPY_OK;
+  const int64_t Q = c0 / V;
+  if (Q > 8) return DCOPY_OK;
+  const int64_t NL = 8 / Q, n1n0 = ge_ceil(n, kNi) * kNi, L = c0 * hw;
+  if ((uint64_t)L * eb >= (1u << 20) || n1n0 * c0 * hw > 0x7FFFFFFFll ||
+      n > 0x7FFFFFFFll || c * hw > 0x7FFFFFFFll)
+    return DCOPY_OK;
+  int64_t words = (L * eb + 3) / 4;
+  words += ((32 / NL - words % 32) % 32 + 32) % 32;
+  const int64_t P = words * 4 / eb;
+  int64_t nb = DCOPY_FZ_BULK_NB;
+  while (nb > NL && (n1n0 % nb || (size_t)(2 * nb * P * eb) > kBulkSmemMax)) nb /= 2;
+  if (n1n0 % nb || (size_t)(2 * nb * P * eb) > kBulkSmemMax || nb < NL) return DCOPY_OK;
+  FzBGeom g{};
+  g.N = (uint32_t)n;
+  g.HW = (uint32_t)hw;
+  g.C0 = (uint32_t)c0;
+  g.NB = (uint32_t)nb;
+  g.P = (uint32_t)P;
+  g.L = (uint32_t)L;
+  g.lq = log2_of((uint64_t)Q);
+  g.lnl = log2_of((uint64_t)NL);
+  g.lnnb = log2_of((uint64_t)(nb / NL));
+  g.nblocks = (uint32_t)(n1n0 / nb);
+  g.C1 = (uint32_t)(c / c0);
+  const uint64_t ntiles = (uint64_t)g.C1 * g.nblocks;
+  if (ntiles == 0 || ntiles > 0x7FFFFFFFull) return DCOPY_OK;
+  g.ntiles = (uint32_t)ntiles;
+  g.f_nblocks = FastDiv(g.nblocks);
+  g.seg_stride = (uint64_t)(c * hw);
+  g.N1N0 = (uint64_t)n1n0;
+  const size_t smem = (size_t)(2 * nb * P * eb);
+  void (*k)(unsigned char *, const unsigned char *, FzBGeom) =
+      eb == 1 ? fz_nchw_bulk_kernel<1> : eb == 2 ? fz_nchw_bulk_kernel<2> : fz_nchw_bulk_kernel<4>;
+  static std::atomic<bool> raised[3][128];
+  const int dev = current_device();
+  const int which = eb == 1 ? 0 : eb == 2 ? 1 : 2;
+  if (dev >= 0 && dev < 128 && !raised[which][dev].load()) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBulkSmemMax);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(fz_nchw_bulk_kernel)");
+    raised[which][dev] = true;
+  }
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kThreads, smem) != cudaSuccess ||
+      per_sm <= 0) {
+    (void)cudaGetLastError();
+    per_sm = 1;
+  }
+  *taken = true;
+  const uint32_t grid =
+      (uint32_t)std::min<uint64_t>(ntiles, (uint64_t)per_sm * (uint64_t)sm_count());
+  return launch(k, std::max(1u, grid), dim3(kThreads), smem, s, "fz_nchw_bulk_kernel",
+                static_cast<unsigned char *>(dst), static_cast<const unsigned char *>(src), g);
+}
+
+}  // namespace
+
+// ORs the bulk FRACTAL_Z kernel's give-up flag into *flag and clears it.
+int fz_error_take(uint32_t *flag) {
+  uint32_t v = 0, zero = 0;
+  DCOPY_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_fz_error, sizeof(uint32_t)));
+  DCOPY_CUDA_TRY(cudaMemcpyToSymbol(g_fz_error, &zero, sizeof(uint32_t)));
+  *flag |= v;
+  return DCOPY_OK;
+}
+
+namespace {
+
 // The vectorised path when its conditions hold; *taken = false otherwise.
 int run_vec(int32_t fmt, void *dst, const void *src, int64_t n, int64_t c, int64_t h, int64_t w,
             int eb, int64_t c0, bool to_fz, cudaStream_t s, bool *taken) {
@@ -530,6 +737,10 @@ int run_vec(int32_t fmt, void *dst, const void *src, int64_t n, int64_t c, int64
 int run_transpose(int32_t fmt, void *dst, const void *src, int64_t n, int64_t c, int64_t h,
                   int64_t w, int eb, int64_t c0, bool to_fz, cudaStream_t s) {
   bool taken = false;
+  if (fmt == kNchw && to_fz) {
+    const int brc = run_nchw_bulk(dst, src, n, c, h * w, eb, c0, s, &taken);
+    if (taken || brc) return brc;
+  }
   const int vrc = run_vec(fmt, dst, src, n, c, h, w, eb, c0, to_fz, s, &taken);
   if (taken || vrc) return vrc;
   const int64_t n1n0 = ge_ceil(n, kNi) * kNi, c1 = ge_ceil(c, c0), hw = h * w;

@@ -106,6 +106,8 @@ int tma_short_bursts(void *dst, const void *src, uint64_t rows, uint64_t row_byt
                      uint64_t src_pitch, uint64_t dst_pitch, cudaStream_t s, bool *taken);
 // ORs the bulk-copy kernel's give-up flag into *flag and clears it.
 int bulk_error_take(uint32_t *flag);
+// The same for the bulk-copied NCHW -> FRACTAL_Z kernel (fz.cu).
+int fz_error_take(uint32_t *flag);
 
 // The reference's pretranspose workflow (asc:144-146): x -> B with RunTiles<1>,
 // then B -> y with RunTiles<2>, through a B buffer of scratch_bytes bytes that

@@ -431,6 +431,7 @@ extern "C" int dcopy_tma_error(uint32_t *flag) {
   uint32_t zero = 0;
   DCOPY_CUDA_TRY(cudaMemcpyFromSymbol(flag, g_tma_error, sizeof(uint32_t)));
   DCOPY_CUDA_TRY(cudaMemcpyToSymbol(g_tma_error, &zero, sizeof(uint32_t)));
-  return bulk_error_take(flag);
+  const int rc = bulk_error_take(flag);
+  return rc ? rc : fz_error_take(flag);
   DCOPY_API_END
 }

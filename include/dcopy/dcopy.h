@@ -280,10 +280,12 @@ int dcopy_copy_nd(void *dst, const void *src, int ndim, const uint64_t *sizes,
  * on every box tried.  No counterpart in the reference. */
 int dcopy_set_nd_tma(int enable, int *previous);
 
-/* Reads and clears the current device's TMA box-copy error word: 1 when a
- * dcopy_copy_nd launch that took the tensor-copy path gave up waiting on one of
- * its own loads (that copy is then incomplete), else 0.  Synchronises the
- * device.  No counterpart in the reference. */
+/* Reads and clears the current device's TMA error words: 1 when a launch that
+ * moved data with the copy engine inside a kernel -- the tensor-copy box path,
+ * the bulk-copy burst path (both with dcopy_set_nd_tma(1)), or the bulk-copied
+ * NCHW -> FRACTAL_Z tiles -- gave up waiting on one of its own loads (that copy
+ * is then incomplete), else 0.  Synchronises the device.  No counterpart in the
+ * reference. */
 int dcopy_tma_error(uint32_t *flag);
 
 /* ---- ND <-> FRACTAL_NZ ------------------------------------------------------ */

@@ -171,3 +171,28 @@ def test_invalid_arguments(torch_cuda, dcopy, cuda_malloc):
             dcopy.from_fractal_z(out, buf, NHWC, [4, 4, 4, 4], 2, 0)
         assert e.value.code == dcopy.ERR_SHAPE_INVALID
         dcopy.to_fractal_z(out, buf, HWCN, [3, 3, 0, 16], 2, 16)  # empty: nothing written
+
+
+@pytest.mark.parametrize("weight,eb,c0", [
+    ((2048, 1024, 3, 3), 2, 16),   # 2048 tiles: every CTA cycles both stages several times
+    ((200, 64, 5, 5), 2, 16),      # padding weights 200..207 in the last tile
+    ((96, 64, 3, 3), 1, 32),
+    ((80, 32, 2, 2), 4, 16),       # even H*W
+    ((33, 16, 1, 1), 4, 8),
+    ((1000, 256, 7, 7), 2, 16),
+], ids=lambda v: "x".join(map(str, v)) if isinstance(v, tuple) else str(v))
+def test_nchw_to_fractal_z_bulk_tiles(torch_cuda, dcopy, oracle, weight, eb, c0):
+    """NCHW -> FRACTAL_Z with whole channel blocks: the bulk-copied, double-buffered tile
+    kernel, against the oracle byte for byte, with no give-up of its bounded waits."""
+    torch = torch_cuda
+    shape = list(weight)
+    src_np = _rand(int(np.prod(shape)) * eb, sum(shape) + eb)
+    expect = oracle.to_fz(_as(src_np, eb).reshape(shape), NCHW, c0)
+    src = torch.from_numpy(src_np).cuda()
+    dst = torch.full((expect.nbytes + 64,), CANARY, dtype=torch.uint8, device="cuda")
+    dcopy.to_fractal_z(dst, src, NCHW, shape, eb, c0)
+    torch.cuda.synchronize()
+    out = dst.cpu().numpy()
+    assert out[:expect.nbytes].tobytes() == expect.tobytes()
+    assert (out[expect.nbytes:] == CANARY).all()
+    assert dcopy.tma_error() == 0
