@@ -571,7 +571,7 @@ __global__ void __launch_bounds__(kThreads) fz_nchw_bulk_kernel(unsigned char *_
 }
 
 #ifndef DCOPY_FZ_NCHW_BULK
-#define DCOPY_FZ_NCHW_BULK 0  // opt-in until measured against fz_vec_kernel
+#define DCOPY_FZ_NCHW_BULK 1
 #endif
 #ifndef DCOPY_FZ_BULK_NB
 #define DCOPY_FZ_BULK_NB 64  // weights per tile (a power of two)
