@@ -477,10 +477,13 @@ struct FzBGeom {
 
 __device__ uint32_t g_fz_error;
 
-template <int EB>
+// kTensor: the whole tile arrives as one 2-D tensor copy (map: [N rows][C*HW],
+// box [NB][P]) instead of one bulk copy per row; rows past N come zero-filled.
+template <int EB, bool kTensor>
 __global__ void __launch_bounds__(kThreads) fz_nchw_bulk_kernel(unsigned char *__restrict__ dst_b,
                                                                 const unsigned char *__restrict__ src_b,
-                                                                FzBGeom g) {
+                                                                FzBGeom g,
+                                                                const __grid_constant__ CUtensorMap map) {
   using T = typename FzLane<EB>::T;
   constexpr int V = FzLane<EB>::V;
   union Pack {
@@ -507,6 +510,21 @@ __global__ void __launch_bounds__(kThreads) fz_nchw_bulk_kernel(unsigned char *_
     const uint32_t c1 = g.f_nblocks.div(t), n0 = (t - c1 * g.nblocks) * g.NB;
     const uint32_t valid = n0 < g.N ? min(g.NB, g.N - n0) : 0;
     T *stage = reinterpret_cast<T *>(fzb_smem) + st * stage_elems;
+    if constexpr (kTensor) {
+      if (threadIdx.x == 0) {
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(
+                         bulk::smem_u32(&bars[st])),
+                     "r"(stage_elems * EB)
+                     : "memory");
+        asm volatile(
+            "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+            " [%0], [%1, {%2, %3}], [%4];" ::"r"(bulk::smem_u32(stage)),
+            "l"(reinterpret_cast<uint64_t>(&map)), "r"((int32_t)(c1 * g.L)), "r"((int32_t)n0),
+            "r"(bulk::smem_u32(&bars[st]))
+            : "memory");
+      }
+      return;
+    }
     if (threadIdx.x < 32) {
       if (threadIdx.x == 0)
         asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(
@@ -573,6 +591,9 @@ __global__ void __launch_bounds__(kThreads) fz_nchw_bulk_kernel(unsigned char *_
 #ifndef DCOPY_FZ_NCHW_BULK
 #define DCOPY_FZ_NCHW_BULK 1
 #endif
+#ifndef DCOPY_FZ_NCHW_TMA
+#define DCOPY_FZ_NCHW_TMA 0  // 1: one 2-D tensor copy per tile when the pitch fits a TMA box
+#endif
 #ifndef DCOPY_FZ_BULK_NB
 #define DCOPY_FZ_BULK_NB 64  // weights per tile (a power of two)
 #endif
@@ -619,11 +640,30 @@ int run_nchw_bulk(void *dst, const void *src, int64_t n, int64_t c, int64_t hw, 
   g.seg_stride = (uint64_t)(c * hw);
   g.N1N0 = (uint64_t)n1n0;
   const size_t smem = (size_t)(2 * nb * P * eb);
-  void (*k)(unsigned char *, const unsigned char *, FzBGeom) =
-      eb == 1 ? fz_nchw_bulk_kernel<1> : eb == 2 ? fz_nchw_bulk_kernel<2> : fz_nchw_bulk_kernel<4>;
-  static std::atomic<bool> raised[3][128];
+  // The tensor copy: a [N][C*HW] view, box [nb][P] (P <= 256 elements).
+  CUtensorMap map{};
+  bool tensor = false;
+  // (Each stage must start on a 128-byte boundary for the tensor copy.)
+  if (DCOPY_FZ_NCHW_TMA && P <= 256 && nb <= 256 && (nb * P * eb) % 128 == 0) {
+    const uint64_t dims[2] = {(uint64_t)(c * hw), (uint64_t)n};
+    const uint64_t strides[1] = {(uint64_t)(c * hw * eb)};
+    const uint32_t box[2] = {(uint32_t)P, (uint32_t)nb};
+    const CUtensorMapDataType dt = eb == 1   ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                   : eb == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16
+                                             : CU_TENSOR_MAP_DATA_TYPE_UINT32;
+    tensor = encode_tiled_map(&map, dt, 2, const_cast<void *>(src), dims, strides, box,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+  }
+  using Kern = void (*)(unsigned char *, const unsigned char *, FzBGeom, const CUtensorMap);
+  Kern k = tensor ? (eb == 1   ? fz_nchw_bulk_kernel<1, true>
+                     : eb == 2 ? fz_nchw_bulk_kernel<2, true>
+                               : fz_nchw_bulk_kernel<4, true>)
+                  : (eb == 1   ? fz_nchw_bulk_kernel<1, false>
+                     : eb == 2 ? fz_nchw_bulk_kernel<2, false>
+                               : fz_nchw_bulk_kernel<4, false>);
+  static std::atomic<bool> raised[6][128];
   const int dev = current_device();
-  const int which = eb == 1 ? 0 : eb == 2 ? 1 : 2;
+  const int which = (eb == 1 ? 0 : eb == 2 ? 1 : 2) + (tensor ? 3 : 0);
   if (dev >= 0 && dev < 128 && !raised[which][dev].load()) {
     const cudaError_t e =
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBulkSmemMax);
@@ -640,7 +680,8 @@ int run_nchw_bulk(void *dst, const void *src, int64_t n, int64_t c, int64_t hw, 
   const uint32_t grid =
       (uint32_t)std::min<uint64_t>(ntiles, (uint64_t)per_sm * (uint64_t)sm_count());
   return launch(k, std::max(1u, grid), dim3(kThreads), smem, s, "fz_nchw_bulk_kernel",
-                static_cast<unsigned char *>(dst), static_cast<const unsigned char *>(src), g);
+                static_cast<unsigned char *>(dst), static_cast<const unsigned char *>(src), g,
+                map);
 }
 
 }  // namespace

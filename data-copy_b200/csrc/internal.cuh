@@ -1,6 +1,7 @@
 // Host-side helpers shared between translation units of libdcopy.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -96,6 +97,13 @@ int nd_copy_tma(void *dst, const void *src, int ndim, const uint64_t *sizes,
 // otherwise nothing is launched.
 int bulk_bursts(void *dst, const void *src, uint64_t rows, uint64_t row_bytes,
                 uint64_t src_pitch, uint64_t dst_pitch, cudaStream_t s, bool *taken);
+// A tiled TMA tensor map (cuTensorMapEncodeTiled through the runtime's driver
+// entry point, no swizzle, no interleave, zero fill): dims innermost first,
+// strides[i] = bytes between steps of dim i+1 (rank - 1 entries).  False when
+// the driver refuses it or lacks the call.
+bool encode_tiled_map(CUtensorMap *map, CUtensorMapDataType dtype, uint32_t rank, void *base,
+                      const uint64_t *dims, const uint64_t *strides, const uint32_t *box,
+                      CUtensorMapL2promotion promotion);
 // Whether the TMA paths are selected (dcopy_set_nd_tma / DCOPY_ND_TMA): the
 // tensor-copy box kernel and the bulk-copy and tensor-copy 2-D burst kernels.
 bool tma_paths_selected();

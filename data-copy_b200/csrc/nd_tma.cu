@@ -388,6 +388,24 @@ int tma_box_copy(void *dst, const void *src, int ndim, const uint64_t *sizes,
 
 bool tma_paths_selected() { return tma_selected(); }
 
+bool encode_tiled_map(CUtensorMap *map, CUtensorMapDataType dtype, uint32_t rank, void *base,
+                      const uint64_t *dims, const uint64_t *strides, const uint32_t *box,
+                      CUtensorMapL2promotion promotion) {
+  PfnEncodeTiled encode = encode_fn();
+  if (!encode || rank < 1 || rank > 5) return false;
+  cuuint64_t d[5], st[5];
+  cuuint32_t b[5], e[5];
+  for (uint32_t i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+    if (i + 1 < rank) st[i] = strides[i];
+  }
+  return encode(map, dtype, rank, base, d, st, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_NONE, promotion,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int nd_copy_tma(void *dst, const void *src, int ndim, const uint64_t *sizes,
                 const int64_t *src_strides, const int64_t *dst_strides, uint32_t eb,
                 dcopy_stream_t stream, bool *taken) {

@@ -19,9 +19,6 @@
 #ifndef DCOPY_P2P_BULK
 #define DCOPY_P2P_BULK 1
 #endif
-#ifndef DCOPY_P2P_BULK_PULL
-#define DCOPY_P2P_BULK_PULL 0
-#endif
 
 namespace dcopy {
 namespace {
@@ -263,14 +260,10 @@ extern "C" int dcopy_p2p_copy(void *dst, const void *src, uint64_t bytes, dcopy_
   // Push to another GPU with the bulk-copy pipeline when everything is 16-byte
   // granular and the source is this GPU's memory; anything else (pulls, odd
   // sizes, local copies) takes the load/store kernel.
-  const bool granular = ((uintptr_t)dst | (uintptr_t)src | bytes) % 16 == 0;
-  const bool src_local = is_local_device_memory(src), dst_local = is_local_device_memory(dst);
-  if (DCOPY_P2P_BULK && granular && src_local && !dst_local)
-    return launch_bulk_push(dst, src, bytes, s);
-  // With DCOPY_P2P_BULK_PULL, a pull (peer source, this GPU's destination)
-  // through the same pipeline: bulk loads from the peer (no multicast), bulk
-  // stores into local memory.
-  if (DCOPY_P2P_BULK_PULL && granular && !src_local && dst_local)
+  // (A bulk-copy pull from the peer measured 666 GB/s per direction in an
+  // exchange against 643 for the load kernel and 702 for this push.)
+  if (DCOPY_P2P_BULK && ((uintptr_t)dst | (uintptr_t)src | bytes) % 16 == 0 &&
+      is_local_device_memory(src) && !is_local_device_memory(dst))
     return launch_bulk_push(dst, src, bytes, s);
   return copy_linear(dst, src, bytes, s);
   DCOPY_API_END
