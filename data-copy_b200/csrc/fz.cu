@@ -588,11 +588,122 @@ __global__ void __launch_bounds__(kThreads) fz_nchw_bulk_kernel(unsigned char *_
   }
 }
 
+// ---- FRACTAL_Z -> NCHW, the mirror of fz_nchw_bulk_kernel -------------------------
+//
+// A tile is NB weights of one channel block.  Its FRACTAL_Z source is HW
+// contiguous runs of NB*C0 elements (one per hw), bulk-copied into one of two
+// "run" stages while the other is processed.  Each warp reads 16-byte FRACTAL_Z
+// vectors (hw, n, q) from the run stage (4 consecutive hw x the C0/V vectors x
+// NL rows: four 128-byte segments per warp read) and scatters their V elements
+// into a row stage laid out as the NCHW rows (n, c0*HW + hw) with the bank-spread
+// pitch of the other direction, so the scatter is conflict-free for odd HW.  The
+// valid rows then leave by bulk stores (one per row); the row stage is reused
+// once those stores have read it.  Waits are bounded as in the other direction.
+template <int EB>
+__global__ void __launch_bounds__(kThreads) fz_to_nchw_bulk_kernel(unsigned char *__restrict__ dst_b,
+                                                                   const unsigned char *__restrict__ src_b,
+                                                                   FzBGeom g) {
+  using T = typename FzLane<EB>::T;
+  constexpr int V = FzLane<EB>::V;
+  union Pack {
+    uint4 u;
+    T e[V];
+  };
+  extern __shared__ __align__(128) unsigned char fzr_smem[];
+  __shared__ __align__(8) uint64_t bars[2];
+  T *dst = reinterpret_cast<T *>(dst_b);
+  const T *src = reinterpret_cast<const T *>(src_b);
+  const uint32_t run = g.NB * g.C0;          // elements of one hw run
+  const uint32_t run_stage = g.HW * run;     // elements of one run stage
+  T *rows = reinterpret_cast<T *>(fzr_smem) + 2 * run_stage;  // NB x P row stage
+  pdl_trigger_at_entry();
+  if (threadIdx.x == 0) {
+    bulk::mbar_init(&bars[0], 1);
+    bulk::mbar_init(&bars[1], 1);
+    bulk::mbar_init_fence();
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_launch_dependents();
+  auto issue = [&](uint32_t t, int st) {
+    if (threadIdx.x >= 32) return;
+    const uint32_t c1 = g.f_nblocks.div(t), n0 = (t - c1 * g.nblocks) * g.NB;
+    T *stage = reinterpret_cast<T *>(fzr_smem) + st * run_stage;
+    if (threadIdx.x == 0)
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(
+                       bulk::smem_u32(&bars[st])),
+                   "r"(run_stage * EB)
+                   : "memory");
+    __syncwarp();
+    const T *base = src + ((uint64_t)c1 * g.HW * g.N1N0 + n0) * g.C0;
+    for (uint32_t hw = threadIdx.x; hw < g.HW; hw += 32)
+      asm volatile(
+          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, "
+          "[%3];" ::"r"(bulk::smem_u32(stage + hw * run)),
+          "l"(base + (uint64_t)hw * g.N1N0 * g.C0), "r"(run * EB), "r"(bulk::smem_u32(&bars[st]))
+          : "memory");
+  };
+  uint32_t k = 0;
+  if (blockIdx.x < g.ntiles) issue(blockIdx.x, 0);
+  bool ok = true, next_issued = false;
+  for (uint32_t t = blockIdx.x; t < g.ntiles; t += gridDim.x, ++k) {
+    const int st = (int)(k & 1);
+    next_issued = t + gridDim.x < g.ntiles;
+    if (next_issued) issue(t + gridDim.x, st ^ 1);
+    const bool arrived = bulk::mbar_wait_bounded(&bars[st], (k >> 1) & 1);
+    // The previous tile's row stores must have read the row stage before it is
+    // overwritten (they were issued by warp 0).
+    if (threadIdx.x < 32) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+    if (__syncthreads_or(!arrived)) {
+      ok = false;
+      break;
+    }
+    const uint32_t c1 = g.f_nblocks.div(t), n0 = (t - c1 * g.nblocks) * g.NB;
+    const uint32_t valid = n0 < g.N ? min(g.NB, g.N - n0) : 0;
+    const T *stage = reinterpret_cast<const T *>(fzr_smem) + st * run_stage;
+    const uint32_t lane = threadIdx.x & 31, q = (lane >> 2) & ((1u << g.lq) - 1);
+    const uint32_t units = ((g.HW + 3) >> 2) << g.lnnb;
+    for (uint32_t un = threadIdx.x >> 5; un < units; un += kThreads / 32) {
+      const uint32_t hw = ((un >> g.lnnb) << 2) + (lane & 3);
+      const uint32_t n = ((un & ((1u << g.lnnb) - 1)) << g.lnl) + (lane >> (2 + g.lq));
+      if (hw >= g.HW || n >= valid) continue;
+      Pack x;
+      x.u = *reinterpret_cast<const uint4 *>(stage + hw * run + n * g.C0 + q * V);
+      const uint32_t at = n * g.P + q * V * g.HW + hw;
+#pragma unroll
+      for (int j = 0; j < V; ++j) rows[at + j * g.HW] = x.e[j];
+    }
+    // Generic-proxy writes of the row stage, then bulk stores read it.
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      T *out = dst + (uint64_t)n0 * g.seg_stride + (uint64_t)c1 * g.L;
+      for (uint32_t r = threadIdx.x; r < valid; r += 32)
+        bulk::store(out + (uint64_t)r * g.seg_stride, rows + r * g.P, g.L * EB);
+      bulk::commit();
+    }
+  }
+  if (!ok) {
+    if (threadIdx.x == 0) atomicExch(&g_fz_error, 1u);
+    (void)bulk::mbar_wait_bounded(&bars[k & 1], (k >> 1) & 1);
+    if (next_issued) (void)bulk::mbar_wait_bounded(&bars[(k + 1) & 1], ((k + 1) >> 1) & 1);
+  }
+  if (threadIdx.x < 32) bulk::wait_all();
+}
+
 #ifndef DCOPY_FZ_NCHW_BULK
 #define DCOPY_FZ_NCHW_BULK 1
 #endif
+#ifndef DCOPY_FZ_NCHW_BULK_FROM
+#define DCOPY_FZ_NCHW_BULK_FROM 0  // FRACTAL_Z -> NCHW through fz_to_nchw_bulk_kernel
+#endif
 #ifndef DCOPY_FZ_NCHW_TMA
-#define DCOPY_FZ_NCHW_TMA 0  // 1: one 2-D tensor copy per tile when the pitch fits a TMA box
+// 1: one 2-D tensor copy per tile of 1- or 2-byte elements when the pitch fits a
+// TMA box.  Measured on B200 (NCHW -> FRACTAL_Z [2048,2048,3,3], three rounds):
+// fp16 5263-5266 GB/s against 4606-4608 with one bulk copy per row; fp32 tiles
+// were 7 % slower as a tensor copy (5263-5266 against 5670-5673), so 4-byte
+// elements keep the row copies.
+#define DCOPY_FZ_NCHW_TMA 1
 #endif
 #ifndef DCOPY_FZ_BULK_NB
 #define DCOPY_FZ_BULK_NB 64  // weights per tile (a power of two)
@@ -644,7 +755,7 @@ int run_nchw_bulk(void *dst, const void *src, int64_t n, int64_t c, int64_t hw, 
   CUtensorMap map{};
   bool tensor = false;
   // (Each stage must start on a 128-byte boundary for the tensor copy.)
-  if (DCOPY_FZ_NCHW_TMA && P <= 256 && nb <= 256 && (nb * P * eb) % 128 == 0) {
+  if (DCOPY_FZ_NCHW_TMA && eb <= 2 && P <= 256 && nb <= 256 && (nb * P * eb) % 128 == 0) {
     const uint64_t dims[2] = {(uint64_t)(c * hw), (uint64_t)n};
     const uint64_t strides[1] = {(uint64_t)(c * hw * eb)};
     const uint32_t box[2] = {(uint32_t)P, (uint32_t)nb};
@@ -682,6 +793,73 @@ int run_nchw_bulk(void *dst, const void *src, int64_t n, int64_t c, int64_t hw, 
   return launch(k, std::max(1u, grid), dim3(kThreads), smem, s, "fz_nchw_bulk_kernel",
                 static_cast<unsigned char *>(dst), static_cast<const unsigned char *>(src), g,
                 map);
+}
+
+// FRACTAL_Z -> NCHW through fz_to_nchw_bulk_kernel under the same conditions.
+int run_nchw_bulk_from(void *dst, const void *src, int64_t n, int64_t c, int64_t hw, int eb,
+                       int64_t c0, cudaStream_t s, bool *taken) {
+  *taken = false;
+  if (!DCOPY_FZ_NCHW_BULK_FROM || (eb != 1 && eb != 2 && eb != 4)) return DCOPY_OK;
+  const int64_t V = 16 / eb;
+  if (c0 <= 0 || (c0 & (c0 - 1)) || c0 % V || c % c0 || (c * hw * eb) % 16) return DCOPY_OK;
+  if (((uintptr_t)dst | (uintptr_t)src) % 16) return DCOPY_OK;
+  if (!is_local_device_memory(src) || !is_local_device_memory(dst)) return DCOPY_OK;
+  const int64_t Q = c0 / V;
+  if (Q > 8) return DCOPY_OK;
+  const int64_t NL = 8 / Q, n1n0 = ge_ceil(n, kNi) * kNi, L = c0 * hw;
+  if ((uint64_t)L * eb >= (1u << 20) || n1n0 * c0 * hw > 0x7FFFFFFFll ||
+      n > 0x7FFFFFFFll || c * hw > 0x7FFFFFFFll || hw > 0xFFFF)
+    return DCOPY_OK;
+  int64_t words = (L * eb + 3) / 4;
+  words += ((32 / NL - words % 32) % 32 + 32) % 32;
+  const int64_t P = words * 4 / eb;
+  auto smem_of = [&](int64_t nb) { return (size_t)((2 * hw * nb * c0 + nb * P) * eb); };
+  int64_t nb = DCOPY_FZ_BULK_NB;
+  while (nb > NL && (n1n0 % nb || smem_of(nb) > kBulkSmemMax)) nb /= 2;
+  if (n1n0 % nb || smem_of(nb) > kBulkSmemMax || nb < NL) return DCOPY_OK;
+  if ((nb * c0 * eb) % 16) return DCOPY_OK;
+  FzBGeom g{};
+  g.N = (uint32_t)n;
+  g.HW = (uint32_t)hw;
+  g.C0 = (uint32_t)c0;
+  g.NB = (uint32_t)nb;
+  g.P = (uint32_t)P;
+  g.L = (uint32_t)L;
+  g.lq = log2_of((uint64_t)Q);
+  g.lnl = log2_of((uint64_t)NL);
+  g.lnnb = log2_of((uint64_t)(nb / NL));
+  g.nblocks = (uint32_t)(n1n0 / nb);
+  g.C1 = (uint32_t)(c / c0);
+  const uint64_t ntiles = (uint64_t)g.C1 * g.nblocks;
+  if (ntiles == 0 || ntiles > 0x7FFFFFFFull) return DCOPY_OK;
+  g.ntiles = (uint32_t)ntiles;
+  g.f_nblocks = FastDiv(g.nblocks);
+  g.seg_stride = (uint64_t)(c * hw);
+  g.N1N0 = (uint64_t)n1n0;
+  const size_t smem = smem_of(nb);
+  using Kern = void (*)(unsigned char *, const unsigned char *, FzBGeom);
+  Kern k = eb == 1 ? fz_to_nchw_bulk_kernel<1>
+           : eb == 2 ? fz_to_nchw_bulk_kernel<2> : fz_to_nchw_bulk_kernel<4>;
+  static std::atomic<bool> raised[3][128];
+  const int dev = current_device();
+  const int which = eb == 1 ? 0 : eb == 2 ? 1 : 2;
+  if (dev >= 0 && dev < 128 && !raised[which][dev].load()) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBulkSmemMax);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(fz_to_nchw_bulk_kernel)");
+    raised[which][dev] = true;
+  }
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kThreads, smem) != cudaSuccess ||
+      per_sm <= 0) {
+    (void)cudaGetLastError();
+    per_sm = 1;
+  }
+  *taken = true;
+  const uint32_t grid =
+      (uint32_t)std::min<uint64_t>(ntiles, (uint64_t)per_sm * (uint64_t)sm_count());
+  return launch(k, std::max(1u, grid), dim3(kThreads), smem, s, "fz_to_nchw_bulk_kernel",
+                static_cast<unsigned char *>(dst), static_cast<const unsigned char *>(src), g);
 }
 
 }  // namespace
@@ -778,8 +956,9 @@ int run_vec(int32_t fmt, void *dst, const void *src, int64_t n, int64_t c, int64
 int run_transpose(int32_t fmt, void *dst, const void *src, int64_t n, int64_t c, int64_t h,
                   int64_t w, int eb, int64_t c0, bool to_fz, cudaStream_t s) {
   bool taken = false;
-  if (fmt == kNchw && to_fz) {
-    const int brc = run_nchw_bulk(dst, src, n, c, h * w, eb, c0, s, &taken);
+  if (fmt == kNchw) {
+    const int brc = to_fz ? run_nchw_bulk(dst, src, n, c, h * w, eb, c0, s, &taken)
+                          : run_nchw_bulk_from(dst, src, n, c, h * w, eb, c0, s, &taken);
     if (taken || brc) return brc;
   }
   const int vrc = run_vec(fmt, dst, src, n, c, h, w, eb, c0, to_fz, s, &taken);
