@@ -695,7 +695,12 @@ __global__ void __launch_bounds__(kThreads) fz_to_nchw_bulk_kernel(unsigned char
 #define DCOPY_FZ_NCHW_BULK 1
 #endif
 #ifndef DCOPY_FZ_NCHW_BULK_FROM
-#define DCOPY_FZ_NCHW_BULK_FROM 0  // FRACTAL_Z -> NCHW through fz_to_nchw_bulk_kernel
+// FRACTAL_Z -> NCHW through fz_to_nchw_bulk_kernel for 4-byte elements.  Measured
+// on B200 ([2048,2048,3,3], three rounds, GB/s against fz_vec_kernel): fp32
+// 5571-5651 vs 4956-5005; fp16 3832-3880 vs 4604-4608, int8 2748-2836 vs
+// 3225-3356, fp16 5x5 3794 vs 4184-4265 -- so 1- and 2-byte elements keep the
+// vector kernel.
+#define DCOPY_FZ_NCHW_BULK_FROM 1
 #endif
 #ifndef DCOPY_FZ_NCHW_TMA
 // 1: one 2-D tensor copy per tile of 1- or 2-byte elements when the pitch fits a
@@ -799,7 +804,7 @@ int run_nchw_bulk(void *dst, const void *src, int64_t n, int64_t c, int64_t hw, 
 int run_nchw_bulk_from(void *dst, const void *src, int64_t n, int64_t c, int64_t hw, int eb,
                        int64_t c0, cudaStream_t s, bool *taken) {
   *taken = false;
-  if (!DCOPY_FZ_NCHW_BULK_FROM || (eb != 1 && eb != 2 && eb != 4)) return DCOPY_OK;
+  if (!DCOPY_FZ_NCHW_BULK_FROM || eb != 4) return DCOPY_OK;
   const int64_t V = 16 / eb;
   if (c0 <= 0 || (c0 & (c0 - 1)) || c0 % V || c % c0 || (c * hw * eb) % 16) return DCOPY_OK;
   if (((uintptr_t)dst | (uintptr_t)src) % 16) return DCOPY_OK;
@@ -838,16 +843,14 @@ int run_nchw_bulk_from(void *dst, const void *src, int64_t n, int64_t c, int64_t
   g.N1N0 = (uint64_t)n1n0;
   const size_t smem = smem_of(nb);
   using Kern = void (*)(unsigned char *, const unsigned char *, FzBGeom);
-  Kern k = eb == 1 ? fz_to_nchw_bulk_kernel<1>
-           : eb == 2 ? fz_to_nchw_bulk_kernel<2> : fz_to_nchw_bulk_kernel<4>;
-  static std::atomic<bool> raised[3][128];
+  Kern k = fz_to_nchw_bulk_kernel<4>;
+  static std::atomic<bool> raised[128];
   const int dev = current_device();
-  const int which = eb == 1 ? 0 : eb == 2 ? 1 : 2;
-  if (dev >= 0 && dev < 128 && !raised[which][dev].load()) {
+  if (dev >= 0 && dev < 128 && !raised[dev].load()) {
     const cudaError_t e =
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBulkSmemMax);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(fz_to_nchw_bulk_kernel)");
-    raised[which][dev] = true;
+    raised[dev] = true;
   }
   int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kThreads, smem) != cudaSuccess ||
