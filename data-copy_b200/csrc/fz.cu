@@ -20,6 +20,9 @@
 #include <algorithm>
 #include <atomic>
 #include <cstring>
+#include <map>
+#include <mutex>
+#include <tuple>
 
 #include "bulk.cuh"
 #include "common.cuh"
@@ -691,6 +694,95 @@ __global__ void __launch_bounds__(kThreads) fz_to_nchw_bulk_kernel(unsigned char
   if (threadIdx.x < 32) bulk::wait_all();
 }
 
+// FRACTAL_Z -> NCHW gathering row vectors straight from the run stage: the HW
+// runs of a tile arrive as in fz_to_nchw_bulk_kernel (run pitch R chosen on the
+// host to spread this kernel's bank pattern); thread u builds the 16-byte row
+// vector v of weight n (u = n * L/V + v) from the V elements (c0, hw) it covers,
+// each at hw*R + n*C0 + c0, and stores it to the NCHW row.
+template <int EB>
+__global__ void __launch_bounds__(kThreads) fz_to_nchw_gather_kernel(unsigned char *__restrict__ dst_b,
+                                                                     const unsigned char *__restrict__ src_b,
+                                                                     FzBGeom g, uint32_t R,
+                                                                     FastDiv f_vpr, FastDiv f_hw) {
+  using T = typename FzLane<EB>::T;
+  constexpr int V = FzLane<EB>::V;
+  union Pack {
+    uint4 u;
+    T e[V];
+  };
+  extern __shared__ __align__(128) unsigned char fzg_smem[];
+  __shared__ __align__(8) uint64_t bars[2];
+  T *dst = reinterpret_cast<T *>(dst_b);
+  const T *src = reinterpret_cast<const T *>(src_b);
+  const uint32_t run = g.NB * g.C0;
+  const uint32_t run_stage = g.HW * R;
+  pdl_trigger_at_entry();
+  if (threadIdx.x == 0) {
+    bulk::mbar_init(&bars[0], 1);
+    bulk::mbar_init(&bars[1], 1);
+    bulk::mbar_init_fence();
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_launch_dependents();
+  auto issue = [&](uint32_t t, int st) {
+    if (threadIdx.x >= 32) return;
+    const uint32_t c1 = g.f_nblocks.div(t), n0 = (t - c1 * g.nblocks) * g.NB;
+    T *stage = reinterpret_cast<T *>(fzg_smem) + st * run_stage;
+    if (threadIdx.x == 0)
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(
+                       bulk::smem_u32(&bars[st])),
+                   "r"(g.HW * run * EB)
+                   : "memory");
+    __syncwarp();
+    const T *base = src + ((uint64_t)c1 * g.HW * g.N1N0 + n0) * g.C0;
+    for (uint32_t hw = threadIdx.x; hw < g.HW; hw += 32)
+      asm volatile(
+          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, "
+          "[%3];" ::"r"(bulk::smem_u32(stage + hw * R)),
+          "l"(base + (uint64_t)hw * g.N1N0 * g.C0), "r"(run * EB), "r"(bulk::smem_u32(&bars[st]))
+          : "memory");
+  };
+  const uint32_t vpr = g.L / V;
+  uint32_t k = 0;
+  if (blockIdx.x < g.ntiles) issue(blockIdx.x, 0);
+  bool ok = true, next_issued = false;
+  for (uint32_t t = blockIdx.x; t < g.ntiles; t += gridDim.x, ++k) {
+    const int st = (int)(k & 1);
+    next_issued = t + gridDim.x < g.ntiles;
+    if (next_issued) issue(t + gridDim.x, st ^ 1);
+    const bool arrived = bulk::mbar_wait_bounded(&bars[st], (k >> 1) & 1);
+    if (__syncthreads_or(!arrived)) {
+      ok = false;
+      break;
+    }
+    const uint32_t c1 = g.f_nblocks.div(t), n0 = (t - c1 * g.nblocks) * g.NB;
+    const uint32_t valid = n0 < g.N ? min(g.NB, g.N - n0) : 0;
+    const T *stage = reinterpret_cast<const T *>(fzg_smem) + st * run_stage;
+    T *out = dst + (uint64_t)n0 * g.seg_stride + (uint64_t)c1 * g.L;
+    for (uint32_t u = threadIdx.x; u < valid * vpr; u += kThreads) {
+      const uint32_t n = f_vpr.div(u), e0 = (u - n * vpr) * V;
+      uint32_t c0 = f_hw.div(e0), hw = e0 - c0 * g.HW;
+      Pack x;
+#pragma unroll
+      for (int j = 0; j < V; ++j) {
+        x.e[j] = stage[hw * R + n * g.C0 + c0];
+        if (++hw == g.HW) {
+          hw = 0;
+          ++c0;
+        }
+      }
+      *reinterpret_cast<uint4 *>(out + (uint64_t)n * g.seg_stride + e0) = x.u;
+    }
+    __syncthreads();  // every read of this stage is done before it is refilled
+  }
+  if (!ok) {
+    if (threadIdx.x == 0) atomicExch(&g_fz_error, 1u);
+    (void)bulk::mbar_wait_bounded(&bars[k & 1], (k >> 1) & 1);
+    if (next_issued) (void)bulk::mbar_wait_bounded(&bars[(k + 1) & 1], ((k + 1) >> 1) & 1);
+  }
+}
+
 #ifndef DCOPY_FZ_NCHW_BULK
 #define DCOPY_FZ_NCHW_BULK 1
 #endif
@@ -701,6 +793,9 @@ __global__ void __launch_bounds__(kThreads) fz_to_nchw_bulk_kernel(unsigned char
 // 3225-3356, fp16 5x5 3794 vs 4184-4265 -- so 1- and 2-byte elements keep the
 // vector kernel.
 #define DCOPY_FZ_NCHW_BULK_FROM 1
+#endif
+#ifndef DCOPY_FZ_FROM_GATHER
+#define DCOPY_FZ_FROM_GATHER 0  // 1/2-byte FRACTAL_Z -> NCHW through fz_to_nchw_gather_kernel
 #endif
 #ifndef DCOPY_FZ_NCHW_TMA
 // 1: one 2-D tensor copy per tile of 1- or 2-byte elements when the pitch fits a
@@ -800,11 +895,100 @@ int run_nchw_bulk(void *dst, const void *src, int64_t n, int64_t c, int64_t hw, 
                 map);
 }
 
+// Run pitch (elements) for fz_to_nchw_gather_kernel: at least NB*C0, a multiple
+// of 16 bytes, with the word residue mod 32 whose simulated warp accesses (the
+// first tile's row vectors) hit the fewest words per bank.
+uint32_t gather_run_pitch_search(int eb, int64_t c0, int64_t hw, int64_t nb) {
+  const int64_t V = 16 / eb, L = c0 * hw, vpr = L / V, run = nb * c0;
+  const int64_t base_w = run * eb / 4;
+  int64_t best_w = base_w, best_cost = -1;
+  for (int64_t res = 0; res < 32; res += 4) {
+    const int64_t rw = base_w + ((res - base_w % 32) % 32 + 32) % 32;
+    int64_t cost = 0;
+    for (int64_t u0 = 0; u0 < nb * vpr; u0 += 32)
+      for (int64_t j = 0; j < V; ++j) {
+        int64_t words[32], banks_max = 0;
+        int cnt = 0;
+        for (int64_t lane = 0; lane < 32 && u0 + lane < nb * vpr; ++lane) {
+          const int64_t u = u0 + lane, n = u / vpr, e = (u % vpr) * V + j;
+          const int64_t c = e / hw, h = e % hw;
+          words[cnt++] = ((h * rw * 4) + (n * c0 + c) * eb) / 4;
+        }
+        for (int b = 0; b < 32; ++b) {  // distinct words in bank b
+          int64_t seen[32];
+          int ns = 0;
+          for (int i = 0; i < cnt; ++i)
+            if (words[i] % 32 == b) {
+              bool dup = false;
+              for (int q = 0; q < ns; ++q) dup = dup || seen[q] == words[i];
+              if (!dup) seen[ns++] = words[i];
+            }
+          banks_max = std::max<int64_t>(banks_max, ns);
+        }
+        cost += banks_max;
+      }
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best_w = rw;
+    }
+  }
+  return (uint32_t)(best_w * 4 / eb);
+}
+
+// The search above, done once per (eb, c0, hw, nb).
+uint32_t gather_run_pitch(int eb, int64_t c0, int64_t hw, int64_t nb) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int64_t, int64_t, int64_t>, uint32_t> cache;
+  const auto key = std::make_tuple(eb, c0, hw, nb);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    const auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  const uint32_t r = gather_run_pitch_search(eb, c0, hw, nb);
+  std::lock_guard<std::mutex> lock(mu);
+  cache[key] = r;
+  return r;
+}
+
+int launch_from_gather(void *dst, const void *src, const FzBGeom &g, int eb, int64_t c0,
+                       int64_t hw, int64_t nb, cudaStream_t s, bool *taken) {
+  const uint32_t R = gather_run_pitch(eb, c0, hw, nb);
+  const size_t smem = (size_t)2 * hw * R * eb;
+  if (smem > kBulkSmemMax) return DCOPY_OK;
+  using Kern = void (*)(unsigned char *, const unsigned char *, FzBGeom, uint32_t, FastDiv,
+                        FastDiv);
+  Kern k = eb == 1 ? fz_to_nchw_gather_kernel<1> : fz_to_nchw_gather_kernel<2>;
+  static std::atomic<bool> raised[2][128];
+  const int dev = current_device();
+  const int which = eb == 1 ? 0 : 1;
+  if (dev >= 0 && dev < 128 && !raised[which][dev].load()) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBulkSmemMax);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(fz_to_nchw_gather_kernel)");
+    raised[which][dev] = true;
+  }
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kThreads, smem) != cudaSuccess ||
+      per_sm <= 0) {
+    (void)cudaGetLastError();
+    per_sm = 1;
+  }
+  *taken = true;
+  const uint32_t grid =
+      (uint32_t)std::min<uint64_t>(g.ntiles, (uint64_t)per_sm * (uint64_t)sm_count());
+  const uint32_t V = 16 / (uint32_t)eb;
+  return launch(k, std::max(1u, grid), dim3(kThreads), smem, s, "fz_to_nchw_gather_kernel",
+                static_cast<unsigned char *>(dst), static_cast<const unsigned char *>(src), g, R,
+                FastDiv(g.L / V), FastDiv(g.HW));
+}
+
 // FRACTAL_Z -> NCHW through fz_to_nchw_bulk_kernel under the same conditions.
 int run_nchw_bulk_from(void *dst, const void *src, int64_t n, int64_t c, int64_t hw, int eb,
                        int64_t c0, cudaStream_t s, bool *taken) {
   *taken = false;
-  if (!DCOPY_FZ_NCHW_BULK_FROM || eb != 4) return DCOPY_OK;
+  const bool gather = DCOPY_FZ_FROM_GATHER && eb <= 2;
+  if (!gather && (!DCOPY_FZ_NCHW_BULK_FROM || eb != 4)) return DCOPY_OK;
   const int64_t V = 16 / eb;
   if (c0 <= 0 || (c0 & (c0 - 1)) || c0 % V || c % c0 || (c * hw * eb) % 16) return DCOPY_OK;
   if (((uintptr_t)dst | (uintptr_t)src) % 16) return DCOPY_OK;
@@ -841,6 +1025,7 @@ int run_nchw_bulk_from(void *dst, const void *src, int64_t n, int64_t c, int64_t
   g.f_nblocks = FastDiv(g.nblocks);
   g.seg_stride = (uint64_t)(c * hw);
   g.N1N0 = (uint64_t)n1n0;
+  if (gather) return launch_from_gather(dst, src, g, eb, c0, hw, nb, s, taken);
   const size_t smem = smem_of(nb);
   using Kern = void (*)(unsigned char *, const unsigned char *, FzBGeom);
   Kern k = fz_to_nchw_bulk_kernel<4>;
