@@ -795,7 +795,11 @@ __global__ void __launch_bounds__(kThreads) fz_to_nchw_gather_kernel(unsigned ch
 #define DCOPY_FZ_NCHW_BULK_FROM 1
 #endif
 #ifndef DCOPY_FZ_FROM_GATHER
-#define DCOPY_FZ_FROM_GATHER 0  // 1/2-byte FRACTAL_Z -> NCHW through fz_to_nchw_gather_kernel
+// 2-byte FRACTAL_Z -> NCHW through fz_to_nchw_gather_kernel.  Measured on B200
+// (three rounds, GB/s against fz_vec_kernel): fp16 [2048,2048,3,3] 5266 vs
+// 4608-4610, fp16 [2048,1024,5,5] 5063-5122 vs 4100-4267; int8 (c0 32) was
+// slower (3074-3206 vs 3351-3356) and keeps the vector kernel.
+#define DCOPY_FZ_FROM_GATHER 1
 #endif
 #ifndef DCOPY_FZ_NCHW_TMA
 // 1: one 2-D tensor copy per tile of 1- or 2-byte elements when the pitch fits a
@@ -958,15 +962,15 @@ int launch_from_gather(void *dst, const void *src, const FzBGeom &g, int eb, int
   if (smem > kBulkSmemMax) return DCOPY_OK;
   using Kern = void (*)(unsigned char *, const unsigned char *, FzBGeom, uint32_t, FastDiv,
                         FastDiv);
-  Kern k = eb == 1 ? fz_to_nchw_gather_kernel<1> : fz_to_nchw_gather_kernel<2>;
-  static std::atomic<bool> raised[2][128];
+  Kern k = fz_to_nchw_gather_kernel<2>;
+  static std::atomic<bool> raised[128];
   const int dev = current_device();
-  const int which = eb == 1 ? 0 : 1;
-  if (dev >= 0 && dev < 128 && !raised[which][dev].load()) {
+  if (eb != 2) return DCOPY_OK;
+  if (dev >= 0 && dev < 128 && !raised[dev].load()) {
     const cudaError_t e =
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBulkSmemMax);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(fz_to_nchw_gather_kernel)");
-    raised[which][dev] = true;
+    raised[dev] = true;
   }
   int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kThreads, smem) != cudaSuccess ||
@@ -987,7 +991,7 @@ int launch_from_gather(void *dst, const void *src, const FzBGeom &g, int eb, int
 int run_nchw_bulk_from(void *dst, const void *src, int64_t n, int64_t c, int64_t hw, int eb,
                        int64_t c0, cudaStream_t s, bool *taken) {
   *taken = false;
-  const bool gather = DCOPY_FZ_FROM_GATHER && eb <= 2;
+  const bool gather = DCOPY_FZ_FROM_GATHER && eb == 2;
   if (!gather && (!DCOPY_FZ_NCHW_BULK_FROM || eb != 4)) return DCOPY_OK;
   const int64_t V = 16 / eb;
   if (c0 <= 0 || (c0 & (c0 - 1)) || c0 % V || c % c0 || (c * hw * eb) % 16) return DCOPY_OK;
@@ -1349,7 +1353,11 @@ int to_fz(void *dst, const void *src, int32_t fmt, const int64_t *s, int rank, i
       default: return launch_groups<uint4>(dst, src, g, s_);
     }
   }
-  if (fmt == kNhwc) return run_nhwc(dst, src, n, c, h, w, eb, c0, true, stream);
+  // An NCHW weight with H = W = 1 is laid out exactly as the NHWC one ([N][C]),
+  // so it takes the NHWC tiles (measured on B200, [2048,8192,1,1] fp16: 1928 GB/s
+  // through the transposing tiles).
+  if (fmt == kNhwc || (fmt == kNchw && h * w == 1))
+    return run_nhwc(dst, src, n, c, h, w, eb, c0, true, stream);
   return run_transpose(fmt, dst, src, n, c, h, w, eb, c0, true, s_);
 }
 
@@ -1390,7 +1398,8 @@ int from_fz(void *dst, const void *src, int32_t fmt, const int64_t *d, int rank,
   if (rc) return rc;
   if (((uintptr_t)src | (uintptr_t)dst) % eb)
     return set_error(DCOPY_ERR_PARAM_INVALID, "buffers must be aligned to the element size");
-  if (fmt == kNhwc) return run_nhwc(dst, src, n, c, h, w, eb, c0, false, stream);
+  if (fmt == kNhwc || (fmt == kNchw && h * w == 1))  // same layout, see to_fz
+    return run_nhwc(dst, src, n, c, h, w, eb, c0, false, stream);
   return run_transpose(fmt, dst, src, n, c, h, w, eb, c0, false,
                        reinterpret_cast<cudaStream_t>(stream));
 }
