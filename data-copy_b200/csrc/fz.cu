@@ -783,6 +783,108 @@ __global__ void __launch_bounds__(kThreads) fz_to_nchw_gather_kernel(unsigned ch
   }
 }
 
+// ---- HWCN -> FRACTAL_Z with tensor-copied, double-buffered tiles ------------------
+//
+// For one hw and channel block c1 the HWCN weight holds C0 rows (channels) of N
+// contiguous outputs; FRACTAL_Z wants the transpose, [n][c0], as one run of
+// N1*16*C0 elements.  A tile is KT consecutive n of that block: one 2-D tensor
+// copy (source view [H*W*C rows][N], box [C0][KT]; outputs past N arrive as
+// zeros) fills one of two shared stages while the other is turned into
+// FRACTAL_Z.  Each warp instruction reads one channel row for 32 consecutive n,
+// so every shared load is conflict-free; lane n stores its 16-byte vector of V
+// consecutive c0.  Waits are bounded as in the NCHW kernels.
+struct FzHGeom {
+  uint32_t HW, C0, KT, N1N0, C;  // C: channels (a multiple of C0)
+  uint32_t ktiles, ntiles;
+  FastDiv f_ktiles, f_hw;
+};
+
+template <int EB>
+__global__ void __launch_bounds__(kThreads) fz_hwcn_tensor_kernel(unsigned char *__restrict__ dst_b,
+                                                                  FzHGeom g,
+                                                                  const __grid_constant__ CUtensorMap map) {
+  using T = typename FzLane<EB>::T;
+  constexpr int V = FzLane<EB>::V;
+  union Pack {
+    uint4 u;
+    T e[V];
+  };
+  extern __shared__ __align__(128) unsigned char fzh_smem[];
+  __shared__ __align__(8) uint64_t bars[2];
+  T *dst = reinterpret_cast<T *>(dst_b);
+  const uint32_t stage_elems = g.C0 * g.KT;
+  pdl_trigger_at_entry();
+  if (threadIdx.x == 0) {
+    bulk::mbar_init(&bars[0], 1);
+    bulk::mbar_init(&bars[1], 1);
+    bulk::mbar_init_fence();
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_launch_dependents();
+  // Tile t: (c1, hw) = divmod(t / ktiles, HW), n block kt = t % ktiles.
+  auto coords = [&](uint32_t t, uint32_t *c1, uint32_t *hw, uint32_t *kt) {
+    const uint32_t q = g.f_ktiles.div(t);
+    *kt = t - q * g.ktiles;
+    *c1 = g.f_hw.div(q);
+    *hw = q - *c1 * g.HW;
+  };
+  auto issue = [&](uint32_t t, int st) {
+    if (threadIdx.x != 0) return;
+    uint32_t c1, hw, kt;
+    coords(t, &c1, &hw, &kt);
+    T *stage = reinterpret_cast<T *>(fzh_smem) + st * stage_elems;
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(
+                     bulk::smem_u32(&bars[st])),
+                 "r"(stage_elems * EB)
+                 : "memory");
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(bulk::smem_u32(stage)),
+        "l"(reinterpret_cast<uint64_t>(&map)), "r"((int32_t)(kt * g.KT)),
+        "r"((int32_t)(hw * g.C + c1 * g.C0)), "r"(bulk::smem_u32(&bars[st]))
+        : "memory");
+  };
+  uint32_t k = 0;
+  if (blockIdx.x < g.ntiles) issue(blockIdx.x, 0);
+  bool ok = true, next_issued = false;
+  for (uint32_t t = blockIdx.x; t < g.ntiles; t += gridDim.x, ++k) {
+    const int st = (int)(k & 1);
+    next_issued = t + gridDim.x < g.ntiles;
+    if (next_issued) issue(t + gridDim.x, st ^ 1);
+    const bool arrived = bulk::mbar_wait_bounded(&bars[st], (k >> 1) & 1);
+    if (__syncthreads_or(!arrived)) {
+      ok = false;
+      break;
+    }
+    uint32_t c1, hw, kt;
+    coords(t, &c1, &hw, &kt);
+    const uint32_t n0 = kt * g.KT, kn = min(g.KT, g.N1N0 - n0);
+    const T *stage = reinterpret_cast<const T *>(fzh_smem) + st * stage_elems;
+    T *out = dst + (((uint64_t)c1 * g.HW + hw) * g.N1N0 + n0) * g.C0;
+    const uint32_t Q = g.C0 / V;
+    for (uint32_t u = threadIdx.x; u < ((kn + 31) & ~31u) * Q; u += kThreads) {
+      // Warp-uniform vector q, 32 consecutive n per warp instruction.
+      const uint32_t q = (u >> 5) % Q, n = ((u >> 5) / Q << 5) + (u & 31);
+      if (n >= kn) continue;
+      Pack x;
+#pragma unroll
+      for (int j = 0; j < V; ++j) x.e[j] = stage[(q * V + j) * g.KT + n];
+      *reinterpret_cast<uint4 *>(out + (uint64_t)n * g.C0 + q * V) = x.u;
+    }
+    __syncthreads();  // every read of this stage is done before it is refilled
+  }
+  if (!ok) {
+    if (threadIdx.x == 0) atomicExch(&g_fz_error, 1u);
+    (void)bulk::mbar_wait_bounded(&bars[k & 1], (k >> 1) & 1);
+    if (next_issued) (void)bulk::mbar_wait_bounded(&bars[(k + 1) & 1], ((k + 1) >> 1) & 1);
+  }
+}
+
+#ifndef DCOPY_FZ_HWCN_TMA
+#define DCOPY_FZ_HWCN_TMA 0  // HWCN -> FRACTAL_Z through fz_hwcn_tensor_kernel
+#endif
+
 #ifndef DCOPY_FZ_NCHW_BULK
 #define DCOPY_FZ_NCHW_BULK 1
 #endif
@@ -987,6 +1089,69 @@ int launch_from_gather(void *dst, const void *src, const FzBGeom &g, int eb, int
                 FastDiv(g.L / V), FastDiv(g.HW));
 }
 
+// HWCN -> FRACTAL_Z through fz_hwcn_tensor_kernel when channel blocks are whole,
+// output rows (N) are 16-byte granules and both buffers are this GPU's memory.
+int run_hwcn_tensor(void *dst, const void *src, int64_t n, int64_t c, int64_t hw, int eb,
+                    int64_t c0, cudaStream_t s, bool *taken) {
+  *taken = false;
+  if (!DCOPY_FZ_HWCN_TMA || (eb != 1 && eb != 2 && eb != 4)) return DCOPY_OK;
+  const int64_t V = 16 / eb;
+  if (c0 <= 0 || (c0 & (c0 - 1)) || c0 % V || c0 > 256 || c % c0 || (n * eb) % 16) return DCOPY_OK;
+  if (((uintptr_t)dst | (uintptr_t)src) % 16) return DCOPY_OK;
+  if (!is_local_device_memory(src) || !is_local_device_memory(dst)) return DCOPY_OK;
+  const int64_t n1n0 = ge_ceil(n, kNi) * kNi;
+  if (n1n0 * c0 * hw * ge_ceil(c, c0) > 0x7FFFFFFFll || hw * c > 0x7FFFFFFFll || n > 0x7FFFFFFFll)
+    return DCOPY_OK;
+  const int64_t KT = 256;  // box width: 256 outputs (a multiple of 16 bytes for every eb)
+  const size_t smem = (size_t)(2 * c0 * KT * eb);
+  if (smem > kBulkSmemMax) return DCOPY_OK;
+  CUtensorMap map{};
+  const uint64_t dims[2] = {(uint64_t)n, (uint64_t)(hw * c)};
+  const uint64_t strides[1] = {(uint64_t)(n * eb)};
+  const uint32_t box[2] = {(uint32_t)KT, (uint32_t)c0};
+  const CUtensorMapDataType dt = eb == 1   ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                 : eb == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16
+                                           : CU_TENSOR_MAP_DATA_TYPE_UINT32;
+  if (!encode_tiled_map(&map, dt, 2, const_cast<void *>(src), dims, strides, box,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
+    return DCOPY_OK;
+  FzHGeom g{};
+  g.HW = (uint32_t)hw;
+  g.C0 = (uint32_t)c0;
+  g.KT = (uint32_t)KT;
+  g.N1N0 = (uint32_t)n1n0;
+  g.C = (uint32_t)c;
+  g.ktiles = (uint32_t)ge_ceil(n1n0, KT);
+  const uint64_t ntiles = (uint64_t)(c / c0) * hw * g.ktiles;
+  if (ntiles == 0 || ntiles > 0x7FFFFFFFull) return DCOPY_OK;
+  g.ntiles = (uint32_t)ntiles;
+  g.f_ktiles = FastDiv(g.ktiles);
+  g.f_hw = FastDiv(g.HW);
+  using Kern = void (*)(unsigned char *, FzHGeom, const CUtensorMap);
+  Kern k = eb == 1 ? fz_hwcn_tensor_kernel<1>
+           : eb == 2 ? fz_hwcn_tensor_kernel<2> : fz_hwcn_tensor_kernel<4>;
+  static std::atomic<bool> raised[3][128];
+  const int dev = current_device();
+  const int which = eb == 1 ? 0 : eb == 2 ? 1 : 2;
+  if (dev >= 0 && dev < 128 && !raised[which][dev].load()) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBulkSmemMax);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(fz_hwcn_tensor_kernel)");
+    raised[which][dev] = true;
+  }
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kThreads, smem) != cudaSuccess ||
+      per_sm <= 0) {
+    (void)cudaGetLastError();
+    per_sm = 1;
+  }
+  *taken = true;
+  const uint32_t grid =
+      (uint32_t)std::min<uint64_t>(ntiles, (uint64_t)per_sm * (uint64_t)sm_count());
+  return launch(k, std::max(1u, grid), dim3(kThreads), smem, s, "fz_hwcn_tensor_kernel",
+                static_cast<unsigned char *>(dst), g, map);
+}
+
 // FRACTAL_Z -> NCHW through fz_to_nchw_bulk_kernel under the same conditions.
 int run_nchw_bulk_from(void *dst, const void *src, int64_t n, int64_t c, int64_t hw, int eb,
                        int64_t c0, cudaStream_t s, bool *taken) {
@@ -1152,6 +1317,10 @@ int run_transpose(int32_t fmt, void *dst, const void *src, int64_t n, int64_t c,
     const int brc = to_fz ? run_nchw_bulk(dst, src, n, c, h * w, eb, c0, s, &taken)
                           : run_nchw_bulk_from(dst, src, n, c, h * w, eb, c0, s, &taken);
     if (taken || brc) return brc;
+  }
+  if (fmt == kHwcn && to_fz) {
+    const int hrc = run_hwcn_tensor(dst, src, n, c, h * w, eb, c0, s, &taken);
+    if (taken || hrc) return hrc;
   }
   const int vrc = run_vec(fmt, dst, src, n, c, h, w, eb, c0, to_fz, s, &taken);
   if (taken || vrc) return vrc;

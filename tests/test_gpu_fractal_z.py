@@ -196,3 +196,27 @@ def test_nchw_to_fractal_z_bulk_tiles(torch_cuda, dcopy, oracle, weight, eb, c0)
     assert out[:expect.nbytes].tobytes() == expect.tobytes()
     assert (out[expect.nbytes:] == CANARY).all()
     assert dcopy.tma_error() == 0
+
+
+@pytest.mark.parametrize("shape,eb,c0", [
+    ((3, 3, 1024, 2048), 2, 16),   # 9216 tiles: every CTA cycles both stages several times
+    ((5, 5, 64, 200), 2, 16),      # N = 200: the last tile is partial, its padding zero-filled
+    ((3, 3, 64, 96), 1, 32),
+    ((2, 2, 32, 80), 4, 16),
+    ((1, 1, 256, 1000), 2, 16),
+], ids=lambda v: "x".join(map(str, v)) if isinstance(v, tuple) else str(v))
+def test_hwcn_to_fractal_z_tensor_tiles(torch_cuda, dcopy, oracle, shape, eb, c0):
+    """HWCN -> FRACTAL_Z with whole channel blocks and 16-byte output rows: the
+    tensor-copied, double-buffered tile kernel, against the oracle byte for byte."""
+    torch = torch_cuda
+    shape = list(shape)
+    src_np = _rand(int(np.prod(shape)) * eb, sum(shape) * 3 + eb)
+    expect = oracle.to_fz(_as(src_np, eb).reshape(shape), HWCN, c0)
+    src = torch.from_numpy(src_np).cuda()
+    dst = torch.full((expect.nbytes + 64,), CANARY, dtype=torch.uint8, device="cuda")
+    dcopy.to_fractal_z(dst, src, HWCN, shape, eb, c0)
+    torch.cuda.synchronize()
+    out = dst.cpu().numpy()
+    assert out[:expect.nbytes].tobytes() == expect.tobytes()
+    assert (out[expect.nbytes:] == CANARY).all()
+    assert dcopy.tma_error() == 0
