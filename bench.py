@@ -350,7 +350,7 @@ def run_dcopy(args, rank, world, local_rank):
                     "d2h_bytes_per_step": ROWS * (C1 - C0) * 4,
                     "steps": e2e_steps,
                     "path": "dcopy_copy_ext_staged on pinned host buffers, 16 MiB device "
-                            "staging: copy-engine gather of the bursts host -> device in 4 "
+                            "staging: copy-engine gather of the bursts host -> device in 6 "
                             "chunks, each chunk returned to host memory by the copy engine on "
                             "a second stream while the next is gathered",
                     "pcie_duplex_ceiling_GBps": pcie["duplex"],
@@ -414,9 +414,11 @@ def ring_shift_measure(torch, dcopy, dev, rank, world, barrier, dist, steps):
     rank (r+1) mod N's receive buffer over NVLink (dcopy_p2p_copy into the CUDA IPC
     mapping), release-stores a sequence number into that rank's flag, and waits for
     its own flag with a bounded device-side wait.  Every received shard is compared
-    whole with the sender's data.  The same exchange with cudaMemcpyAsync (the copy
-    engine) in place of the kernel is timed on the same buffers as the comparator.
-    Timing: CUDA events on each rank's stream, max over ranks."""
+    whole with the sender's data.  Three runs on the same buffers: dcopy_p2p_copy
+    with its automatic engine choice (the reported path), the same call with the SM
+    engine forced (the bulk-copy push kernel), and cudaMemcpyAsync in place of
+    dcopy_p2p_copy (the comparator).  Timing: CUDA events on each rank's stream,
+    max over ranks."""
     from dcopy import multi
     from cuda.bindings import runtime as cudart
     shard = 1 << 30
@@ -442,7 +444,7 @@ def ring_shift_measure(torch, dcopy, dev, rank, world, barrier, dist, steps):
         def exchange(engine):
             nonlocal seq
             seq += 1
-            if engine:
+            if engine == "copy_engine":
                 err, = cudart.cudaMemcpyAsync(peer.recv_ptr, send.data_ptr(), shard,
                                               cudart.cudaMemcpyKind.cudaMemcpyDefault,
                                               stream.cuda_stream)
@@ -454,7 +456,10 @@ def ring_shift_measure(torch, dcopy, dev, rank, world, barrier, dist, steps):
             multi.wait_ring(flags, seq, status, timeout_ns=2_000_000_000, stream=stream)
 
         psteps = max(2, min(steps, 10))
-        for name, engine in (("kernel", False), ("copy_engine", True)):
+        for name in ("dcopy", "sm_push", "copy_engine"):
+            prev_engine = dcopy.set_p2p_engine(
+                dcopy.P2P_ENGINE_SM if name == "sm_push" else dcopy.P2P_ENGINE_AUTO)
+            engine = name
             recv.zero_()
             barrier()
             for _ in range(2):
@@ -477,21 +482,26 @@ def ring_shift_measure(torch, dcopy, dev, rank, world, barrier, dist, steps):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             dist.all_reduce(good, op=dist.ReduceOp.MIN)
             results[name] = (shard * psteps / (float(t.item()) / 1e3) / 1e9, bool(good.item()))
+            dcopy.set_p2p_engine(prev_engine)
         err = dcopy.p2p_error()
     finally:
         barrier()
         peer.release()
-    kern, ce = results["kernel"], results["copy_engine"]
-    return {"per_direction_GBps": round(kern[0], 1), "aggregate_GBps": round(kern[0] * world, 1),
-            "nominal_GBps": 900.0, "frac_of_nominal": round(kern[0] / 900.0, 4),
+    main, sm, ce = results["dcopy"], results["sm_push"], results["copy_engine"]
+    return {"per_direction_GBps": round(main[0], 1), "aggregate_GBps": round(main[0] * world, 1),
+            "nominal_GBps": 900.0, "frac_of_nominal": round(main[0] / 900.0, 4),
             "measured_peer_copy_GBps": 770.0,
-            "frac_of_measured_peer_copy": round(kern[0] / 770.0, 4),
-            "flags_ok": kern[1] and ce[1] and err == 0, "shards_checked": "whole 1 GiB shard",
+            "frac_of_measured_peer_copy": round(main[0] / 770.0, 4),
+            "flags_ok": main[1] and sm[1] and ce[1] and err == 0,
+            "shards_checked": "whole 1 GiB shard, every run",
+            "sm_push_per_direction_GBps": round(sm[0], 1),
             "copy_engine_per_direction_GBps": round(ce[0], 1),
             "bytes_per_rank_per_step": shard, "steps": max(2, min(steps, 10)),
-            "path": "dcopy_p2p_copy (SM bulk-copy push) into the next rank's IPC-mapped "
-                    "buffer + release flag; bounded device-side wait on this rank's flag",
-            "comparator": "cudaMemcpyAsync into the same mapping, same flags"}
+            "path": "dcopy_p2p_copy, automatic engine (pushes of >= 1 MiB on the copy engine) "
+                    "into the next rank's IPC-mapped buffer + release-store flag kernel; "
+                    "bounded device-side wait kernel on this rank's flag",
+            "sm_push_path": "the same with dcopy_set_p2p_engine(SM): p2p_bulk_push_kernel",
+            "comparator": "cudaMemcpyAsync in place of dcopy_p2p_copy, same flags"}
 
 
 def _time_graph(torch, fn, reps=10, warm=3):

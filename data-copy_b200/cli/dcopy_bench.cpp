@@ -34,11 +34,12 @@
 //   dcopy_bench batch [--gathers G] [--reps R] [--device D] [--peak GBPS]
 //       G config-2 gathers as one dcopy_copy_ext_batch against G dcopy_copy_ext calls
 //       (both captured in a CUDA graph), verified; one JSON line.
-//   dcopy_bench p2p [--mib M] [--reps R] [--device D] [--peer P] [--peak GBPS]
-//       NVLink between two GPUs (push, pull, copy engine, and the two halves
-//       split SM push + copy engine or push + pull): dcopy_p2p_copy as a push (launched on the
-//       sending GPU) and as a pull (launched on the receiving GPU), and the copy
-//       engine, each with both GPUs sending at once and with one sending.
+//   dcopy_bench p2p [--mib M | --kib K] [--reps R] [--device D] [--peer P] [--peak GBPS]
+//       NVLink between two GPUs: dcopy_p2p_copy as a push launched on the
+//       sending GPU (automatic engine choice, then the SM engine forced), as a
+//       pull launched on the receiving GPU, cudaMemcpyPeerAsync, and the two
+//       halves split SM push + copy engine or push + pull; each with both GPUs
+//       sending at once and with one sending.
 //
 // Timing: 3 untimed warm-up calls, then CUDA events around each launch (median of
 // 20 reps by default); a 512 MiB read between reps (load-only
@@ -90,6 +91,7 @@ struct Args {
     auto it = opt.find(k);
     return it == opt.end() ? d : std::stod(it->second);
   }
+  bool has(const std::string &k) const { return opt.count(k) != 0; }
   std::string str(const std::string &k, const std::string &d) const {
     auto it = opt.find(k);
     return it == opt.end() ? d : it->second;
@@ -712,7 +714,8 @@ int run_batch(const Args &a) {
 
 int run_p2p(const Args &a) {
   const int dev[2] = {int(a.num("device", 0)), int(a.num("peer", 1))};
-  const uint64_t bytes = uint64_t(a.num("mib", 1024)) << 20;
+  const uint64_t bytes = a.has("kib") ? uint64_t(a.num("kib", 1)) << 10
+                                      : uint64_t(a.num("mib", 1024)) << 20;
   const int reps = int(a.num("reps", 5));
   const double peak = a.num("peak", 770.0);  // measured per-direction peer copy
   CheckD(dcopy_enable_peer_access(dev[0], dev[1]));
@@ -731,11 +734,13 @@ int run_p2p(const Args &a) {
       Check(cudaEventCreate(&ev[i][k][1]), "event");
     }
   }
-  // GPU i sends src[i] to the other GPU's dst.  push: the SM kernel on the
-  // sender; pull: the load kernel on the receiver; ce: cudaMemcpyPeerAsync;
-  // split: SM push of the first half and the copy engine for the second half,
-  // on two streams of the sender; pushpull: SM push of the first half on the
-  // sender and a pull of the second half on the receiver.
+  // GPU i sends src[i] to the other GPU's dst.  push: dcopy_p2p_copy on the
+  // sender with its automatic engine choice; smpush: the same with the SM
+  // engine forced (the bulk-copy push kernel); pull: the load kernel on the
+  // receiver; ce: cudaMemcpyPeerAsync; split: SM push of the first half and the
+  // copy engine for the second half, on two streams of the sender; pushpull: SM
+  // push of the first half on the sender and a pull of the second half on the
+  // receiver.
   const uint64_t half = bytes / 2 / 16 * 16;
   auto push = [&](int on, void *d, const void *sp, uint64_t n, int k) {
     Check(cudaSetDevice(dev[on]), "cudaSetDevice");
@@ -745,7 +750,7 @@ int run_p2p(const Args &a) {
     const int peer = 1 - i;
     uint8_t *d = static_cast<uint8_t *>(dst[peer]->p);
     const uint8_t *sp = static_cast<const uint8_t *>(src[i]->p);
-    if (mode == "push") {
+    if (mode == "push" || mode == "smpush") {
       push(i, d, sp, bytes, 0);
     } else if (mode == "pull") {
       push(peer, d, sp, bytes, 0);
@@ -774,7 +779,10 @@ int run_p2p(const Args &a) {
     }
   };
   std::vector<uint8_t> host(bytes);
-  for (const std::string mode : {"push", "pull", "ce", "split", "pushpull"}) {
+  for (const std::string mode : {"push", "smpush", "pull", "ce", "split", "pushpull"}) {
+    int32_t prev_engine = 0;
+    CheckD(dcopy_set_p2p_engine(mode == "push" ? DCOPY_P2P_ENGINE_AUTO : DCOPY_P2P_ENGINE_SM,
+                                &prev_engine));
     for (int senders = 2; senders >= 1; --senders) {
       for (int i = 0; i < 2; ++i) {
         Check(cudaSetDevice(dev[i]), "cudaSetDevice");
@@ -817,6 +825,7 @@ int run_p2p(const Args &a) {
                 << ", \"frac_of_peer_copy\": " << gbps / peak << ", \"verified\": true}"
                 << std::endl;
     }
+    CheckD(dcopy_set_p2p_engine(prev_engine, nullptr));
   }
   for (int i = 0; i < 2; ++i) {
     Check(cudaSetDevice(dev[i]), "cudaSetDevice");

@@ -29,9 +29,14 @@ int check_launch(const char *kernel);
 // sets DCOPY_CHECK_POINTERS=0.
 int check_device_span(const void *ptr, uint64_t bytes, const char *name);
 // True when ptr is device memory of the current device (not a peer's, not an
-// IPC mapping of another GPU, not host memory).  Kernels L2-prefetch only such
-// sources: a prefetch of another GPU's memory stalls the copy (measured 100x).
+// IPC mapping opened through dcopy_ipc_open_handle, not host memory).  Kernels
+// L2-prefetch only such sources: a prefetch of another GPU's memory stalls the
+// copy (measured 100x).
 bool is_local_device_memory(const void *ptr);
+// Records (opened) or forgets (!opened) the IPC mapping that starts at base;
+// in_ipc_mapping tells whether ptr lies in a recorded one.
+void note_ipc_mapping(const void *base, bool opened);
+bool in_ipc_mapping(const void *ptr);
 // Start address of the allocation holding ptr (0 when it cannot be determined).
 uint64_t allocation_base(const void *ptr);
 // 0 when the byte ranges [a, a+an) and [b, b+bn) are disjoint, else PARAM_INVALID.

@@ -9,6 +9,12 @@
 
 namespace dcopy {
 
+// The unique id of the calling thread's current CUDA context (driver API, looked
+// up through the runtime, so the library needs no link against libcuda); false
+// when there is none or the driver lacks the call.  Caches of per-context
+// objects (addresses, events) compare it to notice a device reset.
+bool current_context_id(unsigned long long *id);
+
 // IsShapeValid (formats_trans_utils.cc:88-107): non-empty, no negative dim,
 // item count below 2^40.
 bool shape_valid(const int64_t *shape, int rank);

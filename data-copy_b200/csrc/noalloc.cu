@@ -52,12 +52,11 @@ struct Slot {
 };
 Slot g_slots[kMaxDevices];
 
+}  // namespace
+
 typedef int (*PfnCtxGetCurrent)(void **);
 typedef int (*PfnCtxGetId)(void *, unsigned long long *);
 
-// The unique id of the calling thread's current context (driver API, looked up
-// through the runtime, so the library needs no link against libcuda); false
-// when there is none or the driver lacks the call.
 bool current_context_id(unsigned long long *id) {
   static PfnCtxGetCurrent get_current = nullptr;
   static PfnCtxGetId get_id = nullptr;
@@ -78,6 +77,8 @@ bool current_context_id(unsigned long long *id) {
   if (!get_current || !get_id || get_current(&ctx) != 0 || !ctx) return false;
   return get_id(ctx, id) == 0 && *id != 0;
 }
+
+namespace {
 
 // Device address of g_pretranspose_b on the current device.  Set-up, once per
 // device (and again after the device's context was replaced), with that device

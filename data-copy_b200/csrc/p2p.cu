@@ -1,8 +1,15 @@
 // Multi-GPU pieces: shard ranges, per-device launches, NVLink P2P copies, CUDA
 // IPC mappings and bounded completion flags.
 //
-// The P2P copy pushes: each thread loads 16-byte units of the local source and
-// stores them to the peer address (posted writes over NVLink); reads stay local.
+// The P2P copy picks its engine.  A push of at least 1 MiB from this GPU to
+// another GPU's memory goes to the copy engine (cudaMemcpyAsync on the caller's
+// stream): in an exchange it moves 766-775 GB/s per direction over NV18, where
+// every SM-issued write path measured settles at 689-715 (bulk-copy pipelines of
+// 8-64 KiB chunks, 2-8 stages, 1-4 CTAs per SM; 128-bit stores; half SM + half
+// engine at 735).  Shorter or unaligned pushes run the SM bulk-copy pipeline
+// (local loads into shared memory, bulk stores over NVLink), and pulls (launched
+// on the receiving GPU, 786 GB/s one way) the 128-bit load/store kernel.
+// dcopy_set_p2p_engine forces either engine.
 // Completion flags use st.release.sys / ld.acquire.sys on a caller-owned word;
 // the waiting kernel has a time bound and an iteration bound and reports a
 // timeout through a caller-owned status word instead of hanging.
@@ -10,6 +17,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <cstdlib>
 #include <cstring>
 
 #include "common.cuh"
@@ -19,9 +27,33 @@
 #ifndef DCOPY_P2P_BULK
 #define DCOPY_P2P_BULK 1
 #endif
+#ifndef DCOPY_P2P_COPY_ENGINE_MIN_KIB
+#define DCOPY_P2P_COPY_ENGINE_MIN_KIB 1024  // shortest push the automatic choice hands to the copy engine
+#endif
 
 namespace dcopy {
 namespace {
+
+std::atomic<int> g_p2p_engine{-1};  // -1: not read from the environment yet
+
+// DCOPY_P2P_ENGINE = auto | sm | copy (or 0 | 1 | 2); unset or unknown: auto.
+int initial_engine() {
+  const char *e = std::getenv("DCOPY_P2P_ENGINE");
+  if (!e) return DCOPY_P2P_ENGINE_AUTO;
+  if (!std::strcmp(e, "sm") || !std::strcmp(e, "1")) return DCOPY_P2P_ENGINE_SM;
+  if (!std::strcmp(e, "copy") || !std::strcmp(e, "2")) return DCOPY_P2P_ENGINE_COPY;
+  return DCOPY_P2P_ENGINE_AUTO;
+}
+
+int p2p_engine() {
+  int v = g_p2p_engine.load(std::memory_order_relaxed);
+  if (v < 0) {
+    int expected = -1;
+    g_p2p_engine.compare_exchange_strong(expected, initial_engine());
+    v = g_p2p_engine.load(std::memory_order_relaxed);
+  }
+  return v;
+}
 
 // RAII restore of the caller's current device.
 struct DeviceGuard {
@@ -182,6 +214,23 @@ __global__ void __launch_bounds__(32) p2p_bulk_push_kernel(uint8_t *__restrict__
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
+// The route of one dcopy_p2p_copy.  The SM paths: a push of 16-byte granular
+// buffers through the bulk-copy pipeline; anything else (pulls, odd sizes,
+// local copies) through the load/store kernel.  (A bulk-copy pull from the peer
+// measured 666 GB/s per direction in an exchange against 643 for the load
+// kernel and 702 for the bulk push.)
+int p2p_route(const void *dst, const void *src, uint64_t bytes) {
+  const int engine = p2p_engine();
+  const bool push = is_local_device_memory(src) && !is_local_device_memory(dst);
+  if (engine == DCOPY_P2P_ENGINE_COPY ||
+      (engine == DCOPY_P2P_ENGINE_AUTO && push &&
+       bytes >= (uint64_t)DCOPY_P2P_COPY_ENGINE_MIN_KIB * 1024))
+    return DCOPY_P2P_ROUTE_COPY_ENGINE;
+  if (DCOPY_P2P_BULK && push && ((uintptr_t)dst | (uintptr_t)src | bytes) % 16 == 0)
+    return DCOPY_P2P_ROUTE_SM_BULK_PUSH;
+  return DCOPY_P2P_ROUTE_SM_LOAD_STORE;
+}
+
 int launch_bulk_push(void *dst, const void *src, uint64_t bytes, cudaStream_t s) {
   static std::atomic<bool> configured[128];
   const int dev = current_device();
@@ -257,15 +306,34 @@ extern "C" int dcopy_p2p_copy(void *dst, const void *src, uint64_t bytes, dcopy_
   if (!rc) rc = check_disjoint(src, bytes, dst, bytes, "p2p_copy");
   if (rc) return rc;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  // Push to another GPU with the bulk-copy pipeline when everything is 16-byte
-  // granular and the source is this GPU's memory; anything else (pulls, odd
-  // sizes, local copies) takes the load/store kernel.
-  // (A bulk-copy pull from the peer measured 666 GB/s per direction in an
-  // exchange against 643 for the load kernel and 702 for this push.)
-  if (DCOPY_P2P_BULK && ((uintptr_t)dst | (uintptr_t)src | bytes) % 16 == 0 &&
-      is_local_device_memory(src) && !is_local_device_memory(dst))
-    return launch_bulk_push(dst, src, bytes, s);
-  return copy_linear(dst, src, bytes, s);
+  switch (p2p_route(dst, src, bytes)) {
+    case DCOPY_P2P_ROUTE_COPY_ENGINE:
+      DCOPY_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, s));
+      return DCOPY_OK;
+    case DCOPY_P2P_ROUTE_SM_BULK_PUSH: return launch_bulk_push(dst, src, bytes, s);
+    default: return copy_linear(dst, src, bytes, s);
+  }
+  DCOPY_API_END
+}
+
+extern "C" int dcopy_p2p_route(const void *dst, const void *src, uint64_t bytes,
+                               int32_t *route) {
+  DCOPY_API_BEGIN
+  if (!route) return set_error(DCOPY_ERR_PARAM_INVALID, "p2p_route: route is NULL");
+  *route = p2p_route(dst, src, bytes);
+  return DCOPY_OK;
+  DCOPY_API_END
+}
+
+extern "C" int dcopy_set_p2p_engine(int32_t engine, int32_t *previous) {
+  DCOPY_API_BEGIN
+  if (engine != DCOPY_P2P_ENGINE_AUTO && engine != DCOPY_P2P_ENGINE_SM &&
+      engine != DCOPY_P2P_ENGINE_COPY)
+    return set_error(DCOPY_ERR_PARAM_INVALID, "set_p2p_engine: engine %d", engine);
+  const int was = p2p_engine();
+  g_p2p_engine.store(engine);
+  if (previous) *previous = was;
+  return DCOPY_OK;
   DCOPY_API_END
 }
 
@@ -309,6 +377,7 @@ extern "C" int dcopy_ipc_open_handle(const void *handle, void **dev_ptr) {
   cudaIpcMemHandle_t h;
   std::memcpy(&h, handle, sizeof(h));
   DCOPY_CUDA_TRY(cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  note_ipc_mapping(*dev_ptr, true);
   return DCOPY_OK;
   DCOPY_API_END
 }
@@ -317,6 +386,7 @@ extern "C" int dcopy_ipc_close_handle(void *dev_ptr) {
   DCOPY_API_BEGIN
   if (!dev_ptr) return DCOPY_OK;
   DCOPY_CUDA_TRY(cudaIpcCloseMemHandle(dev_ptr));
+  note_ipc_mapping(dev_ptr, false);
   return DCOPY_OK;
   DCOPY_API_END
 }

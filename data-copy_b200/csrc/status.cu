@@ -8,6 +8,8 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <utility>
+#include <vector>
 
 #include "common.cuh"
 
@@ -95,9 +97,48 @@ int check_device_span(const void *ptr, uint64_t bytes, const char *name) {
   return DCOPY_OK;
 }
 
+namespace {
+// CUDA IPC mappings opened through dcopy_ipc_open_handle: [base, base + size).
+// The driver reports such a mapping as device memory of the device that opened
+// it, so the ranges are kept here to tell them apart from local allocations.
+std::mutex g_ipc_mu;
+std::vector<std::pair<uint64_t, uint64_t>> g_ipc_ranges;
+std::atomic<int> g_ipc_open{0};
+}  // namespace
+
+void note_ipc_mapping(const void *base, bool opened) {
+  const uint64_t b = (uint64_t)(uintptr_t)base;
+  std::lock_guard<std::mutex> lock(g_ipc_mu);
+  if (opened) {
+    uint64_t size = 1;  // the base alone when the size cannot be read
+    PfnPointerGetAttributes fn = pointer_attrs_fn();
+    size_t n = 0;
+    CUpointer_attribute attr = CU_POINTER_ATTRIBUTE_RANGE_SIZE;
+    void *data = &n;
+    if (fn && fn(1, &attr, &data, (CUdeviceptr)b) == CUDA_SUCCESS && n) size = n;
+    g_ipc_ranges.emplace_back(b, size);
+  } else {
+    for (size_t i = 0; i < g_ipc_ranges.size(); ++i)
+      if (g_ipc_ranges[i].first == b) {
+        g_ipc_ranges.erase(g_ipc_ranges.begin() + (long)i);
+        break;
+      }
+  }
+  g_ipc_open.store((int)g_ipc_ranges.size(), std::memory_order_release);
+}
+
+bool in_ipc_mapping(const void *ptr) {
+  if (g_ipc_open.load(std::memory_order_acquire) == 0) return false;
+  const uint64_t p = (uint64_t)(uintptr_t)ptr;
+  std::lock_guard<std::mutex> lock(g_ipc_mu);
+  for (const auto &r : g_ipc_ranges)
+    if (p >= r.first && p - r.first < r.second) return true;
+  return false;
+}
+
 bool is_local_device_memory(const void *ptr) {
   PfnPointerGetAttributes fn = pointer_attrs_fn();
-  if (!fn || !ptr) return false;
+  if (!fn || !ptr || in_ipc_mapping(ptr)) return false;
   unsigned int mem_type = 0;
   int ordinal = -1;
   CUpointer_attribute attrs[2] = {CU_POINTER_ATTRIBUTE_MEMORY_TYPE,

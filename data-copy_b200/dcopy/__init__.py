@@ -37,7 +37,9 @@ __all__ = [
     "trans_format", "trans_format_check", "trans_shape", "trans_tensor_shape", "transpose",
     "transpose_with_shape_check", "FORMAT", "DATA_TYPE", "TRANSFER_FRACTAL_NZ",
     "TRANSFER_FRACTAL_NZ_ND", "TRANSFER_TRANSPOSE", "shard_range", "enable_peer_access",
-    "p2p_copy", "p2p_ring_shift", "ipc_get_handle", "ipc_open_handle", "ipc_close_handle",
+    "p2p_copy", "set_p2p_engine", "P2P_ENGINE_AUTO", "P2P_ENGINE_SM", "P2P_ENGINE_COPY",
+    "p2p_route", "P2P_ROUTE_COPY_ENGINE", "P2P_ROUTE_SM_BULK_PUSH", "P2P_ROUTE_SM_LOAD_STORE",
+    "p2p_ring_shift", "ipc_get_handle", "ipc_open_handle", "ipc_close_handle",
     "signal", "wait_signal", "p2p_error", "tma_error", "DcopyDevCopy", "copy_ext_multi", "DcopyMemcpyInfo", "memcpy_async",
     "MEMCPY_KIND",
     "OK", "ERR_PARAM_INVALID", "ERR_SHAPE_INVALID", "ERR_DATATYPE_INVALID",
@@ -97,6 +99,13 @@ class DcopyPadParams(ctypes.Structure):
                 ("rightPadding", ctypes.c_uint8), ("reserved", ctypes.c_uint8),
                 ("elemBytes", ctypes.c_uint32), ("paddingValue", ctypes.c_uint64)]
 
+
+P2P_ENGINE_AUTO = 0  # pushes of >= 1 MiB on the copy engine, the rest on SM kernels
+P2P_ENGINE_SM = 1    # SM kernels only
+P2P_ENGINE_COPY = 2  # the copy engine for every p2p_copy
+P2P_ROUTE_COPY_ENGINE = 0
+P2P_ROUTE_SM_BULK_PUSH = 1
+P2P_ROUTE_SM_LOAD_STORE = 2
 
 PAD_NORMAL = 0   # AscendC::PaddingMode::Normal
 PAD_COMPACT = 1  # AscendC::PaddingMode::Compact
@@ -231,6 +240,8 @@ _SIGNATURES = {
     "dcopy_ipc_open_handle": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
     "dcopy_ipc_close_handle": (ctypes.c_int, [_vp]),
     "dcopy_p2p_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32)]),
+    "dcopy_set_p2p_engine": (ctypes.c_int, [ctypes.c_int32, ctypes.POINTER(ctypes.c_int32)]),
+    "dcopy_p2p_route": (ctypes.c_int, [_vp, _vp, ctypes.c_uint64, ctypes.POINTER(ctypes.c_int32)]),
     "dcopy_signal": (ctypes.c_int, [_vp, ctypes.c_uint32, _vp]),
     "dcopy_wait_signal": (ctypes.c_int, [_vp, ctypes.c_uint32, ctypes.c_uint64, _vp, _vp]),
     "dcopy_tma_error": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32)]),
@@ -654,8 +665,24 @@ def enable_peer_access(device: int, peer: int) -> None:
 
 
 def p2p_copy(dst, src, nbytes: int, stream=None) -> None:
-    """nbytes from local src to dst (this GPU's or a peer's memory), pushed over NVLink."""
+    """nbytes from src to dst (this GPU's or a peer's memory): pushes of >= 1 MiB on the
+    copy engine, shorter pushes and pulls on SM kernels (see set_p2p_engine)."""
     _check(lib().dcopy_p2p_copy(_ptr(dst), _ptr(src), nbytes, _stream(stream)), "dcopy_p2p_copy")
+
+
+def set_p2p_engine(engine: int) -> int:
+    """Selects p2p_copy's engine (P2P_ENGINE_AUTO / _SM / _COPY, process-wide);
+    returns the former setting."""
+    prev = ctypes.c_int32(0)
+    _check(lib().dcopy_set_p2p_engine(int(engine), ctypes.byref(prev)), "dcopy_set_p2p_engine")
+    return prev.value
+
+
+def p2p_route(dst, src, nbytes: int) -> int:
+    """The route p2p_copy would take (P2P_ROUTE_*), on the current device."""
+    r = ctypes.c_int32(-1)
+    _check(lib().dcopy_p2p_route(_ptr(dst), _ptr(src), nbytes, ctypes.byref(r)), "dcopy_p2p_route")
+    return r.value
 
 
 def p2p_ring_shift(devices, srcs, dsts, nbytes: int, streams=None) -> None:

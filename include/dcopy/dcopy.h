@@ -150,8 +150,8 @@ int dcopy_copy_ext(void *dst, const void *src, const DcopyExtParams *params,
  * directions are busy at once.  The return write is the copy kernel (dst must
  * be pinned host memory) unless flags has DCOPY_STAGED_COPY_ENGINE_RETURN (any
  * host memory).  `stream` waits for the last write: the call is ordered on it.
- * Staging must hold at least two bursts; four chunks' worth keeps the pipeline
- * full.  Calls on one device share the return stream (they serialise there);
+ * Staging must hold at least two bursts; the whole transfer (six chunks) keeps
+ * the pipeline full.  Calls on one device share the return stream (they serialise there);
  * capturing one in a CUDA graph while another thread issues staged copies on
  * the same device is not supported.  No counterpart in the reference. */
 #define DCOPY_STAGED_COPY_ENGINE_RETURN 1
@@ -531,11 +531,32 @@ int dcopy_copy_ext_multi(const DcopyDevCopy *copies, int32_t n);
  * and released with the process; it changes no setting of the GPU itself. */
 int dcopy_enable_peer_access(int32_t device, int32_t peer);
 
-/* bytes from local `src` to `dst`, which may be another GPU's memory mapped into
- * this process (peer access or IPC).  A push of 16-byte granular buffers to
- * another GPU runs a bulk-copy (TMA, no multicast) pipeline: local loads into
- * shared memory, bulk stores over NVLink; other cases use 128-bit load/store. */
+/* bytes from `src` to `dst`, either of which may be another GPU's memory mapped
+ * into this process (peer access or IPC), on `stream`.  Engine (see
+ * dcopy_set_p2p_engine), automatic choice: a push (src this GPU's memory, dst
+ * not) of at least 1 MiB runs on the copy engine; a shorter push of 16-byte
+ * granular buffers runs an SM bulk-copy (TMA, no multicast) pipeline -- local
+ * loads into shared memory, bulk stores over NVLink; every other case (pulls,
+ * unaligned spans) the 128-bit load/store kernel.  No counterpart in the
+ * reference (its multi-device transfers go through HCCL). */
 int dcopy_p2p_copy(void *dst, const void *src, uint64_t bytes, dcopy_stream_t stream);
+
+/* Engine selection of dcopy_p2p_copy for the whole process; *previous (may be
+ * NULL) receives the former setting.  AUTO as above; SM: the kernels only;
+ * COPY: the copy engine for every transfer.  The initial setting is
+ * DCOPY_P2P_ENGINE from the environment (auto, sm or copy; unset: auto). */
+#define DCOPY_P2P_ENGINE_AUTO 0
+#define DCOPY_P2P_ENGINE_SM 1
+#define DCOPY_P2P_ENGINE_COPY 2
+int dcopy_set_p2p_engine(int32_t engine, int32_t *previous);
+
+/* The route dcopy_p2p_copy(dst, src, bytes, ...) takes under the current engine
+ * setting and the current device, without copying anything or checking the
+ * buffers: the copy engine, the SM bulk-copy push, or the SM load/store kernel. */
+#define DCOPY_P2P_ROUTE_COPY_ENGINE 0
+#define DCOPY_P2P_ROUTE_SM_BULK_PUSH 1
+#define DCOPY_P2P_ROUTE_SM_LOAD_STORE 2
+int dcopy_p2p_route(const void *dst, const void *src, uint64_t bytes, int32_t *route);
 
 /* Reads and clears the current device's P2P error word: 1 when a bulk-copy
  * push gave up waiting on one of its own copies (the copy is then incomplete),
@@ -552,7 +573,10 @@ int dcopy_p2p_ring_shift(const int32_t *devices, void *const *src, void *const *
 /* CUDA IPC (multi-process): the 64-byte handle of the allocation holding
  * dev_ptr and dev_ptr's byte offset inside it; another process of the same node
  * opens the handle (peer access enabled lazily) and adds the offset.  Close the
- * BASE pointer that dcopy_ipc_open_handle returned. */
+ * BASE pointer that dcopy_ipc_open_handle returned.  The library records every
+ * mapping opened here until it is closed: the driver reports an IPC mapping as
+ * memory of the opening GPU, and the record is what makes dcopy_p2p_copy treat
+ * a copy into it as a push to another GPU. */
 #define DCOPY_IPC_HANDLE_BYTES 64
 int dcopy_ipc_get_handle(const void *dev_ptr, void *handle, uint64_t *offset);
 int dcopy_ipc_open_handle(const void *handle, void **base_ptr);

@@ -3,6 +3,7 @@ host-only entry points (planner, NZ shape rules, status mapping, argument
 validation that precedes any launch) agree with the oracle and the reference.
 No kernel is launched here."""
 import json
+import os
 import re
 
 import pytest
@@ -153,6 +154,46 @@ def test_nd_tma_selection_round_trips(dcopy):
     first = dcopy.set_nd_tma(True)
     assert dcopy.set_nd_tma(False) is True
     assert dcopy.set_nd_tma(first) is False
+
+
+def test_p2p_engine_selection(dcopy):
+    """dcopy_set_p2p_engine is host state only: it reports the former setting and
+    refuses an unknown engine without changing the current one."""
+    first = dcopy.set_p2p_engine(dcopy.P2P_ENGINE_SM)
+    assert dcopy.set_p2p_engine(dcopy.P2P_ENGINE_COPY) == dcopy.P2P_ENGINE_SM
+    with pytest.raises(dcopy.DcopyError):
+        dcopy.set_p2p_engine(3)
+    assert dcopy.set_p2p_engine(first) == dcopy.P2P_ENGINE_COPY
+
+
+def test_p2p_route_follows_the_engine(dcopy):
+    """The route query needs no GPU for the forced engines: COPY routes every copy
+    to the copy engine; with SM, memory that is not this GPU's (here: none is)
+    takes the load/store kernel."""
+    prev = dcopy.set_p2p_engine(dcopy.P2P_ENGINE_COPY)
+    try:
+        assert dcopy.p2p_route(0x1000, 0x2000, 1 << 30) == dcopy.P2P_ROUTE_COPY_ENGINE
+        dcopy.set_p2p_engine(dcopy.P2P_ENGINE_SM)
+        assert dcopy.p2p_route(0x1000, 0x2000, 1 << 30) == dcopy.P2P_ROUTE_SM_LOAD_STORE
+    finally:
+        dcopy.set_p2p_engine(prev)
+    assert dcopy.lib().dcopy_p2p_route(None, None, 0, None) == dcopy.ERR_PARAM_INVALID
+
+
+@pytest.mark.parametrize("value,engine", [(None, 0), ("sm", 1), ("copy", 2), ("2", 2),
+                                          ("bogus", 0)])
+def test_p2p_engine_from_environment(value, engine):
+    """DCOPY_P2P_ENGINE sets the initial engine; unset or unknown means automatic."""
+    import subprocess
+    import sys
+    env = {k: v for k, v in os.environ.items() if k != "DCOPY_P2P_ENGINE"}
+    if value is not None:
+        env["DCOPY_P2P_ENGINE"] = value
+    code = ("import sys; sys.path.insert(0, sys.argv[1]); import dcopy; "
+            "print(dcopy.set_p2p_engine(0))")
+    out = subprocess.run([sys.executable, "-c", code, str(ROOT / "data-copy_b200")], env=env, check=True,
+                         capture_output=True, text=True).stdout
+    assert int(out.strip()) == engine
 
 
 def test_copy_ext_batch_argument_checks(dcopy):

@@ -206,8 +206,9 @@ def test_nchw_to_fractal_z_bulk_tiles(torch_cuda, dcopy, oracle, weight, eb, c0)
     ((1, 1, 256, 1000), 2, 16),
 ], ids=lambda v: "x".join(map(str, v)) if isinstance(v, tuple) else str(v))
 def test_hwcn_to_fractal_z_tensor_tiles(torch_cuda, dcopy, oracle, shape, eb, c0):
-    """HWCN -> FRACTAL_Z with whole channel blocks and 16-byte output rows: the
-    tensor-copied, double-buffered tile kernel, against the oracle byte for byte."""
+    """HWCN -> FRACTAL_Z with whole channel blocks and 16-byte output rows (the
+    tensor-copied, double-buffered tile kernel for 1- and 2-byte elements, the vector
+    kernel for 4-byte ones), against the oracle byte for byte."""
     torch = torch_cuda
     shape = list(shape)
     src_np = _rand(int(np.prod(shape)) * eb, sum(shape) * 3 + eb)

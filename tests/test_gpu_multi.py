@@ -58,13 +58,32 @@ def test_wait_signal_counts_a_flag_already_past(torch_cuda, dcopy):
     assert status.item() == 1
 
 
-def test_p2p_copy_same_device(torch_cuda, dcopy):
+def test_p2p_copy_same_device(torch_cuda, dcopy, p2p_engine):
     torch = torch_cuda
     src = torch.randint(0, 255, (1 << 20,), dtype=torch.uint8, device="cuda")
     dst = torch.zeros_like(src)
     dcopy.p2p_copy(dst, src, src.numel())
     torch.cuda.synchronize()
     assert torch.equal(src, dst)
+    want = dcopy.P2P_ROUTE_COPY_ENGINE if p2p_engine == "copy" else dcopy.P2P_ROUTE_SM_LOAD_STORE
+    assert dcopy.p2p_route(dst, src, src.numel()) == want
+
+
+def test_p2p_route_to_a_peer(torch_cuda, dcopy):
+    """Pushes to another GPU's allocation: >= 1 MiB on the copy engine, shorter
+    16-byte granular ones on the bulk-copy push, ragged ones on the load/store
+    kernel; a pull (launched on the receiver) stays on the load/store kernel."""
+    torch = torch_cuda
+    _need_gpus(torch, 2)
+    src = torch.empty(4 << 20, dtype=torch.uint8, device="cuda:0")
+    dst = torch.empty(4 << 20, dtype=torch.uint8, device="cuda:1")
+    with torch.cuda.device(0):
+        assert dcopy.p2p_route(dst, src, 4 << 20) == dcopy.P2P_ROUTE_COPY_ENGINE
+        assert dcopy.p2p_route(dst, src, 1 << 20) == dcopy.P2P_ROUTE_COPY_ENGINE
+        assert dcopy.p2p_route(dst, src, (1 << 20) - 16) == dcopy.P2P_ROUTE_SM_BULK_PUSH
+        assert dcopy.p2p_route(dst, src, 1000) == dcopy.P2P_ROUTE_SM_LOAD_STORE
+    with torch.cuda.device(1):
+        assert dcopy.p2p_route(dst, src, 4 << 20) == dcopy.P2P_ROUTE_SM_LOAD_STORE
 
 
 def test_copy_ext_multi_two_devices(torch_cuda, dcopy):
@@ -80,7 +99,19 @@ def test_copy_ext_multi_two_devices(torch_cuda, dcopy):
         assert torch.equal(dsts[d], srcs[d].view(count, blen + gap)[:, :blen].reshape(-1))
 
 
-def test_ring_shift_single_process(torch_cuda, dcopy):
+@pytest.fixture(params=["auto", "sm", "copy"])
+def p2p_engine(request, dcopy):
+    """Each engine of dcopy_p2p_copy in turn; the former setting is restored."""
+    engine = {"auto": dcopy.P2P_ENGINE_AUTO, "sm": dcopy.P2P_ENGINE_SM,
+              "copy": dcopy.P2P_ENGINE_COPY}[request.param]
+    prev = dcopy.set_p2p_engine(engine)
+    yield request.param
+    dcopy.set_p2p_engine(prev)
+
+
+def test_ring_shift_single_process(torch_cuda, dcopy, p2p_engine):
+    """64 MiB pushes (the copy engine under the automatic choice, the bulk-copy
+    pipeline with the SM engine) and ragged ones, whole buffers compared."""
     torch = torch_cuda
     _need_gpus(torch, 2)
     n = min(torch.cuda.device_count(), 4)
@@ -136,6 +167,15 @@ def _ipc_rank(rank, world, port, outdir):
         torch.cuda.synchronize()
         dist.barrier()
         peer = multi.map_next_peer(recv, flags, rank, world)
+        # The IPC mapping is another GPU's memory: a 32 MiB push goes to the copy
+        # engine under the automatic choice, to the bulk-copy push with the SM engine.
+        route = dcopy.p2p_route(peer.recv_ptr, src, nbytes)
+        assert route == dcopy.P2P_ROUTE_COPY_ENGINE, f"route {route}"
+        prev = dcopy.set_p2p_engine(dcopy.P2P_ENGINE_SM)
+        route = dcopy.p2p_route(peer.recv_ptr, src, nbytes)
+        dcopy.set_p2p_engine(prev)
+        assert route == dcopy.P2P_ROUTE_SM_BULK_PUSH, f"SM route {route}"
+        assert dcopy.p2p_route(recv, src, nbytes) == dcopy.P2P_ROUTE_SM_LOAD_STORE
         multi.ring_shift(src, nbytes, peer, seq=1)
         multi.wait_ring(flags, 1, status, timeout_ns=10_000_000_000)
         torch.cuda.synchronize()
