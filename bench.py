@@ -497,7 +497,7 @@ def ring_shift_measure(torch, dcopy, dev, rank, world, barrier, dist, steps):
             "sm_push_per_direction_GBps": round(sm[0], 1),
             "copy_engine_per_direction_GBps": round(ce[0], 1),
             "bytes_per_rank_per_step": shard, "steps": max(2, min(steps, 10)),
-            "path": "dcopy_p2p_copy, automatic engine (pushes of >= 1 MiB on the copy engine) "
+            "path": "dcopy_p2p_copy, automatic engine (pushes on the copy engine) "
                     "into the next rank's IPC-mapped buffer + release-store flag kernel; "
                     "bounded device-side wait kernel on this rank's flag",
             "sm_push_path": "the same with dcopy_set_p2p_engine(SM): p2p_bulk_push_kernel",

@@ -1,15 +1,17 @@
 // Multi-GPU pieces: shard ranges, per-device launches, NVLink P2P copies, CUDA
 // IPC mappings and bounded completion flags.
 //
-// The P2P copy picks its engine.  A push of at least 1 MiB from this GPU to
-// another GPU's memory goes to the copy engine (cudaMemcpyAsync on the caller's
-// stream): in an exchange it moves 766-775 GB/s per direction over NV18, where
-// every SM-issued write path measured settles at 689-715 (bulk-copy pipelines of
-// 8-64 KiB chunks, 2-8 stages, 1-4 CTAs per SM; 128-bit stores; half SM + half
-// engine at 735).  Shorter or unaligned pushes run the SM bulk-copy pipeline
-// (local loads into shared memory, bulk stores over NVLink), and pulls (launched
-// on the receiving GPU, 786 GB/s one way) the 128-bit load/store kernel.
-// dcopy_set_p2p_engine forces either engine.
+// The P2P copy picks its engine.  A push from this GPU to another GPU's memory
+// goes to the copy engine (cudaMemcpyAsync on the caller's stream): in an
+// exchange of 1 GiB per direction over NV18 it moves 766-775 GB/s, where every
+// SM-issued write path measured settles at 689-715 (bulk-copy pipelines of 8-64
+// KiB chunks, 2-8 stages, 1-4 CTAs per SM; 128-bit stores; half SM + half engine
+// at 735), and it also wins at every shorter size measured (one way, GB/s, copy
+// engine vs SM bulk push: 64 KiB 18.0 vs 10.4, 256 KiB 69.7 vs 51.9, 1 MiB 213 vs
+// 176, 16 MiB 620 vs 591).  Pulls (launched on the receiving GPU, 786 GB/s one
+// way) run the 128-bit load/store kernel.  With the SM engine forced
+// (dcopy_set_p2p_engine) pushes run the SM bulk-copy pipeline: local loads into
+// shared memory, bulk stores over NVLink.
 // Completion flags use st.release.sys / ld.acquire.sys on a caller-owned word;
 // the waiting kernel has a time bound and an iteration bound and reports a
 // timeout through a caller-owned status word instead of hanging.
@@ -26,9 +28,6 @@
 
 #ifndef DCOPY_P2P_BULK
 #define DCOPY_P2P_BULK 1
-#endif
-#ifndef DCOPY_P2P_COPY_ENGINE_MIN_KIB
-#define DCOPY_P2P_COPY_ENGINE_MIN_KIB 1024  // shortest push the automatic choice hands to the copy engine
 #endif
 
 namespace dcopy {
@@ -222,9 +221,7 @@ __global__ void __launch_bounds__(32) p2p_bulk_push_kernel(uint8_t *__restrict__
 int p2p_route(const void *dst, const void *src, uint64_t bytes) {
   const int engine = p2p_engine();
   const bool push = is_local_device_memory(src) && !is_local_device_memory(dst);
-  if (engine == DCOPY_P2P_ENGINE_COPY ||
-      (engine == DCOPY_P2P_ENGINE_AUTO && push &&
-       bytes >= (uint64_t)DCOPY_P2P_COPY_ENGINE_MIN_KIB * 1024))
+  if (engine == DCOPY_P2P_ENGINE_COPY || (engine == DCOPY_P2P_ENGINE_AUTO && push))
     return DCOPY_P2P_ROUTE_COPY_ENGINE;
   if (DCOPY_P2P_BULK && push && ((uintptr_t)dst | (uintptr_t)src | bytes) % 16 == 0)
     return DCOPY_P2P_ROUTE_SM_BULK_PUSH;

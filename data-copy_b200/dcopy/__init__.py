@@ -100,7 +100,7 @@ class DcopyPadParams(ctypes.Structure):
                 ("elemBytes", ctypes.c_uint32), ("paddingValue", ctypes.c_uint64)]
 
 
-P2P_ENGINE_AUTO = 0  # pushes of >= 1 MiB on the copy engine, the rest on SM kernels
+P2P_ENGINE_AUTO = 0  # pushes on the copy engine, pulls and local copies on the SM kernel
 P2P_ENGINE_SM = 1    # SM kernels only
 P2P_ENGINE_COPY = 2  # the copy engine for every p2p_copy
 P2P_ROUTE_COPY_ENGINE = 0
@@ -665,8 +665,8 @@ def enable_peer_access(device: int, peer: int) -> None:
 
 
 def p2p_copy(dst, src, nbytes: int, stream=None) -> None:
-    """nbytes from src to dst (this GPU's or a peer's memory): pushes of >= 1 MiB on the
-    copy engine, shorter pushes and pulls on SM kernels (see set_p2p_engine)."""
+    """nbytes from src to dst (this GPU's or a peer's memory): pushes on the copy engine,
+    pulls on the SM load/store kernel (see set_p2p_engine)."""
     _check(lib().dcopy_p2p_copy(_ptr(dst), _ptr(src), nbytes, _stream(stream)), "dcopy_p2p_copy")
 
 

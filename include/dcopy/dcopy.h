@@ -534,11 +534,12 @@ int dcopy_enable_peer_access(int32_t device, int32_t peer);
 /* bytes from `src` to `dst`, either of which may be another GPU's memory mapped
  * into this process (peer access or IPC), on `stream`.  Engine (see
  * dcopy_set_p2p_engine), automatic choice: a push (src this GPU's memory, dst
- * not) of at least 1 MiB runs on the copy engine; a shorter push of 16-byte
- * granular buffers runs an SM bulk-copy (TMA, no multicast) pipeline -- local
- * loads into shared memory, bulk stores over NVLink; every other case (pulls,
- * unaligned spans) the 128-bit load/store kernel.  No counterpart in the
- * reference (its multi-device transfers go through HCCL). */
+ * not) runs on the copy engine, which measured faster than every SM write path
+ * at every size from 64 KiB to 1 GiB; every other case (pulls, local copies)
+ * runs the 128-bit load/store kernel.  With the SM engine forced, a push of
+ * 16-byte granular buffers runs an SM bulk-copy (TMA, no multicast) pipeline --
+ * local loads into shared memory, bulk stores over NVLink.  No counterpart in
+ * the reference (its multi-device transfers go through HCCL). */
 int dcopy_p2p_copy(void *dst, const void *src, uint64_t bytes, dcopy_stream_t stream);
 
 /* Engine selection of dcopy_p2p_copy for the whole process; *previous (may be

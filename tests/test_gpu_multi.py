@@ -70,18 +70,23 @@ def test_p2p_copy_same_device(torch_cuda, dcopy, p2p_engine):
 
 
 def test_p2p_route_to_a_peer(torch_cuda, dcopy):
-    """Pushes to another GPU's allocation: >= 1 MiB on the copy engine, shorter
-    16-byte granular ones on the bulk-copy push, ragged ones on the load/store
-    kernel; a pull (launched on the receiver) stays on the load/store kernel."""
+    """Pushes to another GPU's allocation run on the copy engine (any size); with the
+    SM engine forced, 16-byte granular pushes run the bulk-copy push and ragged ones
+    the load/store kernel; a pull (launched on the receiver) stays on the load/store
+    kernel."""
     torch = torch_cuda
     _need_gpus(torch, 2)
     src = torch.empty(4 << 20, dtype=torch.uint8, device="cuda:0")
     dst = torch.empty(4 << 20, dtype=torch.uint8, device="cuda:1")
     with torch.cuda.device(0):
-        assert dcopy.p2p_route(dst, src, 4 << 20) == dcopy.P2P_ROUTE_COPY_ENGINE
-        assert dcopy.p2p_route(dst, src, 1 << 20) == dcopy.P2P_ROUTE_COPY_ENGINE
-        assert dcopy.p2p_route(dst, src, (1 << 20) - 16) == dcopy.P2P_ROUTE_SM_BULK_PUSH
-        assert dcopy.p2p_route(dst, src, 1000) == dcopy.P2P_ROUTE_SM_LOAD_STORE
+        for n in (4 << 20, 1 << 20, 4096, 1000):
+            assert dcopy.p2p_route(dst, src, n) == dcopy.P2P_ROUTE_COPY_ENGINE
+        prev = dcopy.set_p2p_engine(dcopy.P2P_ENGINE_SM)
+        try:
+            assert dcopy.p2p_route(dst, src, 4 << 20) == dcopy.P2P_ROUTE_SM_BULK_PUSH
+            assert dcopy.p2p_route(dst, src, 1000) == dcopy.P2P_ROUTE_SM_LOAD_STORE
+        finally:
+            dcopy.set_p2p_engine(prev)
     with torch.cuda.device(1):
         assert dcopy.p2p_route(dst, src, 4 << 20) == dcopy.P2P_ROUTE_SM_LOAD_STORE
 
