@@ -16,6 +16,10 @@
 //                  [--device D]
 //       fp16 ND -> FRACTAL_NZ -> ND (or FRACTAL_ZZ), round trip
 //       verified.
+//   dcopy_bench pcie [--rows R] [--len L] [--pitch P] [--reps N] [--device D]
+//       The copy engine over PCIe as the staged host-to-host copy uses it: 2-D
+//       gathers host -> device, contiguous copies each way, each cut into 1, 4,
+//       16 and 64 copies, and both directions at once; one JSON line per case.
 //   dcopy_bench fz [--n N] [--c C] [--h H] [--w W] [--eb B] [--c0 C0] [--reps R]
 //                  [--device D] [--peak GBPS]
 //       Convolution weights: NCHW / NHWC / HWCN -> FRACTAL_Z -> back, each
@@ -54,6 +58,7 @@
 #include <cstdint>
 #include <cstring>
 #include <fstream>
+#include <functional>
 #include <iostream>
 #include <map>
 #include <memory>
@@ -428,6 +433,93 @@ int run_nz(const Args &a) {
             << ", \"frac_of_peak\": [" << g1 / peak << ", " << g2 / peak
             << "], \"round_trip_bit_exact\": true}" << std::endl;
   cudaStreamDestroy(s);
+  return 0;
+}
+
+// ---- pcie -------------------------------------------------------------------------
+
+// The copy engine over PCIe as dcopy_copy_ext_staged drives it: the 2-D gather
+// host -> device of `rows` bursts of `len` bytes out of `pitch`-byte host rows,
+// a contiguous host -> device copy of the same bytes, and the return device ->
+// host; each cut into k copies issued back to back on one stream (which shows
+// the cost of one copy), then a gather and a return on two streams at once
+// (the duplex rate each direction gets).  Host buffers are pinned.  One JSON
+// line per case, the median of `reps` timed repetitions.
+int run_pcie(const Args &a) {
+  const uint64_t rows = uint64_t(a.num("rows", 4096)), len = uint64_t(a.num("len", 4096));
+  const uint64_t pitch = uint64_t(a.num("pitch", 16384));
+  const int reps = int(a.num("reps", 5));
+  if (pitch < len) throw std::runtime_error("pcie: pitch < len");
+  Check(cudaSetDevice(int(a.num("device", 0))), "cudaSetDevice");
+  const uint64_t bytes = rows * len;
+  void *h_src = nullptr, *h_dst = nullptr;
+  Check(cudaHostAlloc(&h_src, rows * pitch, cudaHostAllocDefault), "cudaHostAlloc");
+  Check(cudaHostAlloc(&h_dst, bytes, cudaHostAllocDefault), "cudaHostAlloc");
+  DevBuf d(bytes), d2(bytes);
+  cudaStream_t st[2];
+  for (auto &x : st) Check(cudaStreamCreateWithFlags(&x, cudaStreamNonBlocking), "stream");
+  cudaEvent_t start, end[2];
+  Check(cudaEventCreate(&start), "event");
+  for (auto &e : end) Check(cudaEventCreate(&e), "event");
+  auto *hs = static_cast<uint8_t *>(h_src);
+  auto *hd = static_cast<uint8_t *>(h_dst);
+  auto *dd = static_cast<uint8_t *>(d.p);
+  auto *dd2 = static_cast<uint8_t *>(d2.p);
+  auto gather = [&](int k, cudaStream_t x) {
+    const uint64_t per = rows / k;
+    for (int i = 0; i < k; ++i)
+      Check(cudaMemcpy2DAsync(dd + i * per * len, len, hs + i * per * pitch, pitch, len, per,
+                              cudaMemcpyHostToDevice, x), "gather");
+  };
+  auto h2d = [&](int k, cudaStream_t x) {
+    const uint64_t per = bytes / k;
+    for (int i = 0; i < k; ++i)
+      Check(cudaMemcpyAsync(dd2 + i * per, hs + i * per, per, cudaMemcpyHostToDevice, x), "h2d");
+  };
+  auto d2h = [&](int k, cudaStream_t x) {
+    const uint64_t per = bytes / k;
+    for (int i = 0; i < k; ++i)
+      Check(cudaMemcpyAsync(hd + i * per, dd + i * per, per, cudaMemcpyDeviceToHost, x), "d2h");
+  };
+  // Median over reps of the span from `start` (both streams wait on it) to the
+  // later of the two streams' end events.
+  auto timed = [&](const std::function<void()> &issue) {
+    issue();  // warm-up
+    Check(cudaDeviceSynchronize(), "sync");
+    std::vector<double> us;
+    for (int r = 0; r < reps; ++r) {
+      Check(cudaEventRecord(start, st[0]), "record");
+      Check(cudaStreamWaitEvent(st[1], start, 0), "wait");
+      issue();
+      for (int i = 0; i < 2; ++i) Check(cudaEventRecord(end[i], st[i]), "record");
+      Check(cudaDeviceSynchronize(), "sync");
+      double worst = 0;
+      for (int i = 0; i < 2; ++i) {
+        float ms = 0;
+        Check(cudaEventElapsedTime(&ms, start, end[i]), "elapsed");
+        worst = std::max(worst, double(ms) * 1e3);
+      }
+      us.push_back(worst);
+    }
+    return median(us);
+  };
+  auto line = [&](const char *name, int k, double us, int directions) {
+    std::cout << "{\"pcie\": \"" << name << "\", \"copies\": " << k << ", \"bytes_per_direction\": "
+              << bytes << ", \"us\": " << us << ", \"GBps_per_direction\": " << bytes / (us * 1e3)
+              << ", \"directions\": " << directions << "}" << std::endl;
+  };
+  for (int k : {1, 4, 16, 64}) {
+    line("gather2d_h2d", k, timed([&] { gather(k, st[0]); }), 1);
+    line("contiguous_h2d", k, timed([&] { h2d(k, st[0]); }), 1);
+    line("contiguous_d2h", k, timed([&] { d2h(k, st[0]); }), 1);
+  }
+  line("gather2d_h2d+d2h", 1, timed([&] { gather(1, st[0]); d2h(1, st[1]); }), 2);
+  line("contiguous_h2d+d2h", 1, timed([&] { h2d(1, st[0]); d2h(1, st[1]); }), 2);
+  cudaEventDestroy(start);
+  for (auto &e : end) cudaEventDestroy(e);
+  for (auto &x : st) cudaStreamDestroy(x);
+  cudaFreeHost(h_src);
+  cudaFreeHost(h_dst);
   return 0;
 }
 
@@ -844,7 +936,7 @@ int run_p2p(const Args &a) {
 
 int main(int argc, char **argv) {
   try {
-    if (argc < 2) throw std::runtime_error("usage: dcopy_bench sweep|standalone|nz|fz|transpose|nd|batch|p2p [options]");
+    if (argc < 2) throw std::runtime_error("usage: dcopy_bench sweep|standalone|nz|fz|transpose|nd|batch|p2p|pcie [options]");
     const std::string cmd = argv[1];
     Args a(argc, argv);
     // --l2-fetch B: the context's L2 fetch-granularity hint (cudaLimitMaxL2FetchGranularity,
@@ -862,6 +954,7 @@ int main(int argc, char **argv) {
     if (cmd == "nz") return run_nz(a);
     if (cmd == "p2p") return run_p2p(a);
     if (cmd == "fz") return run_fz(a);
+    if (cmd == "pcie") return run_pcie(a);
     if (cmd == "transpose") return run_transpose(a);
     if (cmd == "nd") return run_nd(a);
     if (cmd == "batch") return run_batch(a);

@@ -882,11 +882,15 @@ __global__ void __launch_bounds__(kThreads) fz_hwcn_tensor_kernel(unsigned char 
 }
 
 #ifndef DCOPY_FZ_HWCN_TMA
-// HWCN -> FRACTAL_Z through fz_hwcn_tensor_kernel for 1- and 2-byte elements.
-// Measured on B200 (two interleaved rounds, GB/s against fz_vec_kernel): int8
-// [2048,2048,3,3] 4089-4096 vs 3686-3692, fp16 3x3 4999-5098 vs 4915-4918, fp16
-// 1x1 (C 8192) 4686-4692 vs 4096-4104, fp16 5x5 (C 1024) 5253-5324 vs 5392-5394;
-// fp32 3x3 4915 vs 5263-5268, so 4-byte elements keep the vector kernel.
+// HWCN -> FRACTAL_Z through fz_hwcn_tensor_kernel for 1-byte elements.  Measured
+// on B200 as bench.py does (CUDA graph replay of two alternating weight sets, no
+// L2 eviction; three interleaved rounds, GB/s against fz_vec_kernel): int8
+// [2048,2048,3,3] (c0 32) 4613-4619 vs 4331-4347; fp16 3x3 5111-5132 vs
+// 5457-5463, fp16 1x1 (C 8192) 4673-4675 vs 4868-4905, fp16 5x5 (C 1024)
+// 5267-5282 vs 5687-5690, fp16 [4096,2048,3,3] 5230-5247 vs 5876-5885.  (With
+// L2 evicted between reps the fp16 cases had read 2-14 % faster: that timing
+// leaves the writes still dirty in L2 untimed.)  fp32 3x3 was 7 % slower under
+// either timing.  So only 1-byte elements take this kernel.
 #define DCOPY_FZ_HWCN_TMA 1
 #endif
 
@@ -1099,7 +1103,7 @@ int launch_from_gather(void *dst, const void *src, const FzBGeom &g, int eb, int
 int run_hwcn_tensor(void *dst, const void *src, int64_t n, int64_t c, int64_t hw, int eb,
                     int64_t c0, cudaStream_t s, bool *taken) {
   *taken = false;
-  if (!DCOPY_FZ_HWCN_TMA || (eb != 1 && eb != 2)) return DCOPY_OK;
+  if (!DCOPY_FZ_HWCN_TMA || eb != 1) return DCOPY_OK;
   const int64_t V = 16 / eb;
   if (c0 <= 0 || (c0 & (c0 - 1)) || c0 % V || c0 > 256 || c % c0 || (n * eb) % 16) return DCOPY_OK;
   if (((uintptr_t)dst | (uintptr_t)src) % 16) return DCOPY_OK;
@@ -1114,7 +1118,7 @@ int run_hwcn_tensor(void *dst, const void *src, int64_t n, int64_t c, int64_t hw
   const uint64_t dims[2] = {(uint64_t)n, (uint64_t)(hw * c)};
   const uint64_t strides[1] = {(uint64_t)(n * eb)};
   const uint32_t box[2] = {(uint32_t)KT, (uint32_t)c0};
-  const CUtensorMapDataType dt = eb == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
+  const CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
   if (!encode_tiled_map(&map, dt, 2, const_cast<void *>(src), dims, strides, box,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
     return DCOPY_OK;
@@ -1131,15 +1135,14 @@ int run_hwcn_tensor(void *dst, const void *src, int64_t n, int64_t c, int64_t hw
   g.f_ktiles = FastDiv(g.ktiles);
   g.f_hw = FastDiv(g.HW);
   using Kern = void (*)(unsigned char *, FzHGeom, const CUtensorMap);
-  Kern k = eb == 1 ? fz_hwcn_tensor_kernel<1> : fz_hwcn_tensor_kernel<2>;
-  static std::atomic<bool> raised[2][128];
+  Kern k = fz_hwcn_tensor_kernel<1>;
+  static std::atomic<bool> raised[128];
   const int dev = current_device();
-  const int which = eb == 1 ? 0 : 1;
-  if (dev >= 0 && dev < 128 && !raised[which][dev].load()) {
+  if (dev >= 0 && dev < 128 && !raised[dev].load()) {
     const cudaError_t e =
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBulkSmemMax);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(fz_hwcn_tensor_kernel)");
-    raised[which][dev] = true;
+    raised[dev] = true;
   }
   int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kThreads, smem) != cudaSuccess ||

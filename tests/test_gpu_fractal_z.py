@@ -199,16 +199,18 @@ def test_nchw_to_fractal_z_bulk_tiles(torch_cuda, dcopy, oracle, weight, eb, c0)
 
 
 @pytest.mark.parametrize("shape,eb,c0", [
-    ((3, 3, 1024, 2048), 2, 16),   # 9216 tiles: every CTA cycles both stages several times
-    ((5, 5, 64, 200), 2, 16),      # N = 200: the last tile is partial, its padding zero-filled
+    ((3, 3, 1024, 2048), 2, 16),
+    ((5, 5, 64, 200), 2, 16),
+    ((3, 3, 1024, 2048), 1, 32),   # 2304 tiles: every CTA cycles both stages several times
+    ((5, 5, 64, 208), 1, 32),      # N = 208: the last tile is partial, its padding zero-filled
     ((3, 3, 64, 96), 1, 32),
     ((2, 2, 32, 80), 4, 16),
     ((1, 1, 256, 1000), 2, 16),
 ], ids=lambda v: "x".join(map(str, v)) if isinstance(v, tuple) else str(v))
 def test_hwcn_to_fractal_z_tensor_tiles(torch_cuda, dcopy, oracle, shape, eb, c0):
     """HWCN -> FRACTAL_Z with whole channel blocks and 16-byte output rows (the
-    tensor-copied, double-buffered tile kernel for 1- and 2-byte elements, the vector
-    kernel for 4-byte ones), against the oracle byte for byte."""
+    tensor-copied, double-buffered tile kernel for 1-byte elements, the vector kernel
+    for wider ones), against the oracle byte for byte."""
     torch = torch_cuda
     shape = list(shape)
     src_np = _rand(int(np.prod(shape)) * eb, sum(shape) * 3 + eb)
