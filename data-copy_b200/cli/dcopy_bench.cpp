@@ -20,6 +20,9 @@
 //       The copy engine over PCIe as the staged host-to-host copy uses it: 2-D
 //       gathers host -> device, contiguous copies each way, each cut into 1, 4,
 //       16 and 64 copies, and both directions at once; one JSON line per case.
+//   dcopy_bench staged [--calls C] [--reps R] [--device D]
+//       BASELINE config 2 end to end from pinned host memory through
+//       dcopy_copy_ext_staged: device time and host issue time per call, verified.
 //   dcopy_bench fz [--n N] [--c C] [--h H] [--w W] [--eb B] [--c0 C0] [--reps R]
 //                  [--device D] [--peak GBPS]
 //       Convolution weights: NCHW / NHWC / HWCN -> FRACTAL_Z -> back, each
@@ -523,6 +526,64 @@ int run_pcie(const Args &a) {
   return 0;
 }
 
+// ---- staged ---------------------------------------------------------------------
+
+// BASELINE config 2 end to end from pinned host memory through
+// dcopy_copy_ext_staged (copy-engine gather, copy-engine return, 16 MiB device
+// staging): `calls` back-to-back calls between CUDA events, the host time spent
+// issuing them, and a check of the result; one JSON line per repetition.
+int run_staged(const Args &a) {
+  const uint32_t rows = 4096, len = 4096, gap = 12288;
+  const int calls = int(a.num("calls", 30)), reps = int(a.num("reps", 3));
+  Check(cudaSetDevice(int(a.num("device", 0))), "cudaSetDevice");
+  const uint64_t src_bytes = uint64_t(rows) * (len + gap), bytes = uint64_t(rows) * len;
+  void *h_src = nullptr, *h_dst = nullptr;
+  Check(cudaHostAlloc(&h_src, src_bytes, cudaHostAllocDefault), "cudaHostAlloc");
+  Check(cudaHostAlloc(&h_dst, bytes, cudaHostAllocDefault), "cudaHostAlloc");
+  auto *hs = static_cast<uint8_t *>(h_src);
+  auto *hd = static_cast<uint8_t *>(h_dst);
+  for (uint64_t i = 0; i < src_bytes; ++i) hs[i] = uint8_t(i * 131 + (i >> 12));
+  DevBuf staging(16ull << 20);
+  cudaStream_t s;
+  Check(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "stream");
+  const DcopyExtParams p{rows, len, gap, 0};
+  auto call = [&] {
+    CheckD(dcopy_copy_ext_staged(h_dst, h_src, &p, staging.p, staging.n,
+                                 DCOPY_STAGED_COPY_ENGINE_RETURN,
+                                 reinterpret_cast<dcopy_stream_t>(s)));
+  };
+  for (int w = 0; w < 3; ++w) call();
+  Check(cudaStreamSynchronize(s), "sync");
+  cudaEvent_t e0, e1;
+  Check(cudaEventCreate(&e0), "event");
+  Check(cudaEventCreate(&e1), "event");
+  for (int r = 0; r < reps; ++r) {
+    std::memset(h_dst, 0xA5, bytes);
+    Check(cudaEventRecord(e0, s), "record");
+    const auto t0 = std::chrono::steady_clock::now();
+    for (int c = 0; c < calls; ++c) call();
+    const auto t1 = std::chrono::steady_clock::now();
+    Check(cudaEventRecord(e1, s), "record");
+    Check(cudaEventSynchronize(e1), "sync");
+    for (uint32_t row = 0; row < rows; ++row)
+      if (std::memcmp(hd + uint64_t(row) * len, hs + uint64_t(row) * (len + gap), len) != 0)
+        throw std::runtime_error("staged: result differs at row " + std::to_string(row));
+    float ms = 0;
+    Check(cudaEventElapsedTime(&ms, e0, e1), "elapsed");
+    const double dev_us = double(ms) * 1e3 / calls;
+    const double host_us = std::chrono::duration<double, std::micro>(t1 - t0).count() / calls;
+    std::cout << "{\"staged\": \"config2\", \"calls\": " << calls << ", \"GBps\": "
+              << 2.0 * bytes / (dev_us * 1e3) << ", \"device_us_per_call\": " << dev_us
+              << ", \"host_us_per_call\": " << host_us << ", \"verified\": true}" << std::endl;
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  cudaStreamDestroy(s);
+  cudaFreeHost(h_src);
+  cudaFreeHost(h_dst);
+  return 0;
+}
+
 // ---- fz ---------------------------------------------------------------------------
 
 int run_fz(const Args &a) {
@@ -936,7 +997,7 @@ int run_p2p(const Args &a) {
 
 int main(int argc, char **argv) {
   try {
-    if (argc < 2) throw std::runtime_error("usage: dcopy_bench sweep|standalone|nz|fz|transpose|nd|batch|p2p|pcie [options]");
+    if (argc < 2) throw std::runtime_error("usage: dcopy_bench sweep|standalone|nz|fz|transpose|nd|batch|p2p|pcie|staged [options]");
     const std::string cmd = argv[1];
     Args a(argc, argv);
     // --l2-fetch B: the context's L2 fetch-granularity hint (cudaLimitMaxL2FetchGranularity,
@@ -955,6 +1016,7 @@ int main(int argc, char **argv) {
     if (cmd == "p2p") return run_p2p(a);
     if (cmd == "fz") return run_fz(a);
     if (cmd == "pcie") return run_pcie(a);
+    if (cmd == "staged") return run_staged(a);
     if (cmd == "transpose") return run_transpose(a);
     if (cmd == "nd") return run_nd(a);
     if (cmd == "batch") return run_batch(a);
