@@ -414,11 +414,11 @@ def ring_shift_measure(torch, dcopy, dev, rank, world, barrier, dist, steps):
     rank (r+1) mod N's receive buffer over NVLink (dcopy_p2p_copy into the CUDA IPC
     mapping), release-stores a sequence number into that rank's flag, and waits for
     its own flag with a bounded device-side wait.  Every received shard is compared
-    whole with the sender's data.  Three runs on the same buffers: dcopy_p2p_copy
+    whole with the sender's data.  Four runs on the same buffers: dcopy_p2p_copy
     with its automatic engine choice (the reported path), the same call with the SM
-    engine forced (the bulk-copy push kernel), and cudaMemcpyAsync in place of
-    dcopy_p2p_copy (the comparator).  Timing: CUDA events on each rank's stream,
-    max over ranks."""
+    engine forced (the bulk-copy push kernel), cudaMemcpyAsync in place of
+    dcopy_p2p_copy, and NCCL send/recv of the same shards (the comparators).
+    Timing: CUDA events on each rank's stream, max over ranks."""
     from dcopy import multi
     from cuda.bindings import runtime as cudart
     shard = 1 << 30
@@ -441,9 +441,18 @@ def ring_shift_measure(torch, dcopy, dev, rank, world, barrier, dist, steps):
     seq = 0
     results = {}
     try:
+        nxt = (rank + 1) % world
+
         def exchange(engine):
             nonlocal seq
             seq += 1
+            if engine == "nccl":
+                # NCCL send/recv of the same shards: the current stream waits for
+                # NCCL's stream, so the events below bracket the transfer.
+                ops = [dist.P2POp(dist.isend, send, nxt), dist.P2POp(dist.irecv, recv, prev)]
+                for req in dist.batch_isend_irecv(ops):
+                    req.wait()
+                return
             if engine == "copy_engine":
                 err, = cudart.cudaMemcpyAsync(peer.recv_ptr, send.data_ptr(), shard,
                                               cudart.cudaMemcpyKind.cudaMemcpyDefault,
@@ -456,7 +465,7 @@ def ring_shift_measure(torch, dcopy, dev, rank, world, barrier, dist, steps):
             multi.wait_ring(flags, seq, status, timeout_ns=2_000_000_000, stream=stream)
 
         psteps = max(2, min(steps, 10))
-        for name in ("dcopy", "sm_push", "copy_engine"):
+        for name in ("dcopy", "sm_push", "copy_engine", "nccl"):
             prev_engine = dcopy.set_p2p_engine(
                 dcopy.P2P_ENGINE_SM if name == "sm_push" else dcopy.P2P_ENGINE_AUTO)
             engine = name
@@ -487,21 +496,24 @@ def ring_shift_measure(torch, dcopy, dev, rank, world, barrier, dist, steps):
     finally:
         barrier()
         peer.release()
-    main, sm, ce = results["dcopy"], results["sm_push"], results["copy_engine"]
+    main, sm, ce, nc = (results["dcopy"], results["sm_push"], results["copy_engine"],
+                        results["nccl"])
     return {"per_direction_GBps": round(main[0], 1), "aggregate_GBps": round(main[0] * world, 1),
             "nominal_GBps": 900.0, "frac_of_nominal": round(main[0] / 900.0, 4),
             "measured_peer_copy_GBps": 770.0,
             "frac_of_measured_peer_copy": round(main[0] / 770.0, 4),
-            "flags_ok": main[1] and sm[1] and ce[1] and err == 0,
+            "flags_ok": main[1] and sm[1] and ce[1] and nc[1] and err == 0,
             "shards_checked": "whole 1 GiB shard, every run",
             "sm_push_per_direction_GBps": round(sm[0], 1),
             "copy_engine_per_direction_GBps": round(ce[0], 1),
+            "nccl_send_recv_per_direction_GBps": round(nc[0], 1),
             "bytes_per_rank_per_step": shard, "steps": max(2, min(steps, 10)),
             "path": "dcopy_p2p_copy, automatic engine (pushes on the copy engine) "
                     "into the next rank's IPC-mapped buffer + release-store flag kernel; "
                     "bounded device-side wait kernel on this rank's flag",
             "sm_push_path": "the same with dcopy_set_p2p_engine(SM): p2p_bulk_push_kernel",
-            "comparator": "cudaMemcpyAsync in place of dcopy_p2p_copy, same flags"}
+            "comparator": "cudaMemcpyAsync in place of dcopy_p2p_copy, same flags; and NCCL "
+                          "send/recv (batch_isend_irecv) of the same shards"}
 
 
 def _time_graph(torch, fn, reps=10, warm=3):
