@@ -476,7 +476,33 @@ struct FzBGeom {
   uint32_t nblocks, ntiles, C1;
   FastDiv f_nblocks;
   uint64_t seg_stride, N1N0;     // global elements between weights; padded weight count
+  // Tile order (fz_tile): groups of gn weight blocks; inside a group the weight
+  // block varies fastest, then the channel block.  The last group holds gn_last
+  // blocks.  gn = nblocks is one group: weight blocks fastest over the whole tensor.
+  uint32_t gn, last_grp;
+  FastDiv f_group_tiles, f_gn, f_gn_last;  // gn * C1; gn; gn_last
 };
+
+// Tile t -> channel block c1 and weight block nb under the grouped order.
+__device__ __forceinline__ void fz_tile(const FzBGeom &g, uint32_t t, uint32_t *c1,
+                                        uint32_t *nb) {
+  const uint32_t grp = g.f_group_tiles.div(t);
+  const uint32_t r = t - grp * g.f_group_tiles.d;
+  const FastDiv &f = grp == g.last_grp ? g.f_gn_last : g.f_gn;
+  const uint32_t q = f.div(r);
+  *c1 = q;
+  *nb = grp * g.gn + (r - q * f.d);
+}
+
+// One group over the whole tensor (the order the kernels had before grouping).
+void fz_tile_groups(FzBGeom &g, uint32_t gn) {
+  gn = std::max(1u, std::min(gn, g.nblocks));
+  g.gn = gn;
+  g.last_grp = (g.nblocks - 1) / gn;
+  g.f_group_tiles = FastDiv(gn * g.C1);
+  g.f_gn = FastDiv(gn);
+  g.f_gn_last = FastDiv(g.nblocks - g.last_grp * gn);
+}
 
 __device__ uint32_t g_fz_error;
 
@@ -508,9 +534,11 @@ __global__ void __launch_bounds__(kThreads) fz_nchw_bulk_kernel(unsigned char *_
   __syncthreads();
   pdl_wait();
   pdl_launch_dependents();
-  // Tile t: channel block c1 = t / nblocks, weights n0 = (t % nblocks) * NB.
+  // Tile t: channel block c1 and weights n0 = nb * NB in the grouped order (fz_tile).
   auto issue = [&](uint32_t t, int st) {
-    const uint32_t c1 = g.f_nblocks.div(t), n0 = (t - c1 * g.nblocks) * g.NB;
+    uint32_t c1, nb;
+    fz_tile(g, t, &c1, &nb);
+    const uint32_t n0 = nb * g.NB;
     const uint32_t valid = n0 < g.N ? min(g.NB, g.N - n0) : 0;
     T *stage = reinterpret_cast<T *>(fzb_smem) + st * stage_elems;
     if constexpr (kTensor) {
@@ -565,7 +593,9 @@ __global__ void __launch_bounds__(kThreads) fz_nchw_bulk_kernel(unsigned char *_
       ok = false;
       break;
     }
-    const uint32_t c1 = g.f_nblocks.div(t), n0 = (t - c1 * g.nblocks) * g.NB;
+    uint32_t c1, nb;
+    fz_tile(g, t, &c1, &nb);
+    const uint32_t n0 = nb * g.NB;
     const T *stage = reinterpret_cast<const T *>(fzb_smem) + st * stage_elems;
     T *out = dst + ((uint64_t)c1 * g.HW * g.N1N0 + n0) * g.C0;
     const uint32_t lane = threadIdx.x & 31, q = (lane >> 2) & ((1u << g.lq) - 1);
@@ -630,7 +660,9 @@ __global__ void __launch_bounds__(kThreads) fz_to_nchw_bulk_kernel(unsigned char
   pdl_launch_dependents();
   auto issue = [&](uint32_t t, int st) {
     if (threadIdx.x >= 32) return;
-    const uint32_t c1 = g.f_nblocks.div(t), n0 = (t - c1 * g.nblocks) * g.NB;
+    uint32_t c1, nb;
+    fz_tile(g, t, &c1, &nb);
+    const uint32_t n0 = nb * g.NB;
     T *stage = reinterpret_cast<T *>(fzr_smem) + st * run_stage;
     if (threadIdx.x == 0)
       asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(
@@ -661,7 +693,9 @@ __global__ void __launch_bounds__(kThreads) fz_to_nchw_bulk_kernel(unsigned char
       ok = false;
       break;
     }
-    const uint32_t c1 = g.f_nblocks.div(t), n0 = (t - c1 * g.nblocks) * g.NB;
+    uint32_t c1, nb;
+    fz_tile(g, t, &c1, &nb);
+    const uint32_t n0 = nb * g.NB;
     const uint32_t valid = n0 < g.N ? min(g.NB, g.N - n0) : 0;
     const T *stage = reinterpret_cast<const T *>(fzr_smem) + st * run_stage;
     const uint32_t lane = threadIdx.x & 31, q = (lane >> 2) & ((1u << g.lq) - 1);
@@ -727,7 +761,9 @@ __global__ void __launch_bounds__(kThreads) fz_to_nchw_gather_kernel(unsigned ch
   pdl_launch_dependents();
   auto issue = [&](uint32_t t, int st) {
     if (threadIdx.x >= 32) return;
-    const uint32_t c1 = g.f_nblocks.div(t), n0 = (t - c1 * g.nblocks) * g.NB;
+    uint32_t c1, nb;
+    fz_tile(g, t, &c1, &nb);
+    const uint32_t n0 = nb * g.NB;
     T *stage = reinterpret_cast<T *>(fzg_smem) + st * run_stage;
     if (threadIdx.x == 0)
       asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(
@@ -756,7 +792,9 @@ __global__ void __launch_bounds__(kThreads) fz_to_nchw_gather_kernel(unsigned ch
       ok = false;
       break;
     }
-    const uint32_t c1 = g.f_nblocks.div(t), n0 = (t - c1 * g.nblocks) * g.NB;
+    uint32_t c1, nb;
+    fz_tile(g, t, &c1, &nb);
+    const uint32_t n0 = nb * g.NB;
     const uint32_t valid = n0 < g.N ? min(g.NB, g.N - n0) : 0;
     const T *stage = reinterpret_cast<const T *>(fzg_smem) + st * run_stage;
     T *out = dst + (uint64_t)n0 * g.seg_stride + (uint64_t)c1 * g.L;
@@ -920,6 +958,23 @@ __global__ void __launch_bounds__(kThreads) fz_hwcn_tensor_kernel(unsigned char 
 // elements keep the row copies.
 #define DCOPY_FZ_NCHW_TMA 1
 #endif
+#ifndef DCOPY_FZ_GROUP_TILES
+#define DCOPY_FZ_GROUP_TILES 1  // 0: one group (weight blocks fastest over the whole tensor)
+#endif
+#ifndef DCOPY_FZ_ROW_RUN
+// Bytes of an NCHW row that the resident tiles of the bulk / gather kernels
+// cover together (fz_tile_groups).  Measured on B200 (dcopy_bench fz --replay 1,
+// fp16 3x3 [N,2048] to / from FRACTAL_Z, GB/s, against one group over the whole
+// tensor): N 2048 5229-5244 / 5287-5291 vs 5187-5210 / 5113-5127, N 4096
+// 4931-4938 / 4929-4931 vs 4783-4786 / 4582-4585, N 8192 4980-4992 / 4738-4742
+// vs 4777-4779 / 4356-4361; fp16 5x5 [4096,1024] from 5580-5598 vs 5254-5265,
+// [2048,1024] from 5242-5247 vs 5337-5343; fp32 3x3 [4096,2048] 5216-5241 /
+// 5100-5104 vs 5134-5136 / 4935-5000.  16 and 32 KiB runs were in between.
+#define DCOPY_FZ_ROW_RUN 65536
+#endif
+#ifndef DCOPY_FZ_NCHW_TMA_PROMOTION
+#define DCOPY_FZ_NCHW_TMA_PROMOTION CU_TENSOR_MAP_L2_PROMOTION_L2_256B
+#endif
 #ifndef DCOPY_FZ_BULK_NB
 #define DCOPY_FZ_BULK_NB 64  // weights per tile (a power of two)
 #endif
@@ -963,6 +1018,7 @@ int run_nchw_bulk(void *dst, const void *src, int64_t n, int64_t c, int64_t hw, 
   if (ntiles == 0 || ntiles > 0x7FFFFFFFull) return DCOPY_OK;
   g.ntiles = (uint32_t)ntiles;
   g.f_nblocks = FastDiv(g.nblocks);
+  fz_tile_groups(g, g.nblocks);
   g.seg_stride = (uint64_t)(c * hw);
   g.N1N0 = (uint64_t)n1n0;
   const size_t smem = (size_t)(2 * nb * P * eb);
@@ -978,7 +1034,7 @@ int run_nchw_bulk(void *dst, const void *src, int64_t n, int64_t c, int64_t hw, 
                                    : eb == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16
                                              : CU_TENSOR_MAP_DATA_TYPE_UINT32;
     tensor = encode_tiled_map(&map, dt, 2, const_cast<void *>(src), dims, strides, box,
-                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+                              DCOPY_FZ_NCHW_TMA_PROMOTION);
   }
   using Kern = void (*)(unsigned char *, const unsigned char *, FzBGeom, const CUtensorMap);
   Kern k = tensor ? (eb == 1   ? fz_nchw_bulk_kernel<1, true>
@@ -1005,6 +1061,12 @@ int run_nchw_bulk(void *dst, const void *src, int64_t n, int64_t c, int64_t hw, 
   *taken = true;
   const uint32_t grid =
       (uint32_t)std::min<uint64_t>(ntiles, (uint64_t)per_sm * (uint64_t)sm_count());
+  // The resident tiles read, in every NCHW row, the segments of the channel
+  // blocks they cover: group the weight blocks so that run stays near
+  // DCOPY_FZ_ROW_RUN bytes (see fz_tile_groups).
+  if (DCOPY_FZ_GROUP_TILES)
+    fz_tile_groups(g, (uint32_t)std::max<uint64_t>(
+                          1, (uint64_t)grid * g.L * (uint64_t)eb / DCOPY_FZ_ROW_RUN));
   return launch(k, std::max(1u, grid), dim3(kThreads), smem, s, "fz_nchw_bulk_kernel",
                 static_cast<unsigned char *>(dst), static_cast<const unsigned char *>(src), g,
                 map);
@@ -1066,7 +1128,7 @@ uint32_t gather_run_pitch(int eb, int64_t c0, int64_t hw, int64_t nb) {
   return r;
 }
 
-int launch_from_gather(void *dst, const void *src, const FzBGeom &g, int eb, int64_t c0,
+int launch_from_gather(void *dst, const void *src, FzBGeom g, int eb, int64_t c0,
                        int64_t hw, int64_t nb, cudaStream_t s, bool *taken) {
   const uint32_t R = gather_run_pitch(eb, c0, hw, nb);
   const size_t smem = (size_t)2 * hw * R * eb;
@@ -1092,6 +1154,14 @@ int launch_from_gather(void *dst, const void *src, const FzBGeom &g, int eb, int
   *taken = true;
   const uint32_t grid =
       (uint32_t)std::min<uint64_t>(g.ntiles, (uint64_t)per_sm * (uint64_t)sm_count());
+  // The resident tiles write, in every NCHW row, the segments of the channel
+  // blocks they cover; grouping the weight blocks keeps that run of a row near
+  // DCOPY_FZ_ROW_RUN bytes however many weights there are (one group over all
+  // weight blocks left it at grid / nblocks segments: 2 KiB per row for 8192
+  // fp16 3x3 weights).  A run longer than the row covers whole rows.
+  if (DCOPY_FZ_GROUP_TILES)
+    fz_tile_groups(g, (uint32_t)std::max<uint64_t>(
+                          1, (uint64_t)grid * g.L * (uint64_t)eb / DCOPY_FZ_ROW_RUN));
   const uint32_t V = 16 / (uint32_t)eb;
   return launch(k, std::max(1u, grid), dim3(kThreads), smem, s, "fz_to_nchw_gather_kernel",
                 static_cast<unsigned char *>(dst), static_cast<const unsigned char *>(src), g, R,
@@ -1197,6 +1267,7 @@ int run_nchw_bulk_from(void *dst, const void *src, int64_t n, int64_t c, int64_t
   if (ntiles == 0 || ntiles > 0x7FFFFFFFull) return DCOPY_OK;
   g.ntiles = (uint32_t)ntiles;
   g.f_nblocks = FastDiv(g.nblocks);
+  fz_tile_groups(g, g.nblocks);
   g.seg_stride = (uint64_t)(c * hw);
   g.N1N0 = (uint64_t)n1n0;
   if (gather) return launch_from_gather(dst, src, g, eb, c0, hw, nb, s, taken);
@@ -1220,6 +1291,9 @@ int run_nchw_bulk_from(void *dst, const void *src, int64_t n, int64_t c, int64_t
   *taken = true;
   const uint32_t grid =
       (uint32_t)std::min<uint64_t>(ntiles, (uint64_t)per_sm * (uint64_t)sm_count());
+  if (DCOPY_FZ_GROUP_TILES)
+    fz_tile_groups(g, (uint32_t)std::max<uint64_t>(
+                          1, (uint64_t)grid * g.L * (uint64_t)eb / DCOPY_FZ_ROW_RUN));
   return launch(k, std::max(1u, grid), dim3(kThreads), smem, s, "fz_to_nchw_bulk_kernel",
                 static_cast<unsigned char *>(dst), static_cast<const unsigned char *>(src), g);
 }
