@@ -48,8 +48,17 @@ namespace {
 // 1: with the TMA paths selected, gapped 2-D bursts of 16 to 112 bytes (whole
 // 16-byte granules) move as 2-D tensor copies.  Measured on B200 (256 MiB moved,
 // against the load/store kernel): 32 B bursts with 4x / 16x gaps +5 % / +4 %,
-// 32 B with 1x gaps and every 64 B point -4 to -6 %; so it is not the default.
+// 32 B with 1x gaps and every 64 B point -4 to -6 %; so by default only the
+// first kind takes it (DCOPY_TMA_SHORT_AUTO_MAX).
 #define DCOPY_TMA_SHORT_BURSTS 1
+#endif
+#ifndef DCOPY_TMA_SHORT_AUTO_MAX
+// Without the TMA paths selected, bursts of at most this many bytes whose source
+// gap is at least 4x the burst still take the tensor copy: the points where it
+// measured ahead.  bench.py's config 3 sweep (CUDA graph replay, 256 MiB moved,
+// two runs each): 32 B / 4x 4008 vs 3832-3844 GB/s, 32 B / 16x 3505-3533 vs
+// 3431-3458; every other point unchanged.  0: only with the paths selected.
+#define DCOPY_TMA_SHORT_AUTO_MAX 32
 #endif
 #ifndef DCOPY_TMA_SHORT_PROMOTION
 // L2 promotion of those loads: 64 (half lines).  No promotion measured 25-30 %
@@ -418,8 +427,9 @@ int nd_copy_tma(void *dst, const void *src, int ndim, const uint64_t *sizes,
 int tma_short_bursts(void *dst, const void *src, uint64_t rows, uint64_t row_bytes,
                      uint64_t src_pitch, uint64_t dst_pitch, cudaStream_t s, bool *taken) {
   *taken = false;
-  if (!DCOPY_TMA_SHORT_BURSTS || !tma_selected() || row_bytes >= 128 || row_bytes % 16 ||
-      src_pitch == row_bytes)
+  const bool automatic = row_bytes <= DCOPY_TMA_SHORT_AUTO_MAX && src_pitch >= 5 * row_bytes;
+  if (!DCOPY_TMA_SHORT_BURSTS || !(tma_selected() || automatic) || row_bytes >= 128 ||
+      row_bytes % 16 || src_pitch == row_bytes)
     return DCOPY_OK;
   if (rows < 2 || rows > 0x7FFFFFFFull) return DCOPY_OK;
   const uint64_t sizes[2] = {rows, row_bytes};

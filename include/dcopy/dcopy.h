@@ -282,10 +282,11 @@ int dcopy_set_nd_tma(int enable, int *previous);
 
 /* Reads and clears the current device's TMA error words: 1 when a launch that
  * moved data with the copy engine inside a kernel -- the tensor-copy box path,
- * the bulk-copy burst path (both with dcopy_set_nd_tma(1)), or the bulk-copied
- * NCHW -> FRACTAL_Z tiles -- gave up waiting on one of its own loads (that copy
- * is then incomplete), else 0.  Synchronises the device.  No counterpart in the
- * reference. */
+ * the bulk-copy burst path (both with dcopy_set_nd_tma(1)), the tensor copy that
+ * dcopy_copy_ext uses by default for bursts of at most 32 bytes with source gaps
+ * of at least 4x the burst, or the bulk-copied FRACTAL_Z tiles -- gave up waiting
+ * on one of its own loads (that copy is then incomplete), else 0.  Synchronises
+ * the device.  No counterpart in the reference. */
 int dcopy_tma_error(uint32_t *flag);
 
 /* ---- ND <-> FRACTAL_NZ ------------------------------------------------------ */
