@@ -40,6 +40,14 @@ constexpr int kCtasPerSm = 8;
 #define DCOPY_BALANCED 0
 #endif
 
+#ifndef DCOPY_STRIDED_FILL
+// 1: strided copies spread over every resident CTA slot when one chunk per CTA
+// leaves part of the wave empty (config 2: 296 CTAs of 3552 elements instead of
+// 256 of 4096).  Measured on B200 (bench.py headline, three runs each): 0.857-
+// 0.858 of the copy peak against 0.860-0.861, so off.
+#define DCOPY_STRIDED_FILL 0
+#endif
+
 #ifndef DCOPY_U16
 #define DCOPY_U16 4  // 16-byte elements in flight per thread (linear copy)
 #endif
@@ -275,7 +283,33 @@ int launch_strided(uint8_t *dst, const uint8_t *src, uint64_t rows, uint64_t row
     const uint32_t total = (uint32_t)(nr * epr);
     auto kernel = half_line ? strided_copy_kernel<T, U, true> : strided_copy_kernel<T, U, false>;
     const int threads = half_line ? StridedShape<true>::threads : StridedShape<false>::threads;
-    const Split sp = split_work(kernel, total, U, threads);
+    Split sp = split_work(kernel, total, U, threads);
+#if DCOPY_STRIDED_FILL
+    // Spread the elements over every resident CTA slot (ranges of whole 128-byte
+    // lines) when one chunk per CTA leaves part of the wave empty.
+    {
+      static std::atomic<int> per_sm_cache[2][128];
+      const int dev = current_device();
+      std::atomic<int> &cached = per_sm_cache[half_line ? 1 : 0][(dev >= 0 && dev < 128) ? dev : 0];
+      int per_sm = cached.load(std::memory_order_relaxed);
+      if (per_sm <= 0) {
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, 0) !=
+                cudaSuccess ||
+            per_sm <= 0) {
+          (void)cudaGetLastError();
+          per_sm = 1;
+        }
+        cached.store(per_sm, std::memory_order_relaxed);
+      }
+      const uint64_t slots = (uint64_t)per_sm * (uint64_t)sm_count();
+      if (slots > sp.grid && total > slots * 32) {
+        uint64_t per = (total + slots - 1) / slots;
+        per = (per + 31) / 32 * 32;
+        sp.per_cta = per;
+        sp.grid = (unsigned)std::max<uint64_t>(1, (total + per - 1) / per);
+      }
+    }
+#endif
     int rc = launch(kernel, sp.grid, dim3(threads), 0, s, "strided_copy_kernel",
                     dst + r0 * dst_pitch, src + r0 * src_pitch, total, (uint32_t)sp.per_cta, div,
                     src_pitch, dst_pitch, prefetch_src);
