@@ -508,7 +508,16 @@ __device__ uint32_t g_fz_error;
 
 // kTensor: the whole tile arrives as one 2-D tensor copy (map: [N rows][C*HW],
 // box [NB][P]) instead of one bulk copy per row; rows past N come zero-filled.
-template <int EB, bool kTensor>
+// kWordHW (1-byte elements, C0 = 32, H*W = kWordHW): the gather works on 32-bit
+// words instead of single bytes.  A thread takes one weight n and one group of
+// four channels: the group's 4*kWordHW bytes ([c0][hw]) are kWordHW words of the
+// stage row; for each hw, two byte permutes pick the four channels' bytes and a
+// third joins them into the FRACTAL_Z word (c0 4*grp .. 4*grp+3 of (hw, n)).
+// Eight lanes write the 32 bytes of one (hw, n), a warp four consecutive n: a
+// 128-byte segment per hw.  The row pitch is 8 words modulo 32, so a warp's
+// word loads (rows n..n+3, word kWordHW*grp + m) hit 32 distinct banks for
+// kWordHW 9 or 25.  Shared loads per output byte: 1/4 (the byte gather: 1).
+template <int EB, bool kTensor, int kWordHW = 0>
 __global__ void __launch_bounds__(kThreads) fz_nchw_bulk_kernel(unsigned char *__restrict__ dst_b,
                                                                 const unsigned char *__restrict__ src_b,
                                                                 FzBGeom g,
@@ -598,17 +607,41 @@ __global__ void __launch_bounds__(kThreads) fz_nchw_bulk_kernel(unsigned char *_
     const uint32_t n0 = nb * g.NB;
     const T *stage = reinterpret_cast<const T *>(fzb_smem) + st * stage_elems;
     T *out = dst + ((uint64_t)c1 * g.HW * g.N1N0 + n0) * g.C0;
-    const uint32_t lane = threadIdx.x & 31, q = (lane >> 2) & ((1u << g.lq) - 1);
-    const uint32_t units = ((g.HW + 3) >> 2) << g.lnnb;
-    for (uint32_t un = threadIdx.x >> 5; un < units; un += kThreads / 32) {
-      const uint32_t hw = ((un >> g.lnnb) << 2) + (lane & 3);
-      if (hw >= g.HW) continue;
-      const uint32_t n = ((un & ((1u << g.lnnb) - 1)) << g.lnl) + (lane >> (2 + g.lq));
-      const uint32_t at = n * g.P + q * V * g.HW + hw;
-      Pack x;
+    if constexpr (kWordHW > 0) {
+      static_assert(EB == 1, "the word gather moves 1-byte elements");
+      const uint64_t hw_words = (uint64_t)g.N1N0 * 8;  // 32-bit words between hw planes
+      for (uint32_t u = threadIdx.x; u < g.NB * 8; u += kThreads) {
+        const uint32_t n = u >> 3, grp = u & 7;
+        const uint32_t *row =
+            reinterpret_cast<const uint32_t *>(stage + n * g.P) + kWordHW * grp;
+        uint32_t w[kWordHW];
 #pragma unroll
-      for (int j = 0; j < V; ++j) x.e[j] = stage[at + j * g.HW];
-      *reinterpret_cast<uint4 *>(out + (uint64_t)hw * g.N1N0 * g.C0 + n * g.C0 + q * V) = x.u;
+        for (int m = 0; m < kWordHW; ++m) w[m] = row[m];
+        uint32_t *o = reinterpret_cast<uint32_t *>(out + n * 32) + grp;
+#pragma unroll
+        for (int hw = 0; hw < kWordHW; ++hw) {
+          // Channel i of the group sits at byte kWordHW * i + hw of the group.
+          constexpr int k = kWordHW;
+          const uint32_t lo = __byte_perm(w[hw >> 2], w[(k + hw) >> 2],
+                                          (hw & 3) | ((4 + ((k + hw) & 3)) << 4));
+          const uint32_t hi = __byte_perm(w[(2 * k + hw) >> 2], w[(3 * k + hw) >> 2],
+                                          ((2 * k + hw) & 3) | ((4 + ((3 * k + hw) & 3)) << 4));
+          o[(uint64_t)hw * hw_words] = __byte_perm(lo, hi, 0x5410);
+        }
+      }
+    } else {
+      const uint32_t lane = threadIdx.x & 31, q = (lane >> 2) & ((1u << g.lq) - 1);
+      const uint32_t units = ((g.HW + 3) >> 2) << g.lnnb;
+      for (uint32_t un = threadIdx.x >> 5; un < units; un += kThreads / 32) {
+        const uint32_t hw = ((un >> g.lnnb) << 2) + (lane & 3);
+        if (hw >= g.HW) continue;
+        const uint32_t n = ((un & ((1u << g.lnnb) - 1)) << g.lnl) + (lane >> (2 + g.lq));
+        const uint32_t at = n * g.P + q * V * g.HW + hw;
+        Pack x;
+#pragma unroll
+        for (int j = 0; j < V; ++j) x.e[j] = stage[at + j * g.HW];
+        *reinterpret_cast<uint4 *>(out + (uint64_t)hw * g.N1N0 * g.C0 + n * g.C0 + q * V) = x.u;
+      }
     }
     __syncthreads();  // every read of this stage is done before it is refilled
   }
@@ -958,6 +991,9 @@ __global__ void __launch_bounds__(kThreads) fz_hwcn_tensor_kernel(unsigned char 
 // elements keep the row copies.
 #define DCOPY_FZ_NCHW_TMA 1
 #endif
+#ifndef DCOPY_FZ_INT8_WORDS
+#define DCOPY_FZ_INT8_WORDS 0  // int8 NCHW -> FRACTAL_Z 3x3 / 5x5: 32-bit word gather
+#endif
 #ifndef DCOPY_FZ_GROUP_TILES
 #define DCOPY_FZ_GROUP_TILES 1  // 0: one group (weight blocks fastest over the whole tensor)
 #endif
@@ -1043,9 +1079,16 @@ int run_nchw_bulk(void *dst, const void *src, int64_t n, int64_t c, int64_t hw, 
                   : (eb == 1   ? fz_nchw_bulk_kernel<1, false>
                      : eb == 2 ? fz_nchw_bulk_kernel<2, false>
                                : fz_nchw_bulk_kernel<4, false>);
-  static std::atomic<bool> raised[6][128];
+  int which = (eb == 1 ? 0 : eb == 2 ? 1 : 2) + (tensor ? 3 : 0);
+  // 1-byte elements with C0 = 32 and 3x3 or 5x5 windows: the word gather (the
+  // row pitch the formula above gives is then 8 words modulo 32).
+  if (DCOPY_FZ_INT8_WORDS && eb == 1 && c0 == 32 && !tensor && (P / 4) % 32 == 8 &&
+      (hw == 9 || hw == 25)) {
+    k = hw == 9 ? fz_nchw_bulk_kernel<1, false, 9> : fz_nchw_bulk_kernel<1, false, 25>;
+    which = hw == 9 ? 6 : 7;
+  }
+  static std::atomic<bool> raised[8][128];
   const int dev = current_device();
-  const int which = (eb == 1 ? 0 : eb == 2 ? 1 : 2) + (tensor ? 3 : 0);
   if (dev >= 0 && dev < 128 && !raised[which][dev].load()) {
     const cudaError_t e =
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBulkSmemMax);

@@ -177,6 +177,8 @@ def test_invalid_arguments(torch_cuda, dcopy, cuda_malloc):
     ((2048, 1024, 3, 3), 2, 16),   # 2048 tiles: every CTA cycles both stages several times
     ((200, 64, 5, 5), 2, 16),      # padding weights 200..207 in the last tile
     ((96, 64, 3, 3), 1, 32),
+    ((2048, 1024, 3, 3), 1, 32),   # int8 3x3 / 5x5 with C0 32: the 32-bit word gather
+    ((200, 128, 5, 5), 1, 32),     # padding weights in the last tile of the word gather
     ((80, 32, 2, 2), 4, 16),       # even H*W
     ((33, 16, 1, 1), 4, 8),
     ((1000, 256, 7, 7), 2, 16),
