@@ -992,7 +992,12 @@ __global__ void __launch_bounds__(kThreads) fz_hwcn_tensor_kernel(unsigned char 
 #define DCOPY_FZ_NCHW_TMA 1
 #endif
 #ifndef DCOPY_FZ_INT8_WORDS
-#define DCOPY_FZ_INT8_WORDS 0  // int8 NCHW -> FRACTAL_Z 3x3 / 5x5: 32-bit word gather
+// int8 NCHW -> FRACTAL_Z 3x3 / 5x5 (C0 32): the 32-bit word gather of
+// fz_nchw_bulk_kernel.  Measured on B200 (dcopy_bench fz --eb 1 --c0 32 --replay
+// 1, two rounds, GB/s against the byte gather): [2048,2048,3,3] 5258 vs
+// 3874-3878, [4096,2048,3,3] 5575-5626 vs 4584-4589, [2048,1024,5,5] 5344-5360
+// vs 4721-4769, [512,512,3,3] 1141 vs 914.
+#define DCOPY_FZ_INT8_WORDS 1
 #endif
 #ifndef DCOPY_FZ_GROUP_TILES
 #define DCOPY_FZ_GROUP_TILES 1  // 0: one group (weight blocks fastest over the whole tensor)
