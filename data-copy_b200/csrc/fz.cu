@@ -665,7 +665,14 @@ __global__ void __launch_bounds__(kThreads) fz_nchw_bulk_kernel(unsigned char *_
 // pitch of the other direction, so the scatter is conflict-free for odd HW.  The
 // valid rows then leave by bulk stores (one per row); the row stage is reused
 // once those stores have read it.  Waits are bounded as in the other direction.
-template <int EB>
+// kWordHW (1-byte elements, C0 = 32, H*W = kWordHW): the scatter works on 32-bit
+// words, the mirror of the word gather of fz_nchw_bulk_kernel.  A thread takes
+// one weight n and one group of four channels, loads the group's FRACTAL_Z word
+// for every hw (a warp: 32 consecutive words of a run), and writes the group's
+// 4*kWordHW contiguous row bytes as kWordHW words, each joined from the bytes of
+// up to four of those words with three byte permutes; the row pitch of 8 words
+// modulo 32 keeps the warp's word stores conflict-free for kWordHW 9 or 25.
+template <int EB, int kWordHW = 0>
 __global__ void __launch_bounds__(kThreads) fz_to_nchw_bulk_kernel(unsigned char *__restrict__ dst_b,
                                                                    const unsigned char *__restrict__ src_b,
                                                                    FzBGeom g) {
@@ -731,17 +738,40 @@ __global__ void __launch_bounds__(kThreads) fz_to_nchw_bulk_kernel(unsigned char
     const uint32_t n0 = nb * g.NB;
     const uint32_t valid = n0 < g.N ? min(g.NB, g.N - n0) : 0;
     const T *stage = reinterpret_cast<const T *>(fzr_smem) + st * run_stage;
-    const uint32_t lane = threadIdx.x & 31, q = (lane >> 2) & ((1u << g.lq) - 1);
-    const uint32_t units = ((g.HW + 3) >> 2) << g.lnnb;
-    for (uint32_t un = threadIdx.x >> 5; un < units; un += kThreads / 32) {
-      const uint32_t hw = ((un >> g.lnnb) << 2) + (lane & 3);
-      const uint32_t n = ((un & ((1u << g.lnnb) - 1)) << g.lnl) + (lane >> (2 + g.lq));
-      if (hw >= g.HW || n >= valid) continue;
-      Pack x;
-      x.u = *reinterpret_cast<const uint4 *>(stage + hw * run + n * g.C0 + q * V);
-      const uint32_t at = n * g.P + q * V * g.HW + hw;
+    if constexpr (kWordHW > 0) {
+      static_assert(EB == 1, "the word scatter moves 1-byte elements");
+      for (uint32_t u = threadIdx.x; u < valid * 8; u += kThreads) {
+        const uint32_t n = u >> 3, grp = u & 7;
+        uint32_t w[kWordHW];
 #pragma unroll
-      for (int j = 0; j < V; ++j) rows[at + j * g.HW] = x.e[j];
+        for (int hw = 0; hw < kWordHW; ++hw)
+          w[hw] = *reinterpret_cast<const uint32_t *>(stage + hw * run + n * 32 + 4 * grp);
+        uint32_t *o = reinterpret_cast<uint32_t *>(rows + n * g.P) + kWordHW * grp;
+#pragma unroll
+        for (int m = 0; m < kWordHW; ++m) {
+          // Row byte 4m+b of the group is channel (4m+b)/kWordHW at hw (4m+b)%kWordHW,
+          // i.e. byte (4m+b)/kWordHW of FRACTAL_Z word (4m+b)%kWordHW.
+          constexpr int k = kWordHW;
+          const uint32_t lo = __byte_perm(w[(4 * m) % k], w[(4 * m + 1) % k],
+                                          ((4 * m) / k) | ((4 + (4 * m + 1) / k) << 4));
+          const uint32_t hi = __byte_perm(w[(4 * m + 2) % k], w[(4 * m + 3) % k],
+                                          ((4 * m + 2) / k) | ((4 + (4 * m + 3) / k) << 4));
+          o[m] = __byte_perm(lo, hi, 0x5410);
+        }
+      }
+    } else {
+      const uint32_t lane = threadIdx.x & 31, q = (lane >> 2) & ((1u << g.lq) - 1);
+      const uint32_t units = ((g.HW + 3) >> 2) << g.lnnb;
+      for (uint32_t un = threadIdx.x >> 5; un < units; un += kThreads / 32) {
+        const uint32_t hw = ((un >> g.lnnb) << 2) + (lane & 3);
+        const uint32_t n = ((un & ((1u << g.lnnb) - 1)) << g.lnl) + (lane >> (2 + g.lq));
+        if (hw >= g.HW || n >= valid) continue;
+        Pack x;
+        x.u = *reinterpret_cast<const uint4 *>(stage + hw * run + n * g.C0 + q * V);
+        const uint32_t at = n * g.P + q * V * g.HW + hw;
+#pragma unroll
+        for (int j = 0; j < V; ++j) rows[at + j * g.HW] = x.e[j];
+      }
     }
     // Generic-proxy writes of the row stage, then bulk stores read it.
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -998,6 +1028,9 @@ __global__ void __launch_bounds__(kThreads) fz_hwcn_tensor_kernel(unsigned char 
 // 3874-3878, [4096,2048,3,3] 5575-5626 vs 4584-4589, [2048,1024,5,5] 5344-5360
 // vs 4721-4769, [512,512,3,3] 1141 vs 914.
 #define DCOPY_FZ_INT8_WORDS 1
+#endif
+#ifndef DCOPY_FZ_INT8_WORDS_FROM
+#define DCOPY_FZ_INT8_WORDS_FROM 0  // int8 FRACTAL_Z -> NCHW 3x3 / 5x5: 32-bit word scatter
 #endif
 #ifndef DCOPY_FZ_GROUP_TILES
 #define DCOPY_FZ_GROUP_TILES 1  // 0: one group (weight blocks fastest over the whole tensor)
@@ -1280,7 +1313,9 @@ int run_nchw_bulk_from(void *dst, const void *src, int64_t n, int64_t c, int64_t
                        int64_t c0, cudaStream_t s, bool *taken) {
   *taken = false;
   const bool gather = DCOPY_FZ_FROM_GATHER && eb == 2;
-  if (!gather && (!DCOPY_FZ_NCHW_BULK_FROM || eb != 4)) return DCOPY_OK;
+  const bool word_scatter =
+      DCOPY_FZ_INT8_WORDS_FROM && eb == 1 && c0 == 32 && (hw == 9 || hw == 25);
+  if (!gather && !word_scatter && (!DCOPY_FZ_NCHW_BULK_FROM || eb != 4)) return DCOPY_OK;
   const int64_t V = 16 / eb;
   if (c0 <= 0 || (c0 & (c0 - 1)) || c0 % V || c % c0 || (c * hw * eb) % 16) return DCOPY_OK;
   if (((uintptr_t)dst | (uintptr_t)src) % 16) return DCOPY_OK;
@@ -1322,13 +1357,21 @@ int run_nchw_bulk_from(void *dst, const void *src, int64_t n, int64_t c, int64_t
   const size_t smem = smem_of(nb);
   using Kern = void (*)(unsigned char *, const unsigned char *, FzBGeom);
   Kern k = fz_to_nchw_bulk_kernel<4>;
-  static std::atomic<bool> raised[128];
+  int which = 0;
+  if (word_scatter) {
+    // The word scatter needs the row pitch at 8 words modulo 32 (what the pitch
+    // formula above gives for C0 32).
+    if ((P / 4) % 32 != 8) return DCOPY_OK;
+    k = hw == 9 ? fz_to_nchw_bulk_kernel<1, 9> : fz_to_nchw_bulk_kernel<1, 25>;
+    which = hw == 9 ? 1 : 2;
+  }
+  static std::atomic<bool> raised[3][128];
   const int dev = current_device();
-  if (dev >= 0 && dev < 128 && !raised[dev].load()) {
+  if (dev >= 0 && dev < 128 && !raised[which][dev].load()) {
     const cudaError_t e =
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBulkSmemMax);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(fz_to_nchw_bulk_kernel)");
-    raised[dev] = true;
+    raised[which][dev] = true;
   }
   int per_sm = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kThreads, smem) != cudaSuccess ||

@@ -225,3 +225,27 @@ def test_hwcn_to_fractal_z_tensor_tiles(torch_cuda, dcopy, oracle, shape, eb, c0
     assert out[:expect.nbytes].tobytes() == expect.tobytes()
     assert (out[expect.nbytes:] == CANARY).all()
     assert dcopy.tma_error() == 0
+
+
+@pytest.mark.parametrize("weight,eb,c0", [
+    ((2048, 1024, 3, 3), 1, 32),   # int8 3x3 / 5x5 with C0 32: the 32-bit word scatter
+    ((200, 128, 5, 5), 1, 32),     # 200 weights: the last tile has padding rows, not stored
+    ((96, 64, 3, 3), 1, 32),
+    ((2048, 1024, 3, 3), 2, 16),   # the fp16 row-vector gather
+    ((80, 32, 2, 2), 4, 16),       # the fp32 bulk kernel
+], ids=lambda v: "x".join(map(str, v)) if isinstance(v, tuple) else str(v))
+def test_fractal_z_to_nchw_bulk_tiles(torch_cuda, dcopy, oracle, weight, eb, c0):
+    """FRACTAL_Z (made by the oracle) -> NCHW through the bulk-copied tile kernels: the
+    result is the original weight byte for byte, nothing written past it, no give-up."""
+    torch = torch_cuda
+    shape = list(weight)
+    src_np = _rand(int(np.prod(shape)) * eb, sum(shape) * 5 + eb)
+    fz = oracle.to_fz(_as(src_np, eb).reshape(shape), NCHW, c0)
+    z = torch.from_numpy(np.ascontiguousarray(fz).view(np.uint8).reshape(-1)).cuda()
+    back = torch.full((src_np.size + 64,), CANARY, dtype=torch.uint8, device="cuda")
+    dcopy.from_fractal_z(back, z, NCHW, shape, eb, c0)
+    torch.cuda.synchronize()
+    out = back.cpu().numpy()
+    assert out[:src_np.size].tobytes() == src_np.tobytes()
+    assert (out[src_np.size:] == CANARY).all()
+    assert dcopy.tma_error() == 0
