@@ -1030,7 +1030,14 @@ __global__ void __launch_bounds__(kThreads) fz_hwcn_tensor_kernel(unsigned char 
 #define DCOPY_FZ_INT8_WORDS 1
 #endif
 #ifndef DCOPY_FZ_INT8_WORDS_FROM
-#define DCOPY_FZ_INT8_WORDS_FROM 0  // int8 FRACTAL_Z -> NCHW 3x3 / 5x5: 32-bit word scatter
+// int8 FRACTAL_Z -> NCHW 3x3 / 5x5 (C0 32): the 32-bit word scatter of
+// fz_to_nchw_bulk_kernel, when there are at least as many tiles as resident
+// CTAs.  Measured on B200 (dcopy_bench fz --eb 1 --c0 32 --replay 1, two rounds,
+// GB/s against fz_vec_kernel): [2048,2048,3,3] 4091 vs 3868-3876,
+// [4096,2048,3,3] 5086-5099 vs 4334, [2048,1024,5,5] 4650-4657 vs 3578-3586;
+// [512,512,3,3] (128 tiles, no second tile for any CTA) 918 vs 1146, hence the
+// tile-count condition.
+#define DCOPY_FZ_INT8_WORDS_FROM 1
 #endif
 #ifndef DCOPY_FZ_GROUP_TILES
 #define DCOPY_FZ_GROUP_TILES 1  // 0: one group (weight blocks fastest over the whole tensor)
@@ -1379,6 +1386,9 @@ int run_nchw_bulk_from(void *dst, const void *src, int64_t n, int64_t c, int64_t
     (void)cudaGetLastError();
     per_sm = 1;
   }
+  // The word scatter pays only when CTAs get a second tile to overlap with;
+  // fewer tiles than resident CTAs stay on the vector kernel.
+  if (word_scatter && ntiles < (uint64_t)per_sm * (uint64_t)sm_count()) return DCOPY_OK;
   *taken = true;
   const uint32_t grid =
       (uint32_t)std::min<uint64_t>(ntiles, (uint64_t)per_sm * (uint64_t)sm_count());
