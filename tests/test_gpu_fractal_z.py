@@ -229,7 +229,9 @@ def test_hwcn_to_fractal_z_tensor_tiles(torch_cuda, dcopy, oracle, shape, eb, c0
 
 @pytest.mark.parametrize("weight,eb,c0", [
     ((2048, 1024, 3, 3), 1, 32),   # int8 3x3 / 5x5 with C0 32: the 32-bit word scatter
-    ((200, 128, 5, 5), 1, 32),     # 200 weights: the last tile has padding rows, not stored
+    ((2040, 1024, 3, 3), 1, 32),   # word scatter, padding rows 2040..2047 not stored
+    ((1000, 1024, 5, 5), 1, 32),   # word scatter at 5x5, 2016 tiles, padding rows
+    ((200, 128, 5, 5), 1, 32),     # fewer tiles than CTAs: the vector kernel
     ((96, 64, 3, 3), 1, 32),
     ((2048, 1024, 3, 3), 2, 16),   # the fp16 row-vector gather
     ((80, 32, 2, 2), 4, 16),       # the fp32 bulk kernel
