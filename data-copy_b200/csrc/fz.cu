@@ -608,25 +608,38 @@ __global__ void __launch_bounds__(kThreads) fz_nchw_bulk_kernel(unsigned char *_
     const T *stage = reinterpret_cast<const T *>(fzb_smem) + st * stage_elems;
     T *out = dst + ((uint64_t)c1 * g.HW * g.N1N0 + n0) * g.C0;
     if constexpr (kWordHW > 0) {
-      static_assert(EB == 1, "the word gather moves 1-byte elements");
+      static_assert(EB == 1 || EB == 2, "the word gather moves 1- or 2-byte elements");
       const uint64_t hw_words = (uint64_t)g.N1N0 * 8;  // 32-bit words between hw planes
       for (uint32_t u = threadIdx.x; u < g.NB * 8; u += kThreads) {
+        // Group grp: the 4 / EB channels whose elements fill bytes 4*grp..4*grp+3
+        // of a 32-byte FRACTAL_Z row; in the NCHW row they are 4*kWordHW bytes.
         const uint32_t n = u >> 3, grp = u & 7;
         const uint32_t *row =
             reinterpret_cast<const uint32_t *>(stage + n * g.P) + kWordHW * grp;
         uint32_t w[kWordHW];
 #pragma unroll
         for (int m = 0; m < kWordHW; ++m) w[m] = row[m];
-        uint32_t *o = reinterpret_cast<uint32_t *>(out + n * 32) + grp;
+        uint32_t *o = reinterpret_cast<uint32_t *>(reinterpret_cast<unsigned char *>(out) + n * 32) +
+                      grp;
 #pragma unroll
         for (int hw = 0; hw < kWordHW; ++hw) {
-          // Channel i of the group sits at byte kWordHW * i + hw of the group.
+          // Channel i of the group is element kWordHW * i + hw of the group.
           constexpr int k = kWordHW;
-          const uint32_t lo = __byte_perm(w[hw >> 2], w[(k + hw) >> 2],
-                                          (hw & 3) | ((4 + ((k + hw) & 3)) << 4));
-          const uint32_t hi = __byte_perm(w[(2 * k + hw) >> 2], w[(3 * k + hw) >> 2],
-                                          ((2 * k + hw) & 3) | ((4 + ((3 * k + hw) & 3)) << 4));
-          o[(uint64_t)hw * hw_words] = __byte_perm(lo, hi, 0x5410);
+          uint32_t word;
+          if constexpr (EB == 1) {
+            const uint32_t lo = __byte_perm(w[hw >> 2], w[(k + hw) >> 2],
+                                            (hw & 3) | ((4 + ((k + hw) & 3)) << 4));
+            const uint32_t hi =
+                __byte_perm(w[(2 * k + hw) >> 2], w[(3 * k + hw) >> 2],
+                            ((2 * k + hw) & 3) | ((4 + ((3 * k + hw) & 3)) << 4));
+            word = __byte_perm(lo, hi, 0x5410);
+          } else {
+            // Element e is half e & 1 of word e >> 1: bytes 2 * (e & 1) and the next.
+            const uint32_t s0 = 2 * (hw & 1), s1 = 4 + 2 * ((k + hw) & 1);
+            word = __byte_perm(w[hw >> 1], w[(k + hw) >> 1],
+                               s0 | ((s0 + 1) << 4) | (s1 << 8) | ((s1 + 1) << 12));
+          }
+          o[(uint64_t)hw * hw_words] = word;
         }
       }
     } else {
@@ -739,24 +752,33 @@ __global__ void __launch_bounds__(kThreads) fz_to_nchw_bulk_kernel(unsigned char
     const uint32_t valid = n0 < g.N ? min(g.NB, g.N - n0) : 0;
     const T *stage = reinterpret_cast<const T *>(fzr_smem) + st * run_stage;
     if constexpr (kWordHW > 0) {
-      static_assert(EB == 1, "the word scatter moves 1-byte elements");
+      static_assert(EB == 1 || EB == 2, "the word scatter moves 1- or 2-byte elements");
       for (uint32_t u = threadIdx.x; u < valid * 8; u += kThreads) {
         const uint32_t n = u >> 3, grp = u & 7;
         uint32_t w[kWordHW];
 #pragma unroll
         for (int hw = 0; hw < kWordHW; ++hw)
-          w[hw] = *reinterpret_cast<const uint32_t *>(stage + hw * run + n * 32 + 4 * grp);
+          w[hw] = *reinterpret_cast<const uint32_t *>(
+              reinterpret_cast<const unsigned char *>(stage + hw * run) + n * 32 + 4 * grp);
         uint32_t *o = reinterpret_cast<uint32_t *>(rows + n * g.P) + kWordHW * grp;
 #pragma unroll
         for (int m = 0; m < kWordHW; ++m) {
-          // Row byte 4m+b of the group is channel (4m+b)/kWordHW at hw (4m+b)%kWordHW,
-          // i.e. byte (4m+b)/kWordHW of FRACTAL_Z word (4m+b)%kWordHW.
           constexpr int k = kWordHW;
-          const uint32_t lo = __byte_perm(w[(4 * m) % k], w[(4 * m + 1) % k],
-                                          ((4 * m) / k) | ((4 + (4 * m + 1) / k) << 4));
-          const uint32_t hi = __byte_perm(w[(4 * m + 2) % k], w[(4 * m + 3) % k],
-                                          ((4 * m + 2) / k) | ((4 + (4 * m + 3) / k) << 4));
-          o[m] = __byte_perm(lo, hi, 0x5410);
+          if constexpr (EB == 1) {
+            // Row byte 4m+b of the group is channel (4m+b)/k at hw (4m+b)%k, i.e.
+            // byte (4m+b)/k of FRACTAL_Z word (4m+b)%k.
+            const uint32_t lo = __byte_perm(w[(4 * m) % k], w[(4 * m + 1) % k],
+                                            ((4 * m) / k) | ((4 + (4 * m + 1) / k) << 4));
+            const uint32_t hi = __byte_perm(w[(4 * m + 2) % k], w[(4 * m + 3) % k],
+                                            ((4 * m + 2) / k) | ((4 + (4 * m + 3) / k) << 4));
+            o[m] = __byte_perm(lo, hi, 0x5410);
+          } else {
+            // Row element 2m+b of the group is channel (2m+b)/k at hw (2m+b)%k, i.e.
+            // half (2m+b)/k of FRACTAL_Z word (2m+b)%k.
+            const uint32_t s0 = 2 * ((2 * m) / k), s1 = 4 + 2 * ((2 * m + 1) / k);
+            o[m] = __byte_perm(w[(2 * m) % k], w[(2 * m + 1) % k],
+                               s0 | ((s0 + 1) << 4) | (s1 << 8) | ((s1 + 1) << 12));
+          }
         }
       }
     } else {
@@ -1039,6 +1061,12 @@ __global__ void __launch_bounds__(kThreads) fz_hwcn_tensor_kernel(unsigned char 
 // tile-count condition.
 #define DCOPY_FZ_INT8_WORDS_FROM 1
 #endif
+#ifndef DCOPY_FZ_FP16_WORDS
+#define DCOPY_FZ_FP16_WORDS 0  // fp16 NCHW -> FRACTAL_Z 3x3 / 5x5 (C0 16): word gather
+#endif
+#ifndef DCOPY_FZ_FP16_WORDS_FROM
+#define DCOPY_FZ_FP16_WORDS_FROM 0  // fp16 FRACTAL_Z -> NCHW 3x3 / 5x5 (C0 16): word scatter
+#endif
 #ifndef DCOPY_FZ_GROUP_TILES
 #define DCOPY_FZ_GROUP_TILES 1  // 0: one group (weight blocks fastest over the whole tensor)
 #endif
@@ -1125,14 +1153,19 @@ int run_nchw_bulk(void *dst, const void *src, int64_t n, int64_t c, int64_t hw, 
                      : eb == 2 ? fz_nchw_bulk_kernel<2, false>
                                : fz_nchw_bulk_kernel<4, false>);
   int which = (eb == 1 ? 0 : eb == 2 ? 1 : 2) + (tensor ? 3 : 0);
-  // 1-byte elements with C0 = 32 and 3x3 or 5x5 windows: the word gather (the
-  // row pitch the formula above gives is then 8 words modulo 32).
-  if (DCOPY_FZ_INT8_WORDS && eb == 1 && c0 == 32 && !tensor && (P / 4) % 32 == 8 &&
-      (hw == 9 || hw == 25)) {
+  // 1-byte elements with C0 = 32 (or 2-byte with C0 = 16) and 3x3 or 5x5
+  // windows: the word gather (the row pitch the formula above gives is then 8
+  // words modulo 32).
+  const bool pitch_ok = (P * eb / 4) % 32 == 8 && (hw == 9 || hw == 25);
+  if (DCOPY_FZ_INT8_WORDS && eb == 1 && c0 == 32 && !tensor && pitch_ok) {
     k = hw == 9 ? fz_nchw_bulk_kernel<1, false, 9> : fz_nchw_bulk_kernel<1, false, 25>;
     which = hw == 9 ? 6 : 7;
+  } else if (DCOPY_FZ_FP16_WORDS && eb == 2 && c0 == 16 && pitch_ok) {
+    k = tensor ? (hw == 9 ? fz_nchw_bulk_kernel<2, true, 9> : fz_nchw_bulk_kernel<2, true, 25>)
+               : (hw == 9 ? fz_nchw_bulk_kernel<2, false, 9> : fz_nchw_bulk_kernel<2, false, 25>);
+    which = 8 + (hw == 9 ? 0 : 1) + (tensor ? 2 : 0);
   }
-  static std::atomic<bool> raised[8][128];
+  static std::atomic<bool> raised[12][128];
   const int dev = current_device();
   if (dev >= 0 && dev < 128 && !raised[which][dev].load()) {
     const cudaError_t e =
@@ -1321,7 +1354,8 @@ int run_nchw_bulk_from(void *dst, const void *src, int64_t n, int64_t c, int64_t
   *taken = false;
   const bool gather = DCOPY_FZ_FROM_GATHER && eb == 2;
   const bool word_scatter =
-      DCOPY_FZ_INT8_WORDS_FROM && eb == 1 && c0 == 32 && (hw == 9 || hw == 25);
+      (hw == 9 || hw == 25) && ((DCOPY_FZ_INT8_WORDS_FROM && eb == 1 && c0 == 32) ||
+                                (DCOPY_FZ_FP16_WORDS_FROM && eb == 2 && c0 == 16));
   if (!gather && !word_scatter && (!DCOPY_FZ_NCHW_BULK_FROM || eb != 4)) return DCOPY_OK;
   const int64_t V = 16 / eb;
   if (c0 <= 0 || (c0 & (c0 - 1)) || c0 % V || c % c0 || (c * hw * eb) % 16) return DCOPY_OK;
@@ -1360,19 +1394,24 @@ int run_nchw_bulk_from(void *dst, const void *src, int64_t n, int64_t c, int64_t
   fz_tile_groups(g, g.nblocks);
   g.seg_stride = (uint64_t)(c * hw);
   g.N1N0 = (uint64_t)n1n0;
-  if (gather) return launch_from_gather(dst, src, g, eb, c0, hw, nb, s, taken);
+  if (gather && !word_scatter) return launch_from_gather(dst, src, g, eb, c0, hw, nb, s, taken);
   const size_t smem = smem_of(nb);
   using Kern = void (*)(unsigned char *, const unsigned char *, FzBGeom);
   Kern k = fz_to_nchw_bulk_kernel<4>;
   int which = 0;
   if (word_scatter) {
     // The word scatter needs the row pitch at 8 words modulo 32 (what the pitch
-    // formula above gives for C0 32).
-    if ((P / 4) % 32 != 8) return DCOPY_OK;
-    k = hw == 9 ? fz_to_nchw_bulk_kernel<1, 9> : fz_to_nchw_bulk_kernel<1, 25>;
-    which = hw == 9 ? 1 : 2;
+    // formula above gives for 32-byte FRACTAL_Z rows).
+    if ((P * eb / 4) % 32 != 8) return DCOPY_OK;
+    if (eb == 1) {
+      k = hw == 9 ? fz_to_nchw_bulk_kernel<1, 9> : fz_to_nchw_bulk_kernel<1, 25>;
+      which = hw == 9 ? 1 : 2;
+    } else {
+      k = hw == 9 ? fz_to_nchw_bulk_kernel<2, 9> : fz_to_nchw_bulk_kernel<2, 25>;
+      which = hw == 9 ? 3 : 4;
+    }
   }
-  static std::atomic<bool> raised[3][128];
+  static std::atomic<bool> raised[5][128];
   const int dev = current_device();
   if (dev >= 0 && dev < 128 && !raised[which][dev].load()) {
     const cudaError_t e =
