@@ -1062,10 +1062,21 @@ __global__ void __launch_bounds__(kThreads) fz_hwcn_tensor_kernel(unsigned char 
 #define DCOPY_FZ_INT8_WORDS_FROM 1
 #endif
 #ifndef DCOPY_FZ_FP16_WORDS
-#define DCOPY_FZ_FP16_WORDS 0  // fp16 NCHW -> FRACTAL_Z 3x3 / 5x5 (C0 16): word gather
+// fp16 NCHW -> FRACTAL_Z 3x3 / 5x5 (C0 16): the word gather (one byte permute
+// per FRACTAL_Z word).  Measured on B200 (dcopy_bench fz --replay 1, two rounds,
+// GB/s against the element gather): [1024,2048,3,3] 5501-5534 vs 4708-4720,
+// [2048,2048,3,3] 5550-5558 vs 5185, [4096,2048,3,3] 5433-5435 vs 4937-4938,
+// [2048,1024,5,5] 5289-5292 vs 5053-5082, [4096,1024,5,5] 5381-5410 vs
+// 5072-5079, [512,512,3,3] 3031-3035 vs 2292-2293.
+#define DCOPY_FZ_FP16_WORDS 1
 #endif
 #ifndef DCOPY_FZ_FP16_WORDS_FROM
-#define DCOPY_FZ_FP16_WORDS_FROM 0  // fp16 FRACTAL_Z -> NCHW 3x3 / 5x5 (C0 16): word scatter
+// fp16 FRACTAL_Z -> NCHW 3x3 / 5x5 (C0 16): the word scatter instead of the
+// row-vector gather.  Measured the same way: [2048,2048,3,3] 5311-5316 vs
+// 5249-5250, [4096,2048,3,3] 5408-5450 vs 4994-5002, but [1024,2048,3,3]
+// 4311-4312 vs 4574-4585 and 5x5 [2048,1024] 5215-5226 vs 5242-5250, [4096,1024]
+// 5493-5499 vs 5625-5629: not a win across shapes, so off.
+#define DCOPY_FZ_FP16_WORDS_FROM 0
 #endif
 #ifndef DCOPY_FZ_GROUP_TILES
 #define DCOPY_FZ_GROUP_TILES 1  // 0: one group (weight blocks fastest over the whole tensor)
