@@ -2,13 +2,13 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
-#include <utility>
 #include <vector>
 
 #include "common.cuh"
@@ -101,28 +101,36 @@ namespace {
 // CUDA IPC mappings opened through dcopy_ipc_open_handle: [base, base + size).
 // The driver reports such a mapping as device memory of the device that opened
 // it, so the ranges are kept here to tell them apart from local allocations.
+// A base opened more than once (the driver may hand back the same mapping)
+// is counted, and its record stays until the last close.
+struct IpcRange {
+  uint64_t base, size;
+  int opens;
+};
 std::mutex g_ipc_mu;
-std::vector<std::pair<uint64_t, uint64_t>> g_ipc_ranges;
+std::vector<IpcRange> g_ipc_ranges;
 std::atomic<int> g_ipc_open{0};
 }  // namespace
 
 void note_ipc_mapping(const void *base, bool opened) {
   const uint64_t b = (uint64_t)(uintptr_t)base;
   std::lock_guard<std::mutex> lock(g_ipc_mu);
+  auto it = std::find_if(g_ipc_ranges.begin(), g_ipc_ranges.end(),
+                         [b](const IpcRange &r) { return r.base == b; });
   if (opened) {
-    uint64_t size = 1;  // the base alone when the size cannot be read
-    PfnPointerGetAttributes fn = pointer_attrs_fn();
-    size_t n = 0;
-    CUpointer_attribute attr = CU_POINTER_ATTRIBUTE_RANGE_SIZE;
-    void *data = &n;
-    if (fn && fn(1, &attr, &data, (CUdeviceptr)b) == CUDA_SUCCESS && n) size = n;
-    g_ipc_ranges.emplace_back(b, size);
-  } else {
-    for (size_t i = 0; i < g_ipc_ranges.size(); ++i)
-      if (g_ipc_ranges[i].first == b) {
-        g_ipc_ranges.erase(g_ipc_ranges.begin() + (long)i);
-        break;
-      }
+    if (it != g_ipc_ranges.end()) {
+      ++it->opens;
+    } else {
+      uint64_t size = 1;  // the base alone when the size cannot be read
+      PfnPointerGetAttributes fn = pointer_attrs_fn();
+      size_t n = 0;
+      CUpointer_attribute attr = CU_POINTER_ATTRIBUTE_RANGE_SIZE;
+      void *data = &n;
+      if (fn && fn(1, &attr, &data, (CUdeviceptr)b) == CUDA_SUCCESS && n) size = n;
+      g_ipc_ranges.push_back({b, size, 1});
+    }
+  } else if (it != g_ipc_ranges.end() && --it->opens == 0) {
+    g_ipc_ranges.erase(it);
   }
   g_ipc_open.store((int)g_ipc_ranges.size(), std::memory_order_release);
 }
@@ -132,7 +140,7 @@ bool in_ipc_mapping(const void *ptr) {
   const uint64_t p = (uint64_t)(uintptr_t)ptr;
   std::lock_guard<std::mutex> lock(g_ipc_mu);
   for (const auto &r : g_ipc_ranges)
-    if (p >= r.first && p - r.first < r.second) return true;
+    if (p >= r.base && p - r.base < r.size) return true;
   return false;
 }
 
