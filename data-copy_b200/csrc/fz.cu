@@ -668,6 +668,10 @@ __global__ void __launch_bounds__(kThreads) fz_nchw_bulk_kernel(unsigned char *_
 }
 
 // ---- FRACTAL_Z -> NCHW, the mirror of fz_nchw_bulk_kernel -------------------------
+
+#ifndef DCOPY_FZ_FROM_ROWS2
+#define DCOPY_FZ_FROM_ROWS2 0  // 1: fz_to_nchw_bulk_kernel alternates two row stages
+#endif
 //
 // A tile is NB weights of one channel block.  Its FRACTAL_Z source is HW
 // contiguous runs of NB*C0 elements (one per hw), bulk-copied into one of two
@@ -701,7 +705,8 @@ __global__ void __launch_bounds__(kThreads) fz_to_nchw_bulk_kernel(unsigned char
   const T *src = reinterpret_cast<const T *>(src_b);
   const uint32_t run = g.NB * g.C0;          // elements of one hw run
   const uint32_t run_stage = g.HW * run;     // elements of one run stage
-  T *rows = reinterpret_cast<T *>(fzr_smem) + 2 * run_stage;  // NB x P row stage
+  // NB x P row stage(s): with DCOPY_FZ_FROM_ROWS2 two, used by alternate tiles.
+  T *const rows0 = reinterpret_cast<T *>(fzr_smem) + 2 * run_stage;
   pdl_trigger_at_entry();
   if (threadIdx.x == 0) {
     bulk::mbar_init(&bars[0], 1);
@@ -739,9 +744,16 @@ __global__ void __launch_bounds__(kThreads) fz_to_nchw_bulk_kernel(unsigned char
     next_issued = t + gridDim.x < g.ntiles;
     if (next_issued) issue(t + gridDim.x, st ^ 1);
     const bool arrived = bulk::mbar_wait_bounded(&bars[st], (k >> 1) & 1);
-    // The previous tile's row stores must have read the row stage before it is
-    // overwritten (they were issued by warp 0).
-    if (threadIdx.x < 32) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+    // The row stores that read this tile's row stage (the previous tile's, or with
+    // two stages the one before it) must be done reading before it is overwritten;
+    // warp 0 issued them, one bulk group per lane per tile.
+    T *rows = rows0 + (DCOPY_FZ_FROM_ROWS2 ? (k & 1) * g.NB * g.P : 0);
+    if (threadIdx.x < 32) {
+      if (DCOPY_FZ_FROM_ROWS2)
+        asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+      else
+        asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+    }
     if (__syncthreads_or(!arrived)) {
       ok = false;
       break;
@@ -1381,7 +1393,9 @@ int run_nchw_bulk_from(void *dst, const void *src, int64_t n, int64_t c, int64_t
   int64_t words = (L * eb + 3) / 4;
   words += ((32 / NL - words % 32) % 32 + 32) % 32;
   const int64_t P = words * 4 / eb;
-  auto smem_of = [&](int64_t nb) { return (size_t)((2 * hw * nb * c0 + nb * P) * eb); };
+  auto smem_of = [&](int64_t nb) {
+    return (size_t)((2 * hw * nb * c0 + (DCOPY_FZ_FROM_ROWS2 ? 2 : 1) * nb * P) * eb);
+  };
   int64_t nb = DCOPY_FZ_BULK_NB;
   while (nb > NL && (n1n0 % nb || smem_of(nb) > kBulkSmemMax)) nb /= 2;
   if (n1n0 % nb || smem_of(nb) > kBulkSmemMax || nb < NL) return DCOPY_OK;
