@@ -670,7 +670,14 @@ __global__ void __launch_bounds__(kThreads) fz_nchw_bulk_kernel(unsigned char *_
 // ---- FRACTAL_Z -> NCHW, the mirror of fz_nchw_bulk_kernel -------------------------
 
 #ifndef DCOPY_FZ_FROM_ROWS2
-#define DCOPY_FZ_FROM_ROWS2 0  // 1: fz_to_nchw_bulk_kernel alternates two row stages
+// 1: fz_to_nchw_bulk_kernel alternates two row stages, so a tile's scatter need
+// not wait for the previous tile's row stores to read the stage.  Measured on
+// B200 (dcopy_bench fz --replay 1, fp16 word scatter, GB/s, one stage vs two):
+// [1024,2048,3,3] 4257-4291 vs 3773-3787, [2048,2048,3,3] 5327-5331 vs
+// 4332-4334, [4096,2048,3,3] 5442-5452 vs 4831, [2048,1024,5,5] 5220-5239 vs
+// 5553-5580; int8 3x3 4091 vs 3586-3597, fp32 3x3 5155 vs 4963-4972.  The
+// second stage costs a resident CTA per SM; off.
+#define DCOPY_FZ_FROM_ROWS2 0
 #endif
 //
 // A tile is NB weights of one channel block.  Its FRACTAL_Z source is HW
