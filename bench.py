@@ -587,6 +587,27 @@ def run_secondary(torch, dcopy, dev):
         frz[name] = [round(fzb / (ms / 1e3) / 1e9, 1), round(fzb / (ms2 / 1e3) / 1e9, 1)]
     out["fractal_z_fp16_2048x2048x3x3_to_from_GBps"] = frz
     del wts, fzs
+    # The same weights as int8 with C0 = 32 (the 32-bit word paths for NCHW).
+    wts8 = [torch.randint(0, 256, (n * c * h * w,), dtype=torch.uint8, device=dev)
+            for _ in range(2)]
+    fzs8 = [torch.empty(c // 32 * h * w * n * 32, dtype=torch.uint8, device=dev)
+            for _ in range(2)]
+    fzb8 = 2 * wts8[0].numel()
+    frz8 = {}
+    for name, fmt, shape in (("NCHW", 0, [n, c, h, w]), ("NHWC", 1, [n, h, w, c]),
+                             ("HWCN", 16, [h, w, c, n])):
+        def to_fz8():
+            for i in range(2):
+                dcopy.to_fractal_z(fzs8[i], wts8[i], fmt, shape, 1, 32)
+
+        def from_fz8():
+            for i in range(2):
+                dcopy.from_fractal_z(wts8[i], fzs8[i], fmt, shape, 1, 32)
+        ms = _time_graph(torch, to_fz8, reps=10) / 2
+        ms2 = _time_graph(torch, from_fz8, reps=10) / 2
+        frz8[name] = [round(fzb8 / (ms / 1e3) / 1e9, 1), round(fzb8 / (ms2 / 1e3) / 1e9, 1)]
+    out["fractal_z_int8_2048x2048x3x3_to_from_GBps"] = frz8
+    del wts8, fzs8
     # Standalone transpose at the 64 MiB maximum (rows 4088 x cols 4104 int32).
     rows, cols = 4088, 4104
     x = torch.empty(rows * cols, dtype=torch.int32, device=dev)
