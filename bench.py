@@ -385,23 +385,25 @@ def run_dcopy(args, rank, world, local_rank):
                                          "scaling; from profiles/ncu_traffic.json",
                          "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)"},
             "cpu_baseline": cpu,
-            "e2e": {"value": round(e2e_value, 3), "unit": "GB/s",
+            "e2e": {"value": round(two_stream_value, 3), "unit": "GB/s",
                     "h2d_bytes_per_step": ROWS * (C1 - C0) * 4,
                     "d2h_bytes_per_step": ROWS * (C1 - C0) * 4,
                     "steps": e2e_steps,
                     "path": "dcopy_copy_ext_staged on pinned host buffers, 16 MiB device "
                             "staging: copy-engine gather of the bursts host -> device in 6 "
                             "chunks, each chunk returned to host memory by the copy engine on "
-                            "a second stream while the next is gathered",
+                            "the library's return stream while the next is gathered; "
+                            "consecutive steps (independent copies) alternate between two "
+                            "caller streams, each with its own staging buffer and destination, "
+                            "so a step's gather overlaps the previous step's return",
+                    "serial_value": round(e2e_value, 3),
+                    "serial_path": "the same call, every step on one stream (each step's "
+                                   "pipeline fills and drains on its own)",
                     "pcie_duplex_ceiling_GBps": pcie["duplex"],
                     "pcie_h2d_GBps": pcie["h2d"], "pcie_d2h_GBps": pcie["d2h"],
-                    "frac_of_duplex_ceiling": round(e2e_value / world / pcie["duplex"], 4),
+                    "frac_of_duplex_ceiling": round(two_stream_value / world / pcie["duplex"], 4),
                     "pcie_note": "ceiling = 16 MiB pinned H2D and D2H cudaMemcpyAsync on two "
                                  "streams at once (per GPU); e2e moves the same bytes each way",
-                    "two_stream_value": round(two_stream_value, 3),
-                    "two_stream_path": "the same call, consecutive steps alternating between two "
-                                       "streams (own staging buffer and destination each), so a "
-                                       "step's gather overlaps the previous step's return",
                     "zero_copy_value": round(zero_copy_value, 3),
                     "zero_copy_path": "dcopy_copy_ext_32b on the pinned host buffers: the kernel "
                                       "reads and writes host memory over PCIe"},
