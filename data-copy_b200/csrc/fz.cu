@@ -669,6 +669,9 @@ __global__ void __launch_bounds__(kThreads) fz_nchw_bulk_kernel(unsigned char *_
 
 // ---- FRACTAL_Z -> NCHW, the mirror of fz_nchw_bulk_kernel -------------------------
 
+#ifndef DCOPY_FZ_FROM_LSU_ROWS
+#define DCOPY_FZ_FROM_LSU_ROWS 0  // 1: the row stage leaves by 16-byte stores of every thread
+#endif
 #ifndef DCOPY_FZ_FROM_ROWS2
 // 1: fz_to_nchw_bulk_kernel alternates two row stages, so a tile's scatter need
 // not wait for the previous tile's row stores to read the stage.  Measured on
@@ -814,14 +817,29 @@ __global__ void __launch_bounds__(kThreads) fz_to_nchw_bulk_kernel(unsigned char
         for (int j = 0; j < V; ++j) rows[at + j * g.HW] = x.e[j];
       }
     }
-    // Generic-proxy writes of the row stage, then bulk stores read it.
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    __syncthreads();
-    if (threadIdx.x < 32) {
-      T *out = dst + (uint64_t)n0 * g.seg_stride + (uint64_t)c1 * g.L;
-      for (uint32_t r = threadIdx.x; r < valid; r += 32)
-        bulk::store(out + (uint64_t)r * g.seg_stride, rows + r * g.P, g.L * EB);
-      bulk::commit();
+    T *out = dst + (uint64_t)n0 * g.seg_stride + (uint64_t)c1 * g.L;
+    if (DCOPY_FZ_FROM_LSU_ROWS) {
+      // Every thread copies 16-byte vectors of the row stage to the rows; the
+      // barrier after the copy frees the stage for the next tile.
+      __syncthreads();
+      const uint32_t vpr = g.L * EB / 16;  // 16-byte vectors per row
+      for (uint32_t u = threadIdx.x; u < valid * vpr; u += kThreads) {
+        const uint32_t r = u / vpr, v = u - r * vpr;
+        *reinterpret_cast<uint4 *>(reinterpret_cast<unsigned char *>(out + (uint64_t)r * g.seg_stride) +
+                                   16 * v) =
+            *reinterpret_cast<const uint4 *>(reinterpret_cast<const unsigned char *>(rows + r * g.P) +
+                                             16 * v);
+      }
+      __syncthreads();
+    } else {
+      // Generic-proxy writes of the row stage, then bulk stores read it.
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncthreads();
+      if (threadIdx.x < 32) {
+        for (uint32_t r = threadIdx.x; r < valid; r += 32)
+          bulk::store(out + (uint64_t)r * g.seg_stride, rows + r * g.P, g.L * EB);
+        bulk::commit();
+      }
     }
   }
   if (!ok) {
