@@ -670,7 +670,13 @@ __global__ void __launch_bounds__(kThreads) fz_nchw_bulk_kernel(unsigned char *_
 // ---- FRACTAL_Z -> NCHW, the mirror of fz_nchw_bulk_kernel -------------------------
 
 #ifndef DCOPY_FZ_FROM_LSU_ROWS
-#define DCOPY_FZ_FROM_LSU_ROWS 0  // 1: the row stage leaves by 16-byte stores of every thread
+// 1: the row stage of fz_to_nchw_bulk_kernel leaves by 16-byte stores of every
+// thread instead of bulk stores issued by one warp, which the next tile had to
+// wait for before reusing the stage.  Measured on B200 (dcopy_bench fz --replay
+// 1, two rounds, GB/s, bulk stores vs 16-byte stores): int8 [2048,2048,3,3]
+// 4087-4091 vs 5141, [4096,2048,3,3] 5097-5106 vs 5210-5212, [2048,1024,5,5]
+// 4648-4650 vs 5067-5072; fp32 [2048,2048,3,3] 5141-5164 vs 5190-5196.
+#define DCOPY_FZ_FROM_LSU_ROWS 1
 #endif
 #ifndef DCOPY_FZ_FROM_ROWS2
 // 1: fz_to_nchw_bulk_kernel alternates two row stages, so a tile's scatter need
