@@ -1114,12 +1114,16 @@ __global__ void __launch_bounds__(kThreads) fz_hwcn_tensor_kernel(unsigned char 
 #define DCOPY_FZ_FP16_WORDS 1
 #endif
 #ifndef DCOPY_FZ_FP16_WORDS_FROM
-// fp16 FRACTAL_Z -> NCHW 3x3 / 5x5 (C0 16): the word scatter instead of the
-// row-vector gather.  Measured the same way: [2048,2048,3,3] 5311-5316 vs
-// 5249-5250, [4096,2048,3,3] 5408-5450 vs 4994-5002, but [1024,2048,3,3]
-// 4311-4312 vs 4574-4585 and 5x5 [2048,1024] 5215-5226 vs 5242-5250, [4096,1024]
-// 5493-5499 vs 5625-5629: not a win across shapes, so off.
-#define DCOPY_FZ_FP16_WORDS_FROM 0
+// fp16 FRACTAL_Z -> NCHW 3x3 / 5x5 (C0 16): the word scatter of
+// fz_to_nchw_bulk_kernel instead of the row-vector gather, when there are at
+// least as many tiles as resident CTAs.  Measured on B200 (dcopy_bench fz
+// --replay 1, two rounds, GB/s against the gather), with the row stage copied
+// out by 16-byte stores: [1024,2048,3,3] 5236-5250 vs 4573-4579,
+// [2048,2048,3,3] 5300-5316 vs 5270-5283, [4096,2048,3,3] 5127-5134 vs
+// 4843-4959, [2048,1024,5,5] 5550-5556 vs 5245, [4096,1024,5,5] 5942-5943 vs
+// 5606-5611.  (With bulk stores out of the row stage it had lost at
+// [1024,2048,3,3] and 5x5.)
+#define DCOPY_FZ_FP16_WORDS_FROM 1
 #endif
 #ifndef DCOPY_FZ_GROUP_TILES
 #define DCOPY_FZ_GROUP_TILES 1  // 0: one group (weight blocks fastest over the whole tensor)
@@ -1458,7 +1462,8 @@ int run_nchw_bulk_from(void *dst, const void *src, int64_t n, int64_t c, int64_t
   if (word_scatter) {
     // The word scatter needs the row pitch at 8 words modulo 32 (what the pitch
     // formula above gives for 32-byte FRACTAL_Z rows).
-    if ((P * eb / 4) % 32 != 8) return DCOPY_OK;
+    if ((P * eb / 4) % 32 != 8)
+      return gather ? launch_from_gather(dst, src, g, eb, c0, hw, nb, s, taken) : DCOPY_OK;
     if (eb == 1) {
       k = hw == 9 ? fz_to_nchw_bulk_kernel<1, 9> : fz_to_nchw_bulk_kernel<1, 25>;
       which = hw == 9 ? 1 : 2;
@@ -1483,7 +1488,8 @@ int run_nchw_bulk_from(void *dst, const void *src, int64_t n, int64_t c, int64_t
   }
   // The word scatter pays only when CTAs get a second tile to overlap with;
   // fewer tiles than resident CTAs stay on the vector kernel.
-  if (word_scatter && ntiles < (uint64_t)per_sm * (uint64_t)sm_count()) return DCOPY_OK;
+  if (word_scatter && ntiles < (uint64_t)per_sm * (uint64_t)sm_count())
+    return gather ? launch_from_gather(dst, src, g, eb, c0, hw, nb, s, taken) : DCOPY_OK;
   *taken = true;
   const uint32_t grid =
       (uint32_t)std::min<uint64_t>(ntiles, (uint64_t)per_sm * (uint64_t)sm_count());
